@@ -1,0 +1,424 @@
+#!/usr/bin/env python
+"""Benchmark of the NeutronGT hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline (`value`): graph-sparse window attention, forward + backward, in edges/s —
+one 65,536-token window per GPU, in-degree ~ Poisson(32) with uniform
+sources (E ~ 2.09M), 8 heads x head_dim 16, bf16, inputs resident in HBM, L2 flushed
+(256 MiB write) between steps.  A step is one fwd+bwd of the rank's window; with N GPUs
+each rank owns its own window (weak scaling) and value = all ranks' edges x K / the
+slowest rank's device time.
+
+The same JSON line carries:
+  e2e          the same metric through the public API (`sparse_attention_bias` + autograd)
+               with pinned host buffers: inputs copied in and outputs/grads copied out
+               every step, CSR build included;
+  roofline     the dominant kernel (backward) against the measured HBM copy bandwidth;
+  cpu_baseline the reference algorithm on the host cores (CPU restatement), bounded sample;
+  ppr          APPNP PPR + top-k over every seed of the config-2 graph (169,343 nodes);
+  clocks       nvidia-smi samples taken during the timed region.
+
+`--impl reference` times the reference's CPU algorithm for the same metric instead
+(rank 0 only).
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+N_TOKENS = 65536
+MEAN_DEG = 32.0
+HEADS = 8
+HEAD_DIM = 16
+L2_FLUSH_BYTES = 256 << 20
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--skip-ppr", action="store_true")
+    p.add_argument("--skip-cpu", action="store_true")
+    return p.parse_args()
+
+
+# ------------------------------------------------------------------------------------
+# distributed plumbing
+# ------------------------------------------------------------------------------------
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def allreduce_max(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def allreduce_sum(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------------------------
+# clocks during the timed region
+# ------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.proc = None
+        self.path = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            self.target = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+        except Exception:
+            self.target = str(device_index)
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.target, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                rows.append((float(parts[0]), float(parts[1]), parts[4:8]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower().startswith("active")})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+def measured_hbm_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic():
+    """Per-launch DRAM bytes from the committed ncu summary (null when absent)."""
+    path = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except Exception:
+        return {}
+
+
+# ------------------------------------------------------------------------------------
+# workload (config 3)
+# ------------------------------------------------------------------------------------
+def make_window(seed: int):
+    from neutrongt_b200 import synthetic
+    rowptr, col = synthetic.poisson_window_csr(N_TOKENS, MEAN_DEG, seed=seed)
+    ei = synthetic.edge_index_from_dst_csr(rowptr, col)
+    g = torch.Generator().manual_seed(1000 + seed)
+    shape = (N_TOKENS, HEADS, HEAD_DIM)
+    q, k, v, dout = (torch.randn(shape, generator=g).to(torch.bfloat16) for _ in range(4))
+    return q, k, v, dout, ei
+
+
+def algorithmic_bytes(n, e, heads=HEADS, dim=HEAD_DIM, elt=2, idx=4):
+    row = heads * dim * elt
+    fwd = e * (2 * row + idx) + n * (2 * row + 4 + 4 * heads + 4)
+    bwd = e * (4 * row + 2 * 4 * heads + 2 * idx) + n * (8 * row + 8 + 8 * heads)
+    return fwd, bwd
+
+
+def cpu_baseline_sample(q, k, v, dout, ei, rows=16384, repeats=3):
+    """The reference algorithm (torch gathers + index_add scatters, fp32) on the host cores."""
+    from oracle import attention as oatt
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    keep = ei[1] < rows
+    sub = ei[:, keep]
+    qf, kf, vf, gf = (t.float() for t in (q, k, v, dout))
+    times = []
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        oatt.sparse_attention_forward(qf, kf, vf, sub)
+        oatt.sparse_attention_backward(qf, kf, vf, sub, gf)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {"value": sub.shape[1] / t, "unit": "edges/s", "cores": threads, "kind": "port",
+            "sample": f"fwd+bwd of the {rows} lowest destination rows of the window ({sub.shape[1]} edges), "
+                      f"fp32, median of {repeats}; oracle/attention.py restates "
+                      "models/gt_dist_node_level_single_window.py:112-179 with the same torch ops"}
+
+
+# ------------------------------------------------------------------------------------
+# our implementation
+# ------------------------------------------------------------------------------------
+def bench_attention(args, rank, world, dev):
+    from neutrongt_b200 import sparse_attention_bias
+    from neutrongt_b200.attention import WindowAttentionBuffers
+    from neutrongt_b200.edge_csr import build_edge_csr
+
+    q_h, k_h, v_h, g_h, ei_h = make_window(seed=rank)
+    n, e = N_TOKENS, ei_h.shape[1]
+    q, k, v, dout, ei = (t.to(dev) for t in (q_h, k_h, v_h, g_h, ei_h))
+    csr = build_edge_csr(ei, n)
+    buf = WindowAttentionBuffers(q, k, v, csr)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    st = torch.cuda.current_stream(dev)
+
+    for _ in range(args.warmup):
+        buf.forward()
+        buf.backward(dout)
+        flush.fill_(1)
+    barrier(world)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    sampler = ClockSampler(dev.index)
+    sampler.start()
+    barrier(world)
+    for i in range(args.steps):
+        flush.fill_(i & 255)
+        ev[i][0].record(st)
+        buf.forward()
+        ev[i][1].record(st)
+        buf.backward(dout)
+        ev[i][2].record(st)
+    barrier(world)
+    clocks = sampler.stop()
+    t_fwd = sum(a.elapsed_time(b) for a, b, _ in ev) / 1e3
+    t_bwd = sum(b.elapsed_time(c) for _, b, c in ev) / 1e3
+    t_rank = t_fwd + t_bwd
+    t_max = allreduce_max(t_rank, world)
+    edges_all = allreduce_sum(float(e), world)
+    value = edges_all * args.steps / t_max
+
+    fwd_bytes, bwd_bytes = algorithmic_bytes(n, e)
+    peak, peak_kind = measured_hbm_peak()
+    avg_fwd, avg_bwd = t_fwd / args.steps, t_bwd / args.steps
+    traffic = ncu_traffic()
+    dom = "bwd" if avg_bwd >= avg_fwd else "fwd"
+    achieved = (bwd_bytes / avg_bwd if dom == "bwd" else fwd_bytes / avg_fwd) / 1e9
+    roofline = {"bound": "hbm", "kernel": "spattn_delta_vec+spattn_bwd_vec" if dom == "bwd" else "spattn_fwd_vec",
+                "achieved": achieved, "peak": peak, "peak_kind": f"{peak_kind} hbm_gbs (burst)", "unit": "GB/s",
+                "frac": achieved / peak, "traffic": traffic.get(dom),
+                "algorithmic_bytes_per_launch": bwd_bytes if dom == "bwd" else fwd_bytes,
+                "fwd": {"ms": avg_fwd * 1e3, "achieved": fwd_bytes / avg_fwd / 1e9, "frac": fwd_bytes / avg_fwd / 1e9 / peak,
+                        "traffic": traffic.get("fwd")},
+                "bwd": {"ms": avg_bwd * 1e3, "achieved": bwd_bytes / avg_bwd / 1e9, "frac": bwd_bytes / avg_bwd / 1e9 / peak,
+                        "traffic": traffic.get("bwd")},
+                "compulsory_bytes": {"fwd": 4 * n * HEADS * HEAD_DIM * 2 + 4 * (n + 1 + e) + 4 * n * HEADS + 4 * n,
+                                     "note": "Q,K,V,O once + CSR + Z + node scores; K/V (33.5 MB) can stay in L2, "
+                                             "so the no-reuse algorithmic bytes and these bracket the DRAM traffic"}}
+
+    # e2e through the public API with pinned host buffers
+    pin = [t.pin_memory() for t in (q_h, k_h, v_h, g_h, ei_h)]
+    outs = [torch.empty((n, HEADS, HEAD_DIM), dtype=torch.bfloat16).pin_memory() for _ in range(4)]
+    ns_h = torch.empty(n, dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        qd, kd, vd, gd, eid = (t.to(dev, non_blocking=True) for t in pin)
+        qd.requires_grad_(True)
+        kd.requires_grad_(True)
+        vd.requires_grad_(True)
+        x, ns = sparse_attention_bias(qd, kd, vd, eid, None)
+        x.backward(gd)
+        for h, d in zip(outs, (x.detach(), qd.grad, kd.grad, vd.grad)):
+            h.copy_(d, non_blocking=True)
+        ns_h[:ns.numel()].copy_(ns, non_blocking=True)
+
+    for _ in range(max(2, args.warmup)):
+        e2e_step()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(st)
+    barrier(world)
+    t_e2e = allreduce_max(e0.elapsed_time(e1) / 1e3, world)
+    h2d = sum(t.numel() * t.element_size() for t in pin)
+    d2h = sum(t.numel() * t.element_size() for t in outs) + 4 * (csr.node_scores_len)
+    e2e = {"value": edges_all * args.steps / t_e2e, "unit": "edges/s", "h2d_bytes_per_step": h2d,
+           "d2h_bytes_per_step": d2h, "ms_per_step": t_e2e / args.steps * 1e3,
+           "path": "neutrongt_b200.sparse_attention_bias + autograd backward, pinned host buffers, "
+                   "CSR built from the copied edge_index every step"}
+    return {"value": value, "ms_per_step": t_max / args.steps * 1e3, "edges": e, "roofline": roofline,
+            "e2e": e2e, "clocks": clocks, "gpu_launches": 3 * args.steps,
+            "host": (q_h, k_h, v_h, g_h, ei_h)}
+
+
+def bench_ppr(args, rank, world, dev):
+    from neutrongt_b200 import personal_pagerank_appnp, synthetic
+    rowptr, col = synthetic.chung_lu_graph(169343, 1166243, seed=0)
+    n = 169343
+    s0, s1 = (n * rank) // world, (n * (rank + 1)) // world
+    csr = {"rowptr": rowptr.to(dev), "col": col.to(dev)}
+    params = dict(alpha=0.15, topk=8, num_iterations=20, iter_topk=8)
+    personal_pagerank_appnp(None, csr_data=csr, device=dev, source_start=s0, source_end=min(s1, s0 + 2000), **params)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    ei, val = personal_pagerank_appnp(None, csr_data=csr, device=dev, source_start=s0, source_end=s1, **params)
+    e1.record()
+    barrier(world)
+    t = allreduce_max(e0.elapsed_time(e1) / 1e3, world)
+    out = {"workload": "config 2 graph (Chung-Lu, 169,343 nodes, 2,332,486 directed edges), every node a seed, "
+                       "alpha 0.15, 20 iterations, top-k 8 per iteration and at the end",
+           "seeds_per_s": n / t, "seconds": t, "entries": int(allreduce_sum(float(ei.shape[1]), world)),
+           "scaling": "strong (seeds split into contiguous source ranges per rank)"}
+    if rank == 0 and not args.skip_cpu:
+        from oracle import ppr as oppr
+        threads = os.cpu_count() or 1
+        sample = 3000
+        st = {}
+        t0 = time.perf_counter()
+        oppr.personal_pagerank_appnp(None, csr_data={"rowptr": rowptr, "col": col}, source_start=0,
+                                     source_end=sample, nthreads=threads, stats=st, **params)
+        tc = time.perf_counter() - t0
+        out["cpu_baseline"] = {"value": sample / tc, "unit": "seeds/s", "cores": threads, "kind": "port",
+                               "sample": f"seeds 0..{sample - 1}, canonical fp64 restatement in C (oracle/appnp_oracle.c)"}
+        # expansions per seed-iteration measured on the sample, for the bytes model
+        touched = st["edges_touched"] / sample
+        out["adjacency_entries_per_seed"] = touched
+        out["achieved_gbs_adjacency_model"] = touched * n * 4 / t / 1e9
+    return out
+
+
+def run_ours(args):
+    rank, world, local = dist_setup()
+    dev = torch.device("cuda", local)
+    res = bench_attention(args, rank, world, dev)
+    ppr = None if args.skip_ppr else bench_ppr(args, rank, world, dev)
+    cpu = None
+    if rank == 0 and not args.skip_cpu:
+        q, k, v, g, ei = res["host"]
+        cpu = cpu_baseline_sample(q, k, v, g, ei)
+    if rank == 0:
+        line = {
+            "metric": "sparse-attn edges/s (fwd+bwd; BASELINE 'GT epoch time (s) & sparse-attn edges/s')",
+            "value": res["value"], "unit": "edges/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": res["ms_per_step"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "BASELINE config 3: isolated graph-sparse attention fwd+bwd, one 65,536-token "
+                                   "window per GPU, in-degree ~ Poisson(32), uniform sources",
+                       "tokens": N_TOKENS, "edges_per_window": res["edges"], "heads": HEADS, "head_dim": HEAD_DIM,
+                       "l2": "flushed between steps (256 MiB write outside the timed events)",
+                       "parallelism": f"independent windows, dp{world}"},
+            "roofline": res["roofline"], "cpu_baseline": cpu, "e2e": res["e2e"], "gpu_launches": res["gpu_launches"],
+            "clocks": res["clocks"], "ppr": ppr,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    torch.set_num_threads(os.cpu_count() or 1)
+    from oracle import attention as oatt
+    q, k, v, g, ei = make_window(seed=0)
+    rows = 8192
+    sub = ei[:, ei[1] < rows]
+    qf, kf, vf, gf = (t.float() for t in (q, k, v, g))
+    for _ in range(max(1, min(args.warmup, 2))):
+        oatt.sparse_attention_forward(qf, kf, vf, sub)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        oatt.sparse_attention_forward(qf, kf, vf, sub)
+        oatt.sparse_attention_backward(qf, kf, vf, sub, gf)
+        times.append(time.perf_counter() - t0)
+    t = sum(times)
+    value = sub.shape[1] * args.steps / t
+    threads = os.cpu_count() or 1
+    line = {"impl": "reference", "metric": "sparse-attn edges/s (fwd+bwd; BASELINE 'GT epoch time (s) & sparse-attn edges/s')",
+            "value": value, "unit": "edges/s", "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": t / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "BASELINE config 3 window, bounded sample: the in-edges of the lowest "
+                                   f"{rows} destination rows ({sub.shape[1]} edges) per step",
+                       "tokens": N_TOKENS, "heads": HEADS, "head_dim": HEAD_DIM},
+            "cpu_baseline": {"value": value, "unit": "edges/s", "cores": threads, "kind": "port",
+                             "sample": f"{sub.shape[1]} edges per step; the reference's torch gather/scatter "
+                                       "algorithm (oracle/attention.py) in fp32 on the host cores"},
+            "e2e": {"value": value, "unit": "edges/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

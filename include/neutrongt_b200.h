@@ -1,0 +1,169 @@
+/*
+ * neutrongt_b200 — C ABI of the B200 (sm_100a) kernels for NeutronGT's hot path.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t, launches
+ * asynchronously on that stream, allocates nothing, and returns an int status
+ * (NGT_OK = 0).  No exception crosses the ABI.  Pointers are device pointers unless a
+ * parameter says "host".  Workspaces are caller-owned; their size comes from the
+ * matching *_workspace_size query.  Entry points are reentrant: they keep no state
+ * between calls.
+ *
+ * Element layout of attention tensors: row-major [n, heads, head_dim] (the reference's
+ * [1, s, H, D] with b == 1, viewed as [s, H, D] at
+ * NeutronGT/models/gt_dist_node_level_single_window.py:125-127).
+ *
+ * Edge convention (as the reference, :130-131): edge_index[0][e] = source = the K/V
+ * row, edge_index[1][e] = destination = the Q row and the aggregation target.
+ */
+#ifndef NEUTRONGT_B200_H
+#define NEUTRONGT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define NGT_API __attribute__((visibility("default")))
+#else
+#define NGT_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *ngt_stream_t; /* == cudaStream_t */
+
+enum ngt_status {
+    NGT_OK = 0,
+    NGT_ERR_INVALID_ARGUMENT = 1, /* null pointer, negative size, bad dtype */
+    NGT_ERR_UNSUPPORTED = 2,      /* shape/dtype combination without a kernel */
+    NGT_ERR_WORKSPACE = 3,        /* workspace smaller than the size query returned */
+    NGT_ERR_CUDA = 4,             /* a CUDA launch or runtime call failed */
+    NGT_ERR_MISALIGNED = 5,       /* a pointer is not 16-byte aligned where required */
+    NGT_ERR_TOO_LARGE = 6         /* a size exceeds the 32-bit index range */
+};
+
+enum ngt_dtype { NGT_F32 = 0, NGT_BF16 = 1 };
+
+/* ABI version (increments on any signature change) and status names. */
+NGT_API int ngt_abi_version(void);
+NGT_API const char *ngt_status_string(int status);
+
+/* ------------------------------------------------------------------------------------
+ * Window edge list -> CSR (destination-major and source-major, stable).
+ *
+ * Replaces the per-edge index/scatter bookkeeping of `CoreAttention.sparse_attention_bias`
+ * (NeutronGT/models/gt_dist_node_level_single_window.py:130-131, 161-178: gathers by
+ * edge_index[0]/[1] and torch_scatter by edge_index[1]) with two CSR views built once
+ * per window.  Ties keep edge order.
+ *
+ *   edge_index      int64 [2, e] (row 0 = src, row 1 = dst), values must lie in [0, n)
+ *   dst_rowptr      int32 [n+1]; dst_src int32 [e]: source of each dst-major slot
+ *   src_rowptr      int32 [n+1]; src_dst int32 [e]: destination of each src-major slot
+ *   src_to_dst_slot int32 [e] (nullable): dst-major slot of each src-major slot
+ *   info            int32 [2]: info[0] = number of out-of-range indices (0 when valid),
+ *                   info[1] = max destination index, or -1 when e == 0
+ * ---------------------------------------------------------------------------------- */
+NGT_API int ngt_edge_csr_workspace_size(int64_t n, int64_t e, size_t *bytes /* host */);
+NGT_API int ngt_edge_csr_build(int64_t n, int64_t e, const int64_t *edge_index, int32_t *dst_rowptr,
+                       int32_t *dst_src, int32_t *src_rowptr, int32_t *src_dst,
+                       int32_t *src_to_dst_slot, int32_t *info, void *workspace,
+                       size_t workspace_bytes, ngt_stream_t stream);
+
+/* ------------------------------------------------------------------------------------
+ * Graph-sparse window attention, forward.
+ *
+ * Replaces `CoreAttention.sparse_attention_bias` forward
+ * (NeutronGT/models/gt_dist_node_level_single_window.py:112-179; same math in
+ * NeutronGT/models/graphormer_dist_node_level.py:67-98) in one fused pass: per edge
+ * score, clamp to [-5, 5], optional bias, exp, and the weighted sum, with no per-edge
+ * tensor in HBM.
+ *
+ *   q, k, v, out    dtype [n, heads, head_dim]
+ *   edge_bias       float [e, heads] in dst-major slot order (nullable) — the gathered
+ *                   attn_bias[0, h, src, dst] of :142-152
+ *   z               float [n, heads]: sum of exp(score) per row and head (saved for the
+ *                   backward; may be null when no backward follows)
+ *   node_scores     float [node_scores_len]: sum over in-edges of the head-mean of
+ *                   exp(score) (:177-178); the reference's length is max(dst) + 1
+ * ---------------------------------------------------------------------------------- */
+NGT_API int ngt_spattn_forward(int dtype, int64_t n, int64_t e, int heads, int head_dim, const void *q,
+                       const void *k, const void *v, const int32_t *dst_rowptr,
+                       const int32_t *dst_src, const float *edge_bias, void *out, float *z,
+                       float *node_scores, int64_t node_scores_len, ngt_stream_t stream);
+
+/* ------------------------------------------------------------------------------------
+ * Graph-sparse window attention, backward (the autograd graph of :130-175 written out).
+ * Atomic-free: dq from the dst-major CSR, dk/dv from the src-major CSR, in one launch
+ * after a per-row delta = <dout, out> pass.
+ *
+ *   delta           float [n, heads] caller-provided scratch
+ *   dq, dk, dv      dtype [n, heads, head_dim], every row written
+ *   src_to_dst_slot required when edge_bias is given
+ *   dedge_bias      float [e, heads] in dst-major slot order (nullable): gradient of the
+ *                   per-edge bias
+ * ---------------------------------------------------------------------------------- */
+NGT_API int ngt_spattn_backward(int dtype, int64_t n, int64_t e, int heads, int head_dim, const void *q,
+                        const void *k, const void *v, const void *out, const void *dout,
+                        const float *z, const int32_t *dst_rowptr, const int32_t *dst_src,
+                        const int32_t *src_rowptr, const int32_t *src_dst,
+                        const int32_t *src_to_dst_slot, const float *edge_bias, float *delta,
+                        void *dq, void *dk, void *dv, float *dedge_bias, ngt_stream_t stream);
+
+/* ------------------------------------------------------------------------------------
+ * Window subgraph (the window's edge list from the global CSR).
+ *
+ * Replaces `_subgraph_from_csr` (NeutronGT/core/node_level_pipeline/window_state.py:92-119):
+ * for each window node i in window order, its global neighbours in CSR order that are in
+ * the window, relabelled to window positions.  Output edge_index [2, E_w] int64 with
+ * row 0 = i (local source) and row 1 = local destination — the same order as the
+ * reference.  Two calls: _count fills out_rowptr [w+1] (int64, out_rowptr[w] = E_w) and
+ * leaves a node map in the workspace; _fill (same workspace, not modified in between)
+ * writes the edges.  info[0] = count of window nodes that are out of range or repeated.
+ * ---------------------------------------------------------------------------------- */
+NGT_API int ngt_window_subgraph_workspace_size(int64_t num_global_nodes, int64_t window_nodes,
+                                       size_t *bytes /* host */);
+NGT_API int ngt_window_subgraph_count(int64_t num_global_nodes, const int64_t *rowptr, const int64_t *col,
+                              const int64_t *nodes, int64_t window_nodes, int64_t *out_rowptr,
+                              int32_t *info, void *workspace, size_t workspace_bytes,
+                              ngt_stream_t stream);
+NGT_API int ngt_window_subgraph_fill(int64_t num_global_nodes, const int64_t *rowptr, const int64_t *col,
+                             const int64_t *nodes, int64_t window_nodes, const int64_t *out_rowptr,
+                             int64_t *out_edge_index, int64_t num_edges, void *workspace,
+                             size_t workspace_bytes, ngt_stream_t stream);
+
+/* ------------------------------------------------------------------------------------
+ * APPNP personalised PageRank with per-iteration top-k pruning.
+ *
+ * Replaces the propagation loop of `personal_pagerank_appnp`
+ * (NeutronGT/core/ppr_backends/appnp_backend.py:259-305): the cuSPARSE SpGEMM of
+ * `csr_spgemm` (NeutronGT/core/ppr_backends/csrc/cusparse_spgemm.cu:65-267, via
+ * appnp_backend.py:165-200), the teleport merge (`_aggregate_sparse_entries`, :68-77) and
+ * the per-row top-k (`_segment_topk_from_csr`, :102-140) become one kernel that keeps
+ * each seed's row on chip.  Values in fp64 with a canonical order: contributions to a
+ * column are added in ascending source column, ties rank by ascending column.
+ *
+ *   rowptr int64 [n+1], col int32 [rowptr[n]]: the graph (P = D^-1 A, D = max(outdeg,1))
+ *   in_rowptr/in_col the transpose (in-adjacency, sources ascending within a row); read only
+ *                   in dense mode, nullable otherwise
+ *   iter_topk       > 0: entries kept per iteration (1..32); <= 0: no pruning (dense mode)
+ *   final_keep      entries kept at the end (1..32 in dense mode; <= 0 keeps all when pruned)
+ *   out_col int64 / out_val float / out_val64 double (nullable): [num_seeds, keep_stride],
+ *   out_cnt int32 [num_seeds]; entries of seed s in (value desc, column asc) order.
+ *   info int32 [1]: count of seeds whose row did not fit the workspace (0 when OK).
+ * ---------------------------------------------------------------------------------- */
+NGT_API int ngt_ppr_workspace_size(int64_t n, int64_t max_degree, int64_t iter_topk, int64_t num_seeds,
+                           size_t *bytes /* host */);
+NGT_API int ngt_ppr_appnp_topk(int64_t n, const int64_t *rowptr, const int32_t *col,
+                       const int64_t *in_rowptr, const int32_t *in_col, double alpha,
+                       int64_t num_iterations, int64_t iter_topk, int64_t final_keep,
+                       int64_t source_start, int64_t source_end, int64_t max_degree,
+                       int64_t keep_stride, int64_t *out_col, float *out_val, double *out_val64,
+                       int32_t *out_cnt, int32_t *info, void *workspace, size_t workspace_bytes,
+                       ngt_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NEUTRONGT_B200_H */

@@ -1,0 +1,700 @@
+// Graph-sparse window attention: fused forward and atomic-free backward (sm_100a).
+//
+// Forward replaces `CoreAttention.sparse_attention_bias`
+// (NeutronGT/models/gt_dist_node_level_single_window.py:112-179).  The reference builds
+// about eight [E, H, D] tensors per layer (gathers, products, exp, messages) and three
+// atomic scatters; here one warp owns one destination row, walks its in-edges from the
+// dst-major CSR, and keeps the score, exp, normaliser and weighted sum in registers, so
+// per-edge values never reach HBM.  HBM traffic per edge is one gathered K row and one
+// gathered V row (plus a 4-byte column index); per row, one Q row in and one output row
+// out.
+//
+// Backward is the reference's autograd graph written out (see oracle/attention.py for the
+// formulas).  It runs as two launches: a per-row delta = <dout, out> pass, then one launch
+// whose first half of blocks walks the dst-major CSR (dq) and whose second half walks the
+// src-major CSR (dk, dv), recomputing scores instead of storing them.  Every output row is
+// written by exactly one warp, so no atomics and no zero-fill are needed, and reruns are
+// bitwise identical.
+//
+// Lane layout of the vector path: a row of H*D elements is ROW_VECS 16-byte vectors.  A
+// group of G = min(ROW_VECS, 32) lanes cooperates on one edge (lane gl owns vectors
+// gl + G*t), so a warp keeps 32/G edges of the same row in flight, times UNROLL.  A head
+// spans HEAD_VECS consecutive lanes; its dot product is reduced with xor shuffles.
+#include "common.cuh"
+
+namespace ngt {
+namespace {
+
+constexpr float kClamp = 5.0f;
+constexpr float kEps = 1e-6f;
+constexpr int kBlock = 256;
+constexpr int kWarpsPerBlock = kBlock / kWarp;
+
+template <typename T, int HEAD_VECS, int ROW_VECS>
+struct VecLayout {
+    static constexpr int G = ROW_VECS < 32 ? ROW_VECS : 32;
+    static constexpr int VPL = ROW_VECS / G;
+    static constexpr int EPW = 32 / G;
+    static constexpr int VE = Elem<T>::kPerVec;
+    static constexpr int UNROLL = VPL >= 4 ? 1 : 4 / VPL;
+    static_assert(ROW_VECS % G == 0, "row vectors must tile the lane group");
+    static_assert(G % HEAD_VECS == 0, "a head must not straddle lane groups");
+};
+
+template <int HEAD_VECS>
+__device__ __forceinline__ float head_reduce(float x) {
+#pragma unroll
+    for (int off = 1; off < HEAD_VECS; off <<= 1) x += __shfl_xor_sync(0xffffffffu, x, off);
+    return x;
+}
+
+// Sum over the EPW edge slots of a warp (lanes with equal gl in different groups).
+template <int G>
+__device__ __forceinline__ float slot_reduce(float x) {
+#pragma unroll
+    for (int off = G; off < 32; off <<= 1) x += __shfl_xor_sync(0xffffffffu, x, off);
+    return x;
+}
+
+// ------------------------------------------------------------------------------------
+// forward (vector path)
+// ------------------------------------------------------------------------------------
+template <typename T, int HEAD_VECS, int ROW_VECS>
+__global__ void __launch_bounds__(kBlock)
+    spattn_fwd_vec(int n, int heads, float scale_inv, const T *__restrict__ q,
+                   const T *__restrict__ k, const T *__restrict__ v,
+                   const int *__restrict__ rowptr, const int *__restrict__ col,
+                   const float *__restrict__ bias, T *__restrict__ out, float *__restrict__ z,
+                   float *__restrict__ node_scores, int ns_len) {
+    using L = VecLayout<T, HEAD_VECS, ROW_VECS>;
+    constexpr int G = L::G, VPL = L::VPL, EPW = L::EPW, VE = L::VE, UNROLL = L::UNROLL;
+    const int lane = lane_id();
+    const int sub = lane / G;
+    const int gl = lane % G;
+    const int row = blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
+    if (row >= n) return;
+
+    const Vec16 *qv = reinterpret_cast<const Vec16 *>(q) + (size_t)row * ROW_VECS + gl;
+    const Vec16 *kv = reinterpret_cast<const Vec16 *>(k) + gl;
+    const Vec16 *vv = reinterpret_cast<const Vec16 *>(v) + gl;
+
+    float qf[VPL][VE];
+#pragma unroll
+    for (int t = 0; t < VPL; t++) Elem<T>::unpack(ldg16(qv + G * t), qf[t]);
+    float acc[VPL][VE];
+    float zs[VPL];
+#pragma unroll
+    for (int t = 0; t < VPL; t++) {
+        zs[t] = 0.f;
+#pragma unroll
+        for (int i = 0; i < VE; i++) acc[t][i] = 0.f;
+    }
+
+    const int beg = __ldg(rowptr + row);
+    const int end = __ldg(rowptr + row + 1);
+    for (int e0 = beg; e0 < end; e0 += EPW * UNROLL) {
+        int src[UNROLL];
+        bool ok[UNROLL];
+#pragma unroll
+        for (int u = 0; u < UNROLL; u++) {
+            const int e = e0 + sub + EPW * u;
+            ok[u] = e < end;
+            src[u] = ok[u] ? __ldg(col + e) : 0;
+        }
+        Vec16 kr[UNROLL][VPL], vr[UNROLL][VPL];
+#pragma unroll
+        for (int u = 0; u < UNROLL; u++) {
+#pragma unroll
+            for (int t = 0; t < VPL; t++) {
+                kr[u][t] = ldg16(kv + (size_t)src[u] * ROW_VECS + G * t);
+                vr[u][t] = ldg16(vv + (size_t)src[u] * ROW_VECS + G * t);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < UNROLL; u++) {
+            const int e = e0 + sub + EPW * u;
+#pragma unroll
+            for (int t = 0; t < VPL; t++) {
+                float kf[VE], vf[VE];
+                Elem<T>::unpack(kr[u][t], kf);
+                float d = 0.f;
+#pragma unroll
+                for (int i = 0; i < VE; i++) d = fmaf(kf[i], qf[t][i], d);
+                d = head_reduce<HEAD_VECS>(d);
+                float s = fminf(fmaxf(d * scale_inv, -kClamp), kClamp);
+                if (bias != nullptr && ok[u]) s += __ldg(bias + (size_t)e * heads + (gl + G * t) / HEAD_VECS);
+                const float p = ok[u] ? expf(s) : 0.f;
+                zs[t] += p;
+                Elem<T>::unpack(vr[u][t], vf);
+#pragma unroll
+                for (int i = 0; i < VE; i++) acc[t][i] = fmaf(p, vf[i], acc[t][i]);
+            }
+        }
+    }
+    if (EPW > 1) {
+#pragma unroll
+        for (int t = 0; t < VPL; t++) {
+            zs[t] = slot_reduce<G>(zs[t]);
+#pragma unroll
+            for (int i = 0; i < VE; i++) acc[t][i] = slot_reduce<G>(acc[t][i]);
+        }
+    }
+    if (sub == 0) {
+        Vec16 *ov = reinterpret_cast<Vec16 *>(out) + (size_t)row * ROW_VECS + gl;
+#pragma unroll
+        for (int t = 0; t < VPL; t++) {
+            const float inv = 1.0f / (zs[t] + kEps);
+            float o[VE];
+#pragma unroll
+            for (int i = 0; i < VE; i++) o[i] = acc[t][i] * inv;
+            st16(ov + G * t, Elem<T>::pack(o));
+            if (z != nullptr && (gl % HEAD_VECS) == 0) z[(size_t)row * heads + (gl + G * t) / HEAD_VECS] = zs[t];
+        }
+    }
+    // node score: head mean of Z (one lane per head contributes through the xor tree)
+    float hs = 0.f;
+#pragma unroll
+    for (int t = 0; t < VPL; t++) hs += zs[t];
+#pragma unroll
+    for (int off = HEAD_VECS; off < G; off <<= 1) hs += __shfl_xor_sync(0xffffffffu, hs, off);
+    if (lane == 0 && row < ns_len) node_scores[row] = hs / (float)heads;
+}
+
+// ------------------------------------------------------------------------------------
+// backward (vector path)
+// ------------------------------------------------------------------------------------
+template <typename T, int HEAD_VECS, int ROW_VECS>
+__global__ void __launch_bounds__(kBlock)
+    spattn_delta_vec(int n, int heads, const T *__restrict__ out, const T *__restrict__ dout,
+                     float *__restrict__ delta) {
+    using L = VecLayout<T, HEAD_VECS, ROW_VECS>;
+    constexpr int G = L::G, VPL = L::VPL, EPW = L::EPW, VE = L::VE;
+    const int lane = lane_id();
+    const int sub = lane / G;
+    const int gl = lane % G;
+    const int row = (blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5)) * EPW + sub;
+    const bool valid = row < n;
+    const size_t base = (size_t)(valid ? row : 0) * ROW_VECS + gl;
+#pragma unroll
+    for (int t = 0; t < VPL; t++) {
+        float a[VE], b[VE];
+        Elem<T>::unpack(ldg16(reinterpret_cast<const Vec16 *>(out) + base + G * t), a);
+        Elem<T>::unpack(ldg16(reinterpret_cast<const Vec16 *>(dout) + base + G * t), b);
+        float d = 0.f;
+#pragma unroll
+        for (int i = 0; i < VE; i++) d = fmaf(a[i], b[i], d);
+        d = head_reduce<HEAD_VECS>(d);
+        if (valid && (gl % HEAD_VECS) == 0) delta[(size_t)row * heads + (gl + G * t) / HEAD_VECS] = d;
+    }
+}
+
+// Blocks [0, blocks_a) : one warp per destination row -> dq.
+// Blocks [blocks_a, .) : one warp per source row      -> dk, dv.
+template <typename T, int HEAD_VECS, int ROW_VECS>
+__global__ void __launch_bounds__(kBlock)
+    spattn_bwd_vec(int n, int heads, float scale_inv, int blocks_a, const T *__restrict__ q,
+                   const T *__restrict__ k, const T *__restrict__ v, const T *__restrict__ dout,
+                   const float *__restrict__ z, const float *__restrict__ delta,
+                   const int *__restrict__ dst_rowptr, const int *__restrict__ dst_src,
+                   const int *__restrict__ src_rowptr, const int *__restrict__ src_dst,
+                   const int *__restrict__ src_to_dst_slot, const float *__restrict__ bias,
+                   T *__restrict__ dq, T *__restrict__ dk, T *__restrict__ dv,
+                   float *__restrict__ dbias) {
+    using L = VecLayout<T, HEAD_VECS, ROW_VECS>;
+    constexpr int G = L::G, VPL = L::VPL, EPW = L::EPW, VE = L::VE, UNROLL = L::UNROLL;
+    const int lane = lane_id();
+    const int sub = lane / G;
+    const int gl = lane % G;
+    const bool role_a = blockIdx.x < blocks_a;
+    const int row = (role_a ? blockIdx.x : blockIdx.x - blocks_a) * kWarpsPerBlock + (threadIdx.x >> 5);
+    if (row >= n) return;
+    const Vec16 *Q = reinterpret_cast<const Vec16 *>(q) + gl;
+    const Vec16 *K = reinterpret_cast<const Vec16 *>(k) + gl;
+    const Vec16 *V = reinterpret_cast<const Vec16 *>(v) + gl;
+    const Vec16 *DO = reinterpret_cast<const Vec16 *>(dout) + gl;
+    const size_t rbase = (size_t)row * ROW_VECS;
+    int head[VPL];
+#pragma unroll
+    for (int t = 0; t < VPL; t++) head[t] = (gl + G * t) / HEAD_VECS;
+
+    if (role_a) {
+        // ---- dq for destination row `row` ----
+        float qf[VPL][VE], gf[VPL][VE], inv[VPL], dl[VPL], acc[VPL][VE];
+#pragma unroll
+        for (int t = 0; t < VPL; t++) {
+            Elem<T>::unpack(ldg16(Q + rbase + G * t), qf[t]);
+            Elem<T>::unpack(ldg16(DO + rbase + G * t), gf[t]);
+            inv[t] = 1.0f / (__ldg(z + (size_t)row * heads + head[t]) + kEps);
+            dl[t] = __ldg(delta + (size_t)row * heads + head[t]);
+#pragma unroll
+            for (int i = 0; i < VE; i++) acc[t][i] = 0.f;
+        }
+        const int beg = __ldg(dst_rowptr + row), end = __ldg(dst_rowptr + row + 1);
+        for (int e0 = beg; e0 < end; e0 += EPW * UNROLL) {
+            int src[UNROLL];
+            bool ok[UNROLL];
+#pragma unroll
+            for (int u = 0; u < UNROLL; u++) {
+                const int e = e0 + sub + EPW * u;
+                ok[u] = e < end;
+                src[u] = ok[u] ? __ldg(dst_src + e) : 0;
+            }
+            Vec16 kr[UNROLL][VPL], vr[UNROLL][VPL];
+#pragma unroll
+            for (int u = 0; u < UNROLL; u++)
+#pragma unroll
+                for (int t = 0; t < VPL; t++) {
+                    kr[u][t] = ldg16(K + (size_t)src[u] * ROW_VECS + G * t);
+                    vr[u][t] = ldg16(V + (size_t)src[u] * ROW_VECS + G * t);
+                }
+#pragma unroll
+            for (int u = 0; u < UNROLL; u++) {
+                const int e = e0 + sub + EPW * u;
+#pragma unroll
+                for (int t = 0; t < VPL; t++) {
+                    float kf[VE], vf[VE];
+                    Elem<T>::unpack(kr[u][t], kf);
+                    Elem<T>::unpack(vr[u][t], vf);
+                    float dqk = 0.f, dgv = 0.f;
+#pragma unroll
+                    for (int i = 0; i < VE; i++) {
+                        dqk = fmaf(kf[i], qf[t][i], dqk);
+                        dgv = fmaf(gf[t][i], vf[i], dgv);
+                    }
+                    dqk = head_reduce<HEAD_VECS>(dqk);
+                    dgv = head_reduce<HEAD_VECS>(dgv);
+                    const float s = dqk * scale_inv;
+                    const bool inside = s >= -kClamp && s <= kClamp;
+                    float sc = fminf(fmaxf(s, -kClamp), kClamp);
+                    if (bias != nullptr && ok[u]) sc += __ldg(bias + (size_t)e * heads + head[t]);
+                    const float p = expf(sc);
+                    const float dpre = (dgv - dl[t]) * inv[t] * p;
+                    const float ds = (ok[u] && inside) ? dpre : 0.f;
+                    if (dbias != nullptr && ok[u] && (gl % HEAD_VECS) == 0) dbias[(size_t)e * heads + head[t]] = dpre;
+#pragma unroll
+                    for (int i = 0; i < VE; i++) acc[t][i] = fmaf(ds, kf[i], acc[t][i]);
+                }
+            }
+        }
+        if (EPW > 1) {
+#pragma unroll
+            for (int t = 0; t < VPL; t++)
+#pragma unroll
+                for (int i = 0; i < VE; i++) acc[t][i] = slot_reduce<G>(acc[t][i]);
+        }
+        if (sub == 0) {
+            Vec16 *o = reinterpret_cast<Vec16 *>(dq) + rbase + gl;
+#pragma unroll
+            for (int t = 0; t < VPL; t++) {
+                float r[VE];
+#pragma unroll
+                for (int i = 0; i < VE; i++) r[i] = acc[t][i] * scale_inv;
+                st16(o + G * t, Elem<T>::pack(r));
+            }
+        }
+    } else {
+        // ---- dk, dv for source row `row` ----
+        float kf[VPL][VE], vf[VPL][VE], ak[VPL][VE], av[VPL][VE];
+#pragma unroll
+        for (int t = 0; t < VPL; t++) {
+            Elem<T>::unpack(ldg16(K + rbase + G * t), kf[t]);
+            Elem<T>::unpack(ldg16(V + rbase + G * t), vf[t]);
+#pragma unroll
+            for (int i = 0; i < VE; i++) ak[t][i] = av[t][i] = 0.f;
+        }
+        const int beg = __ldg(src_rowptr + row), end = __ldg(src_rowptr + row + 1);
+        for (int e0 = beg; e0 < end; e0 += EPW * UNROLL) {
+            int dst[UNROLL];
+            bool ok[UNROLL];
+#pragma unroll
+            for (int u = 0; u < UNROLL; u++) {
+                const int e = e0 + sub + EPW * u;
+                ok[u] = e < end;
+                dst[u] = ok[u] ? __ldg(src_dst + e) : 0;
+            }
+            Vec16 qr[UNROLL][VPL], gr[UNROLL][VPL];
+            float zr[UNROLL][VPL], dr[UNROLL][VPL];
+#pragma unroll
+            for (int u = 0; u < UNROLL; u++)
+#pragma unroll
+                for (int t = 0; t < VPL; t++) {
+                    qr[u][t] = ldg16(Q + (size_t)dst[u] * ROW_VECS + G * t);
+                    gr[u][t] = ldg16(DO + (size_t)dst[u] * ROW_VECS + G * t);
+                    zr[u][t] = __ldg(z + (size_t)dst[u] * heads + head[t]);
+                    dr[u][t] = __ldg(delta + (size_t)dst[u] * heads + head[t]);
+                }
+#pragma unroll
+            for (int u = 0; u < UNROLL; u++) {
+                const int e = e0 + sub + EPW * u;
+#pragma unroll
+                for (int t = 0; t < VPL; t++) {
+                    float qf[VE], gf[VE];
+                    Elem<T>::unpack(qr[u][t], qf);
+                    Elem<T>::unpack(gr[u][t], gf);
+                    float dqk = 0.f, dgv = 0.f;
+#pragma unroll
+                    for (int i = 0; i < VE; i++) {
+                        dqk = fmaf(kf[t][i], qf[i], dqk);
+                        dgv = fmaf(gf[i], vf[t][i], dgv);
+                    }
+                    dqk = head_reduce<HEAD_VECS>(dqk);
+                    dgv = head_reduce<HEAD_VECS>(dgv);
+                    const float s = dqk * scale_inv;
+                    const bool inside = s >= -kClamp && s <= kClamp;
+                    float sc = fminf(fmaxf(s, -kClamp), kClamp);
+                    if (bias != nullptr && ok[u])
+                        sc += __ldg(bias + (size_t)__ldg(src_to_dst_slot + e) * heads + head[t]);
+                    const float p = ok[u] ? expf(sc) : 0.f;
+                    const float inv = 1.0f / (zr[u][t] + kEps);
+                    const float a = p * inv;
+                    const float dpre = (dgv - dr[u][t]) * inv * p;
+                    const float ds = inside ? dpre : 0.f;
+#pragma unroll
+                    for (int i = 0; i < VE; i++) {
+                        av[t][i] = fmaf(a, gf[i], av[t][i]);
+                        ak[t][i] = fmaf(ds, qf[i], ak[t][i]);
+                    }
+                }
+            }
+        }
+        if (EPW > 1) {
+#pragma unroll
+            for (int t = 0; t < VPL; t++)
+#pragma unroll
+                for (int i = 0; i < VE; i++) {
+                    ak[t][i] = slot_reduce<G>(ak[t][i]);
+                    av[t][i] = slot_reduce<G>(av[t][i]);
+                }
+        }
+        if (sub == 0) {
+            Vec16 *ok_ = reinterpret_cast<Vec16 *>(dk) + rbase + gl;
+            Vec16 *ov = reinterpret_cast<Vec16 *>(dv) + rbase + gl;
+#pragma unroll
+            for (int t = 0; t < VPL; t++) {
+                float r[VE];
+#pragma unroll
+                for (int i = 0; i < VE; i++) r[i] = ak[t][i] * scale_inv;
+                st16(ok_ + G * t, Elem<T>::pack(r));
+                st16(ov + G * t, Elem<T>::pack(av[t]));
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------
+// generic scalar path: one thread per (row, head); any head_dim in the instantiated set,
+// any alignment.  Used for shapes the vector layout does not cover (e.g. head_dim 24).
+// ------------------------------------------------------------------------------------
+template <typename T, int D>
+__global__ void __launch_bounds__(kBlock)
+    spattn_fwd_scalar(int n, int heads, float scale_inv, const T *__restrict__ q,
+                      const T *__restrict__ k, const T *__restrict__ v,
+                      const int *__restrict__ rowptr, const int *__restrict__ col,
+                      const float *__restrict__ bias, T *__restrict__ out, float *__restrict__ z) {
+    const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= (int64_t)n * heads) return;
+    const int row = (int)(gid / heads), h = (int)(gid % heads);
+    const size_t rs = (size_t)heads * D;
+    float qf[D], acc[D];
+#pragma unroll
+    for (int i = 0; i < D; i++) {
+        qf[i] = Elem<T>::load1(q + row * rs + h * D + i);
+        acc[i] = 0.f;
+    }
+    float zs = 0.f;
+    for (int e = rowptr[row]; e < rowptr[row + 1]; e++) {
+        const int s_ = col[e];
+        float d = 0.f;
+#pragma unroll
+        for (int i = 0; i < D; i++) d = fmaf(Elem<T>::load1(k + s_ * rs + h * D + i), qf[i], d);
+        float s = fminf(fmaxf(d * scale_inv, -kClamp), kClamp);
+        if (bias != nullptr) s += bias[(size_t)e * heads + h];
+        const float p = expf(s);
+        zs += p;
+#pragma unroll
+        for (int i = 0; i < D; i++) acc[i] = fmaf(p, Elem<T>::load1(v + s_ * rs + h * D + i), acc[i]);
+    }
+    const float inv = 1.0f / (zs + kEps);
+#pragma unroll
+    for (int i = 0; i < D; i++) Elem<T>::store1(out + row * rs + h * D + i, acc[i] * inv);
+    z[(size_t)row * heads + h] = zs;
+}
+
+__global__ void node_scores_from_z(int n, int heads, const float *__restrict__ z,
+                                   float *__restrict__ node_scores, int ns_len) {
+    const int row = blockIdx.x * blockDim.x + threadIdx.x;
+    if (row >= n || row >= ns_len) return;
+    float s = 0.f;
+    for (int h = 0; h < heads; h++) s += z[(size_t)row * heads + h];
+    node_scores[row] = s / (float)heads;
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kBlock)
+    spattn_delta_scalar(int n, int heads, const T *__restrict__ out, const T *__restrict__ dout,
+                        float *__restrict__ delta) {
+    const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= (int64_t)n * heads) return;
+    const size_t base = (size_t)gid * D;
+    float d = 0.f;
+#pragma unroll
+    for (int i = 0; i < D; i++) d = fmaf(Elem<T>::load1(out + base + i), Elem<T>::load1(dout + base + i), d);
+    delta[gid] = d;
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kBlock)
+    spattn_bwd_scalar(int n, int heads, float scale_inv, const T *__restrict__ q,
+                      const T *__restrict__ k, const T *__restrict__ v, const T *__restrict__ dout,
+                      const float *__restrict__ z, const float *__restrict__ delta,
+                      const int *__restrict__ dst_rowptr, const int *__restrict__ dst_src,
+                      const int *__restrict__ src_rowptr, const int *__restrict__ src_dst,
+                      const int *__restrict__ src_to_dst_slot, const float *__restrict__ bias,
+                      T *__restrict__ dq, T *__restrict__ dk, T *__restrict__ dv,
+                      float *__restrict__ dbias) {
+    const int64_t total = (int64_t)n * heads;
+    int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const bool role_a = gid < total;
+    if (!role_a) gid -= total;
+    if (gid >= total) return;
+    const int row = (int)(gid / heads), h = (int)(gid % heads);
+    const size_t rs = (size_t)heads * D;
+    const size_t me = row * rs + h * D;
+    if (role_a) {
+        float qf[D], gf[D], acc[D];
+#pragma unroll
+        for (int i = 0; i < D; i++) {
+            qf[i] = Elem<T>::load1(q + me + i);
+            gf[i] = Elem<T>::load1(dout + me + i);
+            acc[i] = 0.f;
+        }
+        const float inv = 1.0f / (z[gid] + kEps), dl = delta[gid];
+        for (int e = dst_rowptr[row]; e < dst_rowptr[row + 1]; e++) {
+            const size_t o = (size_t)dst_src[e] * rs + h * D;
+            float dqk = 0.f, dgv = 0.f;
+#pragma unroll
+            for (int i = 0; i < D; i++) {
+                dqk = fmaf(Elem<T>::load1(k + o + i), qf[i], dqk);
+                dgv = fmaf(gf[i], Elem<T>::load1(v + o + i), dgv);
+            }
+            const float s = dqk * scale_inv;
+            float sc = fminf(fmaxf(s, -kClamp), kClamp);
+            if (bias != nullptr) sc += bias[(size_t)e * heads + h];
+            const float p = expf(sc);
+            const float dpre = (dgv - dl) * inv * p;
+            if (dbias != nullptr) dbias[(size_t)e * heads + h] = dpre;
+            const float ds = (s >= -kClamp && s <= kClamp) ? dpre : 0.f;
+#pragma unroll
+            for (int i = 0; i < D; i++) acc[i] = fmaf(ds, Elem<T>::load1(k + o + i), acc[i]);
+        }
+#pragma unroll
+        for (int i = 0; i < D; i++) Elem<T>::store1(dq + me + i, acc[i] * scale_inv);
+    } else {
+        float kf[D], vf[D], ak[D], av[D];
+#pragma unroll
+        for (int i = 0; i < D; i++) {
+            kf[i] = Elem<T>::load1(k + me + i);
+            vf[i] = Elem<T>::load1(v + me + i);
+            ak[i] = av[i] = 0.f;
+        }
+        for (int e = src_rowptr[row]; e < src_rowptr[row + 1]; e++) {
+            const int d_ = src_dst[e];
+            const size_t o = (size_t)d_ * rs + h * D;
+            float dqk = 0.f, dgv = 0.f;
+#pragma unroll
+            for (int i = 0; i < D; i++) {
+                dqk = fmaf(kf[i], Elem<T>::load1(q + o + i), dqk);
+                dgv = fmaf(Elem<T>::load1(dout + o + i), vf[i], dgv);
+            }
+            const float s = dqk * scale_inv;
+            float sc = fminf(fmaxf(s, -kClamp), kClamp);
+            if (bias != nullptr) sc += bias[(size_t)src_to_dst_slot[e] * heads + h];
+            const float p = expf(sc);
+            const float inv = 1.0f / (z[(size_t)d_ * heads + h] + kEps);
+            const float a = p * inv;
+            const float dpre = (dgv - delta[(size_t)d_ * heads + h]) * inv * p;
+            const float ds = (s >= -kClamp && s <= kClamp) ? dpre : 0.f;
+#pragma unroll
+            for (int i = 0; i < D; i++) {
+                const float gq = Elem<T>::load1(q + o + i), gd = Elem<T>::load1(dout + o + i);
+                av[i] = fmaf(a, gd, av[i]);
+                ak[i] = fmaf(ds, gq, ak[i]);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < D; i++) {
+            Elem<T>::store1(dk + me + i, ak[i] * scale_inv);
+            Elem<T>::store1(dv + me + i, av[i]);
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------
+// dispatch
+// ------------------------------------------------------------------------------------
+struct Shape {
+    int head_vecs = 0, row_vecs = 0;
+};
+
+template <typename T>
+Shape vec_shape(int heads, int head_dim) {
+    Shape s;
+    const int hb = head_dim * (int)sizeof(T);
+    if (hb % 16 != 0) return s;
+    const int hv = hb / 16;
+    const int rv = hv * heads;
+    auto pow2 = [](int x) { return x > 0 && (x & (x - 1)) == 0; };
+    if (!pow2(hv) || hv > 8 || !pow2(rv) || rv < 2 || rv > 128) return s;
+    s.head_vecs = hv;
+    s.row_vecs = rv;
+    return s;
+}
+
+#define NGT_VEC_CASES(MACRO)                                                                   \
+    MACRO(1, 2) MACRO(1, 4) MACRO(1, 8) MACRO(1, 16) MACRO(1, 32) MACRO(1, 64) MACRO(1, 128)  \
+    MACRO(2, 2) MACRO(2, 4) MACRO(2, 8) MACRO(2, 16) MACRO(2, 32) MACRO(2, 64) MACRO(2, 128)  \
+    MACRO(4, 4) MACRO(4, 8) MACRO(4, 16) MACRO(4, 32) MACRO(4, 64) MACRO(4, 128)               \
+    MACRO(8, 8) MACRO(8, 16) MACRO(8, 32) MACRO(8, 64) MACRO(8, 128)
+
+#define NGT_SCALAR_DIMS(MACRO) MACRO(4) MACRO(8) MACRO(12) MACRO(16) MACRO(24) MACRO(32) MACRO(48) MACRO(64)
+
+template <typename T>
+int forward_t(int64_t n, int heads, int head_dim, const void *q, const void *k, const void *v,
+              const int32_t *rowptr, const int32_t *col, const float *bias, void *out, float *z,
+              float *ns, int64_t ns_len, cudaStream_t st) {
+    const float scale_inv = 1.0f / sqrtf((float)head_dim);
+    const Shape sh = vec_shape<T>(heads, head_dim);
+    const bool al = aligned16(q) && aligned16(k) && aligned16(v) && aligned16(out);
+    if (n == 0) return NGT_OK;
+    if (sh.head_vecs && al) {
+        const int grid = ceil_div_i(n, kWarpsPerBlock);
+#define NGT_FWD(HV, RV)                                                                          \
+    if (sh.head_vecs == HV && sh.row_vecs == RV) {                                               \
+        spattn_fwd_vec<T, HV, RV><<<grid, kBlock, 0, st>>>(                                      \
+            (int)n, heads, scale_inv, (const T *)q, (const T *)k, (const T *)v, rowptr, col,     \
+            bias, (T *)out, z, ns, (int)ns_len);                                                 \
+        NGT_CHECK_LAUNCH();                                                                      \
+        return NGT_OK;                                                                           \
+    }
+        NGT_VEC_CASES(NGT_FWD)
+#undef NGT_FWD
+    }
+    if (z == nullptr) return NGT_ERR_INVALID_ARGUMENT;  // the scalar path derives scores from z
+    const int grid = ceil_div_i(n * heads, kBlock);
+#define NGT_FWDS(DD)                                                                                 \
+    if (head_dim == DD) {                                                                            \
+        spattn_fwd_scalar<T, DD><<<grid, kBlock, 0, st>>>((int)n, heads, scale_inv, (const T *)q,    \
+                                                          (const T *)k, (const T *)v, rowptr, col,   \
+                                                          bias, (T *)out, z);                        \
+        NGT_CHECK_LAUNCH();                                                                          \
+        node_scores_from_z<<<ceil_div_i(n, kBlock), kBlock, 0, st>>>((int)n, heads, z, ns, (int)ns_len); \
+        NGT_CHECK_LAUNCH();                                                                          \
+        return NGT_OK;                                                                               \
+    }
+    NGT_SCALAR_DIMS(NGT_FWDS)
+#undef NGT_FWDS
+    return NGT_ERR_UNSUPPORTED;
+}
+
+template <typename T>
+int backward_t(int64_t n, int heads, int head_dim, const void *q, const void *k, const void *v,
+               const void *out, const void *dout, const float *z, const int32_t *dst_rowptr,
+               const int32_t *dst_src, const int32_t *src_rowptr, const int32_t *src_dst,
+               const int32_t *s2d, const float *bias, float *delta, void *dq, void *dk, void *dv,
+               float *dbias, cudaStream_t st) {
+    const float scale_inv = 1.0f / sqrtf((float)head_dim);
+    if (n == 0) return NGT_OK;
+    const Shape sh = vec_shape<T>(heads, head_dim);
+    const bool al = aligned16(q) && aligned16(k) && aligned16(v) && aligned16(out) &&
+                    aligned16(dout) && aligned16(dq) && aligned16(dk) && aligned16(dv);
+    if (sh.head_vecs && al) {
+        const int blocks_a = ceil_div_i(n, kWarpsPerBlock);
+#define NGT_BWD(HV, RV)                                                                           \
+    if (sh.head_vecs == HV && sh.row_vecs == RV) {                                                \
+        using Lay = VecLayout<T, HV, RV>;                                                         \
+        spattn_delta_vec<T, HV, RV><<<ceil_div_i(n, (int64_t)kWarpsPerBlock * Lay::EPW), kBlock, 0, st>>>( \
+            (int)n, heads, (const T *)out, (const T *)dout, delta);                               \
+        NGT_CHECK_LAUNCH();                                                                       \
+        spattn_bwd_vec<T, HV, RV><<<2 * blocks_a, kBlock, 0, st>>>(                               \
+            (int)n, heads, scale_inv, blocks_a, (const T *)q, (const T *)k, (const T *)v,         \
+            (const T *)dout, z, delta, dst_rowptr, dst_src, src_rowptr, src_dst, s2d, bias,       \
+            (T *)dq, (T *)dk, (T *)dv, dbias);                                                    \
+        NGT_CHECK_LAUNCH();                                                                       \
+        return NGT_OK;                                                                            \
+    }
+        NGT_VEC_CASES(NGT_BWD)
+#undef NGT_BWD
+    }
+    const int grid1 = ceil_div_i(n * heads, kBlock);
+#define NGT_BWDS(DD)                                                                              \
+    if (head_dim == DD) {                                                                         \
+        spattn_delta_scalar<T, DD><<<grid1, kBlock, 0, st>>>((int)n, heads, (const T *)out,       \
+                                                             (const T *)dout, delta);             \
+        NGT_CHECK_LAUNCH();                                                                       \
+        spattn_bwd_scalar<T, DD><<<2 * grid1, kBlock, 0, st>>>(                                   \
+            (int)n, heads, scale_inv, (const T *)q, (const T *)k, (const T *)v, (const T *)dout,  \
+            z, delta, dst_rowptr, dst_src, src_rowptr, src_dst, s2d, bias, (T *)dq, (T *)dk,      \
+            (T *)dv, dbias);                                                                      \
+        NGT_CHECK_LAUNCH();                                                                       \
+        return NGT_OK;                                                                            \
+    }
+    NGT_SCALAR_DIMS(NGT_BWDS)
+#undef NGT_BWDS
+    return NGT_ERR_UNSUPPORTED;
+}
+
+int check_common(int dtype, int64_t n, int64_t e, int heads, int head_dim) {
+    if (n < 0 || e < 0 || heads <= 0 || head_dim <= 0) return NGT_ERR_INVALID_ARGUMENT;
+    if (dtype != NGT_F32 && dtype != NGT_BF16) return NGT_ERR_INVALID_ARGUMENT;
+    if (n >= (int64_t)INT32_MAX || e >= (int64_t)INT32_MAX) return NGT_ERR_TOO_LARGE;
+    if (n * heads >= (int64_t)INT32_MAX) return NGT_ERR_TOO_LARGE;
+    return NGT_OK;
+}
+
+}  // namespace
+}  // namespace ngt
+
+using namespace ngt;
+
+extern "C" int ngt_spattn_forward(int dtype, int64_t n, int64_t e, int heads, int head_dim,
+                                  const void *q, const void *k, const void *v,
+                                  const int32_t *dst_rowptr, const int32_t *dst_src,
+                                  const float *edge_bias, void *out, float *z, float *node_scores,
+                                  int64_t node_scores_len, ngt_stream_t stream) {
+    int rc = check_common(dtype, n, e, heads, head_dim);
+    if (rc != NGT_OK) return rc;
+    if (n > 0 && (!q || !k || !v || !dst_rowptr || !out)) return NGT_ERR_INVALID_ARGUMENT;
+    if (e > 0 && !dst_src) return NGT_ERR_INVALID_ARGUMENT;
+    if (node_scores_len < 0 || node_scores_len > n || (node_scores_len > 0 && !node_scores))
+        return NGT_ERR_INVALID_ARGUMENT;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (dtype == NGT_F32)
+        return forward_t<float>(n, heads, head_dim, q, k, v, dst_rowptr, dst_src, edge_bias, out, z,
+                                node_scores, node_scores_len, st);
+    return forward_t<__nv_bfloat16>(n, heads, head_dim, q, k, v, dst_rowptr, dst_src, edge_bias, out,
+                                    z, node_scores, node_scores_len, st);
+}
+
+extern "C" int ngt_spattn_backward(int dtype, int64_t n, int64_t e, int heads, int head_dim,
+                                   const void *q, const void *k, const void *v, const void *out,
+                                   const void *dout, const float *z, const int32_t *dst_rowptr,
+                                   const int32_t *dst_src, const int32_t *src_rowptr,
+                                   const int32_t *src_dst, const int32_t *src_to_dst_slot,
+                                   const float *edge_bias, float *delta, void *dq, void *dk,
+                                   void *dv, float *dedge_bias, ngt_stream_t stream) {
+    int rc = check_common(dtype, n, e, heads, head_dim);
+    if (rc != NGT_OK) return rc;
+    if (n > 0 && (!q || !k || !v || !out || !dout || !z || !dst_rowptr || !src_rowptr || !delta ||
+                  !dq || !dk || !dv))
+        return NGT_ERR_INVALID_ARGUMENT;
+    if (e > 0 && (!dst_src || !src_dst)) return NGT_ERR_INVALID_ARGUMENT;
+    if (edge_bias != nullptr && e > 0 && src_to_dst_slot == nullptr) return NGT_ERR_INVALID_ARGUMENT;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (dtype == NGT_F32)
+        return backward_t<float>(n, heads, head_dim, q, k, v, out, dout, z, dst_rowptr, dst_src,
+                                 src_rowptr, src_dst, src_to_dst_slot, edge_bias, delta, dq, dk, dv,
+                                 dedge_bias, st);
+    return backward_t<__nv_bfloat16>(n, heads, head_dim, q, k, v, out, dout, z, dst_rowptr, dst_src,
+                                     src_rowptr, src_dst, src_to_dst_slot, edge_bias, delta, dq, dk,
+                                     dv, dedge_bias, st);
+}

@@ -1,0 +1,88 @@
+"""Per-window CSR views of an attention edge list, built on the device and cached.
+
+The reference indexes Q/K/V by `edge_index` and scatters by destination on every call
+(`NeutronGT/models/gt_dist_node_level_single_window.py:130-178`).  The kernels here
+read two CSR views instead — destination-major (forward, dq) and source-major
+(dk, dv) — built once per edge-list tensor by `ngt_edge_csr_build` and reused by every
+layer of the window's forward and backward.
+
+The cache is keyed by the edge_index tensor object itself (weak reference) plus its
+version counter and the node count, so a freed tensor whose memory is reused can never
+hit a stale entry, and an in-place edit invalidates it.
+"""
+from __future__ import annotations
+
+import weakref
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+
+
+@dataclass
+class EdgeCSR:
+    n: int
+    e: int
+    dst_rowptr: torch.Tensor      # int32 [n+1]
+    dst_src: torch.Tensor         # int32 [e]
+    src_rowptr: torch.Tensor      # int32 [n+1]
+    src_dst: torch.Tensor         # int32 [e]
+    src_to_dst_slot: torch.Tensor  # int32 [e]
+    max_dst: int                  # -1 when e == 0
+
+    @property
+    def node_scores_len(self) -> int:
+        """torch_scatter's output length without dim_size: max(index) + 1 (0 if empty)."""
+        return self.max_dst + 1
+
+    def dst_major_pairs(self):
+        """(src, dst) int64 of every dst-major slot, for gathering per-edge tensors."""
+        counts = (self.dst_rowptr[1:] - self.dst_rowptr[:-1]).to(torch.long)
+        dst = torch.repeat_interleave(torch.arange(self.n, device=counts.device), counts)
+        return self.dst_src.to(torch.long), dst
+
+
+def build_edge_csr(edge_index: torch.Tensor, n: int) -> EdgeCSR:
+    _lib.require_cuda(edge_index)
+    if edge_index.dim() != 2 or edge_index.shape[0] != 2:
+        raise ValueError(f"edge_index must be [2, E], got {tuple(edge_index.shape)}")
+    ei = edge_index.to(torch.long).contiguous()
+    e = int(ei.shape[1])
+    dev = ei.device
+    L = _lib.lib()
+    nbytes = _lib.size_query(L.ngt_edge_csr_workspace_size, n, e)
+    ws = _lib.workspace(nbytes, dev)
+    i32 = dict(dtype=torch.int32, device=dev)
+    dst_rowptr = torch.empty(n + 1, **i32)
+    src_rowptr = torch.empty(n + 1, **i32)
+    dst_src = torch.empty(e, **i32)
+    src_dst = torch.empty(e, **i32)
+    s2d = torch.empty(e, **i32)
+    info = torch.empty(2, **i32)
+    _lib.check(L.ngt_edge_csr_build(n, e, _lib.ptr(ei), _lib.ptr(dst_rowptr), _lib.ptr(dst_src),
+                                    _lib.ptr(src_rowptr), _lib.ptr(src_dst), _lib.ptr(s2d),
+                                    _lib.ptr(info), _lib.ptr(ws), ws.numel(), _lib.stream_of(ei)),
+               "ngt_edge_csr_build")
+    bad, max_dst = (int(x) for x in info.tolist())
+    if bad:
+        raise IndexError(f"edge_index holds {bad} entries outside [0, {n})")
+    return EdgeCSR(n, e, dst_rowptr, dst_src, src_rowptr, src_dst, s2d, max_dst)
+
+
+_cache: "weakref.WeakKeyDictionary[torch.Tensor, tuple]" = weakref.WeakKeyDictionary()
+
+
+def edge_csr_for(edge_index: torch.Tensor, n: int) -> EdgeCSR:
+    """Cached `build_edge_csr` for this edge_index tensor object."""
+    key = (edge_index._version, int(n))
+    hit = _cache.get(edge_index)
+    if hit is not None and hit[0] == key:
+        return hit[1]
+    csr = build_edge_csr(edge_index, n)
+    _cache[edge_index] = (key, csr)
+    return csr
+
+
+def clear_cache() -> None:
+    _cache.clear()

@@ -1,0 +1,48 @@
+"""The C-ABI library loads and exports every symbol include/neutrongt_b200.h declares (no GPU)."""
+import os
+import re
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "neutrongt_b200.h")
+
+
+def _declared():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^NGT_API\s+(?:int|const char \*)\s*(ngt_\w+)\(", text, flags=re.M)))
+
+
+def test_header_declares_the_entry_points():
+    names = _declared()
+    assert "ngt_spattn_forward" in names and "ngt_ppr_appnp_topk" in names
+    assert len(names) >= 11
+
+
+def test_library_exports_every_declared_symbol():
+    from neutrongt_b200 import _lib
+    lib = _lib.lib()
+    for name in _declared():
+        assert hasattr(lib, name), name
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_version_status_and_size_queries():
+    from neutrongt_b200 import _lib
+    lib = _lib.lib()
+    assert lib.ngt_abi_version() == 1
+    assert _lib.status_name(0) == "NGT_OK"
+    assert _lib.status_name(3) == "NGT_ERR_WORKSPACE"
+    assert _lib.size_query(lib.ngt_edge_csr_workspace_size, 65536, 2_000_000) > 2_000_000 * 28
+    assert _lib.size_query(lib.ngt_window_subgraph_workspace_size, 169343, 10000) >= 169343 * 4
+    # pruned PPR on a hub-heavy graph reserves per-CTA overflow tables
+    assert _lib.size_query(lib.ngt_ppr_workspace_size, 169343, 11702, 8, 169343) > 100 * 2**20
+
+
+def test_invalid_arguments_are_rejected_without_a_gpu():
+    import ctypes
+
+    from neutrongt_b200 import _lib
+    lib = _lib.lib()
+    out = ctypes.c_size_t(0)
+    assert lib.ngt_edge_csr_workspace_size(-1, 5, ctypes.byref(out)) == 1
+    assert lib.ngt_spattn_forward(7, 1, 1, 8, 8, *([None] * 9), 0, None) == 1   # bad dtype

@@ -1,0 +1,208 @@
+"""Sparse window attention on the GPU against the reference fixtures and the CPU oracle.
+
+Tolerances (from the build's parity contract): outputs and gradients within 1e-5
+relative error in float32 and 2e-2 in bfloat16, measured as max|a-b| / max|b|.
+"""
+import math
+
+import pytest
+import torch
+
+from conftest import golden, rel_err
+from oracle import attention as oatt
+
+pytestmark = pytest.mark.gpu
+
+F32_TOL = 1e-5
+BF16_TOL = 2e-2
+
+
+def _ours(q, k, v, ei, bias=None, dout=None, device="cuda"):
+    from neutrongt_b200 import sparse_attention_bias
+    qd = q.to(device).requires_grad_(True)
+    kd = k.to(device).requires_grad_(True)
+    vd = v.to(device).requires_grad_(True)
+    bd = bias.to(device).requires_grad_(True) if bias is not None else None
+    x, ns = sparse_attention_bias(qd, kd, vd, ei.to(device), bd)
+    grads = None
+    if dout is not None:
+        (x.float() * dout.to(device).float().reshape(x.shape)).sum().backward()
+        grads = (qd.grad, kd.grad, vd.grad, None if bd is None else bd.grad)
+    return x, ns, grads
+
+
+@pytest.mark.parametrize("case", ["slim_d8", "gt_d16_clamp", "bias_h4", "empty"])
+def test_matches_reference_fixture(cuda, case):
+    g = golden(f"attention_{case}.pt")
+    x, ns, (dq, dk, dv, db) = _ours(g["q"], g["k"], g["v"], g["edge_index"], g["attn_bias"], g["dout"])
+    s, H, D = g["s"], g["H"], g["D"]
+    assert x.shape == (s, H, D) and x.dtype == torch.float32
+    assert ns.shape == g["node_scores64"].shape
+    assert rel_err(x, g["x64"]) < F32_TOL
+    assert rel_err(ns, g["node_scores64"]) < F32_TOL
+    assert rel_err(dq.reshape(1, s, H, D), g["dq64"]) < F32_TOL
+    assert rel_err(dk.reshape(1, s, H, D), g["dk64"]) < F32_TOL
+    assert rel_err(dv.reshape(1, s, H, D), g["dv64"]) < F32_TOL
+    if g["attn_bias"] is not None:
+        assert rel_err(db, g["dbias64"]) < F32_TOL
+
+
+def _random_case(s, E, H, D, seed, scale=1.0, heavy=0):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(s, H, D, generator=g) * scale
+    k = torch.randn(s, H, D, generator=g) * scale
+    v = torch.randn(s, H, D, generator=g)
+    dout = torch.randn(s, H, D, generator=g)
+    src = torch.randint(0, s, (E,), generator=g)
+    dst = torch.randint(0, s, (E,), generator=g)
+    if heavy:
+        dst[:heavy] = 0   # one power-law style row
+    return q, k, v, dout, torch.stack([src, dst])
+
+
+SHAPES = [  # (H, D): vector path (GT, GPH_Slim, config 3), small heads, and the scalar path
+    (8, 16), (8, 8), (4, 8), (8, 4), (32, 24), (8, 24), (2, 64), (1, 32),
+]
+
+
+@pytest.mark.parametrize("H,D", SHAPES)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_against_oracle(cuda, H, D, dtype):
+    q, k, v, dout, ei = _random_case(300, 4000, H, D, seed=H * 100 + D, scale=1.7, heavy=600)
+    q, k, v = (t.to(dtype) for t in (q, k, v))
+    x, ns, (dq, dk, dv, _) = _ours(q, k, v, ei, dout=dout)
+    rx, rns, _, _ = oatt.sparse_attention_forward(q.double(), k.double(), v.double(), ei)
+    rdq, rdk, rdv, _ = oatt.sparse_attention_backward(q.double(), k.double(), v.double(), ei,
+                                                      dout.to(dtype).double())
+    tol = F32_TOL if dtype == torch.float32 else BF16_TOL
+    assert x.dtype == dtype
+    assert rel_err(x, rx) < tol
+    assert rel_err(ns, rns) < tol
+    assert rel_err(dq, rdq) < tol
+    assert rel_err(dk, rdk) < tol
+    assert rel_err(dv, rdv) < tol
+
+
+def test_rows_without_edges_and_short_node_scores(cuda):
+    q, k, v, dout, _ = _random_case(40, 1, 8, 16, seed=5)
+    ei = torch.tensor([[3, 4, 5, 3], [1, 1, 7, 7]])
+    x, ns, (dq, dk, dv, _) = _ours(q, k, v, ei, dout=dout)
+    assert ns.shape == (8,)                       # max(dst) + 1, as torch_scatter gives
+    assert torch.count_nonzero(x[8:]) == 0 and torch.count_nonzero(x[0]) == 0
+    assert torch.count_nonzero(dq[8:]) == 0
+    assert torch.count_nonzero(dk[[0, 1, 2] + list(range(6, 40))]) == 0
+    rx, rns, _, _ = oatt.sparse_attention_forward(q.double(), k.double(), v.double(), ei)
+    assert rel_err(x, rx) < F32_TOL and rel_err(ns, rns) < F32_TOL
+
+
+def test_empty_edge_list(cuda):
+    q, k, v, dout, _ = _random_case(10, 1, 8, 8, seed=6)
+    x, ns, (dq, dk, dv, _) = _ours(q, k, v, torch.empty(2, 0, dtype=torch.long), dout=dout)
+    assert ns.numel() == 0
+    for t in (x, dq, dk, dv):
+        assert torch.count_nonzero(t) == 0
+
+
+def test_single_node_self_loop(cuda):
+    q, k, v, dout, _ = _random_case(1, 1, 8, 16, seed=7)
+    x, ns, (dq, dk, dv, _) = _ours(q, k, v, torch.tensor([[0, 0], [0, 0]]), dout=dout)
+    rx, rns, _, _ = oatt.sparse_attention_forward(q.double(), k.double(), v.double(), torch.tensor([[0, 0], [0, 0]]))
+    assert rel_err(x, rx) < F32_TOL and rel_err(ns, rns) < F32_TOL
+
+
+def test_bitwise_deterministic(cuda):
+    q, k, v, dout, ei = _random_case(2000, 60000, 8, 16, seed=8, heavy=5000)
+    a = _ours(q, k, v, ei, dout=dout)
+    b = _ours(q, k, v, ei, dout=dout)
+    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+    for ga, gb in zip(a[2][:3], b[2][:3]):
+        assert torch.equal(ga, gb)
+
+
+def test_int32_edge_index_and_4d_inputs(cuda):
+    q, k, v, dout, ei = _random_case(100, 900, 8, 8, seed=9)
+    x1, ns1, _ = _ours(q.unsqueeze(0), k.unsqueeze(0), v.unsqueeze(0), ei.to(torch.int32))
+    x2, ns2, _ = _ours(q, k, v, ei)
+    assert torch.equal(x1, x2) and torch.equal(ns1, ns2)
+
+
+def test_out_of_range_index_raises(cuda):
+    from neutrongt_b200 import sparse_attention_bias
+    q = torch.randn(5, 8, 8, device="cuda")
+    with pytest.raises(IndexError):
+        sparse_attention_bias(q, q, q, torch.tensor([[0, 5], [1, 2]], device="cuda"), None)
+
+
+def test_cached_kv_concat_gradients(cuda):
+    """K/V assembled as cat(detached cache, fresh rows), as `…single_window.py:279-283` does."""
+    from neutrongt_b200 import sparse_attention_bias
+    q, k, v, dout, ei = _random_case(64, 700, 8, 16, seed=10)
+    n_dup = 20
+    qd = q.cuda().requires_grad_(True)
+    kd = k[n_dup:].cuda().requires_grad_(True)
+    vd = v[n_dup:].cuda().requires_grad_(True)
+    kk = torch.cat([k[:n_dup].cuda(), kd])
+    vv = torch.cat([v[:n_dup].cuda(), vd])
+    x, _ = sparse_attention_bias(qd.unsqueeze(0), kk.unsqueeze(0), vv.unsqueeze(0), ei.cuda(), None)
+    (x * dout.cuda()).sum().backward()
+    _, rdk, rdv, _ = oatt.sparse_attention_backward(q.double(), k.double(), v.double(), ei, dout.double())
+    assert rel_err(kd.grad, rdk[n_dup:]) < F32_TOL
+    assert rel_err(vd.grad, rdv[n_dup:]) < F32_TOL
+
+
+def test_core_attention_forward_shape(cuda):
+    from neutrongt_b200 import CoreAttention
+    q, k, v, _, ei = _random_case(50, 300, 8, 8, seed=11)
+    attn = CoreAttention(64, 0.5, 8)
+    x, score = attn(q.unsqueeze(0).cuda(), k.unsqueeze(0).cuda(), v.unsqueeze(0).cuda(), None, ei.cuda(), "sparse")
+    assert x.shape == (1, 50, 64)
+    rx, rns, _, _ = oatt.sparse_attention_forward(q.double(), k.double(), v.double(), ei)
+    assert rel_err(x.reshape(50, 8, 8), rx) < F32_TOL
+
+
+# ---------------- full-size window: size-independent properties ----------------
+
+def _config3(device):
+    from neutrongt_b200 import synthetic
+    rowptr, col = synthetic.poisson_window_csr(65536, 32.0, seed=0)
+    ei = synthetic.edge_index_from_dst_csr(rowptr, col)
+    g = torch.Generator(device=device).manual_seed(0)
+    shape = (65536, 8, 16)
+    mk = lambda: torch.randn(shape, generator=g, device=device).to(torch.bfloat16)  # noqa: E731
+    return mk(), mk(), mk(), mk(), ei.to(device)
+
+
+def test_config3_properties(cuda):
+    from neutrongt_b200 import sparse_attention_bias
+    q, k, v, dout, ei = _config3(cuda)
+    qd, kd, vd = (t.clone().requires_grad_(True) for t in (q, k, v))
+    x, ns = sparse_attention_bias(qd, kd, vd, ei, None)
+    x.backward(dout)
+    # 1) forward + dq on 256 random destination rows: their in-edges fully determine them
+    rows = torch.randperm(65536, generator=torch.Generator().manual_seed(1))[:256].to(cuda)
+    keep = torch.isin(ei[1], rows)
+    sub = ei[:, keep].cpu()
+    rx, rns, _, _ = oatt.sparse_attention_forward(q.double().cpu(), k.double().cpu(), v.double().cpu(), sub)
+    rdq, _, _, _ = oatt.sparse_attention_backward(q.double().cpu(), k.double().cpu(), v.double().cpu(), sub,
+                                                  dout.double().cpu())
+    r = rows.cpu()
+    assert rel_err(x[rows], rx[r]) < BF16_TOL
+    assert rel_err(ns[rows], rns[r]) < BF16_TOL
+    assert rel_err(qd.grad[rows], rdq[r]) < BF16_TOL
+    # 2) checksum identities that tie the dst-major and src-major passes together:
+    #    sum_j dv_j = sum_d Z_d/(Z_d+eps) dO_d   and   sum_d <dq_d,q_d> = sum_j <dk_j,k_j> (per head)
+    from neutrongt_b200.edge_csr import edge_csr_for
+    csr = edge_csr_for(ei, 65536)
+    z = torch.zeros(65536, 8, dtype=torch.float64, device=cuda)
+    src, dst = ei[0], ei[1]
+    s_raw = (k[src].double() * q[dst].double()).sum(-1) / math.sqrt(16)
+    p = torch.exp(s_raw.clamp(-5, 5))
+    z.index_add_(0, dst, p)
+    w = z / (z + 1e-6)
+    lhs = vd.grad.double().sum(0)
+    rhs = (w.unsqueeze(-1) * dout.double()).sum(0)
+    assert rel_err(lhs, rhs) < BF16_TOL
+    a = (qd.grad.double() * q.double()).sum(-1).sum(0)
+    b = (kd.grad.double() * k.double()).sum(-1).sum(0)
+    assert rel_err(a, b) < BF16_TOL
+    assert csr.e == ei.shape[1]
