@@ -152,6 +152,8 @@ __device__ int block_merge_topk(TopList<KMAX> &L, int k, MergeSmem &ms, int *out
 struct PrunedSmem {
     int keys[kSmemSlots];
     double vals[kSmemSlots];
+    int touched[kSmemSlots / 2];  // slots claimed this iteration (clear + scan list)
+    int ntouched;
     int st_col[32];      // state sorted by column (expansion order)
     double st_val[32];
     int sel_col[32];     // last selection in rank order
@@ -172,12 +174,22 @@ __global__ void __launch_bounds__(kPprThreads)
                       int source_start, int source_end, int keep_stride, int64_t *__restrict__ out_col,
                       float *__restrict__ out_val, double *__restrict__ out_val64,
                       int *__restrict__ out_cnt, int *__restrict__ info, int *__restrict__ seed_counter,
-                      int *__restrict__ gkeys, double *__restrict__ gvals, int64_t gcap) {
+                      int *__restrict__ gkeys, double *__restrict__ gvals, int *__restrict__ gtouched,
+                      int64_t gcap) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     PrunedSmem &S = *reinterpret_cast<PrunedSmem *>(smem_raw);
     const int tid = threadIdx.x;
     int *my_gkeys = gkeys ? gkeys + (size_t)blockIdx.x * gcap : nullptr;
     double *my_gvals = gvals ? gvals + (size_t)blockIdx.x * gcap : nullptr;
+    int *my_gtouched = gtouched ? gtouched + (size_t)blockIdx.x * (gcap / 2) : nullptr;
+    // tables start empty (the host clears the workspace regions); after every iteration
+    // only the claimed slots are reset, so clearing and scanning cost O(unique columns)
+    for (int s = tid; s < kSmemSlots; s += kPprThreads) {
+        S.keys[s] = kEmpty;
+        S.vals[s] = 0.0;
+    }
+    if (tid == 0) S.ntouched = 0;
+    __syncthreads();
 
     for (;;) {
         if (tid == 0) S.seed = atomicAdd(seed_counter, 1) + source_start;
@@ -202,26 +214,23 @@ __global__ void __launch_bounds__(kPprThreads)
             }
             __syncthreads();
             const int64_t need = 2 * (S.lsum + 1);
-            int *keys;
+            int *keys, *touched;
             double *vals;
             uint32_t cap = 64;
             while ((int64_t)cap < need) cap <<= 1;
             if ((int64_t)cap <= kSmemSlots) {
                 keys = S.keys;
                 vals = S.vals;
+                touched = S.touched;
             } else if (my_gkeys != nullptr && (int64_t)cap <= gcap) {
                 keys = my_gkeys;
                 vals = my_gvals;
+                touched = my_gtouched;
             } else {
                 overflow = true;
                 break;
             }
             const uint32_t mask = cap - 1;
-            for (uint32_t s = tid; s < cap; s += kPprThreads) {
-                keys[s] = kEmpty;
-                vals[s] = 0.0;
-            }
-            __syncthreads();
             const int st_n = S.st_n;
             for (int i = 0; i < st_n; i++) {
                 const int j = S.st_col[i];
@@ -234,6 +243,7 @@ __global__ void __launch_bounds__(kPprThreads)
                     uint32_t slot = hash_slot(c, mask);
                     for (uint32_t probe = 0; probe <= mask; probe++) {
                         const int prev = atomicCAS(keys + slot, kEmpty, c);
+                        if (prev == kEmpty) touched[atomicAdd(&S.ntouched, 1)] = (int)slot;
                         if (prev == kEmpty || prev == c) break;
                         slot = (slot + 1) & mask;
                     }
@@ -245,21 +255,30 @@ __global__ void __launch_bounds__(kPprThreads)
                 uint32_t slot = hash_slot(seed, mask);
                 for (uint32_t probe = 0; probe <= mask; probe++) {
                     const int prev = atomicCAS(keys + slot, kEmpty, seed);
+                    if (prev == kEmpty) touched[S.ntouched++] = (int)slot;
                     if (prev == kEmpty || prev == seed) break;
                     slot = (slot + 1) & mask;
                 }
             }
             __syncthreads();
+            const int nt = S.ntouched;
             TopList<KMAX> L;
             L.init();
-            for (uint32_t s = tid; s < cap; s += kPprThreads) {
+            for (int i = tid; i < nt; i += kPprThreads) {
+                const int s = touched[i];
                 const int c = keys[s];
-                if (c == kEmpty) continue;
                 double v = __dmul_rn(vals[s], oma);
                 if (c == seed) v = __dadd_rn(v, alpha);
                 L.offer(v, c);
             }
             const int cnt = block_merge_topk<KMAX>(L, iter_topk, S.ms, S.sel_col, S.sel_val);
+            for (int i = tid; i < nt; i += kPprThreads) {  // leave the table empty again
+                const int s = touched[i];
+                keys[s] = kEmpty;
+                vals[s] = 0.0;
+            }
+            __syncthreads();
+            if (tid == 0) S.ntouched = 0;
             if (tid == 0) {
                 // next state: the selection sorted by column (insertion sort, <= 32 entries)
                 for (int i = 0; i < cnt; i++) {
@@ -390,6 +409,7 @@ struct PprWs {
     int *counter;
     int *gkeys;
     double *gvals;
+    int *gtouched;
     double *gx;
     unsigned char *gp;
     int64_t gcap;
@@ -413,6 +433,7 @@ PprWs carve_ppr(void *base, int64_t n, int64_t max_degree, int64_t iter_topk, in
         if (w.gcap > kSmemSlots) {
             w.gkeys = reinterpret_cast<int *>(take(sizeof(int) * (size_t)(ctas * w.gcap)));
             w.gvals = reinterpret_cast<double *>(take(sizeof(double) * (size_t)(ctas * w.gcap)));
+            w.gtouched = reinterpret_cast<int *>(take(sizeof(int) * (size_t)(ctas * (w.gcap / 2))));
         } else {
             w.gcap = 0;
         }
@@ -459,6 +480,11 @@ extern "C" int ngt_ppr_appnp_topk(int64_t n, const int64_t *rowptr, const int32_
     cudaMemsetAsync(info, 0, sizeof(int32_t), st);
     cudaMemsetAsync(w.counter, 0, sizeof(int), st);
     if (num_seeds == 0) return NGT_OK;
+    if (!dense && w.gkeys != nullptr) {
+        const int64_t c = num_seeds < kMaxCtas ? num_seeds : kMaxCtas;
+        cudaMemsetAsync(w.gkeys, 0xff, sizeof(int) * (size_t)(c * w.gcap), st);   // kEmpty
+        cudaMemsetAsync(w.gvals, 0, sizeof(double) * (size_t)(c * w.gcap), st);
+    }
     const int ctas = (int)(num_seeds < kMaxCtas ? num_seeds : kMaxCtas);
     const double oma = 1.0 - alpha;
     const int fk = (int)(final_keep > 0 ? final_keep : 0);
@@ -475,7 +501,7 @@ extern "C" int ngt_ppr_appnp_topk(int64_t n, const int64_t *rowptr, const int32_
         ppr_pruned_kernel<KM><<<ctas, kPprThreads, sm, st>>>(                                      \
             (int)n, rowptr, col, alpha, oma, (int)num_iterations, (int)k, fk, (int)source_start,   \
             (int)source_end, (int)keep_stride, out_col, out_val, out_val64, out_cnt, info,         \
-            w.counter, w.gkeys, w.gvals, w.gcap);                                                  \
+            w.counter, w.gkeys, w.gvals, w.gtouched, w.gcap);                                      \
     }                                                                                              \
     NGT_CHECK_LAUNCH();                                                                            \
     return NGT_OK;

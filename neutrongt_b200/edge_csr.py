@@ -70,17 +70,26 @@ def build_edge_csr(edge_index: torch.Tensor, n: int) -> EdgeCSR:
     return EdgeCSR(n, e, dst_rowptr, dst_src, src_rowptr, src_dst, s2d, max_dst)
 
 
-_cache: "weakref.WeakKeyDictionary[torch.Tensor, tuple]" = weakref.WeakKeyDictionary()
+# id(edge_index) -> (weak reference to it, (version, n), csr).  Identity is checked through
+# the weak reference, never with tensor ==; the entry leaves when the tensor is freed.
+_cache: dict = {}
 
 
 def edge_csr_for(edge_index: torch.Tensor, n: int) -> EdgeCSR:
     """Cached `build_edge_csr` for this edge_index tensor object."""
+    k = id(edge_index)
     key = (edge_index._version, int(n))
-    hit = _cache.get(edge_index)
-    if hit is not None and hit[0] == key:
-        return hit[1]
+    hit = _cache.get(k)
+    if hit is not None and hit[0]() is edge_index and hit[1] == key:
+        return hit[2]
     csr = build_edge_csr(edge_index, n)
-    _cache[edge_index] = (key, csr)
+
+    def _drop(ref, k=k):
+        cur = _cache.get(k)
+        if cur is not None and cur[0] is ref:
+            del _cache[k]
+
+    _cache[k] = (weakref.ref(edge_index, _drop), key, csr)
     return csr
 
 

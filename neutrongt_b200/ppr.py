@@ -82,6 +82,11 @@ def personal_pagerank_appnp(edge_index, alpha, topk=100, num_iterations: int = 1
         return empty
     if n >= 2**31 - 1 or col.numel() >= 2**31 - 1:
         raise RuntimeError("graph exceeds the int32 index range of the PPR kernel")
+    # the kernel indexes rowptr by every column it meets: reject malformed graphs up front
+    if int(rowptr[0].item()) != 0 or int(rowptr[-1].item()) != col.numel() or bool((rowptr[1:] < rowptr[:-1]).any()):
+        raise ValueError("CSR rowptr must start at 0, be non-decreasing and end at col.numel()")
+    if col.numel() and (int(col.min().item()) < 0 or int(col.max().item()) >= n):
+        raise ValueError(f"CSR col holds indices outside [0, {n})")
     T, s0, s1, it, final_keep = normalize_args(n, topk, num_iterations, iter_topk, source_start, source_end)
     if s0 >= s1:
         return empty
