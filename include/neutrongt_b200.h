@@ -111,6 +111,36 @@ NGT_API int ngt_spattn_backward(int dtype, int64_t n, int64_t e, int heads, int 
                         void *dq, void *dk, void *dv, float *dedge_bias, ngt_stream_t stream);
 
 /* ------------------------------------------------------------------------------------
+ * Graph-sparse window attention, backward, allocating nothing.  No counterpart in the
+ * reference: an extra entry point of this library.
+ *
+ * Same arguments and results as ngt_spattn_backward minus `delta`: the n * heads floats of
+ * per-row scratch come from a fixed array inside the library (NGT_NOALLOC_MAX_ROWS_X_HEADS
+ * floats = 8 MiB, reserved on every GPU that loads the library until the process exits).
+ * For callers that cannot allocate device memory where they run the backward — e.g. code
+ * running inside a fixed memory budget with no allocator handle, or host runtimes that do
+ * not own a CUDA allocator and may not call cudaMalloc mid-step.  The caller still passes
+ * every input and output buffer.
+ *
+ *   - n * heads above NGT_NOALLOC_MAX_ROWS_X_HEADS returns NGT_ERR_TOO_LARGE, before any work.
+ *   - The first call on a device looks up the array's device address with that device
+ *     current (the current device must be the one the pointers live on); make that first
+ *     call before any stream capture.
+ *   - Every call shares the one array.  Each call writes all the scratch it reads, so no
+ *     clearing is needed, but calls that overlap on the GPU (other streams, other threads)
+ *     race on it: serialise them.
+ * ---------------------------------------------------------------------------------- */
+#define NGT_NOALLOC_MAX_ROWS_X_HEADS 2097152
+NGT_API int ngt_spattn_backward_noalloc(int dtype, int64_t n, int64_t e, int heads, int head_dim,
+                                        const void *q, const void *k, const void *v,
+                                        const void *out, const void *dout, const float *z,
+                                        const int32_t *dst_rowptr, const int32_t *dst_src,
+                                        const int32_t *src_rowptr, const int32_t *src_dst,
+                                        const int32_t *src_to_dst_slot, const float *edge_bias,
+                                        void *dq, void *dk, void *dv, float *dedge_bias,
+                                        ngt_stream_t stream);
+
+/* ------------------------------------------------------------------------------------
  * Window subgraph (the window's edge list from the global CSR).
  *
  * Replaces `_subgraph_from_csr` (NeutronGT/core/node_level_pipeline/window_state.py:92-119):

@@ -20,6 +20,8 @@
 // group of G = min(ROW_VECS, 32) lanes cooperates on one edge (lane gl owns vectors
 // gl + G*t), so a warp keeps 32/G edges of the same row in flight, times UNROLL.  A head
 // spans HEAD_VECS consecutive lanes; its dot product is reduced with xor shuffles.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace ngt {
@@ -697,4 +699,57 @@ extern "C" int ngt_spattn_backward(int dtype, int64_t n, int64_t e, int heads, i
     return backward_t<__nv_bfloat16>(n, heads, head_dim, q, k, v, out, dout, z, dst_rowptr, dst_src,
                                      src_rowptr, src_dst, src_to_dst_slot, edge_bias, delta, dq, dk,
                                      dv, dedge_bias, st);
+}
+
+// ------------------------------------------------------------------------------------
+// Backward without any allocation: the per-row delta scratch lives in a fixed
+// file-scope device array instead of a caller buffer.  For callers that cannot call
+// cudaMalloc (or a caching allocator) at the point where they run the backward.
+// ------------------------------------------------------------------------------------
+namespace {
+
+// n * heads floats of delta scratch; every GPU that loads the library keeps this much
+// (8 MiB) reserved until the process exits.
+static __device__ __align__(256) float g_noalloc_delta[NGT_NOALLOC_MAX_ROWS_X_HEADS];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float *g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of g_noalloc_delta on the current device.  The host-side name is only a
+// stand-in for the symbol, so the address is looked up once per device, with that device
+// current, and cached.
+int noalloc_delta(float **out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return NGT_ERR_CUDA;
+    if (dev < 0 || dev >= kMaxDevices) return NGT_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_ptr[dev] == nullptr) {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_noalloc_delta) != cudaSuccess || p == nullptr) return NGT_ERR_CUDA;
+        g_noalloc_ptr[dev] = static_cast<float *>(p);
+    }
+    *out = g_noalloc_ptr[dev];
+    return NGT_OK;
+}
+
+}  // namespace
+
+extern "C" int ngt_spattn_backward_noalloc(int dtype, int64_t n, int64_t e, int heads, int head_dim,
+                                           const void *q, const void *k, const void *v,
+                                           const void *out, const void *dout, const float *z,
+                                           const int32_t *dst_rowptr, const int32_t *dst_src,
+                                           const int32_t *src_rowptr, const int32_t *src_dst,
+                                           const int32_t *src_to_dst_slot, const float *edge_bias,
+                                           void *dq, void *dk, void *dv, float *dedge_bias,
+                                           ngt_stream_t stream) {
+    int rc = check_common(dtype, n, e, heads, head_dim);
+    if (rc != NGT_OK) return rc;
+    if (n * (int64_t)heads > (int64_t)NGT_NOALLOC_MAX_ROWS_X_HEADS) return NGT_ERR_TOO_LARGE;
+    float *delta = nullptr;
+    rc = noalloc_delta(&delta);
+    if (rc != NGT_OK) return rc;
+    return ngt_spattn_backward(dtype, n, e, heads, head_dim, q, k, v, out, dout, z, dst_rowptr, dst_src,
+                               src_rowptr, src_dst, src_to_dst_slot, edge_bias, delta, dq, dk, dv,
+                               dedge_bias, stream);
 }
