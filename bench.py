@@ -34,6 +34,7 @@ import subprocess
 import sys
 import tempfile
 import time
+from types import SimpleNamespace
 
 import torch
 
@@ -55,6 +56,7 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--skip-ppr", action="store_true")
+    p.add_argument("--skip-epoch", action="store_true")
     p.add_argument("--skip-cpu", action="store_true")
     return p.parse_args()
 
@@ -311,9 +313,114 @@ def bench_attention(args, rank, world, dev):
             "host": (q_h, k_h, v_h, g_h, ei_h)}
 
 
+_GRAPH = {}
+
+
+def config2_graph():
+    """BASELINE config 2 graph: Chung-Lu, 169,343 nodes, 1,166,243 undirected edges (seed 0)."""
+    if "g" not in _GRAPH:
+        from neutrongt_b200 import synthetic
+        _GRAPH["g"] = synthetic.chung_lu_graph(169343, 1166243, seed=0)
+    return _GRAPH["g"]
+
+
+def gt_model(dev):
+    from neutrongt_b200.models import GT_SW
+    torch.manual_seed(0)
+    return GT_SW(n_layers=4, num_heads=8, input_dim=128, hidden_dim=128, output_dim=40, attn_bias_dim=1,
+                 dropout_rate=0.3, input_dropout_rate=0.1, attention_dropout_rate=0.5, ffn_dim=128, num_global_node=1,
+                 args=SimpleNamespace(struct_enc="False"), num_in_degree=0, num_out_degree=0, num_spatial=7,
+                 num_edges=512, max_dist=5, edge_dim=64).to(dev)
+
+
+def bench_gt_epoch(args, rank, world, dev, warm=2, epochs=5):
+    """GT (4 layers, hidden 128, 8 heads, fp32) training epochs over 16 windows."""
+    from neutrongt_b200 import synthetic
+    from neutrongt_b200.train import FlatGradients, build_window_state, train_epoch
+    n = 169343
+    rowptr, col = config2_graph()
+    feature = synthetic.node_features(n, 128, seed=1)
+    y = synthetic.node_labels(n, 40, seed=2)
+    split = synthetic.split_idx(n, seed=3)
+    parts = synthetic.random_partitions(n, 16, seed=0)
+    model = gt_model(dev)
+    grads = FlatGradients(model)
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-4, weight_decay=0.01, fused=True)
+    sched = torch.optim.lr_scheduler.LambdaLR(opt, lambda e: 1.0)
+    a = SimpleNamespace(use_cache=1, attn_type="sparse")
+    feat_dev = feature.to(dev)
+    ws = build_window_state(rowptr, col, parts, rank, world, feat_dev, dev, split)
+
+    def run(feat, k):
+        out = []
+        for _ in range(k):
+            barrier(world)
+            loss, _, _, st = train_epoch(a, model, ws.local_partition_ids, ws.local_partitions, feat, y, opt, sched,
+                                         world, split, dev, 0, ws, grads=grads)
+            out.append((st["epoch_train_total_time"], loss))
+        return out
+
+    run(feat_dev, warm)
+    timed = run(feat_dev, epochs)
+    t_dev = allreduce_max(statistics.mean(t for t, _ in timed), world)
+    run(feature, 1)
+    timed_h = run(feature, epochs)
+    t_host = allreduce_max(statistics.mean(t for t, _ in timed_h), world)
+    e_local = sum(int(e.shape[1]) for e in ws.local_sub_edge_index_for_partition_results)
+    n_local = sum(int(p.numel()) for p in ws.local_partitions)
+    edges_epoch = allreduce_sum(float(e_local), world)
+    out = {"workload": "BASELINE config 2: GT 4L/128/8H fp32, Chung-Lu 169,343 nodes / 1,166,243 undirected "
+                       "edges, 16 seeded random windows (pymetis absent), features N(0,1) dim 128, 40 classes",
+           "epoch_time_s": t_dev, "unit": "s", "higher_is_better": False,
+           "scaling": "strong (16 windows split round-robin over ranks)",
+           "epoch_time_host_features_s": t_host,
+           "loss_last_epoch": timed[-1][1], "windows": len(parts), "window_nodes_mean": n_local / max(1, len(ws.local_partitions)),
+           "attention_edges_per_epoch": edges_epoch,
+           "note": "device-resident features for epoch_time_s; epoch_time_host_features_s gathers each window's "
+                   "features on the host and copies them through pinned memory, as the reference does per window"}
+    if rank == 0 and not args.skip_cpu:
+        out["cpu_baseline"] = gt_epoch_cpu_baseline(model, ws, feature, y, split, len(parts))
+    return out
+
+
+def gt_epoch_cpu_baseline(model_gpu, ws, feature, y, split, n_windows, sample=2):
+    """The same GT model and loop on the host cores, attention = the reference algorithm restated
+    on the CPU (oracle/attention.py, differentiable torch ops); epoch time from a window sample."""
+    import copy
+    import torch.nn.functional as F
+    from oracle import attention as oatt
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    model = copy.deepcopy(model_gpu).cpu()
+
+    def attn(q, k, v, ei, bias):
+        x, ns, _, _ = oatt.sparse_attention_forward(q, k, v, ei, bias)
+        return x, ns
+
+    for layer in model.layers:
+        layer.self_attention.local_attn.sparse_attention_bias = attn
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-4, weight_decay=0.01)
+    train = split["train"]
+    times = []
+    for i in range(min(sample, len(ws.local_partitions))):
+        idx = ws.local_partitions[i]
+        ei = ws.local_sub_edge_index_for_partition_results[i].cpu()
+        t0 = time.perf_counter()
+        out, _, _, _ = model(feature[idx], None, ei, None, None, None, None, attn_type="sparse")
+        mask = torch.isin(idx, train)
+        loss = F.nll_loss(out, y[idx], reduction="none")[mask].mean()
+        opt.zero_grad(set_to_none=True)
+        loss.backward()
+        opt.step()
+        times.append(time.perf_counter() - t0)
+    per_window = statistics.mean(times)
+    return {"value": per_window * n_windows, "unit": "s per epoch (window sample x windows)", "cores": threads,
+            "kind": "port", "sample": f"{len(times)} windows fwd+bwd+AdamW on the host, scaled to {n_windows} windows"}
+
+
 def bench_ppr(args, rank, world, dev):
-    from neutrongt_b200 import personal_pagerank_appnp, synthetic
-    rowptr, col = synthetic.chung_lu_graph(169343, 1166243, seed=0)
+    from neutrongt_b200 import personal_pagerank_appnp
+    rowptr, col = config2_graph()
     n = 169343
     s0, s1 = (n * rank) // world, (n * (rank + 1)) // world
     csr = {"rowptr": rowptr.to(dev), "col": col.to(dev)}
@@ -353,6 +460,7 @@ def run_ours(args):
     dev = torch.device("cuda", local)
     res = bench_attention(args, rank, world, dev)
     ppr = None if args.skip_ppr else bench_ppr(args, rank, world, dev)
+    epoch = None if args.skip_epoch else bench_gt_epoch(args, rank, world, dev)
     cpu = None
     if rank == 0 and not args.skip_cpu:
         q, k, v, g, ei = res["host"]
@@ -369,7 +477,7 @@ def run_ours(args):
                        "l2": "flushed between steps (256 MiB write outside the timed events)",
                        "parallelism": f"independent windows, dp{world}"},
             "roofline": res["roofline"], "cpu_baseline": cpu, "e2e": res["e2e"], "gpu_launches": res["gpu_launches"],
-            "clocks": res["clocks"], "ppr": ppr,
+            "clocks": res["clocks"], "gt_epoch": epoch, "ppr": ppr,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

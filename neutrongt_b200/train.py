@@ -1,0 +1,188 @@
+"""Window-parallel training loop: the caller of the sparse attention.
+
+`train_epoch` keeps the signature and semantics of the reference's
+`NeutronGT/core/node_level_pipeline/train_eval.py:197-343`: every rank walks its own
+windows; a rank with fewer windows takes zero-gradient steps so all ranks take the same
+number of all-reduces (`:211-217, 284-285`); per window: gather features, forward,
+masked NLL on the window's train nodes, backward, gradients averaged over ranks
+(`:289-295`), optimizer step; the scheduler steps once per epoch.  It returns
+`(loss_mean, scores_by_pid, kv_cache_per_partition, time_stats)`.
+
+Changes of mechanism (not of results):
+* window edge lists stay on the device (built once by `window.subgraph_from_csr`), so
+  the per-step host->device copy of `edge_index` (`:244`) disappears, and the window's
+  CSR views are built once and reused by every layer and epoch;
+* features are gathered on the device when the feature matrix lives there; a host feature
+  matrix is gathered on the host and copied through a pinned staging buffer;
+* gradients live in one flat buffer (each parameter's .grad is a view of it), so the
+  average over ranks is one NCCL all-reduce per step instead of one per parameter;
+* the window losses stay on the device and are read once per epoch, and the per-stage
+  `torch.cuda.synchronize()` calls used for wall-clock timing are replaced by CUDA events.
+
+`build_window_state` produces the per-rank fields the loop reads from the reference's
+`StructInfo` (`struct_info.py:16-36`): round-robin window assignment (`window_state.py:210`),
+duplicate-first ordering and the duplicate-feature cache (`window_state.py:52-73, 181-205`),
+and window edge lists (`window_state.py:122-140`).
+"""
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+
+from .window import compute_local_duplicate_nodes, subgraph_from_csr
+
+
+@dataclass
+class WindowState:
+    local_partition_ids: list
+    local_partitions: list
+    local_sub_edge_index_for_partition_results: list
+    local_dup_indices: list
+    local_dup_nodes_per_partition_feature: torch.Tensor
+    local_train_masks: list = field(default_factory=list)
+    graph_in_degree: torch.Tensor | None = None
+    graph_out_degree: torch.Tensor | None = None
+    local_spatial_pos_by_pid: list = field(default_factory=list)
+
+
+def build_window_state(rowptr, col, partitions, rank, world_size, feature, device, split_idx=None,
+                       use_cache=True) -> WindowState:
+    ids = list(range(rank, len(partitions), world_size))
+    parts = [partitions[p].to(torch.long).cpu() for p in ids]
+    dups = [torch.empty(0, dtype=torch.long) for _ in parts]
+    if use_cache:
+        parts, dups = compute_local_duplicate_nodes(parts)
+    nonempty = [d for d in dups if d.numel() > 0]
+    if nonempty:
+        dup_sorted = torch.unique(torch.cat(nonempty), sorted=True)
+        dup_idx = [torch.searchsorted(dup_sorted, d).to(device) for d in dups]
+        dup_feat = feature[dup_sorted.to(feature.device)].to(device)
+    else:
+        dup_idx = [torch.empty(0, dtype=torch.long, device=device) for _ in dups]
+        dup_feat = feature.new_empty((0, feature.shape[1]), device=device)
+    rp, cl = rowptr.to(device), col.to(device)
+    edges = [subgraph_from_csr(p, rp, cl, device=device) for p in parts]
+    masks = []
+    if split_idx is not None:
+        train = split_idx["train"].to(device)
+        masks = [torch.isin(p.to(device), train) for p in parts]
+    return WindowState(ids, parts, edges, dup_idx, dup_feat, masks)
+
+
+class FlatGradients:
+    """All parameters' gradients as views of one flat buffer (one all-reduce per step)."""
+
+    def __init__(self, model: torch.nn.Module):
+        self.params = [p for p in model.parameters() if p.requires_grad]
+        total = sum(p.numel() for p in self.params)
+        dev = self.params[0].device
+        self.flat = torch.zeros(total, dtype=self.params[0].dtype, device=dev)
+        off = 0
+        for p in self.params:
+            p.grad = self.flat[off:off + p.numel()].view_as(p)
+            off += p.numel()
+
+    def zero(self):
+        self.flat.zero_()
+
+    def average(self, world_size: int, group=None):
+        if world_size > 1:
+            self.flat.div_(world_size)
+            dist.all_reduce(self.flat, op=dist.ReduceOp.SUM, group=group)
+
+
+def _window_features(feature, idx_i, dup_index_i, dup_cache, device, staging=None):
+    n_dup = int(dup_index_i.numel())
+    rest = idx_i[n_dup:]
+    if feature.device == torch.device(device) or feature.is_cuda:
+        x = feature[rest.to(feature.device)].to(device)
+    else:
+        host = feature[rest]
+        if staging is not None:
+            buf = staging(host.shape, host.dtype)
+            buf.copy_(host)
+            x = buf.to(device, non_blocking=True)
+        else:
+            x = host.to(device)
+    if n_dup > 0:
+        x = torch.cat([dup_cache[dup_index_i], x], dim=0)
+    return x
+
+
+def train_epoch(args, model, local_partition_ids, local_partitions, feature, y, optimizer, lr_scheduler,
+                world_size, split_idx, device, epoch, structInfo, grads: FlatGradients | None = None,
+                group=None):
+    model.train()
+    edges = structInfo.local_sub_edge_index_for_partition_results
+    dup_idx = structInfo.local_dup_indices
+    dup_cache = structInfo.local_dup_nodes_per_partition_feature
+    masks = getattr(structInfo, "local_train_masks", None) or []
+    use_cache = bool(getattr(args, "use_cache", 1))
+    if grads is None:
+        grads = FlatGradients(model)
+    local_count = len(local_partitions)
+    max_steps = local_count
+    if world_size > 1:
+        t = torch.tensor([local_count], device=device, dtype=torch.long)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+        max_steps = int(t.item())
+    device = torch.device(device)
+    y_dev = y.to(device)
+    on_gpu = device.type == "cuda"
+    staging = _PinnedStaging() if (on_gpu and not feature.is_cuda) else None
+    if on_gpu:
+        ev_start = torch.cuda.Event(enable_timing=True)
+        ev_end = torch.cuda.Event(enable_timing=True)
+        ev_start.record()
+    else:
+        t0 = time.perf_counter()
+    losses, scores_by_pid = [], {}
+    for i in range(max_steps):
+        grads.zero()
+        if i < local_count:
+            pid = local_partition_ids[i]
+            idx_i = local_partitions[i]
+            di = dup_idx[i] if use_cache and dup_idx else idx_i.new_empty(0)
+            x_i = _window_features(feature, idx_i, di, dup_cache, device, staging)
+            out_i, _, score_spe, _ = model(x_i, None, edges[i], None, None, None, None,
+                                           attn_type=getattr(args, "attn_type", "sparse"))
+            scores_by_pid[pid] = score_spe[-1]
+            idx_dev = idx_i.to(device)
+            mask = masks[i] if masks else torch.isin(idx_dev, split_idx["train"].to(device))
+            loss_all = F.nll_loss(out_i, y_dev[idx_dev].long(), reduction="none")
+            # mean over the window's train nodes (0 when it has none, as `build_zero_loss` gives),
+            # written without boolean indexing so no step waits on the host
+            m = mask.to(loss_all.dtype)
+            loss = (loss_all * m).sum() / m.sum().clamp_min(1.0)
+            losses.append(loss.detach())
+            loss.backward()
+        grads.average(world_size, group)
+        optimizer.step()
+    lr_scheduler.step()
+    if on_gpu:
+        ev_end.record()
+        ev_end.synchronize()
+        elapsed = ev_start.elapsed_time(ev_end) / 1e3
+    else:
+        elapsed = time.perf_counter() - t0
+    loss_mean = float(torch.stack(losses).mean()) if losses else 0.0
+    stats = {"epoch_train_total_time": elapsed, "num_processed_windows": local_count,
+             "max_window_steps": max_steps}
+    return loss_mean, scores_by_pid, None, stats
+
+
+class _PinnedStaging:
+    """Reusable pinned host buffers for host-resident feature matrices."""
+
+    def __init__(self):
+        self._bufs = {}
+
+    def __call__(self, shape, dtype):
+        key = (tuple(shape), dtype)
+        if key not in self._bufs:
+            self._bufs[key] = torch.empty(shape, dtype=dtype, pin_memory=True)
+        return self._bufs[key]
