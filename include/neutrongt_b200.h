@@ -141,6 +141,40 @@ NGT_API int ngt_spattn_backward_noalloc(int dtype, int64_t n, int64_t e, int hea
                                         ngt_stream_t stream);
 
 /* ------------------------------------------------------------------------------------
+ * Dense full-attention window, forward, on the tcgen05 tensor cores.
+ *
+ * Replaces `CoreAttention.full_attention` (NeutronGT/models/gt_dist_node_level_single_window.py:56-109,
+ * graphormer_dist_node_level.py:42-65) for attn_bias = mask = pruning_mask = None:
+ *   S = scale * q k^T (the reference's scale is sqrt(head_dim), multiplied), P = softmax(S),
+ *   dropout(P) with keep probability 1 - dropout_p, out = P v,
+ *   node_scores[j] += score_scale * sum_i |S[i, j]|   (score_scale = 1 / total heads gives the
+ *   reference's head mean; the caller zeroes node_scores once per call of all heads).
+ *
+ *   q, k, v, out    bf16 [s, heads, head_dim], head_dim a multiple of 8 and <= 64, 16-byte aligned
+ *   lse             float [heads, s]: log-sum-exp of each row of S (for the backward)
+ *   status          int32 [1] device flag, set to 1 if a bounded wait inside the kernel gave up
+ * ---------------------------------------------------------------------------------- */
+NGT_API int ngt_dense_attn_forward(int64_t s, int heads, int head_dim, float scale, float score_scale,
+                                   float dropout_p, uint64_t seed, const void *q, const void *k,
+                                   const void *v, void *out, float *lse, float *node_scores,
+                                   int32_t *status, ngt_stream_t stream);
+
+/* ------------------------------------------------------------------------------------
+ * Dense full-attention window, backward (the autograd graph of full_attention written out,
+ * dropout mask regenerated from the same seed).
+ *
+ *   lse             float [heads, s] from ngt_dense_attn_forward
+ *   delta           float [heads, s] caller scratch
+ *   dq_accum        float [s, heads, head_dim] caller scratch (zeroed by this call)
+ *   dq, dk, dv      bf16 [s, heads, head_dim]
+ * ---------------------------------------------------------------------------------- */
+NGT_API int ngt_dense_attn_backward(int64_t s, int heads, int head_dim, float scale, float dropout_p,
+                                    uint64_t seed, const void *q, const void *k, const void *v,
+                                    const void *out, const void *dout, const float *lse, float *delta,
+                                    float *dq_accum, void *dq, void *dk, void *dv, int32_t *status,
+                                    ngt_stream_t stream);
+
+/* ------------------------------------------------------------------------------------
  * Window subgraph (the window's edge list from the global CSR).
  *
  * Replaces `_subgraph_from_csr` (NeutronGT/core/node_level_pipeline/window_state.py:92-119):

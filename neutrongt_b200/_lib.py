@@ -32,6 +32,10 @@ SIGNATURES = {
                             _p, _p, _p, _p, _p, _p, _p],
     "ngt_spattn_backward_noalloc": [_i32, _i64, _i64, _i32, _i32, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
                                     _p, _p, _p, _p, _p, _p, _p],
+    "ngt_dense_attn_forward": [_i64, _i32, _i32, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_uint64,
+                               _p, _p, _p, _p, _p, _p, _p, _p],
+    "ngt_dense_attn_backward": [_i64, _i32, _i32, ctypes.c_float, ctypes.c_float, ctypes.c_uint64, _p, _p, _p, _p,
+                                _p, _p, _p, _p, _p, _p, _p, _p, _p],
     "ngt_window_subgraph_workspace_size": [_i64, _i64, _sz_p],
     "ngt_window_subgraph_count": [_i64, _p, _p, _p, _i64, _p, _p, _p, ctypes.c_size_t, _p],
     "ngt_window_subgraph_fill": [_i64, _p, _p, _p, _i64, _p, _p, _i64, _p, ctypes.c_size_t, _p],

@@ -1,0 +1,93 @@
+"""Dense full-attention windows on the tcgen05 tensor cores.
+
+`full_attention(k, q, v, attn_bias, mask, pruning_mask, scale, dropout_p)` keeps the contract of
+`CoreAttention.full_attention` (`NeutronGT/models/gt_dist_node_level_single_window.py:56-109`,
+note the (k, q, v) argument order): q, k, v are [b, s, H, D] with b == 1; it returns
+x [b, s, H, D] and node_scores [s] = sum over queries of the head-mean of |S|, where
+S = (q * sqrt(D)) k^T — the reference multiplies by sqrt(D), and so does this kernel.
+Gradients flow to q, k and v (`csrc/dense_attn.cu` backward); node_scores carries none.
+
+The kernels compute in bfloat16 with fp32 accumulation; float32 inputs are rounded to
+bfloat16 on entry and the output is returned in the input dtype.  Attention dropout uses a
+counter-based hash of (seed, head, query, key), regenerated in the backward; it matches
+torch's dropout in distribution, not bit for bit.  The optional dense attn_bias / mask /
+pruning_mask tensors ([b, H, s, s]) are not supported: NeutronGT's training loop passes
+None for all three.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+
+
+def _check_status(status):
+    if int(status.item()) != 0:
+        raise RuntimeError("dense attention kernel timed out waiting for the tensor core")
+
+
+class _DenseAttention(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, scale, dropout_p, seed, score_heads, check):
+        s, heads, dim = q.shape
+        out = torch.empty_like(q)
+        lse = torch.empty(heads, s, dtype=torch.float32, device=q.device)
+        ns = torch.zeros(s, dtype=torch.float32, device=q.device)
+        status = torch.zeros(1, dtype=torch.int32, device=q.device)
+        _lib.check(_lib.lib().ngt_dense_attn_forward(s, heads, dim, float(scale), 1.0 / score_heads,
+                                                     float(dropout_p), int(seed), _lib.ptr(q), _lib.ptr(k),
+                                                     _lib.ptr(v), _lib.ptr(out), _lib.ptr(lse), _lib.ptr(ns),
+                                                     _lib.ptr(status), _lib.stream_of(q)),
+                   "ngt_dense_attn_forward")
+        if check:
+            _check_status(status)
+        ctx.save_for_backward(q, k, v, out, lse)
+        ctx.args = (scale, dropout_p, seed, check)
+        ctx.mark_non_differentiable(ns)
+        return out, ns
+
+    @staticmethod
+    def backward(ctx, dout, _dns):
+        q, k, v, out, lse = ctx.saved_tensors
+        scale, dropout_p, seed, check = ctx.args
+        s, heads, dim = q.shape
+        dout = dout.to(torch.bfloat16).contiguous()
+        delta = torch.empty(heads, s, dtype=torch.float32, device=q.device)
+        dq_acc = torch.empty(s, heads, dim, dtype=torch.float32, device=q.device)
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        status = torch.zeros(1, dtype=torch.int32, device=q.device)
+        _lib.check(_lib.lib().ngt_dense_attn_backward(s, heads, dim, float(scale), float(dropout_p), int(seed),
+                                                      _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(out),
+                                                      _lib.ptr(dout), _lib.ptr(lse), _lib.ptr(delta), _lib.ptr(dq_acc),
+                                                      _lib.ptr(dq), _lib.ptr(dk), _lib.ptr(dv), _lib.ptr(status),
+                                                      _lib.stream_of(q)),
+                   "ngt_dense_attn_backward")
+        if check:
+            _check_status(status)
+        return dq, dk, dv, None, None, None, None, None
+
+
+def dense_attention(q, k, v, scale, dropout_p=0.0, seed=0, score_heads=None, check_status=True):
+    """q, k, v: bf16 [s, H, D] -> (out [s, H, D], node_scores [s]); differentiable in q, k, v."""
+    heads = q.shape[1]
+    return _DenseAttention.apply(q, k, v, scale, dropout_p, seed & (2**64 - 1),
+                                 heads if score_heads is None else score_heads, check_status)
+
+
+def full_attention(k, q, v, attn_bias=None, mask=None, pruning_mask=None, scale=None, dropout_p=0.0, seed=None,
+                   check_status=True):
+    if attn_bias is not None or mask is not None or pruning_mask is not None:
+        raise NotImplementedError("dense attention with attn_bias / mask / pruning_mask is not supported")
+    _lib.require_cuda(q, k, v)
+    b, s, heads, dim = q.shape
+    if b != 1:
+        raise ValueError("windows are one sequence (batch 1)")
+    scale = math.sqrt(dim) if scale is None else scale
+    if seed is None:
+        seed = int(torch.randint(0, 2**62, (1,)).item()) if dropout_p > 0 else 0
+    dt = q.dtype
+    q3, k3, v3 = (t.reshape(s, heads, dim).to(torch.bfloat16).contiguous() for t in (q, k, v))
+    out, ns = dense_attention(q3, k3, v3, scale, dropout_p, seed, check_status=check_status)
+    return out.to(dt).reshape(b, s, heads, dim), ns

@@ -1,0 +1,103 @@
+"""Dense full-attention window (tcgen05 kernels) against an fp32 torch restatement of
+`CoreAttention.full_attention` (`…single_window.py:56-109`) on the same bf16 inputs, forward
+and backward.  bf16 tolerance: 2e-2 relative (max|a-b| / max|b|)."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+BF16_TOL = 2e-2
+
+
+def _mix32(x):
+    m = np.uint64(0xFFFFFFFF)
+    x = x & m
+    x ^= x >> np.uint64(16)
+    x = (x * np.uint64(0x7FEB352D)) & m
+    x ^= x >> np.uint64(15)
+    x = (x * np.uint64(0x846CA68B)) & m
+    x ^= x >> np.uint64(16)
+    return x
+
+
+def keep_mask(seed, s, heads, p):
+    """The kernels' dropout keep decisions, restated in numpy: [H, s, s] bool."""
+    sd = np.uint64((seed ^ (seed >> 32)) & 0xFFFFFFFF)
+    thr = np.uint64(min(int(p * 2**32), 2**32 - 1))
+    m = np.uint64(0xFFFFFFFF)
+    i = np.arange(s, dtype=np.uint64)[None, :, None]
+    j = np.arange(s, dtype=np.uint64)[None, None, :]
+    h = np.arange(heads, dtype=np.uint64)[:, None, None]
+    inner = _mix32((i * np.uint64(0x9E3779B1) + h * np.uint64(0x85EBCA77)) & m)
+    x = _mix32(sd ^ inner ^ ((j * np.uint64(0xC2B2AE3D)) & m))
+    return torch.from_numpy(x >= thr)
+
+
+def _reference(q, k, v, scale, keep=None, p=0.0):
+    """fp32 restatement; returns (x, node_scores) with autograd through q, k, v."""
+    qf, kf, vf = (t.float().transpose(0, 1) for t in (q, k, v))      # [H, s, D]
+    score = torch.matmul(qf * scale, kf.transpose(1, 2))              # [H, s, s]
+    prob = torch.softmax(score, dim=-1)
+    if keep is not None:
+        prob = prob * keep.to(prob.device, prob.dtype) / (1.0 - p)
+    x = torch.matmul(prob, vf).transpose(0, 1)                        # [s, H, D]
+    ns = score.detach().abs().mean(dim=0).sum(dim=0)
+    return x, ns
+
+
+def _inputs(s, H, D, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    return [torch.randn(s, H, D, generator=g, device="cuda").to(torch.bfloat16) * 0.5 for _ in range(4)]
+
+
+@pytest.mark.parametrize("s,H,D", [(128, 1, 32), (128, 2, 24), (200, 4, 24), (1000, 2, 16), (300, 1, 64),
+                                   (1024, 4, 24)])
+def test_forward_and_backward_match_reference(cuda, s, H, D):
+    from neutrongt_b200.dense_attention import dense_attention
+    q, k, v, dout = _inputs(s, H, D, s + H + D)
+    qd, kd, vd = (t.clone().requires_grad_(True) for t in (q, k, v))
+    x, ns = dense_attention(qd, kd, vd, math.sqrt(D))
+    x.backward(dout)
+    qr, kr, vr = (t.float().clone().requires_grad_(True) for t in (q, k, v))
+    rx, rns = _reference(qr, kr, vr, math.sqrt(D))
+    rx.backward(dout.float())
+    assert x.shape == (s, H, D)
+    assert rel_err(x, rx) < BF16_TOL
+    assert rel_err(ns, rns) < BF16_TOL
+    assert rel_err(qd.grad, qr.grad) < BF16_TOL
+    assert rel_err(kd.grad, kr.grad) < BF16_TOL
+    assert rel_err(vd.grad, vr.grad) < BF16_TOL
+
+
+def test_dropout_matches_mask_restatement(cuda):
+    from neutrongt_b200.dense_attention import dense_attention
+    s, H, D, p, seed = 256, 2, 24, 0.5, 123456789
+    q, k, v, dout = _inputs(s, H, D, 7)
+    qd, kd, vd = (t.clone().requires_grad_(True) for t in (q, k, v))
+    x, _ = dense_attention(qd, kd, vd, math.sqrt(D), dropout_p=p, seed=seed)
+    x.backward(dout)
+    keep = keep_mask(seed, s, H, p)
+    assert 0.45 < float(keep.float().mean()) < 0.55
+    qr, kr, vr = (t.float().clone().requires_grad_(True) for t in (q, k, v))
+    rx, _ = _reference(qr, kr, vr, math.sqrt(D), keep=keep, p=p)
+    rx.backward(dout.float())
+    assert rel_err(x, rx) < BF16_TOL
+    assert rel_err(qd.grad, qr.grad) < BF16_TOL
+    assert rel_err(kd.grad, kr.grad) < BF16_TOL
+    assert rel_err(vd.grad, vr.grad) < BF16_TOL
+
+
+def test_full_attention_contract(cuda):
+    from neutrongt_b200 import CoreAttention
+    s, H, D = 300, 4, 24
+    q, k, v, _ = _inputs(s, H, D, 9)
+    attn = CoreAttention(H * D, 0.0, H).eval()
+    x, score = attn(q.unsqueeze(0), k.unsqueeze(0), v.unsqueeze(0), None, None, "full")
+    rx, rns = _reference(q, k, v, math.sqrt(D))
+    assert x.shape == (1, s, H * D)
+    assert rel_err(x.reshape(s, H, D), rx) < BF16_TOL
+    assert rel_err(score, rns) < BF16_TOL
