@@ -57,6 +57,7 @@ def parse_args():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--skip-ppr", action="store_true")
     p.add_argument("--skip-epoch", action="store_true")
+    p.add_argument("--skip-dense", action="store_true")
     p.add_argument("--skip-cpu", action="store_true")
     return p.parse_args()
 
@@ -418,6 +419,73 @@ def gt_epoch_cpu_baseline(model_gpu, ws, feature, y, split, n_windows, sample=2)
             "kind": "port", "sample": f"{len(times)} windows fwd+bwd+AdamW on the host, scaled to {n_windows} windows"}
 
 
+def measured_bf16_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def bench_dense(args, rank, world, dev, steps=5, warm=2):
+    """Dense attention windows (per-rank share): S = 32,768 tokens of one window,
+    the rank's 4 of 32 heads after the Ulysses exchange (head_dim 24), bf16, fwd + bwd.  With N > 1
+    the exchange (NCCL all_to_all_single) of q, k, v and the output is inside the timed step."""
+    import math as _m
+    from neutrongt_b200.dense_attention import dense_attention
+    from neutrongt_b200.ulysses import _SeqAllToAll
+    S, H_total, D = 32768, 32, 24
+    H_local = 4
+    g = torch.Generator(device=dev).manual_seed(rank)
+    if world == 1:
+        q, k, v, dy = (torch.randn(S, H_local, D, generator=g, device=dev).to(torch.bfloat16) * 0.5 for _ in range(4))
+    else:
+        # per-rank sequence shard of the heads the exchange distributes: world * 4 heads in total
+        q, k, v, dy = (torch.randn(1, S // world, H_local * world, D, generator=g, device=dev).to(torch.bfloat16) * 0.5
+                       for _ in range(4))
+    qd, kd, vd = (t.requires_grad_(True) for t in (q, k, v))
+    grp = None
+    import torch.distributed as _dist
+    if world > 1:
+        grp = _dist.group.WORLD
+
+    def step():
+        if world == 1:
+            x, _ = dense_attention(qd, kd, vd, _m.sqrt(D), score_heads=H_total, check_status=False)
+            x.backward(dy)
+        else:
+            ql = _SeqAllToAll.apply(grp, qd, 2, 1)[0]
+            kl = _SeqAllToAll.apply(grp, kd, 2, 1)[0]
+            vl = _SeqAllToAll.apply(grp, vd, 2, 1)[0]
+            x, _ = dense_attention(ql, kl, vl, _m.sqrt(D), score_heads=H_total, check_status=False)
+            y = _SeqAllToAll.apply(grp, x.unsqueeze(0), 1, 2)
+            y.backward(dy)
+
+    for _ in range(warm):
+        step()
+    barrier(world)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for a, b in ev:
+        a.record()
+        step()
+        b.record()
+    barrier(world)
+    t = allreduce_max(sum(a.elapsed_time(b) for a, b in ev) / steps / 1e3, world)
+    fwd_flops = 4.0 * S * S * H_local * D
+    flops = fwd_flops * 3.5            # forward + backward (recompute S, dP, dV, dK, dQ)
+    peak, kind = measured_bf16_peak()
+    achieved = flops / t / 1e12
+    return {"workload": "BASELINE config 4 per-rank share: one window of 32,768 tokens, 4 heads of 32 "
+                        "(after the Ulysses exchange), head_dim 24, bf16, dense attention fwd+bwd",
+            "ms_per_step": t * 1e3, "tflops_algorithmic": achieved,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
+                         "peak_kind": f"{kind} bf16_tflops (burst)", "unit": "TFLOP/s", "frac": achieved / peak,
+                         "note": "algorithmic flops 3.5 x 4 S^2 H D; head_dim 24 runs padded to 32 in the MMAs, "
+                                 "and the S^2 exponentials (MUFU) bound this shape before the tensor pipe"},
+            "n_gpus": world, "ulysses": world > 1}
+
+
 def bench_ppr(args, rank, world, dev):
     from neutrongt_b200 import personal_pagerank_appnp
     rowptr, col = config2_graph()
@@ -461,6 +529,7 @@ def run_ours(args):
     res = bench_attention(args, rank, world, dev)
     ppr = None if args.skip_ppr else bench_ppr(args, rank, world, dev)
     epoch = None if args.skip_epoch else bench_gt_epoch(args, rank, world, dev)
+    dense = None if args.skip_dense else bench_dense(args, rank, world, dev)
     cpu = None
     if rank == 0 and not args.skip_cpu:
         q, k, v, g, ei = res["host"]
@@ -477,7 +546,7 @@ def run_ours(args):
                        "l2": "flushed between steps (256 MiB write outside the timed events)",
                        "parallelism": f"independent windows, dp{world}"},
             "roofline": res["roofline"], "cpu_baseline": cpu, "e2e": res["e2e"], "gpu_launches": res["gpu_launches"],
-            "clocks": res["clocks"], "gt_epoch": epoch, "ppr": ppr,
+            "clocks": res["clocks"], "gt_epoch": epoch, "dense": dense, "ppr": ppr,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -1,0 +1,73 @@
+"""Ulysses exchange around the tcgen05 dense-attention kernel on 2 GPUs (NCCL).
+
+Each rank holds a sequence shard of q, k, v; after the head-scatter exchange it runs the CUDA
+kernel on its head group, and the gathered output, node scores and gradients must equal the
+single-GPU kernel on the whole sequence.  Needs two CUDA devices (skipped otherwise).
+"""
+import math
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _inputs():
+    g = torch.Generator().manual_seed(5)
+    return [torch.randn(1, 512, 8, 24, generator=g).to(torch.bfloat16) * 0.5 for _ in range(4)]
+
+
+def _worker(rank, world, port, out):
+    import datetime
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    from neutrongt_b200 import CoreAttention
+    from neutrongt_b200.ulysses import DistributedAttentionNodeLevel
+    q, k, v, dy = (t.cuda() for t in _inputs())
+    S = q.shape[1]
+    sl = slice(rank * S // world, (rank + 1) * S // world)
+    layer = DistributedAttentionNodeLevel(CoreAttention(8 * 24, 0.0, 8 // world), dist.group.WORLD).train()
+    ql, kl, vl = (t[:, sl].clone().requires_grad_(True) for t in (q, k, v))
+    y, score = layer(ql, kl, vl, None, None, "full")
+    y.backward(dy[:, sl].reshape(y.shape))
+    torch.cuda.synchronize()
+    out[rank] = tuple(t.detach().float().cpu() for t in (y, score, ql.grad, kl.grad, vl.grad))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_ulysses_dense_matches_single_gpu(cuda):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from neutrongt_b200.dense_attention import dense_attention
+    port = _free_port()
+    with mp.Manager() as m:
+        res = m.dict()
+        mp.spawn(_worker, args=(2, port, res), nprocs=2, join=True)
+        res = dict(res)
+    q, k, v, dy = (t.cuda() for t in _inputs())
+    qr, kr, vr = (t[0].clone().requires_grad_(True) for t in (q, k, v))
+    y, score = dense_attention(qr, kr, vr, math.sqrt(24))
+    y.backward(dy[0])
+    S = 512
+    for r in range(2):
+        sl = slice(r * S // 2, (r + 1) * S // 2)
+        yr, sr, gq, gk, gv = res[r]
+        ref = (y[sl].reshape(S // 2, -1), score[sl], qr.grad[sl], kr.grad[sl], vr.grad[sl])
+        for a, b in zip((yr.reshape(1, S // 2, -1), sr, gq, gk, gv), ref):
+            b = b.detach().float().cpu().reshape(a.shape)
+            assert float((a - b).abs().max() / b.abs().max()) < 2e-2
