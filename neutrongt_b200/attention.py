@@ -159,7 +159,10 @@ class CoreAttention(nn.Module):
         self.attention_dropout_rate = attention_dropout_rate
 
     def sparse_attention_bias(self, q, k, v, edge_index, attn_bias):
-        return sparse_attention_bias(q, k, v, edge_index, attn_bias, num_heads=self.num_heads)
+        # heads come from the [b, s, H, D] tensor itself, so a head-group shard (after the
+        # Ulysses exchange) works too; without sequence parallelism H == num_heads
+        return sparse_attention_bias(q, k, v, edge_index, attn_bias,
+                                     num_heads=q.shape[-2] if q.dim() == 4 else self.num_heads)
 
     def full_attention(self, k, q, v, attn_bias, mask=None, pruning_mask=None):
         from .dense_attention import full_attention

@@ -12,8 +12,10 @@
 //   * S = Q K^T and O += P V run as tcgen05.mma (bf16 in, fp32 accumulate in TMEM);
 //     V is read as an MN-major operand, so it is staged exactly like K;
 //   * online softmax (base-2, one TMEM lane = one query row per thread) rescales O in TMEM;
-//   * the node-score column sums sum_i |S_ij| run on the tensor core as ones * |S|^T, with
-//     |S| written once to shared memory as an MN-major operand, then one atomic add per key.
+//   * the node-score column sums sum_i |S_ij| run on the tensor core as |S|^T * ones (|S|
+//     written once to shared memory and read as an MN-major operand), one atomic add per key;
+//   * two CTAs share an SM and the next K/V block is prefetched into registers during the
+//     current block's MMA and softmax.
 // Every mbarrier wait is bounded; on timeout the CTA records a status, waits (bounded) for
 // its own MMAs, frees its TMEM and exits.
 #include "tc.cuh"
@@ -53,19 +55,22 @@ __device__ __forceinline__ bool keep_elem(uint32_t seed, int h, int i, int j, ui
 template <int DP>
 struct FwdSmem {
     static constexpr int CH = DP / 8;
+    static constexpr int kOnesRows = 16;
     static constexpr uint32_t kQ = 0;
     static constexpr uint32_t kK = kQ + BM * DP * 2;
     static constexpr uint32_t kV = kK + BN * DP * 2;
     static constexpr uint32_t kP = kV + BN * DP * 2;
     static constexpr uint32_t kAbs = kP + BM * BN * 2;
     static constexpr uint32_t kOnes = kAbs + BM * BN * 2;
-    static constexpr uint32_t kBar = kOnes + BM * BN * 2;
+    static constexpr uint32_t kBar = kOnes + kOnesRows * BM * 2;
     static constexpr uint32_t kTmemSlot = kBar + 16;
     static constexpr uint32_t kBytes = kTmemSlot + 16;
 };
 
+// Two CTAs share an SM (<= 113 KiB shared memory and 256 TMEM columns each), so one CTA's
+// softmax overlaps the other's tensor-core work.
 template <int DP>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     dense_fwd_kernel(int s, int H, int D, float scale, float score_scale, float drop_p, uint32_t seed,
                      const __nv_bfloat16 *__restrict__ q, const __nv_bfloat16 *__restrict__ k,
                      const __nv_bfloat16 *__restrict__ v, __nv_bfloat16 *__restrict__ out,
@@ -75,7 +80,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t *bar = reinterpret_cast<uint64_t *>(smem + L::kBar);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::kTmemSlot);
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tid = threadIdx.x, warp = tid >> 5;
     const int q0 = blockIdx.x * BM, h = blockIdx.y;
     const size_t rs = (size_t)H * D;
 
@@ -84,7 +89,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::mbar_init(bar, 1);
         tc::mbar_init_fence();
     }
-    {   // Q row `tid` (zero padded) and the all-ones operand of the column sums
+    {   // Q row `tid` (zero padded) and the 16 x 128 all-ones operand of the column sums
         const int qi = q0 + tid;
 #pragma unroll
         for (int c = 0; c < CH; c++) {
@@ -92,10 +97,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (qi < s && c * 8 < D) val = *reinterpret_cast<const uint4 *>(q + qi * rs + (size_t)h * D + c * 8);
             *reinterpret_cast<uint4 *>(smem + L::kQ + core_off(tid, c, CH)) = val;
         }
-        const uint4 ones = make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);
+        if (tid < L::kOnesRows) {
+            const uint4 ones = make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);
 #pragma unroll
-        for (int c = 0; c < BN / 8; c++) *reinterpret_cast<uint4 *>(smem + L::kOnes + core_off(tid, c, BN / 8)) = ones;
+            for (int c = 0; c < BM / 8; c++) *reinterpret_cast<uint4 *>(smem + L::kOnes + core_off(tid, c, BM / 8)) = ones;
+        }
     }
+    // first K/V block in registers; every later block is prefetched during the previous one
+    uint4 nk[CH], nv[CH];
+    auto fetch_kv = [&](int k0) {
+        const int kj = k0 + tid;
+#pragma unroll
+        for (int c = 0; c < CH; c++) {
+            nk[c] = make_uint4(0, 0, 0, 0);
+            nv[c] = make_uint4(0, 0, 0, 0);
+            if (kj < s && c * 8 < D) {
+                nk[c] = *reinterpret_cast<const uint4 *>(k + kj * rs + (size_t)h * D + c * 8);
+                nv[c] = *reinterpret_cast<const uint4 *>(v + kj * rs + (size_t)h * D + c * 8);
+            }
+        }
+    };
+    fetch_kv(0);
     tc::fence_smem_for_async();
     tc::fence_before_sync();
     __syncthreads();
@@ -108,8 +130,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                    aAbs = tc::smem_addr(smem + L::kAbs), aOnes = tc::smem_addr(smem + L::kOnes);
     constexpr uint32_t idesc_s = tc::idesc_bf16(BM, BN, false, false);
     constexpr uint32_t idesc_pv = tc::idesc_bf16(BM, DP, false, true);
-    constexpr uint32_t idesc_c = tc::idesc_bf16(BM, BN, false, true);
+    constexpr uint32_t idesc_c = tc::idesc_bf16(BN, L::kOnesRows, true, false);
     const float sl2 = scale * kLog2e;
+    const float col_scale = scale * score_scale;
     const uint32_t drop_threshold = drop_p > 0.f ? (uint32_t)fminf(drop_p * 4294967296.0f, 4294967295.0f) : 0u;
     const float keep_scale = drop_p > 0.f ? 1.0f / (1.0f - drop_p) : 1.0f;
     const int qi = q0 + tid;
@@ -121,18 +144,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int nkb = (s + BN - 1) / BN;
     for (int kb = 0; kb < nkb; kb++) {
         const int k0 = kb * BN;
-        {   // K and V rows of this block
-            const int kj = k0 + tid;
 #pragma unroll
-            for (int c = 0; c < CH; c++) {
-                uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-                if (kj < s && c * 8 < D) {
-                    kv = *reinterpret_cast<const uint4 *>(k + kj * rs + (size_t)h * D + c * 8);
-                    vv = *reinterpret_cast<const uint4 *>(v + kj * rs + (size_t)h * D + c * 8);
-                }
-                *reinterpret_cast<uint4 *>(smem + L::kK + core_off(tid, c, CH)) = kv;
-                *reinterpret_cast<uint4 *>(smem + L::kV + core_off(tid, c, CH)) = vv;
-            }
+        for (int c = 0; c < CH; c++) {   // the previous block's MMAs are complete: reuse the tiles
+            *reinterpret_cast<uint4 *>(smem + L::kK + core_off(tid, c, CH)) = nk[c];
+            *reinterpret_cast<uint4 *>(smem + L::kV + core_off(tid, c, CH)) = nv[c];
         }
         tc::fence_smem_for_async();
         tc::fence_before_sync();
@@ -145,55 +160,77 @@ __global__ void __launch_bounds__(kThreads, 1)
                              idesc_s, kk > 0);
             tc::commit(bar);
         }
+        if (kb + 1 < nkb) fetch_kv(k0 + BN);   // global loads overlap the MMA and the softmax
         if (tc::mbar_wait_bounded(bar, phase, kWaitLimit)) phase ^= 1;
         else failed = 1;
-        if (__syncthreads_or(failed)) break;
+        failed = __syncthreads_or(failed);
+        if (failed) break;
         tc::fence_after_sync();
 
-        float sv[BN];
+        const bool full_block = k0 + BN <= s;   // every key of the block is real
+        // pass 1: row max of the raw scores (scale > 0, so the max commutes with scaling)
+        float mraw = -INFINITY;
+#pragma unroll 1
+        for (int c4 = 0; c4 < BN / 32; c4++) {
+            float t[32];
+            tc::ld32(tS + lane_off + c4 * 32, t);
+            if (full_block) {
 #pragma unroll
+                for (int i = 0; i < 32; i++) mraw = fmaxf(mraw, t[i]);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; i++)
+                    if (k0 + c4 * 32 + i < s) mraw = fmaxf(mraw, t[i]);
+            }
+        }
+        const float m_new = fmaxf(m2, mraw * sl2);
+        const float alpha = (m_new == -INFINITY) ? 1.f : tc::ex2(m2 - m_new);
+        l *= alpha;
+        m2 = m_new;
+        // pass 2: probabilities (dropout applied to what multiplies V, not to the normaliser)
+        // and |S| in natural units for the node scores
+#pragma unroll 1
         for (int c4 = 0; c4 < BN / 32; c4++) {
             float t[32];
             tc::ld32(tS + lane_off + c4 * 32, t);
 #pragma unroll
-            for (int i = 0; i < 32; i++) sv[c4 * 32 + i] = t[i];
-        }
-        // online softmax in base 2; |S| (natural units) for the node scores
-        float mloc = -INFINITY;
+            for (int c = 0; c < 4; c++) {
+                uint32_t pw[4], aw[4];
+                if (full_block && row_ok && !drop_threshold) {   // common case: no checks per element
 #pragma unroll
-        for (int j = 0; j < BN; j++) {
-            const bool ok = (k0 + j) < s;
-            sv[j] = ok ? sv[j] * sl2 : -INFINITY;
-            mloc = fmaxf(mloc, sv[j]);
-        }
-        const float m_new = fmaxf(m2, mloc);
-        const float alpha = (m_new == -INFINITY) ? 1.f : tc::ex2(m2 - m_new);
-        l *= alpha;
-        m2 = m_new;
+                    for (int e = 0; e < 8; e += 2) {
+                        const float p0 = tc::ex2(fmaf(t[c * 8 + e], sl2, -m_new));
+                        const float p1 = tc::ex2(fmaf(t[c * 8 + e + 1], sl2, -m_new));
+                        l += p0 + p1;
+                        pw[e / 2] = tc::pack_bf16(p0, p1);
+                        aw[e / 2] = tc::pack_bf16(fabsf(t[c * 8 + e]), fabsf(t[c * 8 + e + 1]));
+                    }
+                } else {
 #pragma unroll
-        for (int c = 0; c < BN / 8; c++) {
-            uint32_t pw[4], aw[4];
+                    for (int e = 0; e < 8; e += 2) {
+                        float pv[2], av[2];
 #pragma unroll
-            for (int e = 0; e < 8; e += 2) {
-                float pv[2], av[2];
-#pragma unroll
-                for (int u = 0; u < 2; u++) {
-                    const int j = c * 8 + e + u;
-                    const bool ok = sv[j] != -INFINITY;
-                    const float p = ok ? tc::ex2(sv[j] - m_new) : 0.f;
-                    l += p;
-                    float pd = p;
-                    if (drop_threshold) pd = keep_elem(seed, h, qi, k0 + j, drop_threshold) ? p * keep_scale : 0.f;
-                    pv[u] = pd;
-                    av[u] = (ok && row_ok) ? fabsf(sv[j]) * kLn2 : 0.f;
+                        for (int u = 0; u < 2; u++) {
+                            const int jj = c * 8 + e + u;
+                            const int key = k0 + c4 * 32 + jj;
+                            const bool ok = key < s;
+                            const float p = ok ? tc::ex2(fmaf(t[jj], sl2, -m_new)) : 0.f;
+                            l += p;
+                            float pd = p;
+                            if (drop_threshold) pd = keep_elem(seed, h, qi, key, drop_threshold) ? p * keep_scale : 0.f;
+                            pv[u] = pd;
+                            av[u] = (ok && row_ok) ? fabsf(t[jj]) : 0.f;
+                        }
+                        pw[e / 2] = tc::pack_bf16(pv[0], pv[1]);
+                        aw[e / 2] = tc::pack_bf16(av[0], av[1]);
+                    }
                 }
-                pw[e / 2] = tc::pack_bf16(pv[0], pv[1]);
-                aw[e / 2] = tc::pack_bf16(av[0], av[1]);
+                const int chunk = c4 * 4 + c;
+                *reinterpret_cast<uint4 *>(smem + L::kP + core_off(tid, chunk, BN / 8)) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
+                *reinterpret_cast<uint4 *>(smem + L::kAbs + core_off(tid, chunk, BN / 8)) = make_uint4(aw[0], aw[1], aw[2], aw[3]);
             }
-            *reinterpret_cast<uint4 *>(smem + L::kP + core_off(tid, c, BN / 8)) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
-            *reinterpret_cast<uint4 *>(smem + L::kAbs + core_off(tid, c, BN / 8)) = make_uint4(aw[0], aw[1], aw[2], aw[3]);
         }
-        if (kb > 0) {   // rescale the running output by exp(m_old - m_new)
+        if (kb > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {   // rescale O by exp(m_old - m_new)
 #pragma unroll
             for (int c4 = 0; c4 < DP / 32; c4++) {
                 float o[32];
@@ -213,24 +250,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc::mma_bf16(tO, tc::smem_desc(aP + kk * 256, 128, (BN / 8) * 128),
                              tc::smem_desc(aV + kk * 2 * CH * 128, CH * 128, 128), idesc_pv, (kb > 0 || kk > 0));
 #pragma unroll
-            for (int kk = 0; kk < BM / 16; kk++)   // C = ones |S|^T: column sums over the 128 queries
-                tc::mma_bf16(tS, tc::smem_desc(aOnes + kk * 256, 128, (BN / 8) * 128),
-                             tc::smem_desc(aAbs + kk * 2 * (BN / 8) * 128, (BN / 8) * 128, 128), idesc_c, kk > 0);
+            for (int kk = 0; kk < BM / 16; kk++)   // C = |S|^T ones: row j of C = sum_i |S_ij| (|S| read MN-major)
+                tc::mma_bf16(tS, tc::smem_desc(aAbs + kk * 2 * (BN / 8) * 128, (BN / 8) * 128, 128),
+                             tc::smem_desc(aOnes + kk * 256, 128, (BM / 8) * 128), idesc_c, kk > 0);
             tc::commit(bar);
         }
         if (tc::mbar_wait_bounded(bar, phase, kWaitLimit)) phase ^= 1;
         else failed = 1;
-        if (__syncthreads_or(failed)) break;
+        failed = __syncthreads_or(failed);
+        if (failed) break;
         tc::fence_after_sync();
-        {   // every row of C holds the column sums; warp w publishes keys [32w, 32w + 32)
+        {   // lane `tid` of C holds the column sum of key k0 + tid
             float cs[32];
-            tc::ld32(tS + lane_off + warp * 32, cs);
-            float mine = 0.f;
-#pragma unroll
-            for (int i = 0; i < 32; i++)
-                if (i == lane) mine = cs[i];
-            const int key = k0 + warp * 32 + lane;
-            if (key < s) atomicAdd(node_scores + key, mine * score_scale);
+            tc::ld32(tS + lane_off, cs);
+            const int key = k0 + tid;
+            if (key < s) atomicAdd(node_scores + key, cs[0] * col_scale);   // |S| was staged unscaled
         }
         tc::fence_before_sync();
         __syncthreads();
@@ -294,7 +328,7 @@ extern "C" int ngt_dense_attn_forward(int64_t s, int heads, int head_dim, float 
     if (s < 0 || heads <= 0 || head_dim <= 0 || !status) return NGT_ERR_INVALID_ARGUMENT;
     if (s > 0 && (!q || !k || !v || !out || !lse || !node_scores)) return NGT_ERR_INVALID_ARGUMENT;
     if (head_dim % 8 != 0 || head_dim > 64) return NGT_ERR_UNSUPPORTED;
-    if (!(dropout_p >= 0.f && dropout_p < 1.f)) return NGT_ERR_INVALID_ARGUMENT;
+    if (!(dropout_p >= 0.f && dropout_p < 1.f) || !(scale > 0.f)) return NGT_ERR_INVALID_ARGUMENT;
     if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)) return NGT_ERR_MISALIGNED;
     if (s * (int64_t)heads * head_dim >= (int64_t)INT32_MAX) return NGT_ERR_TOO_LARGE;
     if (s == 0) return NGT_OK;
@@ -319,7 +353,7 @@ extern "C" int ngt_dense_attn_forward(int64_t s, int heads, int head_dim, float 
 namespace ngt {
 namespace {
 
-constexpr uint32_t kBwdTmemCols = 512;
+constexpr uint32_t kBwdTmemCols = 256;   // two CTAs per SM
 
 template <int DP>
 struct BwdSmem {
@@ -334,8 +368,7 @@ struct BwdSmem {
     static constexpr uint32_t kDelta = kLse + BM * 4;
     static constexpr uint32_t kBar = kDelta + BM * 4;
     static constexpr uint32_t kTmemSlot = kBar + 16;
-    // at least 116 KiB, so one CTA per SM: each CTA holds all 512 TMEM columns
-    static constexpr uint32_t kBytes = (kTmemSlot + 16) > (116u << 10) ? (kTmemSlot + 16) : (116u << 10);
+    static constexpr uint32_t kBytes = kTmemSlot + 16;
 };
 
 __device__ __forceinline__ void stage_rows(uint8_t *dst, const __nv_bfloat16 *src, int row0, int s, size_t rs,
@@ -349,7 +382,7 @@ __device__ __forceinline__ void stage_rows(uint8_t *dst, const __nv_bfloat16 *sr
 }
 
 template <int DP>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     dense_bwd_kernel(int s, int H, int D, float scale, float drop_p, uint32_t seed,
                      const __nv_bfloat16 *__restrict__ q, const __nv_bfloat16 *__restrict__ k,
                      const __nv_bfloat16 *__restrict__ v, const __nv_bfloat16 *__restrict__ dout,
@@ -379,12 +412,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t tS = tmem, tDP = tmem + 128, tDV = tmem + 256, tDK = tmem + 256 + DP, tDQ = tmem + 256 + 2 * DP;
+    // TMEM: S and dP of one 64-query half side by side, then the dV and dK accumulators;
+    // the dQ partial reuses the S/dP columns once both halves have been read
+    constexpr int QH = BM / 2;
+    const uint32_t tS = tmem, tDP = tmem + QH, tDV = tmem + 2 * QH, tDK = tmem + 2 * QH + DP, tDQ = tmem;
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
     const uint32_t aK = tc::smem_addr(smem + L::kK), aV = tc::smem_addr(smem + L::kV),
                    aQ = tc::smem_addr(smem + L::kQ), aDO = tc::smem_addr(smem + L::kDO),
                    aPt = tc::smem_addr(smem + L::kPt), aDSt = tc::smem_addr(smem + L::kDSt);
-    constexpr uint32_t idesc_sq = tc::idesc_bf16(BN, BM, false, false);      // [keys x queries], both K-major
+    constexpr uint32_t idesc_sq = tc::idesc_bf16(BN, QH, false, false);      // [keys x 64 queries], K-major
     constexpr uint32_t idesc_acc = tc::idesc_bf16(BN, DP, false, true);      // [keys x d], B MN-major
     constexpr uint32_t idesc_dq = tc::idesc_bf16(BM, DP, true, true);        // [queries x d], A and B MN-major
     const float sl2 = scale * kLog2e;
@@ -396,7 +432,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t phase = 0;
     int failed = 0;
     const int nqb = (s + BM - 1) / BM;
-    for (int qb = 0; qb < nqb; qb++) {
+    for (int qb = 0; qb < nqb && !failed; qb++) {
         const int q0 = qb * BM;
         stage_rows(smem + L::kQ, q, q0, s, rs, h, D, CH, tid);
         stage_rows(smem + L::kDO, dout, q0, s, rs, h, D, CH, tid);
@@ -408,55 +444,62 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::fence_smem_for_async();
         tc::fence_before_sync();
         __syncthreads();
-        if (tid == 0) {
-            tc::fence_after_sync();
+        for (int half = 0; half < 2; half++) {
+            if (tid == 0) {
+                tc::fence_after_sync();
+                const uint32_t qoff = half * (QH / 8) * CH * 128;   // 8 row groups of 8 queries
 #pragma unroll
-            for (int kk = 0; kk < DP / 16; kk++) {
-                tc::mma_bf16(tS, tc::smem_desc(aK + kk * 256, 128, CH * 128), tc::smem_desc(aQ + kk * 256, 128, CH * 128),
-                             idesc_sq, kk > 0);
-                tc::mma_bf16(tDP, tc::smem_desc(aV + kk * 256, 128, CH * 128), tc::smem_desc(aDO + kk * 256, 128, CH * 128),
-                             idesc_sq, kk > 0);
-            }
-            tc::commit(bar);
-        }
-        if (tc::mbar_wait_bounded(bar, phase, kWaitLimit)) phase ^= 1;
-        else failed = 1;
-        if (__syncthreads_or(failed)) break;
-        tc::fence_after_sync();
-#pragma unroll 1
-        for (int c4 = 0; c4 < BM / 32; c4++) {
-            float sv[32], dp[32];
-            tc::ld32(tS + lane_off + c4 * 32, sv);
-            tc::ld32(tDP + lane_off + c4 * 32, dp);
-#pragma unroll
-            for (int c = 0; c < 4; c++) {
-                uint32_t pw[4], dw[4];
-#pragma unroll
-                for (int e = 0; e < 8; e += 2) {
-                    float pv[2], dv2[2];
-#pragma unroll
-                    for (int u = 0; u < 2; u++) {
-                        const int j = c * 8 + e + u;          // query index within the 32-chunk
-                        const int qq = c4 * 32 + j;           // query index within the block
-                        float p = key_ok ? tc::ex2(sv[j] * sl2 - s_lse[qq]) : 0.f;
-                        float g = dp[j];
-                        float pd = p;
-                        if (drop_threshold) {
-                            const bool keep = keep_elem(seed, h, q0 + qq, kj, drop_threshold);
-                            pd = keep ? p * keep_scale : 0.f;
-                            g = keep ? g * keep_scale : 0.f;
-                        }
-                        pv[u] = pd;
-                        dv2[u] = p * (g - s_delta[qq]);
-                    }
-                    pw[e / 2] = tc::pack_bf16(pv[0], pv[1]);
-                    dw[e / 2] = tc::pack_bf16(dv2[0], dv2[1]);
+                for (int kk = 0; kk < DP / 16; kk++) {
+                    tc::mma_bf16(tS, tc::smem_desc(aK + kk * 256, 128, CH * 128),
+                                 tc::smem_desc(aQ + qoff + kk * 256, 128, CH * 128), idesc_sq, kk > 0);
+                    tc::mma_bf16(tDP, tc::smem_desc(aV + kk * 256, 128, CH * 128),
+                                 tc::smem_desc(aDO + qoff + kk * 256, 128, CH * 128), idesc_sq, kk > 0);
                 }
-                const int chunk = c4 * 4 + c;
-                *reinterpret_cast<uint4 *>(smem + L::kPt + core_off(tid, chunk, BM / 8)) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
-                *reinterpret_cast<uint4 *>(smem + L::kDSt + core_off(tid, chunk, BM / 8)) = make_uint4(dw[0], dw[1], dw[2], dw[3]);
+                tc::commit(bar);
             }
+            if (tc::mbar_wait_bounded(bar, phase, kWaitLimit)) phase ^= 1;
+            else failed = 1;
+            failed = __syncthreads_or(failed);
+        if (failed) break;
+            tc::fence_after_sync();
+#pragma unroll 1
+            for (int c4 = 0; c4 < QH / 32; c4++) {
+                float sv[32], dp[32];
+                tc::ld32(tS + lane_off + c4 * 32, sv);
+                tc::ld32(tDP + lane_off + c4 * 32, dp);
+#pragma unroll
+                for (int c = 0; c < 4; c++) {
+                    uint32_t pw[4], dw[4];
+#pragma unroll
+                    for (int e = 0; e < 8; e += 2) {
+                        float pv[2], dv2[2];
+#pragma unroll
+                        for (int u = 0; u < 2; u++) {
+                            const int j = c * 8 + e + u;                   // query within the 32-chunk
+                            const int qq = half * QH + c4 * 32 + j;        // query within the block
+                            const float p = key_ok ? tc::ex2(fmaf(sv[j], sl2, -s_lse[qq])) : 0.f;
+                            float g = dp[j];
+                            float pd = p;
+                            if (drop_threshold) {
+                                const bool keep = keep_elem(seed, h, q0 + qq, kj, drop_threshold);
+                                pd = keep ? p * keep_scale : 0.f;
+                                g = keep ? g * keep_scale : 0.f;
+                            }
+                            pv[u] = pd;
+                            dv2[u] = p * (g - s_delta[qq]);
+                        }
+                        pw[e / 2] = tc::pack_bf16(pv[0], pv[1]);
+                        dw[e / 2] = tc::pack_bf16(dv2[0], dv2[1]);
+                    }
+                    const int chunk = half * (QH / 8) + c4 * 4 + c;
+                    *reinterpret_cast<uint4 *>(smem + L::kPt + core_off(tid, chunk, BM / 8)) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
+                    *reinterpret_cast<uint4 *>(smem + L::kDSt + core_off(tid, chunk, BM / 8)) = make_uint4(dw[0], dw[1], dw[2], dw[3]);
+                }
+            }
+            tc::fence_before_sync();
+            __syncthreads();   // S/dP of this half read by every thread before they are overwritten
         }
+        if (failed) break;
         tc::fence_smem_for_async();
         tc::fence_before_sync();
         __syncthreads();
@@ -479,7 +522,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (tc::mbar_wait_bounded(bar, phase, kWaitLimit)) phase ^= 1;
         else failed = 1;
-        if (__syncthreads_or(failed)) break;
+        failed = __syncthreads_or(failed);
+        if (failed) break;
         tc::fence_after_sync();
         {   // this thread's lane is query q0 + tid for the dQ partial
             const int qi = q0 + tid;

@@ -186,3 +186,113 @@ class _PinnedStaging:
         if key not in self._bufs:
             self._bufs[key] = torch.empty(shape, dtype=dtype, pin_memory=True)
         return self._bufs[key]
+
+
+class GraphedWindowTrainer:
+    """An epoch of `train_epoch` as replays of captured CUDA graphs, one per local window.
+
+    Each graph holds the whole window step: feature gather, forward, masked NLL, backward into
+    the flat gradient buffer, the gradient average over ranks (NCCL all-reduce) and the
+    optimizer step.  A rank with fewer windows replays a zero-gradient step graph, so every
+    rank issues the same all-reduces in the same order (`train_eval.py:211-217`).  Shapes and
+    edge lists of the windows are fixed (`use_cache == 1`), which is what makes one capture per
+    window reusable for every epoch; the launch overhead of the eager loop (hundreds of small
+    kernels per window) collapses into one graph launch per window.
+
+    Requirements: device-resident features and labels, an optimizer built with
+    `capturable=True`, and a learning rate that changes (if at all) as a tensor in place.
+    """
+
+    def __init__(self, args, model, structInfo, feature, y, optimizer, world_size, device, group=None,
+                 split_idx=None):
+        device = torch.device(device)
+        if not feature.is_cuda or not y.is_cuda:
+            raise ValueError("graph replay needs device-resident features and labels")
+        for g in optimizer.param_groups:
+            if not g.get("capturable", False):
+                raise ValueError("graph replay needs an optimizer created with capturable=True")
+        self.model, self.opt, self.world, self.group, self.dev = model, optimizer, world_size, group, device
+        self.attn_type = getattr(args, "attn_type", "sparse")
+        self.grads = FlatGradients(model)
+        self.edges = structInfo.local_sub_edge_index_for_partition_results
+        self.ids = structInfo.local_partition_ids
+        parts = structInfo.local_partitions
+        masks = getattr(structInfo, "local_train_masks", None) or []
+        dups = structInfo.local_dup_indices or [None] * len(parts)
+        dup_cache = structInfo.local_dup_nodes_per_partition_feature
+        self.windows = []
+        for i, idx in enumerate(parts):
+            idx_dev = idx.to(device)
+            n_dup = int(dups[i].numel()) if dups[i] is not None else 0
+            mask = masks[i] if masks else torch.isin(idx_dev, split_idx["train"].to(device))
+            self.windows.append(dict(rest=idx_dev[n_dup:], dup=dups[i] if n_dup else None, y=y[idx_dev].long(),
+                                     m=mask.to(torch.float32)))
+        self.feature, self.dup_cache = feature, dup_cache
+        self.max_steps = len(parts)
+        if world_size > 1:
+            t = torch.tensor([len(parts)], device=device, dtype=torch.long)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+            self.max_steps = int(t.item())
+        self._capture()
+
+    def _step(self, i):
+        self.grads.zero()
+        loss = None
+        scores = None
+        if i is not None:
+            w = self.windows[i]
+            x = self.feature[w["rest"]]
+            if w["dup"] is not None:
+                x = torch.cat([self.dup_cache[w["dup"]], x], dim=0)
+            out, _, score_spe, _ = self.model(x, None, self.edges[i], None, None, None, None, attn_type=self.attn_type)
+            loss_all = F.nll_loss(out, w["y"], reduction="none")
+            loss = (loss_all * w["m"]).sum() / w["m"].sum().clamp_min(1.0)
+            loss.backward()
+            scores = score_spe[-1]
+        self.grads.average(self.world, self.group)
+        self.opt.step()
+        return loss, scores
+
+    def _capture(self):
+        self.model.train()
+        side = torch.cuda.Stream(self.dev)
+        side.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(side):        # warm-up: CSR caches, allocator, NCCL, optimizer state
+            for i in range(len(self.windows)):
+                self._step(i)
+            if self.max_steps > len(self.windows):
+                self._step(None)
+        torch.cuda.current_stream(self.dev).wait_stream(side)
+        torch.cuda.synchronize(self.dev)
+        self.pool = torch.cuda.graph_pool_handle()
+        self.graphs, self.outputs = [], []
+        for i in range(len(self.windows)):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, pool=self.pool):
+                out = self._step(i)
+            self.graphs.append(g)
+            self.outputs.append(out)
+        self.dummy = None
+        if self.max_steps > len(self.windows):
+            self.dummy = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.dummy, pool=self.pool):
+                self._step(None)
+        torch.cuda.synchronize(self.dev)
+
+    def run_epoch(self, lr_scheduler=None):
+        """Returns (loss_mean, scores_by_pid, elapsed seconds by CUDA events)."""
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for i in range(self.max_steps):
+            if i < len(self.graphs):
+                self.graphs[i].replay()
+            else:
+                self.dummy.replay()
+        if lr_scheduler is not None:
+            lr_scheduler.step()
+        end.record()
+        end.synchronize()
+        losses = [o[0] for o in self.outputs]
+        loss_mean = float(torch.stack(losses).mean()) if losses else 0.0
+        scores = {pid: o[1] for pid, o in zip(self.ids, self.outputs)}
+        return loss_mean, scores, start.elapsed_time(end) / 1e3

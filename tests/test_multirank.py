@@ -62,7 +62,7 @@ def _worker(rank, world, port, results):
 
 def test_two_ranks_stay_in_lockstep_and_identical():
     port = _free_port()
-    with mp.Manager() as m:
+    with mp.get_context("spawn").Manager() as m:
         results = m.dict()
         mp.spawn(_worker, args=(2, port, results), nprocs=2, join=True)
         r0, r1 = results[0], results[1]

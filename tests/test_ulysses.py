@@ -55,7 +55,7 @@ def _worker(rank, world, port, out):
 
 def test_distributed_attention_matches_single_process():
     port = _free_port()
-    with mp.Manager() as m:
+    with mp.get_context("spawn").Manager() as m:
         res = m.dict()
         mp.spawn(_worker, args=(2, port, res), nprocs=2, join=True)
         res = dict(res)

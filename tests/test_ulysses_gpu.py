@@ -40,7 +40,8 @@ def _worker(rank, world, port, out):
     q, k, v, dy = (t.cuda() for t in _inputs())
     S = q.shape[1]
     sl = slice(rank * S // world, (rank + 1) * S // world)
-    layer = DistributedAttentionNodeLevel(CoreAttention(8 * 24, 0.0, 8 // world), dist.group.WORLD).train()
+    # constructed as the reference does: hidden size and the TOTAL head count
+    layer = DistributedAttentionNodeLevel(CoreAttention(8 * 24, 0.0, 8), dist.group.WORLD).train()
     ql, kl, vl = (t[:, sl].clone().requires_grad_(True) for t in (q, k, v))
     y, score = layer(ql, kl, vl, None, None, "full")
     y.backward(dy[:, sl].reshape(y.shape))
@@ -55,7 +56,7 @@ def test_ulysses_dense_matches_single_gpu(cuda):
         pytest.skip("needs 2 GPUs")
     from neutrongt_b200.dense_attention import dense_attention
     port = _free_port()
-    with mp.Manager() as m:
+    with mp.get_context("spawn").Manager() as m:
         res = m.dict()
         mp.spawn(_worker, args=(2, port, res), nprocs=2, join=True)
         res = dict(res)
