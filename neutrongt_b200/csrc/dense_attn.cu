@@ -371,6 +371,12 @@ struct BwdSmem {
     static constexpr uint32_t kBytes = kTmemSlot + 16;
 };
 
+// Four fp32 additions to consecutive, 16-byte aligned global addresses in one reduction.
+__device__ __forceinline__ void red_add_v4(float *p, float a, float b, float c, float d) {
+    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
+                 : "memory");
+}
+
 __device__ __forceinline__ void stage_rows(uint8_t *dst, const __nv_bfloat16 *src, int row0, int s, size_t rs,
                                            int h, int D, int CH, int tid) {
     const int r = row0 + tid;
@@ -432,18 +438,37 @@ __global__ void __launch_bounds__(kThreads, 2)
     uint32_t phase = 0;
     int failed = 0;
     const int nqb = (s + BM - 1) / BM;
+    // the next query block's rows are fetched into registers while the current one is processed
+    uint4 nq[CH], ndo[CH];
+    float nlse = INFINITY, ndl = 0.f;
+    auto fetch_q = [&](int q0) {
+        const int qi = q0 + tid;
+#pragma unroll
+        for (int c = 0; c < CH; c++) {
+            nq[c] = make_uint4(0, 0, 0, 0);
+            ndo[c] = make_uint4(0, 0, 0, 0);
+            if (qi < s && c * 8 < D) {
+                nq[c] = *reinterpret_cast<const uint4 *>(q + qi * rs + (size_t)h * D + c * 8);
+                ndo[c] = *reinterpret_cast<const uint4 *>(dout + qi * rs + (size_t)h * D + c * 8);
+            }
+        }
+        nlse = qi < s ? lse[(size_t)h * s + qi] * kLog2e : INFINITY;   // invalid query -> P = 0
+        ndl = qi < s ? delta[(size_t)h * s + qi] : 0.f;
+    };
+    fetch_q(0);
     for (int qb = 0; qb < nqb && !failed; qb++) {
         const int q0 = qb * BM;
-        stage_rows(smem + L::kQ, q, q0, s, rs, h, D, CH, tid);
-        stage_rows(smem + L::kDO, dout, q0, s, rs, h, D, CH, tid);
-        {
-            const int qi = q0 + tid;
-            s_lse[tid] = qi < s ? lse[(size_t)h * s + qi] * kLog2e : INFINITY;  // invalid query -> P = 0
-            s_delta[tid] = qi < s ? delta[(size_t)h * s + qi] : 0.f;
+#pragma unroll
+        for (int c = 0; c < CH; c++) {
+            *reinterpret_cast<uint4 *>(smem + L::kQ + core_off(tid, c, CH)) = nq[c];
+            *reinterpret_cast<uint4 *>(smem + L::kDO + core_off(tid, c, CH)) = ndo[c];
         }
+        s_lse[tid] = nlse;
+        s_delta[tid] = ndl;
         tc::fence_smem_for_async();
         tc::fence_before_sync();
         __syncthreads();
+        if (qb + 1 < nqb) fetch_q(q0 + BM);
         for (int half = 0; half < 2; half++) {
             if (tid == 0) {
                 tc::fence_after_sync();
@@ -531,10 +556,12 @@ __global__ void __launch_bounds__(kThreads, 2)
             for (int c4 = 0; c4 < DP / 32; c4++) {
                 float g[32];
                 tc::ld32(tDQ + lane_off + c4 * 32, g);
-                if (qi < s) {
+                if (qi < s) {   // dq_acc rows are 16-byte aligned: D % 8 == 0 and fp32
+                    float *dst = dq_acc + qi * rs + (size_t)h * D + c4 * 32;
 #pragma unroll
-                    for (int d = 0; d < 32; d++)
-                        if (c4 * 32 + d < D) atomicAdd(dq_acc + qi * rs + (size_t)h * D + c4 * 32 + d, g[d] * scale);
+                    for (int d = 0; d < 32; d += 4)
+                        if (c4 * 32 + d < D)
+                            red_add_v4(dst + d, g[d] * scale, g[d + 1] * scale, g[d + 2] * scale, g[d + 3] * scale);
                 }
             }
         }
