@@ -18,6 +18,7 @@
 //     current block's MMA and softmax.
 // Every mbarrier wait is bounded; on timeout the CTA records a status, waits (bounded) for
 // its own MMAs, frees its TMEM and exits.
+#include "dense_tma.h"
 #include "tc.cuh"
 
 namespace ngt {
@@ -334,9 +335,9 @@ extern "C" int ngt_dense_attn_forward(int64_t s, int heads, int head_dim, float 
     if (s == 0) return NGT_OK;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const uint32_t sd = (uint32_t)(seed ^ (seed >> 32));
-    if (head_dim <= 32)
-        return launch_fwd<32>(s, heads, head_dim, scale, score_scale, dropout_p, sd, q, k, v, out, lse, node_scores,
-                              status, st);
+    if (head_dim <= 32)   // warp-specialised TMA kernel
+        return dense_fwd_tma(s, heads, head_dim, scale, score_scale, dropout_p, sd, q, k, v, out, lse, node_scores,
+                             status, st);
     return launch_fwd<64>(s, heads, head_dim, scale, score_scale, dropout_p, sd, q, k, v, out, lse, node_scores,
                           status, st);
 }
@@ -627,14 +628,20 @@ int launch_bwd(int64_t s, int heads, int head_dim, float scale, float drop_p, ui
     cudaMemsetAsync(dq_acc, 0, sizeof(float) * (size_t)n, st);
     dense_delta_kernel<<<(unsigned)((s * heads + 255) / 256), 256, 0, st>>>(
         (int)s, heads, head_dim, (const __nv_bfloat16 *)out, (const __nv_bfloat16 *)dout, delta);
-    auto fn = dense_bwd_kernel<DP>;
-    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kBytes) != cudaSuccess)
-        return NGT_ERR_CUDA;
-    dim3 grid((unsigned)((s + BN - 1) / BN), (unsigned)heads);
-    fn<<<grid, kThreads, L::kBytes, st>>>((int)s, heads, head_dim, scale, drop_p, seed, (const __nv_bfloat16 *)q,
-                                          (const __nv_bfloat16 *)k, (const __nv_bfloat16 *)v,
-                                          (const __nv_bfloat16 *)dout, lse, delta, dq_acc, (__nv_bfloat16 *)dk,
-                                          (__nv_bfloat16 *)dv, status);
+    if constexpr (DP == 32) {   // head_dim <= 32: the warp-specialised TMA kernel
+        const int rc = dense_bwd_tma(s, heads, head_dim, scale, drop_p, seed, q, k, v, dout, lse, delta, dq_acc, dk,
+                                     dv, status, st);
+        if (rc != NGT_OK) return rc;
+    } else {
+        auto fn = dense_bwd_kernel<DP>;
+        if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kBytes) != cudaSuccess)
+            return NGT_ERR_CUDA;
+        dim3 grid((unsigned)((s + BN - 1) / BN), (unsigned)heads);
+        fn<<<grid, kThreads, L::kBytes, st>>>((int)s, heads, head_dim, scale, drop_p, seed, (const __nv_bfloat16 *)q,
+                                              (const __nv_bfloat16 *)k, (const __nv_bfloat16 *)v,
+                                              (const __nv_bfloat16 *)dout, lse, delta, dq_acc, (__nv_bfloat16 *)dk,
+                                              (__nv_bfloat16 *)dv, status);
+    }
     dense_dq_cast_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(n, dq_acc, (__nv_bfloat16 *)dq);
     NGT_CHECK_LAUNCH();
     return NGT_OK;

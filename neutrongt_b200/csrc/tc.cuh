@@ -79,6 +79,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+// Arrive and raise the phase's expected transaction bytes (for TMA completions).
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+// 4-D tiled TMA load global -> shared, completion counted in bytes on `bar`.  No multicast.
+__device__ __forceinline__ void tma_load_4d(void *dst, const void *tmap, int c0, int c1, int c2, int c3,
+                                            uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_addr(bar))
+        : "memory");
+}
+
 // Bounded wait: returns false if the phase did not complete within `limit` polls.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint32_t limit) {
     for (uint32_t i = 0; i < limit; i++)
@@ -133,6 +153,18 @@ __device__ __forceinline__ void st32(uint32_t taddr, const float (&v)[32]) {
           "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
           "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
         : "memory");
+}
+
+// One fp32 column of this thread's TMEM lane.
+__device__ __forceinline__ float ld1(uint32_t taddr) {
+    uint32_t r;
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r)
+        : "r"(taddr)
+        : "memory");
+    return __uint_as_float(r);
 }
 
 __device__ __forceinline__ void wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }

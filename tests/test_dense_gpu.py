@@ -55,7 +55,8 @@ def _inputs(s, H, D, seed):
 
 
 @pytest.mark.parametrize("s,H,D", [(128, 1, 32), (128, 2, 24), (200, 4, 24), (1000, 2, 16), (300, 1, 64),
-                                   (1024, 4, 24)])
+                                   (1024, 4, 24), (129, 1, 16), (640, 1, 24), (1500, 3, 8), (4096, 2, 32),
+                                   (700, 2, 40)])
 def test_forward_and_backward_match_reference(cuda, s, H, D):
     from neutrongt_b200.dense_attention import dense_attention
     q, k, v, dout = _inputs(s, H, D, s + H + D)
