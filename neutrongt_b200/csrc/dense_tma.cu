@@ -105,13 +105,6 @@ __device__ __forceinline__ bool try_wait_sleep(uint64_t *bar, uint32_t parity) {
 }
 constexpr uint32_t kSleepPolls = 1u << 21;   // x <= 1 us each: a bound of ~2 s
 
-// Wait by one thread (bounded); on timeout raise the abort.
-__device__ __forceinline__ bool wait1(uint64_t *bar, uint32_t parity, const Abort &ab) {
-    if (tc::mbar_wait_bounded(bar, parity, kWaitLimit)) return true;
-    ab.raise();
-    return false;
-}
-
 // Warp-uniform wait: every lane polls (its own acquire), one vote decides for the warp.
 __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, const Abort &ab) {
     bool ok = false;
@@ -574,33 +567,36 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------------------------
-// Backward: one CTA = one head x one 128-key tile; loops over 128-query blocks, each in two
-// 64-query halves (softmax warpgroup b owns half b):
-//   S^T_b = K Q_b^T, dP^T_b = V dO_b^T               (TMEM, lanes = keys)
-//   P = exp2(S * scale * log2e - lse * log2e), dS = P (dP - delta)   (registers -> smem)
-//   dV += P^T dO, dK += dS^T Q                        (TMEM accumulators, whole loop)
-//   dQ_part = dS K  (both halves, K = 128 keys)      (TMEM, two buffers) -> fp32 atomics
+// Backward: one CTA = one head x one 128-key tile; loops over 128-query blocks qb.  Lanes are
+// queries (so lse and delta are per-thread constants), the key tile is split in two 64-key
+// halves, each with its own softmax warpgroup and its own S / dP MMA warp; a third MMA warp
+// accumulates once both halves of a query block are staged:
+//   S_b = Q K_b^T, dP_b = dO V_b^T                    (TMEM, lanes = queries)
+//   P = 2^(S * scale * log2e - lse * log2e), dS = P (dP - delta)   (registers -> shared memory)
+//   dV += P^T dO, dK += dS^T Q   (P, dS read MN-major: lanes = keys)
+//   dQ(qb) = dS K                 (TMEM, two buffers) -> fp32 atomics by the epilogue warps
 // ------------------------------------------------------------------------------------
 struct BwdL {
     static constexpr int NST = 3;   // Q / dO / lse / delta stages
     static constexpr uint32_t kK = 0;
     static constexpr uint32_t kV = kK + kTileBytes;
     static constexpr uint32_t kStage = kV + kTileBytes;
-    static constexpr uint32_t kStageBytes = 2 * kTileBytes + 2 * TILE * 4;   // Q, dO, lse, delta
-    static constexpr uint32_t kPS = kStage + NST * kStageBytes;              // 2 x {P^T, dS^T}
+    static constexpr uint32_t kStageBytes = 2 * kTileBytes + 2 * TILE * 4;   // Q, dO, -lse*log2e, -delta
+    static constexpr uint32_t kPS = kStage + NST * kStageBytes;              // 2 x {P, dS} [128 q x 128 keys]
     static constexpr uint32_t kPSBytes = 2 * TILE * TILE * 2;
     static constexpr uint32_t kBars = kPS + 2 * kPSBytes;
     enum {
         KVF = 0,
         QF = 1,
-        QE = QF + NST,
-        SF = QE + NST,   // [2] S^T_b, dP^T_b in TMEM
-        SD = SF + 2,     // [2] half b: TMEM read, P^T / dS^T staged
-        PE = SD + 2,     // [2] P^T / dS^T buffer (query-block parity) read by its MMAs
-        DQF = PE + 2,    // [2] dQ partial in TMEM
-        DQE = DQF + 2,   // [2] dQ partial read
-        ACC = DQE + 2,   // all MMAs done
-        NB = ACC + 1
+        QE = QF + NST,   // count 11: three MMA warps' commits + the 8 softmax warps
+        SF = QE + NST,   // [half] S_b, dP_b in TMEM
+        SR = SF + 2,     // [half] S_b, dP_b read from TMEM (the buffer may be overwritten)
+        DS = SR + 2,     // [parity] P / dS of both halves staged (count 8)
+        PE = DS + 2,     // [parity] P / dS buffer read by the accumulating MMAs
+        DQF = PE + 2,    // [parity] dQ partial in TMEM
+        DQE = DQF + 2,   // [parity] dQ partial read
+        ACC = DQE + 2,   // [3] each MMA warp's MMAs done
+        NB = ACC + 3
     };
     static constexpr uint32_t kSlot = kBars + NB * 8;
     static constexpr uint32_t kAbort = kSlot + 4;
@@ -610,6 +606,36 @@ static_assert(BwdL::kStage % 1024 == 0 && BwdL::kStageBytes % 1024 == 0 && BwdL:
               "TMA destinations 1 KiB aligned");
 static_assert(BwdL::kBytes <= 232448, "shared memory");
 
+// 32 keys of one query row (no dropout): P = 2^(s * sl2 + nl), dS = P (dp + nd) with the row's
+// nl = -lse * log2e and nd = -delta; P and dS as bf16 into the row's next four 16-byte chunks
+// (chunk stride 128 bytes).  One pair in four takes the polynomial exp2.
+__device__ __forceinline__ void bwd_chunk_fast(const float (&sv)[32], const float (&dp)[32], f32x2 sl2x2, f32x2 nl2,
+                                               f32x2 nd2, uint8_t *prow, uint8_t *drow) {
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        uint32_t pw[4], dw[4];
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+            const f32x2 x = ffma2(pk(sv[c * 8 + e], sv[c * 8 + e + 1]), sl2x2, nl2);
+            float x0, x1, p0, p1;
+            upk(x, x0, x1);
+            if (e == 0) {
+                exp2_poly(x0, x1, p0, p1);
+            } else {
+                p0 = tc::ex2(x0);
+                p1 = tc::ex2(x1);
+            }
+            const f32x2 ds = fmul2(pk(p0, p1), fadd2(pk(dp[c * 8 + e], dp[c * 8 + e + 1]), nd2));
+            float d0, d1;
+            upk(ds, d0, d1);
+            pw[e / 2] = tc::pack_bf16(p0, p1);
+            dw[e / 2] = tc::pack_bf16(d0, d1);
+        }
+        st16(prow + c * 128, pw[0], pw[1], pw[2], pw[3]);
+        st16(drow + c * 128, dw[0], dw[1], dw[2], dw[3]);
+    }
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     dense_bwd_tma_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do, int s,
@@ -618,7 +644,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                          __nv_bfloat16 *__restrict__ dv, int *__restrict__ status) {
     using L = BwdL;
     constexpr int NST = L::NST;
-    constexpr int QH = TILE / 2;
+    constexpr int KH = TILE / 2;   // keys per half
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::kBars);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::kSlot);
@@ -632,16 +658,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::mbar_init(&bars[L::KVF], 1);
         for (int i = 0; i < NST; i++) {
             tc::mbar_init(&bars[L::QF + i], 2);
-            tc::mbar_init(&bars[L::QE + i], 1 + 8);   // MMA commit + the 8 softmax warps
+            tc::mbar_init(&bars[L::QE + i], 3 + 8);
         }
         for (int b = 0; b < 2; b++) {
             tc::mbar_init(&bars[L::SF + b], 1);
-            tc::mbar_init(&bars[L::SD + b], 4);
+            tc::mbar_init(&bars[L::SR + b], 4);
+            tc::mbar_init(&bars[L::DS + b], 8);
             tc::mbar_init(&bars[L::PE + b], 1);
             tc::mbar_init(&bars[L::DQF + b], 1);
             tc::mbar_init(&bars[L::DQE + b], 4);
         }
-        tc::mbar_init(&bars[L::ACC], 1);
+        for (int i = 0; i < 3; i++) tc::mbar_init(&bars[L::ACC + i], 1);
         *reinterpret_cast<volatile int *>(smem + L::kAbort) = 0;
         tc::mbar_init_fence();
     }
@@ -649,7 +676,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
-    // TMEM columns: S^T_b at b * 128, dP^T_b at b * 128 + 64, dV at 256, dK at 288, dQ_c at 320 + c * 32
+    // TMEM columns: S_b at b * 128, dP_b at b * 128 + 64 (lanes = queries); dV at 256, dK at 288
+    // (lanes = keys); dQ_c at 320 + c * 32 (lanes = queries)
     const uint32_t tDV = tmem + 256, tDK = tmem + 256 + DP, tDQ0 = tmem + 256 + 2 * DP;
 
     if (warp == 0) {
@@ -660,6 +688,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc::tma_load_4d(smem + L::kK, &tm_k, 0, k0, 0, h, &bars[L::KVF]);
             tc::tma_load_4d(smem + L::kV, &tm_v, 0, k0, 0, h, &bars[L::KVF]);
         }
+        // lse and delta of a query block are read one block ahead, so their global-load latency
+        // overlaps the wait for a free stage; rows past s get P = 0
+        float nl4[TILE / 32], nd4[TILE / 32];
+        auto load_rows = [&](int q0) {
+#pragma unroll
+            for (int k = 0; k < TILE / 32; k++) {
+                const int qi = q0 + lane + 32 * k;
+                nl4[k] = qi < s ? -lse[(size_t)h * s + qi] * kLog2e : -INFINITY;
+                nd4[k] = qi < s ? -delta[(size_t)h * s + qi] : 0.f;
+            }
+        };
+        load_rows(0);
         for (int qb = 0; qb < nqb; qb++) {
             if (ab.set()) break;
             const int st = qb % NST, q0 = qb * TILE;
@@ -670,91 +710,111 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc::tma_load_4d(sb, &tm_q, 0, q0, 0, h, &bars[L::QF + st]);
                 tc::tma_load_4d(sb + kTileBytes, &tm_do, 0, q0, 0, h, &bars[L::QF + st]);
             }
-            float *sl = reinterpret_cast<float *>(sb + 2 * kTileBytes), *sd = sl + TILE;
-            for (int i = lane; i < TILE; i += 32) {   // rows past s: P = 0
-                const int qi = q0 + i;
-                sl[i] = qi < s ? lse[(size_t)h * s + qi] * kLog2e : INFINITY;
-                sd[i] = qi < s ? delta[(size_t)h * s + qi] : 0.f;
+            float *nl = reinterpret_cast<float *>(sb + 2 * kTileBytes), *nd = nl + TILE;
+#pragma unroll
+            for (int k = 0; k < TILE / 32; k++) {
+                nl[lane + 32 * k] = nl4[k];
+                nd[lane + 32 * k] = nd4[k];
             }
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&bars[L::QF + st]);
             issued = qb + 1;
+            if (qb + 1 < nqb) load_rows(q0 + TILE);
         }
         if (lane == 0) {
             tc::mbar_wait_bounded(&bars[L::KVF], 0, kWaitLimit);
             for (int qb = issued - NST < 0 ? 0 : issued - NST; qb < issued; qb++)
                 tc::mbar_wait_bounded(&bars[L::QF + qb % NST], (qb / NST) & 1, kWaitLimit);
         }
-    } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
-        if (lane == 0) {
-            constexpr uint32_t idesc_sq = tc::idesc_bf16(TILE, QH, false, false);   // [keys x 64 queries]
-            constexpr uint32_t idesc_acc = tc::idesc_bf16(TILE, DP, false, true);   // [keys x d]
-            constexpr uint32_t idesc_dq = tc::idesc_bf16(TILE, DP, true, true);     // [queries x d]
-            const uint32_t aK = tc::smem_addr(smem + L::kK), aV = tc::smem_addr(smem + L::kV),
-                           aSt = tc::smem_addr(smem + L::kStage), aPS = tc::smem_addr(smem + L::kPS);
-            auto issue_sdp = [&](int qb, int b) {
-                const uint32_t aq = aSt + (qb % NST) * L::kStageBytes + b * QH * 16, ado = aq + kTileBytes;
+    } else if (warp == 1 || warp == 2) {
+        // ---------------- S / dP MMA warp of key half b ----------------
+        const int b = warp - 1;
+        constexpr uint32_t idesc_s = tc::idesc_bf16(TILE, KH, false, false);   // [queries x 64 keys]
+        const uint32_t aK = tc::smem_addr(smem + L::kK) + b * KH * 16, aV = tc::smem_addr(smem + L::kV) + b * KH * 16,
+                       aSt = tc::smem_addr(smem + L::kStage);
+        const uint32_t tS = tmem + b * TILE;
+        const bool leader = lane == 0;
+        auto issue_sdp = [&](int qb) {   // S_b(qb), dP_b(qb); the stage's Q / dO reads end with them
+            if (leader) {
+                const uint32_t aq = aSt + (qb % NST) * L::kStageBytes, ado = aq + kTileBytes;
 #pragma unroll
                 for (int kk = 0; kk < DP / 16; kk++) {
-                    tc::mma_bf16(tmem + b * TILE, kmajor_tma(aK + kk * 4096), kmajor_tma(aq + kk * 4096), idesc_sq,
-                                 kk > 0);
-                    tc::mma_bf16(tmem + b * TILE + QH, kmajor_tma(aV + kk * 4096), kmajor_tma(ado + kk * 4096),
-                                 idesc_sq, kk > 0);
+                    tc::mma_bf16(tS, kmajor_tma(aq + kk * 4096), kmajor_tma(aK + kk * 4096), idesc_s, kk > 0);
+                    tc::mma_bf16(tS + KH, kmajor_tma(ado + kk * 4096), kmajor_tma(aV + kk * 4096), idesc_s, kk > 0);
                 }
                 tc::commit(&bars[L::SF + b]);
-            };
-            bool ok = wait1(&bars[L::KVF], 0, ab) && wait1(&bars[L::QF], 0, ab);
-            if (ok) {
-                tc::fence_after_sync();
-                issue_sdp(0, 0);
-                issue_sdp(0, 1);
+                tc::commit(&bars[L::QE + qb % NST]);
             }
-            for (int qb = 0; ok && qb < nqb; qb++) {
-                const int st = qb % NST, par = qb & 1;
+            __syncwarp();
+        };
+        bool ok = warp_wait(&bars[L::KVF], 0, ab) && warp_wait(&bars[L::QF], 0, ab);
+        if (ok) {
+            tc::fence_after_sync();
+            issue_sdp(0);
+        }
+        for (int qb = 0; ok && qb + 1 < nqb; qb++) {
+            if (!(ok = warp_wait(&bars[L::SR + b], qb & 1, ab))) break;
+            if (!(ok = warp_wait(&bars[L::QF + (qb + 1) % NST], ((qb + 1) / NST) & 1, ab))) break;
+            tc::fence_after_sync();
+            issue_sdp(qb + 1);
+        }
+        if (leader) {
+            tc::commit(&bars[L::ACC + b]);
+            tc::mbar_wait_bounded(&bars[L::ACC + b], 0, kWaitLimit);   // own MMAs drained
+        }
+        __syncwarp();
+    } else if (warp == 3) {
+        // ---------------- accumulating MMA warp: dV, dK, dQ ----------------
+        constexpr uint32_t idesc_kv = tc::idesc_bf16(TILE, DP, true, true);    // [keys x d], P / dS read MN-major
+        constexpr uint32_t idesc_dq = tc::idesc_bf16(TILE, DP, false, true);   // [queries x d]
+        const uint32_t aK = tc::smem_addr(smem + L::kK), aSt = tc::smem_addr(smem + L::kStage),
+                       aPS = tc::smem_addr(smem + L::kPS);
+        const bool leader = lane == 0;
+        bool ok = warp_wait(&bars[L::KVF], 0, ab);
+        for (int qb = 0; ok && qb < nqb; qb++) {
+            const int st = qb % NST, par = qb & 1;
+            if (!(ok = warp_wait(&bars[L::DS + par], (qb >> 1) & 1, ab))) break;
+            if (!(ok = warp_wait(&bars[L::QF + st], (qb / NST) & 1, ab))) break;
+            if (!(ok = warp_wait(&bars[L::DQE + par], ((qb >> 1) & 1) ^ 1, ab))) break;
+            tc::fence_after_sync();
+            if (leader) {
                 const uint32_t aq = aSt + st * L::kStageBytes, ado = aq + kTileBytes;
-                const uint32_t apt = aPS + par * L::kPSBytes, adst = apt + TILE * TILE * 2;
-                for (int b = 0; b < 2; b++) {
-                    if (!(ok = wait1(&bars[L::SD + b], qb & 1, ab))) break;
-                    tc::fence_after_sync();
+                const uint32_t ap = aPS + par * L::kPSBytes, ads = ap + TILE * TILE * 2;
 #pragma unroll
-                    for (int kk = 0; kk < QH / 16; kk++) {   // K = queries of half b
-                        const int qc = b * (QH / 8) + kk * 2;          // query chunk in P^T / dS^T
-                        const uint32_t qrow = (b * QH + kk * 16) * 16;   // query row in the Q / dO tiles
-                        const uint32_t acc = (qb > 0 || b > 0 || kk > 0);
-                        tc::mma_bf16(tDV, kmajor_sq(apt + qc * 128), mnmajor_tma(ado + qrow), idesc_acc, acc);
-                        tc::mma_bf16(tDK, kmajor_sq(adst + qc * 128), mnmajor_tma(aq + qrow), idesc_acc, acc);
-                    }
-                    if (b == 0 && qb + 1 < nqb) {
-                        if (!(ok = wait1(&bars[L::QF + (qb + 1) % NST], ((qb + 1) / NST) & 1, ab))) break;
-                        tc::fence_after_sync();
-                        issue_sdp(qb + 1, 0);
-                    }
+                for (int kk = 0; kk < TILE / 16; kk++) {   // K = 128 queries
+                    const uint32_t acc = (qb > 0 || kk > 0);
+                    tc::mma_bf16(tDV, mnmajor_sq(ap + kk * 4096), mnmajor_tma(ado + kk * 256), idesc_kv, acc);
+                    tc::mma_bf16(tDK, mnmajor_sq(ads + kk * 4096), mnmajor_tma(aq + kk * 256), idesc_kv, acc);
                 }
-                if (!ok) break;
-                if (!(ok = wait1(&bars[L::DQE + par], ((qb >> 1) & 1) ^ 1, ab))) break;
-                tc::fence_after_sync();
 #pragma unroll
-                for (int kk = 0; kk < TILE / 16; kk++)   // dQ = dS K: dS^T read MN-major, K read MN-major
-                    tc::mma_bf16(tDQ0 + par * DP, mnmajor_sq(adst + kk * 4096), mnmajor_tma(aK + kk * 256),
-                                 idesc_dq, kk > 0);
+                for (int kk = 0; kk < TILE / 16; kk++)   // K = 128 keys: dS read K-major, K read MN-major
+                    tc::mma_bf16(tDQ0 + par * DP, kmajor_sq(ads + kk * 256), mnmajor_tma(aK + kk * 256), idesc_dq,
+                                 kk > 0);
                 tc::commit(&bars[L::DQF + par]);
                 tc::commit(&bars[L::PE + par]);
                 tc::commit(&bars[L::QE + st]);
-                if (qb + 1 < nqb) issue_sdp(qb + 1, 1);
             }
-            tc::commit(&bars[L::ACC]);
-            tc::mbar_wait_bounded(&bars[L::ACC], 0, kWaitLimit);   // own MMAs drained
+            __syncwarp();
         }
+        if (leader) {
+            tc::commit(&bars[L::ACC + 2]);
+            tc::mbar_wait_bounded(&bars[L::ACC + 2], 0, kWaitLimit);
+        }
+        __syncwarp();
     } else if (warp >= 4 && warp < 12) {
-        // ---------------- softmax warpgroups: half b, key row r ----------------
+        // ---------------- softmax warpgroups: key half b, query row r ----------------
         const int b = (warp - 4) >> 2, r = tid & 127;
-        const int kj = k0 + r;
         const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-        const uint32_t tS = tmem + b * TILE, tDP = tS + QH;
+        const uint32_t tS = tmem + b * TILE + lane_off, tDP = tS + KH;
         const float sl2 = scale * kLog2e;
+        const f32x2 sl2x2 = pk(sl2, sl2);
         const uint32_t thr = drop_p > 0.f ? (uint32_t)fminf(drop_p * 4294967296.0f, 4294967295.0f) : 0u;
         const float keep_scale = drop_p > 0.f ? 1.0f / (1.0f - drop_p) : 1.0f;
+        auto release_s = [&](int half) {
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&bars[L::SR + half]);
+        };
         for (int qb = 0; qb < nqb; qb++) {
             const int st = qb % NST, par = qb & 1;
             if (ab.set()) break;
@@ -762,48 +822,52 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!warp_wait(&bars[L::QF + st], (qb / NST) & 1, ab)) break;   // lse / delta visible
             if (!warp_wait(&bars[L::PE + par], ((qb >> 1) & 1) ^ 1, ab)) break;
             tc::fence_after_sync();
-            const uint8_t *sb = smem + L::kStage + st * L::kStageBytes;
-            const float4 *sl4 = reinterpret_cast<const float4 *>(sb + 2 * kTileBytes) + b * (QH / 4);
-            const float4 *sd4 = sl4 + TILE / 4;
+            const float *sl = reinterpret_cast<const float *>(smem + L::kStage + st * L::kStageBytes + 2 * kTileBytes);
+            const float nl = sl[r], nd = sl[TILE + r];
             uint8_t *pt = smem + L::kPS + par * L::kPSBytes, *dst = pt + TILE * TILE * 2;
-            const int q0 = qb * TILE;
+            const int qi = qb * TILE + r;
+            if (!thr) {
+                const f32x2 nl2 = pk(nl, nl), nd2 = pk(nd, nd);
 #pragma unroll 1
-            for (int c4 = 0; c4 < QH / 32; c4++) {
-                float sv[32], dp[32];
-                tc::ld32(tS + lane_off + c4 * 32, sv);
-                tc::ld32(tDP + lane_off + c4 * 32, dp);
+                for (int c4 = 0; c4 < KH / 32; c4++) {
+                    float sv[32], dp[32];
+                    tc::ld32(tS + c4 * 32, sv);
+                    tc::ld32(tDP + c4 * 32, dp);
+                    if (c4 == KH / 32 - 1) release_s(b);   // the next S_b, dP_b may overwrite the buffer
+                    const int chunk = b * (KH / 8) + c4 * 4;
+                    bwd_chunk_fast(sv, dp, sl2x2, nl2, nd2, pt + sq_off(r, chunk), dst + sq_off(r, chunk));
+                }
+            } else {   // attention dropout: P and dP masked by the forward's keep decisions
+#pragma unroll 1
+                for (int c4 = 0; c4 < KH / 32; c4++) {
+                    float sv[32], dp[32];
+                    tc::ld32(tS + c4 * 32, sv);
+                    tc::ld32(tDP + c4 * 32, dp);
+                    if (c4 == KH / 32 - 1) release_s(b);
 #pragma unroll
-                for (int c = 0; c < 4; c++) {
-                    const float4 la = sl4[c4 * 8 + c * 2], lb = sl4[c4 * 8 + c * 2 + 1];
-                    const float4 da = sd4[c4 * 8 + c * 2], db = sd4[c4 * 8 + c * 2 + 1];
-                    const float lq[8] = {la.x, la.y, la.z, la.w, lb.x, lb.y, lb.z, lb.w};
-                    const float dq[8] = {da.x, da.y, da.z, da.w, db.x, db.y, db.z, db.w};
-                    float pv[8], dsv[8];
+                    for (int c = 0; c < 4; c++) {
+                        float pv[8], dsv[8];
 #pragma unroll
-                    for (int e = 0; e < 8; e++) {
-                        const int j = c * 8 + e;
-                        const float p = tc::ex2(fmaf(sv[j], sl2, -lq[e]));
-                        float g = dp[j], pd = p;
-                        if (thr) {
-                            const bool keep = keep_elem(seed, h, q0 + b * QH + c4 * 32 + j, kj, thr);
-                            pd = keep ? p * keep_scale : 0.f;
-                            g = keep ? g * keep_scale : 0.f;
+                        for (int e = 0; e < 8; e++) {
+                            const int j = c * 8 + e;
+                            const float p = tc::ex2(fmaf(sv[j], sl2, nl));
+                            const bool keep = keep_elem(seed, h, qi, k0 + b * KH + c4 * 32 + j, thr);
+                            pv[e] = keep ? p * keep_scale : 0.f;
+                            dsv[e] = p * ((keep ? dp[j] * keep_scale : 0.f) + nd);
                         }
-                        pv[e] = pd;
-                        dsv[e] = p * (g - dq[e]);
+                        const int chunk = b * (KH / 8) + c4 * 4 + c;
+                        st16(pt + sq_off(r, chunk), tc::pack_bf16(pv[0], pv[1]), tc::pack_bf16(pv[2], pv[3]),
+                             tc::pack_bf16(pv[4], pv[5]), tc::pack_bf16(pv[6], pv[7]));
+                        st16(dst + sq_off(r, chunk), tc::pack_bf16(dsv[0], dsv[1]), tc::pack_bf16(dsv[2], dsv[3]),
+                             tc::pack_bf16(dsv[4], dsv[5]), tc::pack_bf16(dsv[6], dsv[7]));
                     }
-                    const int chunk = b * (QH / 8) + c4 * 4 + c;
-                    st16(pt + sq_off(r, chunk), tc::pack_bf16(pv[0], pv[1]), tc::pack_bf16(pv[2], pv[3]),
-                         tc::pack_bf16(pv[4], pv[5]), tc::pack_bf16(pv[6], pv[7]));
-                    st16(dst + sq_off(r, chunk), tc::pack_bf16(dsv[0], dsv[1]), tc::pack_bf16(dsv[2], dsv[3]),
-                         tc::pack_bf16(dsv[4], dsv[5]), tc::pack_bf16(dsv[6], dsv[7]));
                 }
             }
             tc::fence_smem_for_async();
             tc::fence_before_sync();
             __syncwarp();
             if (lane == 0) {
-                tc::mbar_arrive(&bars[L::SD + b]);
+                tc::mbar_arrive(&bars[L::DS + par]);
                 tc::mbar_arrive(&bars[L::QE + st]);
             }
         }
@@ -815,7 +879,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (int qb = 0; qb < nqb; qb++) {
             const int par = qb & 1;
-            if (ab.set() || !(ok = warp_wait(&bars[L::DQF + par], (qb >> 1) & 1, ab))) { ok = false; break; }
+            if (ab.set() || !(ok = warp_wait(&bars[L::DQF + par], (qb >> 1) & 1, ab))) {
+                ok = false;
+                break;
+            }
             tc::fence_after_sync();
             float g[32];
             tc::ld32(tDQ0 + par * DP + lane_off, g);
@@ -830,24 +897,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (d < D) red_add_v4(p + d, g[d] * scale, g[d + 1] * scale, g[d + 2] * scale, g[d + 3] * scale);
             }
         }
-        if (ok && warp_wait(&bars[L::ACC], 0, ab) && !ab.set()) {
+        if (ok && warp_wait(&bars[L::ACC + 2], 0, ab) && !ab.set()) {
             tc::fence_after_sync();
-            float gv[32], gk[32];
-            tc::ld32(tDV + lane_off, gv);
-            tc::ld32(tDK + lane_off, gk);
             const int kj = k0 + r;
-            if (kj < s) {
+#pragma unroll 1
+            for (int which = 0; which < 2; which++) {   // dV, then dK * scale
+                float g[32];
+                tc::ld32((which ? tDK : tDV) + lane_off, g);
+                const float f = which ? scale : 1.f;
+                __nv_bfloat16 *dst = (which ? dk : dv) + (size_t)kj * rs + (size_t)h * D;
+                if (kj < s) {
 #pragma unroll
-                for (int c = 0; c < 4; c++) {
-                    if (c * 8 >= D) continue;
-                    st16(reinterpret_cast<uint8_t *>(dv + (size_t)kj * rs + (size_t)h * D + c * 8),
-                         tc::pack_bf16(gv[c * 8], gv[c * 8 + 1]), tc::pack_bf16(gv[c * 8 + 2], gv[c * 8 + 3]),
-                         tc::pack_bf16(gv[c * 8 + 4], gv[c * 8 + 5]), tc::pack_bf16(gv[c * 8 + 6], gv[c * 8 + 7]));
-                    st16(reinterpret_cast<uint8_t *>(dk + (size_t)kj * rs + (size_t)h * D + c * 8),
-                         tc::pack_bf16(gk[c * 8] * scale, gk[c * 8 + 1] * scale),
-                         tc::pack_bf16(gk[c * 8 + 2] * scale, gk[c * 8 + 3] * scale),
-                         tc::pack_bf16(gk[c * 8 + 4] * scale, gk[c * 8 + 5] * scale),
-                         tc::pack_bf16(gk[c * 8 + 6] * scale, gk[c * 8 + 7] * scale));
+                    for (int c = 0; c < 4; c++) {
+                        if (c * 8 >= D) continue;
+                        st16(reinterpret_cast<uint8_t *>(dst + c * 8), tc::pack_bf16(g[c * 8] * f, g[c * 8 + 1] * f),
+                             tc::pack_bf16(g[c * 8 + 2] * f, g[c * 8 + 3] * f),
+                             tc::pack_bf16(g[c * 8 + 4] * f, g[c * 8 + 5] * f),
+                             tc::pack_bf16(g[c * 8 + 6] * f, g[c * 8 + 7] * f));
+                    }
                 }
             }
         }
