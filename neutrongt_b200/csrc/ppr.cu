@@ -8,23 +8,27 @@
 // independent, so here one CTA owns one seed's row for all iterations and the row never
 // leaves the chip between steps:
 //
-//   pruned mode (iter_topk > 0, the scripts' setting): the row's state has <= k entries;
-//   its expansion sum_j contrib_j * e_adj(j) is accumulated in an open-addressing hash
-//   table (shared memory, or a per-CTA region of the workspace when the expansion of a
-//   hub-heavy state does not fit), the teleport is added, and the top-k is selected with
-//   per-thread register lists merged by a block tournament.
+//   pruned mode (iter_topk > 0, the scripts' setting): the row's state has <= k entries and
+//   its expansion sum_j contrib_j * e_adj(j) is a k-way merge of the state's adjacency lists
+//   (CSR rows with ascending columns, as the reference's CSR writer produces them): the lists
+//   are staged in shared memory (read in place from global memory when they do not fit),
+//   every thread owns a column range (split at quantiles of the longest list) and merges its
+//   part of every list, adding each column's contributions in list order; the teleport is
+//   added and the top-k is selected from per-thread register lists, merged per warp with
+//   shuffles and then across warps by one warp.
 //
 //   dense mode (iter_topk <= 0): the state is a dense vector of n doubles per CTA in the
 //   workspace and each step pulls over the in-adjacency (transpose CSR).
 //
 // Canonical arithmetic (identical to oracle/appnp_oracle.c, bit for bit): fp64;
 // contrib_j = state_j * (1 / max(deg_j, 1)); contributions to a column are added in
-// ascending source column (pruned: the state entries are expanded one at a time with a
-// barrier between them, and within one entry every column is distinct — or, for repeated
-// edges, receives the same value twice, which commutes; dense: the pull walks in-neighbours
-// in ascending order); value = acc * (1 - alpha) [+ alpha at the seed]; ranking by
+// ascending source column (pruned: the merge visits the state's lists in column order and a
+// repeated edge adds its contribution once per copy; dense: the pull walks in-neighbours in
+// ascending order); value = acc * (1 - alpha) [+ alpha at the seed]; ranking by
 // (value desc, column asc).  All products/sums use explicit round-to-nearest intrinsics so
 // no FMA contraction can change a bit.
+#include <climits>
+
 #include "common.cuh"
 
 namespace ngt {
@@ -33,8 +37,7 @@ namespace {
 constexpr int kPprThreads = 256;
 constexpr int kPprWarps = kPprThreads / 32;
 constexpr int kMaxCtas = 148 * 4;
-constexpr int kSmemSlots = 4096;  // 48 KiB of keys + values
-constexpr int kEmpty = -1;
+constexpr int kStageCap = 12288;  // staged adjacency entries (48 KiB)
 
 struct Cand {
     double v;
@@ -45,9 +48,6 @@ __device__ __forceinline__ bool ranks_before(double va, int ca, double vb, int c
     return va > vb || (va == vb && ca < cb);
 }
 
-__device__ __forceinline__ uint32_t hash_slot(int c, uint32_t mask) {
-    return ((uint32_t)c * 2654435761u) & mask;
-}
 
 // Per-thread sorted list of its best KMAX candidates (registers, static indexing only).
 template <int KMAX>
@@ -149,20 +149,143 @@ __device__ int block_merge_topk(TopList<KMAX> &L, int k, MergeSmem &ms, int *out
     return count;
 }
 
+// Exact top-k of the block's per-thread lists without block-wide barriers per round: every
+// warp extracts its k best with shuffles (k rounds of a warp arg-max), warp 0 merges the
+// warps' lists the same way.  Writes up to k entries in rank order to (out_c, out_v) and
+// returns the count (valid in every thread after the trailing barrier).
+template <int KMAX>
+__device__ int block_topk(TopList<KMAX> &L, int k, double *wv, int *wc, int *count_out, int *out_c, double *out_v) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int r = 0; r < k; r++) {   // warp level
+        double bv = L.v[0];
+        int bc = L.c[0], bt = lane;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const double ov = __shfl_xor_sync(0xffffffffu, bv, off);
+            const int oc = __shfl_xor_sync(0xffffffffu, bc, off);
+            const int ot = __shfl_xor_sync(0xffffffffu, bt, off);
+            if (ranks_before(ov, oc, bv, bc)) {
+                bv = ov;
+                bc = oc;
+                bt = ot;
+            }
+        }
+        if (lane == bt) L.pop();
+        if (lane == 0) {
+            wv[warp * KMAX + r] = bv;
+            wc[warp * KMAX + r] = bc;
+        }
+    }
+    __syncthreads();
+    if (warp == 0) {   // lane takes candidates lane, lane + 32, ... of the warps' lists laid end to end
+        constexpr int PER = (kPprWarps * KMAX + 31) / 32;
+        TopList<PER> M;
+        M.init();
+        for (int f = lane; f < kPprWarps * k; f += 32) M.offer(wv[(f / k) * KMAX + f % k], wc[(f / k) * KMAX + f % k]);
+        int cnt = 0;
+        for (int r = 0; r < k; r++) {
+            double bv = M.v[0];
+            int bc = M.c[0], bt = lane;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) {
+                const double ov = __shfl_xor_sync(0xffffffffu, bv, off);
+                const int oc = __shfl_xor_sync(0xffffffffu, bc, off);
+                const int ot = __shfl_xor_sync(0xffffffffu, bt, off);
+                if (ranks_before(ov, oc, bv, bc)) {
+                    bv = ov;
+                    bc = oc;
+                    bt = ot;
+                }
+            }
+            if (bv < 0.0) break;   // fewer than k candidates
+            if (lane == bt) M.pop();
+            if (lane == 0) {
+                out_c[r] = bc;
+                out_v[r] = bv;
+            }
+            cnt = r + 1;
+        }
+        if (lane == 0) *count_out = cnt;
+    }
+    __syncthreads();
+    return *count_out;
+}
+
 struct PrunedSmem {
-    int keys[kSmemSlots];
-    double vals[kSmemSlots];
-    int touched[kSmemSlots / 2];  // slots claimed this iteration (clear + scan list)
-    int ntouched;
-    int st_col[32];      // state sorted by column (expansion order)
+    int stage[kStageCap];   // the state's adjacency lists, concatenated, when they fit
+    int st_col[32];         // state sorted by column (list order = canonical add order)
     double st_val[32];
-    int sel_col[32];     // last selection in rank order
+    int sel_col[32];        // last selection in rank order
     double sel_val[32];
-    int st_n;
-    int64_t lsum;
-    int seed;
-    MergeSmem ms;
+    double contrib[32];     // state value / max(degree, 1) per list
+    int64_t lbeg[32];       // list start in col[]
+    int llen[32];
+    int wbeg[32];           // this column window's part of each list: [wbeg, wbeg + wlen)
+    int wlen[32];
+    int loff[33];           // window part start in stage[]
+    int bounds[kPprThreads + 1];
+    double wv[kPprWarps * 32];
+    int wc[kPprWarps * 32];
+    int st_n, staged, longest, total, cnt, seed;
 };
+
+// First index of a sorted list whose column is >= x.
+template <typename Rd>
+__device__ __forceinline__ int lower_bound(const Rd &rd, int len, int x) {
+    int lo = 0, hi = len;
+    while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (rd(mid) < x) lo = mid + 1;
+        else hi = mid;
+    }
+    return lo;
+}
+
+// Merge this thread's column range [lo, hi) of the state's lists into L.  `rd(i, p)` reads
+// entry p of list i.  Each column's contributions are added in list order, starting at 0.0.
+template <int KMAX, typename Rd>
+__device__ __forceinline__ void merge_range(const PrunedSmem &S, const Rd &rd, int st_n, int lo, int hi, int seed,
+                                            double alpha, double oma, TopList<KMAX> &L) {
+    int p[KMAX], e[KMAX], head[KMAX];
+#pragma unroll
+    for (int i = 0; i < KMAX; i++) {
+        p[i] = e[i] = 0;
+        head[i] = INT_MAX;
+        if (i < st_n) {
+            const int len = S.wlen[i];
+            // lists whose span misses [lo, hi) need no search
+            if (len > 0 && rd(i, len - 1) >= lo && rd(i, 0) < hi) {
+                p[i] = lower_bound([&](int q) { return rd(i, q); }, len, lo);
+                e[i] = hi == INT_MAX ? len : lower_bound([&](int q) { return rd(i, q); }, len, hi);
+                if (p[i] < e[i]) head[i] = rd(i, p[i]);
+            }
+        }
+    }
+    bool seed_seen = false;
+    for (;;) {
+        int v = INT_MAX;
+#pragma unroll
+        for (int i = 0; i < KMAX; i++) v = min(v, head[i]);
+        if (v == INT_MAX) break;
+        double acc = 0.0;
+#pragma unroll
+        for (int i = 0; i < KMAX; i++) {
+            while (head[i] == v) {   // a repeated edge adds once per copy
+                acc = __dadd_rn(acc, S.contrib[i]);
+                p[i]++;
+                head[i] = p[i] < e[i] ? rd(i, p[i]) : INT_MAX;
+            }
+        }
+        double val = __dmul_rn(acc, oma);
+        if (v == seed) {
+            val = __dadd_rn(val, alpha);
+            seed_seen = true;
+        }
+        L.offer(val, v);
+    }
+    // the teleport target always exists in the merged row
+    if (!seed_seen && seed >= lo && seed < hi) L.offer(__dadd_rn(__dmul_rn(0.0, oma), alpha), seed);
+}
 
 // ------------------------------------------------------------------------------------
 // pruned mode
@@ -173,23 +296,10 @@ __global__ void __launch_bounds__(kPprThreads)
                       double alpha, double oma, int iters, int iter_topk, int final_keep,
                       int source_start, int source_end, int keep_stride, int64_t *__restrict__ out_col,
                       float *__restrict__ out_val, double *__restrict__ out_val64,
-                      int *__restrict__ out_cnt, int *__restrict__ info, int *__restrict__ seed_counter,
-                      int *__restrict__ gkeys, double *__restrict__ gvals, int *__restrict__ gtouched,
-                      int64_t gcap) {
+                      int *__restrict__ out_cnt, int *__restrict__ seed_counter) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     PrunedSmem &S = *reinterpret_cast<PrunedSmem *>(smem_raw);
-    const int tid = threadIdx.x;
-    int *my_gkeys = gkeys ? gkeys + (size_t)blockIdx.x * gcap : nullptr;
-    double *my_gvals = gvals ? gvals + (size_t)blockIdx.x * gcap : nullptr;
-    int *my_gtouched = gtouched ? gtouched + (size_t)blockIdx.x * (gcap / 2) : nullptr;
-    // tables start empty (the host clears the workspace regions); after every iteration
-    // only the claimed slots are reset, so clearing and scanning cost O(unique columns)
-    for (int s = tid; s < kSmemSlots; s += kPprThreads) {
-        S.keys[s] = kEmpty;
-        S.vals[s] = 0.0;
-    }
-    if (tid == 0) S.ntouched = 0;
-    __syncthreads();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
     for (;;) {
         if (tid == 0) S.seed = atomicAdd(seed_counter, 1) + source_start;
@@ -204,115 +314,138 @@ __global__ void __launch_bounds__(kPprThreads)
             S.sel_val[0] = 1.0;
         }
         __syncthreads();
-        bool overflow = false;
-        for (int it = 0; it < iters && !overflow; it++) {
-            // expansion size of this step
-            if (tid == 0) {
-                int64_t l = 0;
-                for (int i = 0; i < S.st_n; i++) l += rowptr[S.st_col[i] + 1] - rowptr[S.st_col[i]];
-                S.lsum = l;
-            }
-            __syncthreads();
-            const int64_t need = 2 * (S.lsum + 1);
-            int *keys, *touched;
-            double *vals;
-            uint32_t cap = 64;
-            while ((int64_t)cap < need) cap <<= 1;
-            if ((int64_t)cap <= kSmemSlots) {
-                keys = S.keys;
-                vals = S.vals;
-                touched = S.touched;
-            } else if (my_gkeys != nullptr && (int64_t)cap <= gcap) {
-                keys = my_gkeys;
-                vals = my_gvals;
-                touched = my_gtouched;
-            } else {
-                overflow = true;
-                break;
-            }
-            const uint32_t mask = cap - 1;
+        for (int it = 0; it < iters; it++) {
             const int st_n = S.st_n;
-            for (int i = 0; i < st_n; i++) {
-                const int j = S.st_col[i];
-                const int64_t b = rowptr[j], e = rowptr[j + 1];
-                const int64_t deg = e - b;
-                const double inv = __ddiv_rn(1.0, (double)(deg > 0 ? deg : 1));
-                const double contrib = __dmul_rn(S.st_val[i], inv);
-                for (int64_t p = b + tid; p < e; p += kPprThreads) {
-                    const int c = __ldg(col + p);
-                    uint32_t slot = hash_slot(c, mask);
-                    for (uint32_t probe = 0; probe <= mask; probe++) {
-                        const int prev = atomicCAS(keys + slot, kEmpty, c);
-                        if (prev == kEmpty) touched[atomicAdd(&S.ntouched, 1)] = (int)slot;
-                        if (prev == kEmpty || prev == c) break;
-                        slot = (slot + 1) & mask;
-                    }
-                    atomicAdd(vals + slot, contrib);
+            if (warp == 0) {   // list bounds, contributions, the longest list, total length
+                int len = 0;
+                if (lane < st_n) {
+                    const int j = S.st_col[lane];
+                    const int64_t b = rowptr[j], e = rowptr[j + 1];
+                    len = (int)(e - b);
+                    S.lbeg[lane] = b;
+                    S.llen[lane] = len;
+                    S.contrib[lane] = __dmul_rn(S.st_val[lane], __ddiv_rn(1.0, (double)(len > 0 ? len : 1)));
                 }
-                __syncthreads();  // contributions of entry i land before entry i+1's
-            }
-            if (tid == 0) {  // the teleport target always exists in the merged row
-                uint32_t slot = hash_slot(seed, mask);
-                for (uint32_t probe = 0; probe <= mask; probe++) {
-                    const int prev = atomicCAS(keys + slot, kEmpty, seed);
-                    if (prev == kEmpty) touched[S.ntouched++] = (int)slot;
-                    if (prev == kEmpty || prev == seed) break;
-                    slot = (slot + 1) & mask;
+                int tot = len, best = len, bi = lane;   // longest list (first on ties)
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    tot += __shfl_xor_sync(0xffffffffu, tot, o);
+                    const int ob = __shfl_xor_sync(0xffffffffu, best, o), oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                    if (ob > best || (ob == best && oi < bi)) {
+                        best = ob;
+                        bi = oi;
+                    }
+                }
+                if (lane == 0) {
+                    S.total = tot;
+                    S.longest = bi;
                 }
             }
             __syncthreads();
-            const int nt = S.ntouched;
             TopList<KMAX> L;
             L.init();
-            for (int i = tid; i < nt; i += kPprThreads) {
-                const int s = touched[i];
-                const int c = keys[s];
-                double v = __dmul_rn(vals[s], oma);
-                if (c == seed) v = __dadd_rn(v, alpha);
-                L.offer(v, c);
-            }
-            const int cnt = block_merge_topk<KMAX>(L, iter_topk, S.ms, S.sel_col, S.sel_val);
-            for (int i = tid; i < nt; i += kPprThreads) {  // leave the table empty again
-                const int s = touched[i];
-                keys[s] = kEmpty;
-                vals[s] = 0.0;
-            }
-            __syncthreads();
-            if (tid == 0) S.ntouched = 0;
-            if (tid == 0) {
-                // next state: the selection sorted by column (insertion sort, <= 32 entries)
-                for (int i = 0; i < cnt; i++) {
-                    const int c = S.sel_col[i];
-                    const double v = S.sel_val[i];
-                    int p = i;
-                    while (p > 0 && S.st_col[p - 1] > c) {
-                        S.st_col[p] = S.st_col[p - 1];
-                        S.st_val[p] = S.st_val[p - 1];
-                        p--;
+            // Column windows: one when the lists fit the stage; otherwise the longest list is cut
+            // into equal parts and every list contributes its entries inside each part's column
+            // range, so a window holds about stage * 3 / 4 entries.
+            const int li = S.longest, llen = S.llen[li];
+            const int nwin = S.total <= kStageCap ? 1 : (S.total + (kStageCap * 3 / 4) - 1) / (kStageCap * 3 / 4);
+            for (int w = 0; w < nwin; w++) {
+                const int c_lo = w == 0 ? INT_MIN : __ldg(col + S.lbeg[li] + (int)(((int64_t)w * llen) / nwin));
+                const int c_hi = w + 1 == nwin ? INT_MAX : __ldg(col + S.lbeg[li] + (int)(((int64_t)(w + 1) * llen) / nwin));
+                if (warp == 0) {   // this window's part of every list and its place in the stage
+                    int wb = 0, wl = 0;
+                    if (lane < st_n) {
+                        const int *lst = col + S.lbeg[lane];
+                        const int len = S.llen[lane];
+                        if (nwin == 1) {
+                            wl = len;
+                        } else {
+                            wb = c_lo == INT_MIN ? 0 : lower_bound([&](int q) { return __ldg(lst + q); }, len, c_lo);
+                            const int we = c_hi == INT_MAX ? len : lower_bound([&](int q) { return __ldg(lst + q); }, len, c_hi);
+                            wl = we - wb;
+                        }
+                        S.wbeg[lane] = wb;
+                        S.wlen[lane] = wl;
                     }
-                    S.st_col[p] = c;
-                    S.st_val[p] = v;
+                    int incl = wl;
+#pragma unroll
+                    for (int o = 1; o < 32; o <<= 1) {
+                        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+                        if (lane >= o) incl += t;
+                    }
+                    const int total = __shfl_sync(0xffffffffu, incl, 31);
+                    if (lane < st_n) S.loff[lane] = incl - wl;
+                    if (lane == 0) {
+                        S.loff[st_n] = total;
+                        S.staged = total <= kStageCap;
+                    }
                 }
-                S.st_n = cnt;
+                __syncthreads();
+                const bool staged = S.staged;
+                if (staged) {
+                    for (int i = 0; i < st_n; i++) {
+                        const int len = S.wlen[i], o = S.loff[i];
+                        const int *src = col + S.lbeg[i] + S.wbeg[i];
+                        for (int q = tid; q < len; q += kPprThreads) S.stage[o + q] = __ldg(src + q);
+                    }
+                }
+                __syncthreads();
+                {   // thread column ranges inside the window: quantiles of the longest list's part
+                    const int len = S.wlen[li];
+                    if (tid == 0) {
+                        S.bounds[0] = c_lo;
+                        S.bounds[kPprThreads] = c_hi;
+                    } else {
+                        const int q = (int)(((int64_t)tid * len) / kPprThreads);
+                        S.bounds[tid] = q >= len ? c_hi
+                                                 : (staged ? S.stage[S.loff[li] + q] : __ldg(col + S.lbeg[li] + S.wbeg[li] + q));
+                    }
+                }
+                __syncthreads();
+                const int lo = S.bounds[tid], hi = S.bounds[tid + 1];
+                if (lo < hi) {
+                    if (staged) {
+                        int base[KMAX];
+#pragma unroll
+                        for (int i = 0; i < KMAX; i++) base[i] = i < st_n ? S.loff[i] : 0;
+                        merge_range<KMAX>(S, [&](int i, int q) { return S.stage[base[i] + q]; }, st_n, lo, hi, seed, alpha,
+                                          oma, L);
+                    } else {   // a window still too large for the stage: read the lists in place
+                        merge_range<KMAX>(S, [&](int i, int q) { return __ldg(col + S.lbeg[i] + S.wbeg[i] + q); }, st_n,
+                                          lo, hi, seed, alpha, oma, L);
+                    }
+                }
+                __syncthreads();   // the stage is refilled by the next window
+            }
+            const int cnt = block_topk<KMAX>(L, iter_topk, S.wv, S.wc, &S.cnt, S.sel_col, S.sel_val);
+            if (warp == 0) {   // next state: the selection sorted by column (distinct columns)
+                int c = INT_MAX;
+                double v = 0.0;
+                if (lane < cnt) {
+                    c = S.sel_col[lane];
+                    v = S.sel_val[lane];
+                }
+                int rank = 0;
+                for (int o = 0; o < cnt; o++) rank += __shfl_sync(0xffffffffu, c, o) < c;
+                if (lane < cnt) {
+                    S.st_col[rank] = c;
+                    S.st_val[rank] = v;
+                }
+                if (lane == 0) S.st_n = cnt;
             }
             __syncthreads();
         }
         if (tid == 0) {
             const int slot = seed - source_start;
-            if (overflow) {
-                atomicAdd(info, 1);
-                out_cnt[slot] = 0;
-            } else {
-                int keep = S.st_n;
-                if (final_keep > 0 && final_keep < keep) keep = final_keep;
-                if (keep > keep_stride) keep = keep_stride;
-                for (int i = 0; i < keep; i++) {
-                    out_col[(size_t)slot * keep_stride + i] = S.sel_col[i];
-                    out_val[(size_t)slot * keep_stride + i] = (float)S.sel_val[i];
-                    if (out_val64) out_val64[(size_t)slot * keep_stride + i] = S.sel_val[i];
-                }
-                out_cnt[slot] = keep;
+            int keep = S.st_n;
+            if (final_keep > 0 && final_keep < keep) keep = final_keep;
+            if (keep > keep_stride) keep = keep_stride;
+            for (int i = 0; i < keep; i++) {
+                out_col[(size_t)slot * keep_stride + i] = S.sel_col[i];
+                out_val[(size_t)slot * keep_stride + i] = (float)S.sel_val[i];
+                if (out_val64) out_val64[(size_t)slot * keep_stride + i] = S.sel_val[i];
             }
+            out_cnt[slot] = keep;
         }
         __syncthreads();
     }
@@ -398,21 +531,10 @@ __global__ void __launch_bounds__(kPprThreads)
     }
 }
 
-int64_t pruned_gcap(int64_t max_degree, int64_t iter_topk) {
-    const int64_t need = 2 * (iter_topk * (max_degree > 0 ? max_degree : 1) + 1);
-    int64_t cap = 64;
-    while (cap < need) cap <<= 1;
-    return cap;
-}
-
 struct PprWs {
     int *counter;
-    int *gkeys;
-    double *gvals;
-    int *gtouched;
     double *gx;
     unsigned char *gp;
-    int64_t gcap;
     size_t used;
 };
 
@@ -428,16 +550,8 @@ PprWs carve_ppr(void *base, int64_t n, int64_t max_degree, int64_t iter_topk, in
     };
     const int64_t ctas = num_seeds < kMaxCtas ? (num_seeds > 0 ? num_seeds : 1) : kMaxCtas;
     w.counter = reinterpret_cast<int *>(take(sizeof(int)));
-    if (iter_topk > 0) {
-        w.gcap = pruned_gcap(max_degree, iter_topk);
-        if (w.gcap > kSmemSlots) {
-            w.gkeys = reinterpret_cast<int *>(take(sizeof(int) * (size_t)(ctas * w.gcap)));
-            w.gvals = reinterpret_cast<double *>(take(sizeof(double) * (size_t)(ctas * w.gcap)));
-            w.gtouched = reinterpret_cast<int *>(take(sizeof(int) * (size_t)(ctas * (w.gcap / 2))));
-        } else {
-            w.gcap = 0;
-        }
-    } else {
+    (void)max_degree;   // the pruned mode needs no per-CTA tables
+    if (iter_topk <= 0) {
         w.gx = reinterpret_cast<double *>(take(sizeof(double) * (size_t)(ctas * 2 * n)));
         w.gp = reinterpret_cast<unsigned char *>(take((size_t)(ctas * 2 * n)));
     }
@@ -480,11 +594,6 @@ extern "C" int ngt_ppr_appnp_topk(int64_t n, const int64_t *rowptr, const int32_
     cudaMemsetAsync(info, 0, sizeof(int32_t), st);
     cudaMemsetAsync(w.counter, 0, sizeof(int), st);
     if (num_seeds == 0) return NGT_OK;
-    if (!dense && w.gkeys != nullptr) {
-        const int64_t c = num_seeds < kMaxCtas ? num_seeds : kMaxCtas;
-        cudaMemsetAsync(w.gkeys, 0xff, sizeof(int) * (size_t)(c * w.gcap), st);   // kEmpty
-        cudaMemsetAsync(w.gvals, 0, sizeof(double) * (size_t)(c * w.gcap), st);
-    }
     const int ctas = (int)(num_seeds < kMaxCtas ? num_seeds : kMaxCtas);
     const double oma = 1.0 - alpha;
     const int fk = (int)(final_keep > 0 ? final_keep : 0);
@@ -500,8 +609,7 @@ extern "C" int ngt_ppr_appnp_topk(int64_t n, const int64_t *rowptr, const int32_
                              (int)sm);                                                             \
         ppr_pruned_kernel<KM><<<ctas, kPprThreads, sm, st>>>(                                      \
             (int)n, rowptr, col, alpha, oma, (int)num_iterations, (int)k, fk, (int)source_start,   \
-            (int)source_end, (int)keep_stride, out_col, out_val, out_val64, out_cnt, info,         \
-            w.counter, w.gkeys, w.gvals, w.gtouched, w.gcap);                                      \
+            (int)source_end, (int)keep_stride, out_col, out_val, out_val64, out_cnt, w.counter);   \
     }                                                                                              \
     NGT_CHECK_LAUNCH();                                                                            \
     return NGT_OK;

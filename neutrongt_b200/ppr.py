@@ -105,6 +105,14 @@ def personal_pagerank_appnp(edge_index, alpha, topk=100, num_iterations: int = 1
     else:
         if it > 32:
             raise NotImplementedError("iter_topk above 32 is not supported by the PPR kernel")
+        # the pruned kernel merges adjacency rows, so each row's columns must ascend (the
+        # reference's CSR writer emits them that way); sort the rows of any other input once
+        if col.numel() > 1:
+            row_of = torch.repeat_interleave(torch.arange(n, device=device), deg)
+            desc = (col[1:] < col[:-1]) & (row_of[1:] == row_of[:-1])
+            if bool(desc.any()):
+                order = torch.argsort(row_of * n + col, stable=True)
+                col32 = col32[order].contiguous()
     stride = final_keep if final_keep > 0 else it
     nseeds = s1 - s0
     L = _lib.lib()
