@@ -207,14 +207,16 @@ NGT_API int ngt_window_subgraph_fill(int64_t num_global_nodes, const int64_t *ro
  * each seed's row on chip.  Values in fp64 with a canonical order: contributions to a
  * column are added in ascending source column, ties rank by ascending column.
  *
- *   rowptr int64 [n+1], col int32 [rowptr[n]]: the graph (P = D^-1 A, D = max(outdeg,1))
+ *   rowptr int64 [n+1], col int32 [rowptr[n]]: the graph (P = D^-1 A, D = max(outdeg,1));
+ *                   pruned mode merges rows, so each row's columns must ascend (repeats allowed)
  *   in_rowptr/in_col the transpose (in-adjacency, sources ascending within a row); read only
  *                   in dense mode, nullable otherwise
  *   iter_topk       > 0: entries kept per iteration (1..32); <= 0: no pruning (dense mode)
  *   final_keep      entries kept at the end (1..32 in dense mode; <= 0 keeps all when pruned)
  *   out_col int64 / out_val float / out_val64 double (nullable): [num_seeds, keep_stride],
  *   out_cnt int32 [num_seeds]; entries of seed s in (value desc, column asc) order.
- *   info int32 [1]: count of seeds whose row did not fit the workspace (0 when OK).
+ *   info int32 [1]: set to 0 (kept for the ABI; every row now fits: large expansions are
+ *                   processed in column windows).
  * ---------------------------------------------------------------------------------- */
 NGT_API int ngt_ppr_workspace_size(int64_t n, int64_t max_degree, int64_t iter_topk, int64_t num_seeds,
                            size_t *bytes /* host */);

@@ -5,7 +5,8 @@
 note the (k, q, v) argument order): q, k, v are [b, s, H, D] with b == 1; it returns
 x [b, s, H, D] and node_scores [s] = sum over queries of the head-mean of |S|, where
 S = (q * sqrt(D)) k^T — the reference multiplies by sqrt(D), and so does this kernel.
-Gradients flow to q, k and v (`csrc/dense_attn.cu` backward); node_scores carries none.
+Gradients flow to q, k and v (`csrc/dense_tma.cu` backward for head_dim <= 32,
+`csrc/dense_attn.cu` for 33..64); node_scores carries none.
 
 The kernels compute in bfloat16 with fp32 accumulation; float32 inputs are rounded to
 bfloat16 on entry and the output is returned in the input dtype.  Attention dropout uses a

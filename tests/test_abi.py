@@ -35,7 +35,10 @@ def test_version_status_and_size_queries():
     assert _lib.size_query(lib.ngt_edge_csr_workspace_size, 65536, 2_000_000) > 2_000_000 * 28
     assert _lib.size_query(lib.ngt_window_subgraph_workspace_size, 169343, 10000) >= 169343 * 4
     # pruned PPR on a hub-heavy graph reserves per-CTA overflow tables
-    assert _lib.size_query(lib.ngt_ppr_workspace_size, 169343, 11702, 8, 169343) > 100 * 2**20
+    # pruned PPR keeps every row on chip (a work counter only); unpruned needs two dense
+    # fp64 vectors and presence flags per CTA
+    assert 0 < _lib.size_query(lib.ngt_ppr_workspace_size, 169343, 11702, 8, 169343) < 4096
+    assert _lib.size_query(lib.ngt_ppr_workspace_size, 10000, 100, 0, 100) >= 100 * 2 * 10000 * 9
 
 
 def test_invalid_arguments_are_rejected_without_a_gpu():
