@@ -451,10 +451,11 @@ def measured_bf16_peak():
 def bench_dense(args, rank, world, dev, steps=5, warm=2):
     """Dense attention windows (per-rank share): S = 32,768 tokens of one window,
     the rank's 4 of 32 heads after the Ulysses exchange (head_dim 24), bf16, fwd + bwd.  With N > 1
-    the exchange (NCCL all_to_all_single) of q, k, v and the output is inside the timed step."""
+    the step is the reference's `DistributedAttentionNodeLevel` layer: the exchange (NCCL
+    all_to_all_single) of q, k, v and the output is inside the timed step, pipelined in two head
+    chunks so that NCCL overlaps the kernels."""
     import math as _m
     from neutrongt_b200.dense_attention import dense_attention
-    from neutrongt_b200.ulysses import _SeqAllToAll
     S, H_total, D = 32768, 32, 24
     H_local = 4
     g = torch.Generator(device=dev).manual_seed(rank)
@@ -470,17 +471,19 @@ def bench_dense(args, rank, world, dev, steps=5, warm=2):
     if world > 1:
         grp = _dist.group.WORLD
 
+    layer = None
+    if world > 1:   # the reference's layer, with the head exchange pipelined in two chunks
+        from neutrongt_b200 import CoreAttention
+        from neutrongt_b200.ulysses import DistributedAttentionNodeLevel
+        layer = DistributedAttentionNodeLevel(CoreAttention(H_total * D, 0.0, H_total), grp, head_chunks=2).train()
+
     def step():
         if world == 1:
             x, _ = dense_attention(qd, kd, vd, _m.sqrt(D), score_heads=H_total, check_status=False)
             x.backward(dy)
         else:
-            ql = _SeqAllToAll.apply(grp, qd, 2, 1)[0]
-            kl = _SeqAllToAll.apply(grp, kd, 2, 1)[0]
-            vl = _SeqAllToAll.apply(grp, vd, 2, 1)[0]
-            x, _ = dense_attention(ql, kl, vl, _m.sqrt(D), score_heads=H_total, check_status=False)
-            y = _SeqAllToAll.apply(grp, x.unsqueeze(0), 1, 2)
-            y.backward(dy)
+            y, _ = layer(qd, kd, vd, None, None, "full")
+            y.backward(dy.reshape(y.shape))
 
     for _ in range(warm):
         step()

@@ -33,7 +33,7 @@ class _TorchDense(torch.nn.Module):
         return x, score.detach().abs().mean(dim=1).squeeze(0).sum(dim=0)
 
 
-def _worker(rank, world, port, out):
+def _worker(rank, world, port, out, chunks=1):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     from neutrongt_b200.ulysses import DistributedAttentionNodeLevel, _SeqAllToAll
@@ -45,7 +45,7 @@ def _worker(rank, world, port, out):
     x = _SeqAllToAll.apply(None, q[:, sl].contiguous(), 2, 1)
     hs = slice(rank * H // world, (rank + 1) * H // world)
     exch_ok = torch.equal(x, q[:, :, hs])
-    layer = DistributedAttentionNodeLevel(_TorchDense(), None).train()
+    layer = DistributedAttentionNodeLevel(_TorchDense(), None, head_chunks=chunks).train()
     ql, kl, vl = (t[:, sl].clone().requires_grad_(True) for t in (q, k, v))
     y, score = layer(ql, kl, vl, None, None, "full")
     y.backward(dy[:, sl].reshape(y.shape))
@@ -53,11 +53,16 @@ def _worker(rank, world, port, out):
     dist.destroy_process_group()
 
 
-def test_distributed_attention_matches_single_process():
+import pytest
+
+
+@pytest.mark.parametrize("chunks", [1, 2])
+def test_distributed_attention_matches_single_process(chunks):
+    """chunks == 2: the pipelined exchange (one head per chunk and rank) gives the same values."""
     port = _free_port()
     with mp.get_context("spawn").Manager() as m:
         res = m.dict()
-        mp.spawn(_worker, args=(2, port, res), nprocs=2, join=True)
+        mp.spawn(_worker, args=(2, port, res, chunks), nprocs=2, join=True)
         res = dict(res)
     S, H, D = 12, 4, 3
     g = torch.Generator().manual_seed(0)

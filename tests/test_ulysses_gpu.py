@@ -29,7 +29,7 @@ def _inputs():
     return [torch.randn(1, 512, 8, 24, generator=g).to(torch.bfloat16) * 0.5 for _ in range(4)]
 
 
-def _worker(rank, world, port, out):
+def _worker(rank, world, port, out, chunks=1):
     import datetime
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.cuda.set_device(rank)
@@ -41,7 +41,7 @@ def _worker(rank, world, port, out):
     S = q.shape[1]
     sl = slice(rank * S // world, (rank + 1) * S // world)
     # constructed as the reference does: hidden size and the TOTAL head count
-    layer = DistributedAttentionNodeLevel(CoreAttention(8 * 24, 0.0, 8), dist.group.WORLD).train()
+    layer = DistributedAttentionNodeLevel(CoreAttention(8 * 24, 0.0, 8), dist.group.WORLD, head_chunks=chunks).train()
     ql, kl, vl = (t[:, sl].clone().requires_grad_(True) for t in (q, k, v))
     y, score = layer(ql, kl, vl, None, None, "full")
     y.backward(dy[:, sl].reshape(y.shape))
@@ -51,14 +51,16 @@ def _worker(rank, world, port, out):
     dist.destroy_process_group()
 
 
-def test_ulysses_dense_matches_single_gpu(cuda):
+@pytest.mark.parametrize("chunks", [1, 2])
+def test_ulysses_dense_matches_single_gpu(cuda, chunks):
+    """chunks == 2: the pipelined exchange (two heads per chunk and rank, NCCL overlapping the kernels)."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     from neutrongt_b200.dense_attention import dense_attention
     port = _free_port()
     with mp.get_context("spawn").Manager() as m:
         res = m.dict()
-        mp.spawn(_worker, args=(2, port, res), nprocs=2, join=True)
+        mp.spawn(_worker, args=(2, port, res, chunks), nprocs=2, join=True)
         res = dict(res)
     q, k, v, dy = (t.cuda() for t in _inputs())
     qr, kr, vr = (t[0].clone().requires_grad_(True) for t in (q, k, v))
