@@ -228,6 +228,24 @@ NGT_API int ngt_ppr_appnp_topk(int64_t n, const int64_t *rowptr, const int32_t *
                        int32_t *out_cnt, int32_t *info, void *workspace, size_t workspace_bytes,
                        ngt_stream_t stream);
 
+/* ----------------------------------------------------------------------------------
+ * Row-wise fp32 operators of the GT / Graphormer layers: LayerNorm forward / backward and the
+ * column sum that is a Linear layer's bias gradient.  Replace torch's nn.LayerNorm kernels and
+ * the `grad.sum(0)` of nn.Linear's backward in the models' layers
+ * (NeutronGT/models/gt_dist_node_level_single_window.py:311-325, graphormer_dist_node_level.py:179,
+ * 183, 286).  x, y, dy, dx are row-major [rows, cols] fp32 with cols % 4 == 0 and cols <= 1024,
+ * 16-byte aligned; mean and rstd are [rows]; gamma, beta, dgamma, dbeta are [cols].  Column
+ * sums are added in a fixed order (no atomics).  workspace: ngt_rowops_workspace_size bytes.
+ * ---------------------------------------------------------------------------------- */
+NGT_API int ngt_rowops_workspace_size(int64_t rows, int cols, size_t *bytes /* host */);
+NGT_API int ngt_layernorm_forward(int64_t rows, int cols, const float *x, const float *gamma, const float *beta,
+                                  float eps, float *y, float *mean, float *rstd, ngt_stream_t stream);
+NGT_API int ngt_layernorm_backward(int64_t rows, int cols, const float *x, const float *dy, const float *gamma,
+                                   const float *mean, const float *rstd, float *dx, float *dgamma, float *dbeta,
+                                   void *workspace, size_t workspace_bytes, ngt_stream_t stream);
+NGT_API int ngt_column_sum(int64_t rows, int cols, const float *x, float *out, void *workspace,
+                           size_t workspace_bytes, ngt_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,120 @@
+"""LayerNorm and Linear for the GT / Graphormer mirrors, with their row-wise work on our kernels.
+
+`LayerNorm` and `Linear` subclass `nn.LayerNorm` / `nn.Linear`: same constructor, parameter names
+(`weight`, `bias`) and state_dict, so reference checkpoints load unchanged.  On CUDA fp32 inputs:
+
+* `LayerNorm` runs `ngt_layernorm_forward` / `ngt_layernorm_backward` (one warp per row, column
+  sums of the weight / bias gradients in a fixed order);
+* `Linear` keeps the GEMMs on cuBLAS (`addmm`, `mm`) and computes the bias gradient with
+  `ngt_column_sum` instead of torch's `grad.sum(0)`.
+
+torch's kernels for these ops take 15-60 us per call on the models' [~10^4, 64..1024] fp32
+windows; these take a few.  Other devices, dtypes or shapes (cols not a multiple of 4 or above
+1024) use the torch operators.  Reference layers: NeutronGT/models/gt_dist_node_level_single_window.py:
+239-241, 311-325, 360-361, 537, 565; graphormer_dist_node_level.py:179, 183, 286.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import _lib
+
+
+def _rows_ok(x: torch.Tensor, cols: int) -> bool:
+    return x.is_cuda and x.dtype == torch.float32 and cols % 4 == 0 and 0 < cols <= 1024
+
+
+_WS_BYTES: dict = {}
+
+
+def _ws(rows: int, cols: int, device) -> torch.Tensor:
+    key = (rows, cols)
+    nbytes = _WS_BYTES.get(key)
+    if nbytes is None:
+        nbytes = _WS_BYTES[key] = _lib.size_query(_lib.lib().ngt_rowops_workspace_size, rows, cols)
+    return _lib.workspace(nbytes, device)
+
+
+def column_sum(g: torch.Tensor) -> torch.Tensor:
+    """Sum over the rows of a [rows, cols] fp32 CUDA tensor (fixed-order reduction)."""
+    g = g.contiguous()
+    rows, cols = g.shape
+    out = torch.empty(cols, dtype=torch.float32, device=g.device)
+    ws = _ws(rows, cols, g.device)
+    _lib.check(_lib.lib().ngt_column_sum(rows, cols, _lib.ptr(g), _lib.ptr(out), _lib.ptr(ws), ws.numel(),
+                                         _lib.stream_of(g)), "ngt_column_sum")
+    return out
+
+
+class _LayerNormFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, bias, eps):
+        shape = x.shape
+        cols = shape[-1]
+        x2 = x.reshape(-1, cols).contiguous()
+        rows = x2.shape[0]
+        y = torch.empty_like(x2)
+        mean = torch.empty(rows, dtype=torch.float32, device=x.device)
+        rstd = torch.empty_like(mean)
+        _lib.check(_lib.lib().ngt_layernorm_forward(rows, cols, _lib.ptr(x2), _lib.ptr(weight), _lib.ptr(bias),
+                                                    float(eps), _lib.ptr(y), _lib.ptr(mean), _lib.ptr(rstd),
+                                                    _lib.stream_of(x2)), "ngt_layernorm_forward")
+        ctx.save_for_backward(x2, weight, mean, rstd)
+        ctx.shape = shape
+        return y.view(shape)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, weight, mean, rstd = ctx.saved_tensors
+        rows, cols = x2.shape
+        dy2 = dy.reshape(rows, cols).contiguous().float()
+        dx = torch.empty_like(x2)
+        dw = torch.empty(cols, dtype=torch.float32, device=x2.device)
+        db = torch.empty_like(dw)
+        ws = _ws(rows, cols, x2.device)
+        _lib.check(_lib.lib().ngt_layernorm_backward(rows, cols, _lib.ptr(x2), _lib.ptr(dy2), _lib.ptr(weight),
+                                                     _lib.ptr(mean), _lib.ptr(rstd), _lib.ptr(dx), _lib.ptr(dw),
+                                                     _lib.ptr(db), _lib.ptr(ws), ws.numel(), _lib.stream_of(x2)),
+                   "ngt_layernorm_backward")
+        return dx.view(ctx.shape), dw, db, None
+
+
+class _LinearFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, bias):
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1])
+        y = torch.addmm(bias, x2, weight.t())
+        ctx.save_for_backward(x2, weight)
+        ctx.shape = shape
+        return y.view(*shape[:-1], weight.shape[0])
+
+    @staticmethod
+    def backward(ctx, g):
+        x2, weight = ctx.saved_tensors
+        g2 = g.reshape(-1, weight.shape[0]).contiguous()
+        dx = dw = db = None
+        if ctx.needs_input_grad[0]:
+            dx = g2.mm(weight).view(ctx.shape)
+        if ctx.needs_input_grad[1]:
+            dw = g2.t().mm(x2)
+        if ctx.needs_input_grad[2]:
+            db = column_sum(g2) if (g2.is_cuda and g2.dtype == torch.float32) else g2.sum(0)
+        return dx, dw, db
+
+
+class LayerNorm(nn.LayerNorm):
+    def forward(self, x):
+        if (self.elementwise_affine and self.bias is not None and len(self.normalized_shape) == 1
+                and _rows_ok(x, self.normalized_shape[0]) and x.numel() > 0):
+            return _LayerNormFn.apply(x, self.weight, self.bias, self.eps)
+        return super().forward(x)
+
+
+class Linear(nn.Linear):
+    def forward(self, x):
+        if self.bias is not None and _rows_ok(x, 4) and self.weight.dtype == torch.float32 and x.numel() > 0:
+            return _LinearFn.apply(x, self.weight, self.bias)
+        return F.linear(x, self.weight, self.bias)

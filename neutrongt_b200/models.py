@@ -5,7 +5,9 @@ mirrors `NeutronGT/models/graphormer_dist_node_level.py:240-381`: same construct
 same submodule and parameter names (so a state_dict saved by the reference loads here
 unchanged), same forward signature and return tuple
 `(log_softmax(out), score_agg, [per-layer node scores], kv_cache)`.  The attention itself
-is `attention.CoreAttention` (sparse: `csrc/spattn.cu`).
+is `attention.CoreAttention` (sparse: `csrc/spattn.cu`).  LayerNorm and Linear are
+`layers.LayerNorm` / `layers.Linear`: the torch modules' parameters and math, with the LayerNorm
+passes and the bias gradients on `csrc/rowops.cu`.
 
 Behaviour kept from the reference on purpose (it changes results, so parity needs it):
 * GT_SW's encoder feeds the FFN with the attention branch `y`, not the residual stream
@@ -25,6 +27,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .attention import CoreAttention
+from .layers import LayerNorm, Linear
 
 
 def init_params(module, n_layers):
@@ -103,12 +106,12 @@ class MultiHeadAttention(nn.Module):
         super().__init__()
         self.num_heads = num_heads
         self.att_size = hidden_size // num_heads
-        self.linear_q = nn.Linear(hidden_size, num_heads * self.att_size)
-        self.linear_k = nn.Linear(hidden_size, num_heads * self.att_size)
-        self.linear_v = nn.Linear(hidden_size, num_heads * self.att_size)
+        self.linear_q = Linear(hidden_size, num_heads * self.att_size)
+        self.linear_k = Linear(hidden_size, num_heads * self.att_size)
+        self.linear_v = Linear(hidden_size, num_heads * self.att_size)
         self.local_attn = CoreAttention(hidden_size, attention_dropout_rate, num_heads)
         if output_layer:
-            self.output_layer = nn.Linear(num_heads * self.att_size, hidden_size)
+            self.output_layer = Linear(num_heads * self.att_size, hidden_size)
         else:
             self.dist_attn = _DistributedAttentionSlot(self.local_attn)
             self.output_layer = None
@@ -129,14 +132,14 @@ class MultiHeadAttention(nn.Module):
 class GTEncoderLayer(nn.Module):
     def __init__(self, hidden_size, ffn_size, dropout_rate, attention_dropout_rate, num_heads):
         super().__init__()
-        self.self_attention_norm = nn.LayerNorm(hidden_size)
+        self.self_attention_norm = LayerNorm(hidden_size)
         self.self_attention = MultiHeadAttention(hidden_size, attention_dropout_rate, num_heads)
         self.self_attention_dropout = nn.Dropout(dropout_rate)
-        self.O = nn.Linear(hidden_size, hidden_size)
-        self.layer_norm1 = nn.LayerNorm(hidden_size)
-        self.FFN_layer1 = nn.Linear(hidden_size, hidden_size * 2)
-        self.FFN_layer2 = nn.Linear(hidden_size * 2, hidden_size)
-        self.layer_norm2 = nn.LayerNorm(hidden_size)
+        self.O = Linear(hidden_size, hidden_size)
+        self.layer_norm1 = LayerNorm(hidden_size)
+        self.FFN_layer1 = Linear(hidden_size, hidden_size * 2)
+        self.FFN_layer2 = Linear(hidden_size * 2, hidden_size)
+        self.layer_norm2 = LayerNorm(hidden_size)
 
     def forward(self, x, attn_bias=None, edge_index=None, attn_type=None, mask=None, pruning_mask=None,
                 dup_nodes_kv_cache=None, layer: int = 0):
@@ -153,8 +156,8 @@ class GTEncoderLayer(nn.Module):
 class MLPReadout(nn.Module):
     def __init__(self, input_dim, output_dim, L=2):
         super().__init__()
-        layers = [nn.Linear(input_dim // 2 ** l, input_dim // 2 ** (l + 1), bias=True) for l in range(L)]
-        layers.append(nn.Linear(input_dim // 2 ** L, output_dim, bias=True))
+        layers = [Linear(input_dim // 2 ** l, input_dim // 2 ** (l + 1), bias=True) for l in range(L)]
+        layers.append(Linear(input_dim // 2 ** L, output_dim, bias=True))
         self.FC_layers = nn.ModuleList(layers)
         self.L = L
 
@@ -194,14 +197,14 @@ class GT_SW(nn.Module):
                  num_out_degree: int, num_spatial, num_edges, max_dist, edge_dim):
         super().__init__()
         self.args = args
-        self.node_encoder = nn.Linear(input_dim, hidden_dim)
+        self.node_encoder = Linear(input_dim, hidden_dim)
         self.centrality_encoding = CentralityEncodingLayer(hidden_dim, num_in_degree, num_out_degree)
         self.attention_bias = AttnBias(num_heads, num_spatial, num_edges, max_dist, edge_dim)
         self.input_dropout = nn.Dropout(input_dropout_rate)
         self.layers = nn.ModuleList([GTEncoderLayer(hidden_dim, ffn_dim, dropout_rate, attention_dropout_rate, num_heads)
                                      for _ in range(n_layers)])
         self.MLP_layer = MLPReadout(hidden_dim, output_dim)
-        self.downstream_out_proj = nn.Linear(hidden_dim, output_dim)
+        self.downstream_out_proj = Linear(hidden_dim, output_dim)
         self.apply(lambda m: init_params(m, n_layers=n_layers))
 
     def forward(self, x, attn_bias, edge_index, in_degree, out_degree, spatial_pos, edge_input, perturb=None,
@@ -226,14 +229,14 @@ class GT_SW(nn.Module):
 class GraphormerEncoderLayer(nn.Module):
     def __init__(self, hidden_size, ffn_size, dropout_rate, attention_dropout_rate, num_heads):
         super().__init__()
-        self.self_attention_norm = nn.LayerNorm(hidden_size)
+        self.self_attention_norm = LayerNorm(hidden_size)
         self.self_attention = MultiHeadAttention(hidden_size, attention_dropout_rate, num_heads, output_layer=True)
         self.self_attention_dropout = nn.Dropout(dropout_rate)
-        self.ffn_norm = nn.LayerNorm(hidden_size)
+        self.ffn_norm = LayerNorm(hidden_size)
         self.ffn = nn.Module()
-        self.ffn.layer1 = nn.Linear(hidden_size, ffn_size)
+        self.ffn.layer1 = Linear(hidden_size, ffn_size)
         self.ffn.gelu = nn.GELU()
-        self.ffn.layer2 = nn.Linear(ffn_size, hidden_size)
+        self.ffn.layer2 = Linear(ffn_size, hidden_size)
         self.ffn_dropout = nn.Dropout(dropout_rate)
 
     def forward(self, x, attn_bias=None, edge_index=None, attn_type=None, mask=None, pruning_mask=None,
@@ -255,14 +258,14 @@ class Graphormer(nn.Module):
         super().__init__()
         self.args = args
         self.num_heads = num_heads
-        self.node_encoder = nn.Linear(input_dim, hidden_dim)
+        self.node_encoder = Linear(input_dim, hidden_dim)
         self.centrality_encoding = CentralityEncodingLayer(hidden_dim, num_in_degree, num_out_degree, clamp_first=True)
         self.attention_bias = AttnBias(num_heads, num_spatial, num_edges, max_dist, edge_dim)
         self.input_dropout = nn.Dropout(input_dropout_rate)
         self.layers = nn.ModuleList([GraphormerEncoderLayer(hidden_dim, ffn_dim, dropout_rate, attention_dropout_rate,
                                                             num_heads) for _ in range(n_layers)])
-        self.final_ln = nn.LayerNorm(hidden_dim)
-        self.downstream_out_proj = nn.Linear(hidden_dim, output_dim)
+        self.final_ln = LayerNorm(hidden_dim)
+        self.downstream_out_proj = Linear(hidden_dim, output_dim)
         self.n_layers = n_layers
         self.apply(lambda m: init_params(m, n_layers=n_layers))
 
