@@ -49,3 +49,10 @@ def test_invalid_arguments_are_rejected_without_a_gpu():
     out = ctypes.c_size_t(0)
     assert lib.ngt_edge_csr_workspace_size(-1, 5, ctypes.byref(out)) == 1
     assert lib.ngt_spattn_forward(7, 1, 1, 8, 8, *([None] * 9), 0, None) == 1   # bad dtype
+    # row-wise operators: size query, unsupported widths and null pointers fail before any launch
+    assert _lib.size_query(lib.ngt_rowops_workspace_size, 10583, 128) >= 2 * 128 * 4
+    assert lib.ngt_layernorm_forward(10, 130, *([None] * 3), 1e-5, *([None] * 3), None) == 2
+    assert lib.ngt_layernorm_forward(10, 2048, *([None] * 3), 1e-5, *([None] * 3), None) == 2
+    assert lib.ngt_layernorm_forward(10, 128, *([None] * 3), 1e-5, *([None] * 3), None) == 1
+    assert lib.ngt_layernorm_forward(0, 128, *([None] * 3), 1e-5, *([None] * 3), None) == 0
+    assert lib.ngt_column_sum(-1, 128, None, None, None, 0, None) == 1
