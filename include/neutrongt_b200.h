@@ -234,8 +234,9 @@ NGT_API int ngt_ppr_appnp_topk(int64_t n, const int64_t *rowptr, const int32_t *
  * the `grad.sum(0)` of nn.Linear's backward in the models' layers
  * (NeutronGT/models/gt_dist_node_level_single_window.py:311-325, graphormer_dist_node_level.py:179,
  * 183, 286).  x, y, dy, dx are row-major [rows, cols] fp32 with cols % 4 == 0 and cols <= 1024,
- * 16-byte aligned; mean and rstd are [rows]; gamma, beta, dgamma, dbeta are [cols].  Column
- * sums are added in a fixed order (no atomics).  workspace: ngt_rowops_workspace_size bytes.
+ * 16-byte aligned; mean and rstd are [rows]; gamma, beta, dgamma, dbeta, out are [cols], 16-byte
+ * aligned.  Column sums are added in a fixed order (no atomics).  workspace (16-byte aligned):
+ * ngt_rowops_workspace_size bytes.
  * ---------------------------------------------------------------------------------- */
 NGT_API int ngt_rowops_workspace_size(int64_t rows, int cols, size_t *bytes /* host */);
 NGT_API int ngt_layernorm_forward(int64_t rows, int cols, const float *x, const float *gamma, const float *beta,
@@ -245,6 +246,30 @@ NGT_API int ngt_layernorm_backward(int64_t rows, int cols, const float *x, const
                                    void *workspace, size_t workspace_bytes, ngt_stream_t stream);
 NGT_API int ngt_column_sum(int64_t rows, int cols, const float *x, float *out, void *workspace,
                            size_t workspace_bytes, ngt_stream_t stream);
+
+/* ----------------------------------------------------------------------------------
+ * fp32 Linear layers of the GT / Graphormer models (y = x W^T + b): replace the GEMMs torch
+ * runs for nn.Linear's forward and backward (NeutronGT/models/gt_dist_node_level_single_window.py:
+ * 235-237, 313-318, 361; graphormer_dist_node_level.py:179, 183, 286).  All tensors row-major fp32,
+ * 16-byte aligned: x / dx [rows, in_features], y / dy [rows, out_features], weight / dweight
+ * [out_features, in_features], bias / dbias [out_features] (bias and dbias may be NULL).
+ * in_features and out_features are multiples of 4.  CUDA-core FFMA, no TF32.
+ *   ngt_linear_forward         y = x W^T + b          in_features  <= 256 (else NGT_ERR_UNSUPPORTED)
+ *   ngt_linear_backward_input  dx = dy W              out_features <= 256 (else NGT_ERR_UNSUPPORTED)
+ *   ngt_linear_backward_weight dW = dy^T x, db = column sums of dy; any size; summed in a fixed
+ *                              order (bitwise reproducible); workspace from
+ *                              ngt_linear_weight_workspace_size (depends on the current device's
+ *                              SM count: query on the device that runs the call).
+ * ---------------------------------------------------------------------------------- */
+NGT_API int ngt_linear_forward(int64_t rows, int in_features, int out_features, const float *x,
+                               const float *weight, const float *bias, float *y, ngt_stream_t stream);
+NGT_API int ngt_linear_backward_input(int64_t rows, int in_features, int out_features, const float *dy,
+                                      const float *weight, float *dx, ngt_stream_t stream);
+NGT_API int ngt_linear_weight_workspace_size(int64_t rows, int in_features, int out_features,
+                                             size_t *bytes /* host */);
+NGT_API int ngt_linear_backward_weight(int64_t rows, int in_features, int out_features, const float *x,
+                                       const float *dy, float *dweight, float *dbias, void *workspace,
+                                       size_t workspace_bytes, ngt_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -46,6 +46,10 @@ SIGNATURES = {
     "ngt_layernorm_forward": [_i64, _i32, _p, _p, _p, ctypes.c_float, _p, _p, _p, _p],
     "ngt_layernorm_backward": [_i64, _i32, _p, _p, _p, _p, _p, _p, _p, _p, _p, ctypes.c_size_t, _p],
     "ngt_column_sum": [_i64, _i32, _p, _p, _p, ctypes.c_size_t, _p],
+    "ngt_linear_forward": [_i64, _i32, _i32, _p, _p, _p, _p, _p],
+    "ngt_linear_backward_input": [_i64, _i32, _i32, _p, _p, _p, _p],
+    "ngt_linear_weight_workspace_size": [_i64, _i32, _i32, _sz_p],
+    "ngt_linear_backward_weight": [_i64, _i32, _i32, _p, _p, _p, _p, _p, ctypes.c_size_t, _p],
 }
 
 NGT_F32 = 0

@@ -9,6 +9,7 @@
 // Reference: the models' nn.LayerNorm and nn.Linear layers
 // (NeutronGT/models/gt_dist_node_level_single_window.py:239-241, 311-325, 360-361, 537, 565;
 // graphormer_dist_node_level.py:179, 183, 286).
+#include "chunk_sum.cuh"
 #include "common.cuh"
 
 namespace ngt {
@@ -16,7 +17,7 @@ namespace {
 
 constexpr int kRowThreads = 256;             // 8 warps, one row per warp
 constexpr int kColThreads = 256;             // column-sum blocks
-constexpr int kRowsPerPartial = 128;         // rows summed by one block of the column-sum kernels
+constexpr int kRowsPerPartial = 64;          // rows summed by one block of the column-sum kernels
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -75,58 +76,79 @@ __global__ void __launch_bounds__(kRowThreads)
 }
 
 // dx = rstd * (g - mean(g) - xhat * mean(g * xhat)), g = dy * gamma; per-block partial column sums
-// of dy * xhat and dy go to part[blockIdx.x][2][cols] (a block covers 8 rows x kRowsPerPartial / 8
-// row groups, i.e. kRowsPerPartial rows).
+// of dy * xhat and dy go to part[blockIdx.x][2][cols] (a block's 8 warps take rows warp, warp + 8,
+// ... of its kRowsPerPartial rows).  A warp loads kBatch rows before computing them, so their
+// loads overlap; rows are still added to the partials in row order.
 template <int VPL>
 __global__ void __launch_bounds__(kRowThreads)
     layernorm_bwd_kernel(int64_t rows, int cols, const float *__restrict__ x, const float *__restrict__ dy,
                          const float *__restrict__ gamma, const float *__restrict__ mean,
                          const float *__restrict__ rstd, float *__restrict__ dx, float *__restrict__ part) {
     constexpr int kWarps = kRowThreads / 32;
+    constexpr int kBatch = VPL >= 4 ? 1 : 4 / VPL;
     __shared__ float4 red[2][kWarps][32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    float4 ag[VPL], ab[VPL];
+    float4 ag[VPL], ab[VPL], gm[VPL];
 #pragma unroll
-    for (int j = 0; j < VPL; j++) ag[j] = ab[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int k = 0; k < kRowsPerPartial / kWarps; k++) {
-        const int64_t row = (int64_t)blockIdx.x * kRowsPerPartial + (int64_t)k * kWarps + warp;
-        if (row >= rows) break;
-        const float mu = mean[row], r = rstd[row];
-        float4 xh[VPL], g[VPL], d[VPL];
-        float s1 = 0.f, s2 = 0.f;
+    for (int j = 0; j < VPL; j++) {
+        const int c = 4 * lane + 128 * j;
+        ag[j] = ab[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        gm[j] = c < cols ? __ldg(reinterpret_cast<const float4 *>(gamma + c)) : ag[j];
+    }
+    const int64_t base = (int64_t)blockIdx.x * kRowsPerPartial + warp;
+    for (int k0 = 0; k0 < kRowsPerPartial / kWarps; k0 += kBatch) {
+        float mu[kBatch], r[kBatch];
+        float4 xv[kBatch][VPL], d[kBatch][VPL];
 #pragma unroll
-        for (int j = 0; j < VPL; j++) {
-            const int c = 4 * lane + 128 * j;
-            xh[j] = g[j] = d[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (c < cols) {
-                const float4 xv = *reinterpret_cast<const float4 *>(x + row * cols + c);
-                d[j] = *reinterpret_cast<const float4 *>(dy + row * cols + c);
-                const float4 gm = *reinterpret_cast<const float4 *>(gamma + c);
-                xh[j] = make_float4((xv.x - mu) * r, (xv.y - mu) * r, (xv.z - mu) * r, (xv.w - mu) * r);
-                g[j] = make_float4(d[j].x * gm.x, d[j].y * gm.y, d[j].z * gm.z, d[j].w * gm.w);
-                s1 += (g[j].x + g[j].y) + (g[j].z + g[j].w);
-                s2 += (g[j].x * xh[j].x + g[j].y * xh[j].y) + (g[j].z * xh[j].z + g[j].w * xh[j].w);
-                ag[j].x += d[j].x * xh[j].x;
-                ag[j].y += d[j].y * xh[j].y;
-                ag[j].z += d[j].z * xh[j].z;
-                ag[j].w += d[j].w * xh[j].w;
-                ab[j].x += d[j].x;
-                ab[j].y += d[j].y;
-                ab[j].z += d[j].z;
-                ab[j].w += d[j].w;
+        for (int u = 0; u < kBatch; u++) {          // loads of the batch (zero past the last row)
+            const int64_t row = base + (int64_t)(k0 + u) * kWarps;
+            const bool ok = row < rows;
+            mu[u] = ok ? mean[row] : 0.f;
+            r[u] = ok ? rstd[row] : 0.f;
+#pragma unroll
+            for (int j = 0; j < VPL; j++) {
+                const int c = 4 * lane + 128 * j;
+                const bool okc = ok && c < cols;
+                xv[u][j] = okc ? *reinterpret_cast<const float4 *>(x + row * cols + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+                d[u][j] = okc ? *reinterpret_cast<const float4 *>(dy + row * cols + c) : make_float4(0.f, 0.f, 0.f, 0.f);
             }
         }
-        const float a = warp_sum(s1) / (float)cols, b = warp_sum(s2) / (float)cols;
 #pragma unroll
-        for (int j = 0; j < VPL; j++) {
-            const int c = 4 * lane + 128 * j;
-            if (c < cols) {
-                float4 o;
-                o.x = r * (g[j].x - a - xh[j].x * b);
-                o.y = r * (g[j].y - a - xh[j].y * b);
-                o.z = r * (g[j].z - a - xh[j].z * b);
-                o.w = r * (g[j].w - a - xh[j].w * b);
-                *reinterpret_cast<float4 *>(dx + row * cols + c) = o;
+        for (int u = 0; u < kBatch; u++) {
+            const int64_t row = base + (int64_t)(k0 + u) * kWarps;
+            float4 xh[VPL], g[VPL];
+            float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+            for (int j = 0; j < VPL; j++) {
+                const float4 &dv = d[u][j];
+                xh[j] = make_float4((xv[u][j].x - mu[u]) * r[u], (xv[u][j].y - mu[u]) * r[u],
+                                    (xv[u][j].z - mu[u]) * r[u], (xv[u][j].w - mu[u]) * r[u]);
+                g[j] = make_float4(dv.x * gm[j].x, dv.y * gm[j].y, dv.z * gm[j].z, dv.w * gm[j].w);
+                s1 += (g[j].x + g[j].y) + (g[j].z + g[j].w);
+                s2 += (g[j].x * xh[j].x + g[j].y * xh[j].y) + (g[j].z * xh[j].z + g[j].w * xh[j].w);
+                ag[j].x += dv.x * xh[j].x;
+                ag[j].y += dv.y * xh[j].y;
+                ag[j].z += dv.z * xh[j].z;
+                ag[j].w += dv.w * xh[j].w;
+                ab[j].x += dv.x;
+                ab[j].y += dv.y;
+                ab[j].z += dv.z;
+                ab[j].w += dv.w;
+            }
+            const float a = warp_sum(s1) / (float)cols, b = warp_sum(s2) / (float)cols;
+            if (row < rows) {
+#pragma unroll
+                for (int j = 0; j < VPL; j++) {
+                    const int c = 4 * lane + 128 * j;
+                    if (c < cols) {
+                        float4 o;
+                        o.x = r[u] * (g[j].x - a - xh[j].x * b);
+                        o.y = r[u] * (g[j].y - a - xh[j].y * b);
+                        o.z = r[u] * (g[j].z - a - xh[j].z * b);
+                        o.w = r[u] * (g[j].w - a - xh[j].w * b);
+                        *reinterpret_cast<float4 *>(dx + row * cols + c) = o;
+                    }
+                }
             }
         }
     }
@@ -153,17 +175,6 @@ __global__ void __launch_bounds__(kRowThreads)
     }
 }
 
-// out[k][c] = sum over blocks b of part[b][k][c], blocks in order (k < nk).
-__global__ void partial_sum_kernel(int nblocks, int nk, int cols, const float *__restrict__ part,
-                                   float *__restrict__ out0, float *__restrict__ out1) {
-    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= nk * cols) return;
-    const int k = idx / cols, c = idx % cols;
-    float s = 0.f;
-    for (int b = 0; b < nblocks; b++) s += part[((size_t)b * nk + k) * cols + c];
-    (k == 0 ? out0 : out1)[c] = s;
-}
-
 // part[blockIdx.x][c] = sum of x[r][c] over the block's kRowsPerPartial rows, in row order.
 __global__ void __launch_bounds__(kColThreads)
     column_partial_kernel(int64_t rows, int cols, const float *__restrict__ x, float *__restrict__ part) {
@@ -172,6 +183,7 @@ __global__ void __launch_bounds__(kColThreads)
     const int64_t r0 = (int64_t)blockIdx.x * kRowsPerPartial;
     const int64_t r1 = r0 + kRowsPerPartial < rows ? r0 + kRowsPerPartial : rows;
     float s = 0.f;
+#pragma unroll 8
     for (int64_t r = r0; r < r1; r++) s += x[r * cols + c];
     part[(size_t)blockIdx.x * cols + c] = s;
 }
@@ -241,7 +253,8 @@ extern "C" int ngt_layernorm_backward(int64_t rows, int cols, const float *x, co
         return NGT_OK;
     }
     if (!x || !dy || !gamma || !mean || !rstd || !dx || !workspace) return NGT_ERR_INVALID_ARGUMENT;
-    if (!aligned16(x) || !aligned16(dy) || !aligned16(gamma) || !aligned16(dx) || !aligned16(workspace))
+    if (!aligned16(x) || !aligned16(dy) || !aligned16(gamma) || !aligned16(dx) || !aligned16(workspace) ||
+        !aligned16(dgamma) || !aligned16(dbeta))
         return NGT_ERR_MISALIGNED;
     size_t need = 0;
     ngt_rowops_workspace_size(rows, cols, &need);
@@ -255,7 +268,7 @@ extern "C" int ngt_layernorm_backward(int64_t rows, int cols, const float *x, co
     default: launch_ln_bwd<8>(rows, cols, x, dy, gamma, mean, rstd, dx, part, st); break;
     }
     const int nb = (int)((rows + kRowsPerPartial - 1) / kRowsPerPartial);
-    partial_sum_kernel<<<(2 * cols + 255) / 256, 256, 0, st>>>(nb, 2, cols, part, dgamma, dbeta);
+    launch_chunk_sum(nb, cols, 2 * (int64_t)cols, part, dgamma, dbeta, st);
     NGT_CHECK_LAUNCH();
     return NGT_OK;
 }
@@ -270,6 +283,7 @@ extern "C" int ngt_column_sum(int64_t rows, int cols, const float *x, float *out
         return NGT_OK;
     }
     if (!x || !workspace) return NGT_ERR_INVALID_ARGUMENT;
+    if (!aligned16(out) || !aligned16(workspace)) return NGT_ERR_MISALIGNED;
     size_t need = 0;
     ngt_rowops_workspace_size(rows, cols, &need);
     if (workspace_bytes < need) return NGT_ERR_WORKSPACE;
@@ -277,7 +291,7 @@ extern "C" int ngt_column_sum(int64_t rows, int cols, const float *x, float *out
     float *part = static_cast<float *>(workspace);
     column_partial_kernel<<<dim3((unsigned)nb, (unsigned)((cols + kColThreads - 1) / kColThreads)), kColThreads, 0,
                             st>>>(rows, cols, x, part);
-    partial_sum_kernel<<<(cols + 255) / 256, 256, 0, st>>>(nb, 1, cols, part, out, out);
+    launch_chunk_sum(nb, cols, cols, part, out, nullptr, st);
     NGT_CHECK_LAUNCH();
     return NGT_OK;
 }

@@ -1,17 +1,19 @@
-"""LayerNorm and Linear for the GT / Graphormer mirrors, with their row-wise work on our kernels.
+"""LayerNorm and Linear for the GT / Graphormer mirrors, with their work on our kernels.
 
 `LayerNorm` and `Linear` subclass `nn.LayerNorm` / `nn.Linear`: same constructor, parameter names
 (`weight`, `bias`) and state_dict, so reference checkpoints load unchanged.  On CUDA fp32 inputs:
 
 * `LayerNorm` runs `ngt_layernorm_forward` / `ngt_layernorm_backward` (one warp per row, column
   sums of the weight / bias gradients in a fixed order);
-* `Linear` keeps the GEMMs on cuBLAS (`addmm`, `mm`) and computes the bias gradient with
-  `ngt_column_sum` instead of torch's `grad.sum(0)`.
+* `Linear` runs `ngt_linear_forward` (y = x W^T + b), `ngt_linear_backward_input` (dx = dy W) and
+  `ngt_linear_backward_weight` (dW = dy^T x and db = column sums of dy, one pass, fixed-order
+  reduction): fp32 FFMA GEMMs sized to the SM count for the windows' thin shapes.
 
-torch's kernels for these ops take 15-60 us per call on the models' [~10^4, 64..1024] fp32
-windows; these take a few.  Other devices, dtypes or shapes (cols not a multiple of 4 or above
-1024) use the torch operators.  Reference layers: NeutronGT/models/gt_dist_node_level_single_window.py:
-239-241, 311-325, 360-361, 537, 565; graphormer_dist_node_level.py:179, 183, 286.
+torch's kernels for these ops take 15-60 us per call on the models' [~10^4, 32..256] fp32
+windows; these take a few.  Other devices, dtypes or shapes (features not a multiple of 4, a
+LayerNorm wider than 1024, a Linear inner dimension above 256) use the torch operators.  Reference
+layers: NeutronGT/models/gt_dist_node_level_single_window.py:235-241, 311-325, 360-361, 537, 565;
+graphormer_dist_node_level.py:179, 183, 286.
 """
 from __future__ import annotations
 
@@ -81,27 +83,63 @@ class _LayerNormFn(torch.autograd.Function):
         return dx.view(ctx.shape), dw, db, None
 
 
+_WSL: dict = {}
+
+
+def _linear_ws(rows: int, in_f: int, out_f: int, device) -> torch.Tensor:
+    key = (rows, in_f, out_f, device.index)
+    nbytes = _WSL.get(key)
+    if nbytes is None:
+        nbytes = _WSL[key] = _lib.size_query(_lib.lib().ngt_linear_weight_workspace_size, rows, in_f, out_f)
+    return _lib.workspace(nbytes, device)
+
+
+_MAX_INNER = 256     # ngt_linear_forward / ngt_linear_backward_input keep W's inner dimension on chip
+
+
 class _LinearFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, weight, bias):
         shape = x.shape
-        x2 = x.reshape(-1, shape[-1])
-        y = torch.addmm(bias, x2, weight.t())
+        out_f, in_f = weight.shape
+        x2 = x.reshape(-1, in_f).contiguous()
+        rows = x2.shape[0]
+        if in_f <= _MAX_INNER:
+            y = torch.empty(rows, out_f, dtype=torch.float32, device=x.device)
+            _lib.check(_lib.lib().ngt_linear_forward(rows, in_f, out_f, _lib.ptr(x2), _lib.ptr(weight), _lib.ptr(bias),
+                                                     _lib.ptr(y), _lib.stream_of(x2)), "ngt_linear_forward")
+        else:
+            y = torch.addmm(bias, x2, weight.t())
         ctx.save_for_backward(x2, weight)
         ctx.shape = shape
-        return y.view(*shape[:-1], weight.shape[0])
+        return y.view(*shape[:-1], out_f)
 
     @staticmethod
     def backward(ctx, g):
         x2, weight = ctx.saved_tensors
-        g2 = g.reshape(-1, weight.shape[0]).contiguous()
+        out_f, in_f = weight.shape
+        g2 = g.reshape(-1, out_f).contiguous()
+        rows = g2.shape[0]
         dx = dw = db = None
         if ctx.needs_input_grad[0]:
-            dx = g2.mm(weight).view(ctx.shape)
+            if out_f <= _MAX_INNER:
+                dx = torch.empty(rows, in_f, dtype=torch.float32, device=g2.device)
+                _lib.check(_lib.lib().ngt_linear_backward_input(rows, in_f, out_f, _lib.ptr(g2), _lib.ptr(weight),
+                                                                _lib.ptr(dx), _lib.stream_of(g2)),
+                           "ngt_linear_backward_input")
+            else:
+                dx = g2.mm(weight)
+            dx = dx.view(ctx.shape)
         if ctx.needs_input_grad[1]:
-            dw = g2.t().mm(x2)
-        if ctx.needs_input_grad[2]:
-            db = column_sum(g2) if (g2.is_cuda and g2.dtype == torch.float32) else g2.sum(0)
+            dw = torch.empty(out_f, in_f, dtype=torch.float32, device=g2.device)
+            if ctx.needs_input_grad[2]:
+                db = torch.empty(out_f, dtype=torch.float32, device=g2.device)
+            ws = _linear_ws(rows, in_f, out_f, g2.device)
+            _lib.check(_lib.lib().ngt_linear_backward_weight(rows, in_f, out_f, _lib.ptr(x2), _lib.ptr(g2),
+                                                             _lib.ptr(dw), _lib.ptr(db), _lib.ptr(ws), ws.numel(),
+                                                             _lib.stream_of(g2)), "ngt_linear_backward_weight")
+        elif ctx.needs_input_grad[2]:
+            db = column_sum(g2)
         return dx, dw, db
 
 
@@ -115,6 +153,7 @@ class LayerNorm(nn.LayerNorm):
 
 class Linear(nn.Linear):
     def forward(self, x):
-        if self.bias is not None and _rows_ok(x, 4) and self.weight.dtype == torch.float32 and x.numel() > 0:
+        if (self.bias is not None and _rows_ok(x, 4) and self.weight.dtype == torch.float32 and x.numel() > 0
+                and self.in_features % 4 == 0 and self.out_features % 4 == 0):
             return _LinearFn.apply(x, self.weight, self.bias)
         return F.linear(x, self.weight, self.bias)

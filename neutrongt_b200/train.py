@@ -74,19 +74,37 @@ def build_window_state(rowptr, col, partitions, rank, world_size, feature, devic
 
 
 class FlatGradients:
-    """All parameters' gradients as views of one flat buffer (one all-reduce per step)."""
+    """All parameters' gradients as views of one flat buffer (one all-reduce per step).
+
+    `zero(set_to_none=True)` is the single-process form of the reference loop
+    (`optimizer.zero_grad(set_to_none=True)`, train_eval.py:287): gradients start as None, a
+    parameter without a gradient in the window is skipped by the optimizer, and backward hands
+    each fresh gradient to its parameter without an accumulate kernel.  With more than one rank
+    the reference gives every parameter a gradient (zeros where none was produced) and
+    all-reduces them (train_eval.py:289-295): `zero()` keeps the flat views for that."""
 
     def __init__(self, model: torch.nn.Module):
         self.params = [p for p in model.parameters() if p.requires_grad]
         total = sum(p.numel() for p in self.params)
         dev = self.params[0].device
         self.flat = torch.zeros(total, dtype=self.params[0].dtype, device=dev)
+        self._bind()
+
+    def _bind(self):
         off = 0
         for p in self.params:
             p.grad = self.flat[off:off + p.numel()].view_as(p)
             off += p.numel()
+        self.bound = True
 
-    def zero(self):
+    def zero(self, set_to_none: bool = False):
+        if set_to_none:
+            for p in self.params:
+                p.grad = None
+            self.bound = False
+            return
+        if not self.bound:
+            self._bind()
         self.flat.zero_()
 
     def average(self, world_size: int, group=None):
@@ -142,7 +160,7 @@ def train_epoch(args, model, local_partition_ids, local_partitions, feature, y, 
         t0 = time.perf_counter()
     losses, scores_by_pid = [], {}
     for i in range(max_steps):
-        grads.zero()
+        grads.zero(set_to_none=world_size == 1)
         if i < local_count:
             pid = local_partition_ids[i]
             idx_i = local_partitions[i]
@@ -236,7 +254,7 @@ class GraphedWindowTrainer:
         self._capture()
 
     def _step(self, i):
-        self.grads.zero()
+        self.grads.zero(set_to_none=self.world == 1)
         loss = None
         scores = None
         if i is not None:

@@ -56,3 +56,9 @@ def test_invalid_arguments_are_rejected_without_a_gpu():
     assert lib.ngt_layernorm_forward(10, 128, *([None] * 3), 1e-5, *([None] * 3), None) == 1
     assert lib.ngt_layernorm_forward(0, 128, *([None] * 3), 1e-5, *([None] * 3), None) == 0
     assert lib.ngt_column_sum(-1, 128, None, None, None, 0, None) == 1
+    # fp32 Linear: workspace query; inner dimensions above 256 are refused before any launch
+    assert _lib.size_query(lib.ngt_linear_weight_workspace_size, 10583, 128, 256) >= (128 * 256 + 256) * 4
+    assert lib.ngt_linear_forward(4, 260, 8, *([None] * 4), None) == 2
+    assert lib.ngt_linear_backward_input(4, 8, 260, *([None] * 3), None) == 2
+    assert lib.ngt_linear_forward(4, 6, 8, *([None] * 4), None) == 1           # features % 4 != 0
+    assert lib.ngt_linear_forward(0, 8, 8, *([None] * 4), None) == 0

@@ -1,0 +1,89 @@
+"""fp32 Linear layers on csrc/linear.cu (forward, input grad, weight + bias grad) against torch.
+
+Tolerance: relative (max|a-b| / max|b|) against an fp64 torch restatement, 1e-5 -- fp32 FFMA in a
+different summation order than cuBLAS; torch's own fp32 result is held to the same bound.
+"""
+import ctypes
+
+import pytest
+import torch
+
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-5
+
+# (rows, in, out): the GT / Graphormer window shapes, ragged and tiny row counts, the largest
+# inner dimension kept on chip (256), several column tiles, many row tiles per CTA
+SHAPES = [(10583, 128, 128), (10583, 128, 256), (10583, 256, 128), (10583, 128, 64), (10583, 64, 32),
+          (10583, 32, 40), (1, 4, 4), (5, 8, 12), (100, 64, 64), (1001, 256, 512), (200000, 128, 128),
+          (3, 300, 8)]
+
+
+def _ref(x, w, b, dy):
+    xd, wd, bd, dyd = (t.double() for t in (x, w, b, dy))
+    y = xd @ wd.t() + bd
+    return y, dyd @ wd, dyd.t() @ xd, dyd.sum(0)
+
+
+@pytest.mark.parametrize("rows,fin,fout", SHAPES)
+def test_linear_matches_fp64(cuda, rows, fin, fout):
+    from neutrongt_b200.layers import Linear
+    g = torch.Generator(device="cuda").manual_seed(rows * 7 + fin + fout)
+    x = torch.randn(1, rows, fin, generator=g, device="cuda")
+    dy = torch.randn(1, rows, fout, generator=g, device="cuda")
+    lin = Linear(fin, fout).cuda()
+    xa = x.clone().requires_grad_(True)
+    y = lin(xa)
+    y.backward(dy)
+    ry, rdx, rdw, rdb = _ref(x[0], lin.weight.detach(), lin.bias.detach(), dy[0])
+    assert rel_err(y[0], ry) < TOL
+    assert rel_err(xa.grad[0], rdx) < TOL
+    assert rel_err(lin.weight.grad, rdw) < TOL
+    assert rel_err(lin.bias.grad, rdb) < TOL
+    # torch's fp32 Linear meets the same bound (the tolerance is fp32's, not loosened for us)
+    ref = torch.nn.Linear(fin, fout).cuda()
+    ref.load_state_dict(lin.state_dict())
+    assert rel_err(ref(x)[0], ry) < TOL
+
+
+def test_weight_grad_is_bitwise_reproducible(cuda):
+    from neutrongt_b200.layers import Linear
+    x = torch.randn(10583, 128, device="cuda")
+    dy = torch.randn(10583, 256, device="cuda")
+    lin = Linear(128, 256).cuda()
+    grads = []
+    for _ in range(3):
+        lin.zero_grad(set_to_none=True)
+        lin(x).backward(dy)
+        grads.append((lin.weight.grad.clone(), lin.bias.grad.clone()))
+    for w, b in grads[1:]:
+        assert torch.equal(w, grads[0][0]) and torch.equal(b, grads[0][1])
+
+
+def test_c_abi_without_bias_and_empty_rows(cuda):
+    from neutrongt_b200 import _lib
+    lib = _lib.lib()
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    x = torch.randn(333, 96, device="cuda")
+    w = torch.randn(20, 96, device="cuda")
+    y = torch.empty(333, 20, device="cuda")
+    assert lib.ngt_linear_forward(333, 96, 20, _lib.ptr(x), _lib.ptr(w), None, _lib.ptr(y), st) == 0
+    assert rel_err(y, x.double() @ w.double().t()) < TOL
+    dy = torch.randn(333, 20, device="cuda")
+    dw = torch.full((20, 96), 7.0, device="cuda")
+    ws = _lib.workspace(_lib.size_query(lib.ngt_linear_weight_workspace_size, 333, 96, 20), "cuda")
+    assert lib.ngt_linear_backward_weight(333, 96, 20, _lib.ptr(x), _lib.ptr(dy), _lib.ptr(dw), None,
+                                          _lib.ptr(ws), ws.numel(), st) == 0
+    assert rel_err(dw, dy.double().t() @ x.double()) < TOL
+    # zero rows: zero gradients; inner dimension above 256 is refused, not computed
+    db = torch.full((20,), 3.0, device="cuda")
+    assert lib.ngt_linear_backward_weight(0, 96, 20, None, None, _lib.ptr(dw), _lib.ptr(db), None, 0, st) == 0
+    torch.cuda.synchronize()
+    assert not dw.any() and not db.any()
+    assert lib.ngt_linear_forward(4, 260, 8, _lib.ptr(x), _lib.ptr(w), None, _lib.ptr(y), st) == 2
+    assert lib.ngt_linear_backward_input(4, 8, 260, _lib.ptr(x), _lib.ptr(w), _lib.ptr(y), st) == 2
+    small = _lib.workspace(16, "cuda")
+    assert lib.ngt_linear_backward_weight(333, 96, 20, _lib.ptr(x), _lib.ptr(dy), _lib.ptr(dw), None,
+                                          _lib.ptr(small), 16, st) == 3

@@ -1,4 +1,4 @@
-"""LayerNorm forward/backward and the Linear bias gradient on csrc/rowops.cu against torch fp32."""
+"""LayerNorm forward/backward and the column sum on csrc/rowops.cu against torch fp32."""
 import pytest
 import torch
 
@@ -29,25 +29,6 @@ def test_layernorm_matches_torch(cuda, rows, cols):
     assert rel_err(ya, yb) < TOL
     assert rel_err(xa.grad, xb.grad) < TOL
     assert rel_err(ours.weight.grad, ref.weight.grad) < TOL
-    assert rel_err(ours.bias.grad, ref.bias.grad) < TOL
-
-
-@pytest.mark.parametrize("rows,cols,out", [(10583, 128, 384), (77, 256, 40), (1, 8, 3)])
-def test_linear_matches_torch(cuda, rows, cols, out):
-    from neutrongt_b200.layers import Linear
-    g = torch.Generator(device="cuda").manual_seed(rows)
-    x = torch.randn(1, rows, cols, generator=g, device="cuda")
-    dy = torch.randn(1, rows, out, generator=g, device="cuda")
-    ours = Linear(cols, out).cuda()
-    ref = torch.nn.Linear(cols, out).cuda()
-    ref.load_state_dict(ours.state_dict())
-    xa, xb = x.clone().requires_grad_(True), x.clone().requires_grad_(True)
-    ya, yb = ours(xa), ref(xb)
-    ya.backward(dy)
-    yb.backward(dy)
-    assert torch.equal(ya, yb)   # same addmm
-    assert torch.equal(xa.grad, xb.grad)
-    assert torch.equal(ours.weight.grad, ref.weight.grad)
     assert rel_err(ours.bias.grad, ref.bias.grad) < TOL
 
 
