@@ -71,6 +71,25 @@ NGT_API int ngt_edge_csr_build(int64_t n, int64_t e, const int64_t *edge_index, 
                        size_t workspace_bytes, ngt_stream_t stream);
 
 /* ------------------------------------------------------------------------------------
+ * Heavy-row segments of both CSR views (no counterpart in the reference: a scheduling table for
+ * the kernels below).  In power-law windows a few hub rows hold hundreds of entries while most
+ * rows hold one or two; one warp per row would make the hub's warp the whole kernel's critical
+ * path.  A row of degree d > seg_edges is cut into ceil(d / seg_edges) segments of seg_edges
+ * consecutive entries, each processed by its own warp; the partial sums are added in segment
+ * order afterwards, so results do not depend on scheduling.
+ *   seg_first  int32 [2n]: entries 0..n-1 for the destination view, n..2n-1 for the source view;
+ *              the first segment number of a heavy row, -1 for other rows
+ *   seg_row    int32 [2 * cap]: [0, cap) destination view, [cap, 2 cap) source view; the row
+ *              of each segment; cap from ngt_edge_csr_segment_capacity(e, seg_edges)
+ *   counts     int32 [2] (device): segments of the destination and of the source view
+ * Segment numbers within a view are dense in [0, counts[view]).
+ * ---------------------------------------------------------------------------------- */
+NGT_API int ngt_edge_csr_segment_capacity(int64_t e, int32_t seg_edges, int64_t *cap /* host */);
+NGT_API int ngt_edge_csr_segments(int64_t n, int64_t e, const int32_t *dst_rowptr, const int32_t *src_rowptr,
+                                  int32_t seg_edges, int32_t *seg_first, int32_t *seg_row, int32_t *counts,
+                                  ngt_stream_t stream);
+
+/* ------------------------------------------------------------------------------------
  * Graph-sparse window attention, forward.
  *
  * Replaces `CoreAttention.sparse_attention_bias` forward
@@ -130,6 +149,32 @@ NGT_API int ngt_spattn_backward(int dtype, int64_t n, int64_t e, int heads, int 
  *     clearing is needed, but calls that overlap on the GPU (other streams, other threads)
  *     race on it: serialise them.
  * ---------------------------------------------------------------------------------- */
+/* ------------------------------------------------------------------------------------
+ * Sparse attention with heavy rows split into segments (tables from ngt_edge_csr_segments;
+ * same results as ngt_spattn_forward / ngt_spattn_backward up to fp32 summation order).
+ *   seg_edges, *_seg_first, *_seg_row, *_nseg: one view's tables (nseg == 0: none)
+ *   seg_part   fp32 scratch, 16-byte aligned, ngt_spattn_seg_part_size(pass, ...) bytes
+ *              (pass 0: forward, pass 1: backward)
+ * Shapes outside the vector layout (see above) run unsegmented and ignore the tables.
+ * ---------------------------------------------------------------------------------- */
+NGT_API int ngt_spattn_seg_part_size(int pass, int heads, int head_dim, int64_t dst_nseg, int64_t src_nseg,
+                                     size_t *bytes /* host */);
+NGT_API int ngt_spattn_forward_seg(int dtype, int64_t n, int64_t e, int heads, int head_dim, const void *q,
+                                   const void *k, const void *v, const int32_t *dst_rowptr,
+                                   const int32_t *dst_src, const float *edge_bias, void *out, float *z,
+                                   float *node_scores, int64_t node_scores_len, int32_t seg_edges,
+                                   const int32_t *dst_seg_first, const int32_t *dst_seg_row, int64_t dst_nseg,
+                                   float *seg_part, ngt_stream_t stream);
+NGT_API int ngt_spattn_backward_seg(int dtype, int64_t n, int64_t e, int heads, int head_dim, const void *q,
+                                    const void *k, const void *v, const void *out, const void *dout,
+                                    const float *z, const int32_t *dst_rowptr, const int32_t *dst_src,
+                                    const int32_t *src_rowptr, const int32_t *src_dst,
+                                    const int32_t *src_to_dst_slot, const float *edge_bias, float *delta,
+                                    void *dq, void *dk, void *dv, float *dedge_bias, int32_t seg_edges,
+                                    const int32_t *dst_seg_first, const int32_t *dst_seg_row, int64_t dst_nseg,
+                                    const int32_t *src_seg_first, const int32_t *src_seg_row, int64_t src_nseg,
+                                    float *seg_part, ngt_stream_t stream);
+
 #define NGT_NOALLOC_MAX_ROWS_X_HEADS 2097152
 NGT_API int ngt_spattn_backward_noalloc(int dtype, int64_t n, int64_t e, int heads, int head_dim,
                                         const void *q, const void *k, const void *v,

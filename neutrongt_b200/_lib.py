@@ -32,6 +32,13 @@ SIGNATURES = {
                             _p, _p, _p, _p, _p, _p, _p],
     "ngt_spattn_backward_noalloc": [_i32, _i64, _i64, _i32, _i32, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
                                     _p, _p, _p, _p, _p, _p, _p],
+    "ngt_edge_csr_segment_capacity": [_i64, _i32, ctypes.POINTER(ctypes.c_int64)],
+    "ngt_edge_csr_segments": [_i64, _i64, _p, _p, _i32, _p, _p, _p, _p],
+    "ngt_spattn_seg_part_size": [_i32, _i32, _i32, _i64, _i64, _sz_p],
+    "ngt_spattn_forward_seg": [_i32, _i64, _i64, _i32, _i32, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64,
+                               _i32, _p, _p, _i64, _p, _p],
+    "ngt_spattn_backward_seg": [_i32, _i64, _i64, _i32, _i32, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
+                                _p, _p, _p, _p, _p, _p, _p, _i32, _p, _p, _i64, _p, _p, _i64, _p, _p],
     "ngt_dense_attn_forward": [_i64, _i32, _i32, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_uint64,
                                _p, _p, _p, _p, _p, _p, _p, _p],
     "ngt_dense_attn_backward": [_i64, _i32, _i32, ctypes.c_float, ctypes.c_float, ctypes.c_uint64, _p, _p, _p, _p,

@@ -34,11 +34,14 @@ class _SparseWindowAttention(torch.autograd.Function):
         z = torch.empty(s, heads, dtype=torch.float32, device=q.device)
         ns = torch.empty(csr.node_scores_len, dtype=torch.float32, device=q.device)
         L = _lib.lib()
-        _lib.check(L.ngt_spattn_forward(_lib.dtype_code(q.dtype), s, csr.e, heads, dim, _lib.ptr(q),
-                                        _lib.ptr(k), _lib.ptr(v), _lib.ptr(csr.dst_rowptr),
-                                        _lib.ptr(csr.dst_src), _lib.ptr(edge_bias), _lib.ptr(out),
-                                        _lib.ptr(z), _lib.ptr(ns), ns.numel(), _lib.stream_of(q)),
-                   "ngt_spattn_forward")
+        first, rows, nseg = csr.seg_tables(0)
+        part = _seg_part(0, heads, dim, nseg, 0, q.device)
+        _lib.check(L.ngt_spattn_forward_seg(_lib.dtype_code(q.dtype), s, csr.e, heads, dim, _lib.ptr(q),
+                                            _lib.ptr(k), _lib.ptr(v), _lib.ptr(csr.dst_rowptr),
+                                            _lib.ptr(csr.dst_src), _lib.ptr(edge_bias), _lib.ptr(out),
+                                            _lib.ptr(z), _lib.ptr(ns), ns.numel(), csr.seg_edges, _lib.ptr(first),
+                                            _lib.ptr(rows), nseg, _lib.ptr(part), _lib.stream_of(q)),
+                   "ngt_spattn_forward_seg")
         ctx.save_for_backward(q, k, v, out, z, edge_bias)
         ctx.csr = csr
         ctx.mark_non_differentiable(ns)
@@ -60,15 +63,27 @@ class _SparseWindowAttention(torch.autograd.Function):
         if edge_bias is not None and ctx.needs_input_grad[3]:
             dbias = torch.empty_like(edge_bias)
         L = _lib.lib()
-        _lib.check(L.ngt_spattn_backward(_lib.dtype_code(q.dtype), s, csr.e, heads, dim, _lib.ptr(q),
-                                         _lib.ptr(k), _lib.ptr(v), _lib.ptr(out), _lib.ptr(dout),
-                                         _lib.ptr(z), _lib.ptr(csr.dst_rowptr), _lib.ptr(csr.dst_src),
-                                         _lib.ptr(csr.src_rowptr), _lib.ptr(csr.src_dst),
-                                         _lib.ptr(csr.src_to_dst_slot), _lib.ptr(edge_bias),
-                                         _lib.ptr(delta), _lib.ptr(dq), _lib.ptr(dk), _lib.ptr(dv),
-                                         _lib.ptr(dbias), _lib.stream_of(q)),
-                   "ngt_spattn_backward")
+        fd, rd, nd = csr.seg_tables(0)
+        fs, rs, ns_ = csr.seg_tables(1)
+        part = _seg_part(1, heads, dim, nd, ns_, q.device)
+        _lib.check(L.ngt_spattn_backward_seg(_lib.dtype_code(q.dtype), s, csr.e, heads, dim, _lib.ptr(q),
+                                             _lib.ptr(k), _lib.ptr(v), _lib.ptr(out), _lib.ptr(dout),
+                                             _lib.ptr(z), _lib.ptr(csr.dst_rowptr), _lib.ptr(csr.dst_src),
+                                             _lib.ptr(csr.src_rowptr), _lib.ptr(csr.src_dst),
+                                             _lib.ptr(csr.src_to_dst_slot), _lib.ptr(edge_bias),
+                                             _lib.ptr(delta), _lib.ptr(dq), _lib.ptr(dk), _lib.ptr(dv),
+                                             _lib.ptr(dbias), csr.seg_edges, _lib.ptr(fd), _lib.ptr(rd), nd,
+                                             _lib.ptr(fs), _lib.ptr(rs), ns_, _lib.ptr(part), _lib.stream_of(q)),
+                   "ngt_spattn_backward_seg")
         return dq, dk, dv, dbias, None
+
+
+def _seg_part(pass_: int, heads: int, dim: int, nseg_dst: int, nseg_src: int, device):
+    """fp32 scratch for the heavy-row segment partial sums (None when there are no segments)."""
+    if nseg_dst == 0 and nseg_src == 0:
+        return None
+    nbytes = _lib.size_query(_lib.lib().ngt_spattn_seg_part_size, pass_, heads, dim, nseg_dst, nseg_src)
+    return _lib.workspace(nbytes, device)
 
 
 class WindowAttentionBuffers:
@@ -91,26 +106,37 @@ class WindowAttentionBuffers:
         self.dk = torch.empty_like(k)
         self.dv = torch.empty_like(v)
         self.code = _lib.dtype_code(q.dtype)
+        self.segs = (csr.seg_tables(0), csr.seg_tables(1))
+        nd, ns_ = self.segs[0][2], self.segs[1][2]
+        self.part_f = _seg_part(0, heads, dim, nd, 0, dev)
+        self.part_b = _seg_part(1, heads, dim, nd, ns_, dev)
 
     def forward(self):
         s, heads, dim = self.shape
         c = self.csr
-        _lib.check(_lib.lib().ngt_spattn_forward(self.code, s, c.e, heads, dim, _lib.ptr(self.q), _lib.ptr(self.k),
-                                                 _lib.ptr(self.v), _lib.ptr(c.dst_rowptr), _lib.ptr(c.dst_src), None,
-                                                 _lib.ptr(self.out), _lib.ptr(self.z), _lib.ptr(self.ns),
-                                                 self.ns.numel(), _lib.stream_of(self.q)), "ngt_spattn_forward")
+        (fd, rd, nd), _ = self.segs
+        _lib.check(_lib.lib().ngt_spattn_forward_seg(self.code, s, c.e, heads, dim, _lib.ptr(self.q),
+                                                     _lib.ptr(self.k), _lib.ptr(self.v), _lib.ptr(c.dst_rowptr),
+                                                     _lib.ptr(c.dst_src), None, _lib.ptr(self.out),
+                                                     _lib.ptr(self.z), _lib.ptr(self.ns), self.ns.numel(),
+                                                     c.seg_edges, _lib.ptr(fd), _lib.ptr(rd), nd,
+                                                     _lib.ptr(self.part_f), _lib.stream_of(self.q)),
+                   "ngt_spattn_forward_seg")
         return self.out, self.ns
 
     def backward(self, dout):
         s, heads, dim = self.shape
         c = self.csr
-        _lib.check(_lib.lib().ngt_spattn_backward(self.code, s, c.e, heads, dim, _lib.ptr(self.q), _lib.ptr(self.k),
-                                                  _lib.ptr(self.v), _lib.ptr(self.out), _lib.ptr(dout),
-                                                  _lib.ptr(self.z), _lib.ptr(c.dst_rowptr), _lib.ptr(c.dst_src),
-                                                  _lib.ptr(c.src_rowptr), _lib.ptr(c.src_dst), None, None,
-                                                  _lib.ptr(self.delta), _lib.ptr(self.dq), _lib.ptr(self.dk),
-                                                  _lib.ptr(self.dv), None, _lib.stream_of(self.q)),
-                   "ngt_spattn_backward")
+        (fd, rd, nd), (fs, rs, ns_) = self.segs
+        _lib.check(_lib.lib().ngt_spattn_backward_seg(self.code, s, c.e, heads, dim, _lib.ptr(self.q),
+                                                      _lib.ptr(self.k), _lib.ptr(self.v), _lib.ptr(self.out),
+                                                      _lib.ptr(dout), _lib.ptr(self.z), _lib.ptr(c.dst_rowptr),
+                                                      _lib.ptr(c.dst_src), _lib.ptr(c.src_rowptr),
+                                                      _lib.ptr(c.src_dst), None, None, _lib.ptr(self.delta),
+                                                      _lib.ptr(self.dq), _lib.ptr(self.dk), _lib.ptr(self.dv), None,
+                                                      c.seg_edges, _lib.ptr(fd), _lib.ptr(rd), nd, _lib.ptr(fs),
+                                                      _lib.ptr(rs), ns_, _lib.ptr(self.part_b),
+                                                      _lib.stream_of(self.q)), "ngt_spattn_backward_seg")
         return self.dq, self.dk, self.dv
 
 

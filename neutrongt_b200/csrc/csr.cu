@@ -166,10 +166,63 @@ SubWs carve_sub(void *base, size_t cap, int64_t num_global, int64_t w, size_t *u
     return s;
 }
 
+// Upper bound on the segments of one view: each heavy row has more than seg_edges entries, so
+// sum ceil(d / seg_edges) <= e / seg_edges + (heavy rows) <= 2 e / seg_edges.
+int64_t segment_capacity(int64_t e, int seg_edges) { return 2 * ((e + seg_edges - 1) / seg_edges) + 1; }
+
+// Heavy-row segments of both CSR views.  Thread i < n handles destination row i, thread n + i
+// source row i.  A row of degree d > seg_edges gets ceil(d / seg_edges) consecutive segment
+// numbers from its view's counter (their position among rows depends on scheduling; the rows a
+// segment covers and the order its partial sums are combined in do not); other rows get -1.
+__global__ void csr_segments_kernel(int n, const int32_t *__restrict__ dst_rowptr,
+                                    const int32_t *__restrict__ src_rowptr, int seg_edges, int64_t cap,
+                                    int32_t *__restrict__ seg_first, int32_t *__restrict__ seg_row,
+                                    int32_t *__restrict__ counts) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= 2 * (int64_t)n) return;
+    const int view = i >= n;
+    const int r = (int)(view ? i - n : i);
+    const int32_t *rp = view ? src_rowptr : dst_rowptr;
+    const int deg = rp[r + 1] - rp[r];
+    if (deg <= seg_edges) {
+        seg_first[i] = -1;
+        return;
+    }
+    const int ns = (deg + seg_edges - 1) / seg_edges;
+    const int s0 = atomicAdd(counts + view, ns);
+    seg_first[i] = s0;
+    for (int j = 0; j < ns; j++)
+        if (s0 + j < cap) seg_row[(size_t)view * cap + s0 + j] = r;
+}
+
 }  // namespace
 }  // namespace ngt
 
 using namespace ngt;
+
+extern "C" int ngt_edge_csr_segment_capacity(int64_t e, int32_t seg_edges, int64_t *cap) {
+    if (e < 0 || seg_edges <= 0 || !cap) return NGT_ERR_INVALID_ARGUMENT;
+    *cap = segment_capacity(e, seg_edges);
+    return NGT_OK;
+}
+
+extern "C" int ngt_edge_csr_segments(int64_t n, int64_t e, const int32_t *dst_rowptr, const int32_t *src_rowptr,
+                                     int32_t seg_edges, int32_t *seg_first, int32_t *seg_row, int32_t *counts,
+                                     ngt_stream_t stream) {
+    if (n < 0 || e < 0 || seg_edges <= 0 || !counts) return NGT_ERR_INVALID_ARGUMENT;
+    if (n >= (int64_t)INT32_MAX || e >= (int64_t)INT32_MAX) return NGT_ERR_TOO_LARGE;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    cudaMemsetAsync(counts, 0, 2 * sizeof(int32_t), st);
+    if (n > 0) {
+        if (!dst_rowptr || !src_rowptr || !seg_first || (e > 0 && !seg_row)) return NGT_ERR_INVALID_ARGUMENT;
+        const int64_t cap = segment_capacity(e, seg_edges);
+        const unsigned g = (unsigned)((2 * n + kThreads - 1) / kThreads);
+        csr_segments_kernel<<<g, kThreads, 0, st>>>((int)n, dst_rowptr, src_rowptr, seg_edges, cap, seg_first,
+                                                    seg_row, counts);
+    }
+    NGT_CHECK_LAUNCH();
+    return NGT_OK;
+}
 
 extern "C" int ngt_edge_csr_workspace_size(int64_t n, int64_t e, size_t *bytes) {
     if (n < 0 || e < 0 || !bytes) return NGT_ERR_INVALID_ARGUMENT;

@@ -58,23 +58,82 @@ __device__ __forceinline__ float slot_reduce(float x) {
     return x;
 }
 
+// Heavy-row segments of one CSR view (all null / 0: every row is one warp's work).  A row with
+// more than `edges` entries is split into consecutive segments of `edges` entries; segment s
+// covers entries [rowptr[row[s]] + (s - first[row[s]]) * edges, +edges) of row row[s].  Its warp
+// writes partial sums to part[s]; a finish pass adds a row's partials in segment order.
+struct SegView {
+    int edges;
+    const int32_t *first;   // [n] first segment of a heavy row, -1 for other rows
+    const int32_t *row;     // [nseg] row of each segment
+    int nseg;
+    float *part;            // [nseg][record]
+};
+
+__host__ __device__ inline int fwd_record(int heads, int row_floats) { return row_floats + ((heads + 3) & ~3); }
+
 // ------------------------------------------------------------------------------------
 // forward (vector path)
 // ------------------------------------------------------------------------------------
+// Output row, Z and node score of a finished row (acc and zs complete in every lane group).
+template <typename T, int HEAD_VECS, int ROW_VECS>
+__device__ __forceinline__ void fwd_finish(int row, int heads, const float (&acc)[VecLayout<T, HEAD_VECS, ROW_VECS>::VPL][VecLayout<T, HEAD_VECS, ROW_VECS>::VE],
+                                           const float (&zs)[VecLayout<T, HEAD_VECS, ROW_VECS>::VPL], T *__restrict__ out,
+                                           float *__restrict__ z, float *__restrict__ node_scores, int ns_len) {
+    using L = VecLayout<T, HEAD_VECS, ROW_VECS>;
+    constexpr int G = L::G, VPL = L::VPL, VE = L::VE;
+    const int lane = lane_id();
+    const int sub = lane / G;
+    const int gl = lane % G;
+    if (sub == 0) {
+        Vec16 *ov = reinterpret_cast<Vec16 *>(out) + (size_t)row * ROW_VECS + gl;
+#pragma unroll
+        for (int t = 0; t < VPL; t++) {
+            const float inv = 1.0f / (zs[t] + kEps);
+            float o[VE];
+#pragma unroll
+            for (int i = 0; i < VE; i++) o[i] = acc[t][i] * inv;
+            st16(ov + G * t, Elem<T>::pack(o));
+            if (z != nullptr && (gl % HEAD_VECS) == 0) z[(size_t)row * heads + (gl + G * t) / HEAD_VECS] = zs[t];
+        }
+    }
+    // node score: head mean of Z (one lane per head contributes through the xor tree)
+    float hs = 0.f;
+#pragma unroll
+    for (int t = 0; t < VPL; t++) hs += zs[t];
+#pragma unroll
+    for (int off = HEAD_VECS; off < G; off <<= 1) hs += __shfl_xor_sync(0xffffffffu, hs, off);
+    if (lane == 0 && row < ns_len) node_scores[row] = hs / (float)heads;
+}
+
 template <typename T, int HEAD_VECS, int ROW_VECS>
 __global__ void __launch_bounds__(kBlock)
     spattn_fwd_vec(int n, int heads, float scale_inv, const T *__restrict__ q,
                    const T *__restrict__ k, const T *__restrict__ v,
                    const int *__restrict__ rowptr, const int *__restrict__ col,
                    const float *__restrict__ bias, T *__restrict__ out, float *__restrict__ z,
-                   float *__restrict__ node_scores, int ns_len) {
+                   float *__restrict__ node_scores, int ns_len, int row_blocks, SegView sg) {
     using L = VecLayout<T, HEAD_VECS, ROW_VECS>;
     constexpr int G = L::G, VPL = L::VPL, EPW = L::EPW, VE = L::VE, UNROLL = L::UNROLL;
     const int lane = lane_id();
     const int sub = lane / G;
     const int gl = lane % G;
-    const int row = blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
-    if (row >= n) return;
+    const int wid = threadIdx.x >> 5;
+    // blocks [0, row_blocks): one warp per row; after them: one warp per heavy-row segment
+    int row, beg, end, seg = -1;
+    if ((int)blockIdx.x < row_blocks) {
+        row = blockIdx.x * kWarpsPerBlock + wid;
+        if (row >= n) return;
+        if (sg.first != nullptr && __ldg(sg.first + row) >= 0) return;   // done by its segments
+        beg = __ldg(rowptr + row);
+        end = __ldg(rowptr + row + 1);
+    } else {
+        seg = ((int)blockIdx.x - row_blocks) * kWarpsPerBlock + wid;
+        if (seg >= sg.nseg) return;
+        row = __ldg(sg.row + seg);
+        beg = __ldg(rowptr + row) + (seg - __ldg(sg.first + row)) * sg.edges;
+        end = min(__ldg(rowptr + row + 1), beg + sg.edges);
+    }
 
     const Vec16 *qv = reinterpret_cast<const Vec16 *>(q) + (size_t)row * ROW_VECS + gl;
     const Vec16 *kv = reinterpret_cast<const Vec16 *>(k) + gl;
@@ -92,8 +151,6 @@ __global__ void __launch_bounds__(kBlock)
         for (int i = 0; i < VE; i++) acc[t][i] = 0.f;
     }
 
-    const int beg = __ldg(rowptr + row);
-    const int end = __ldg(rowptr + row + 1);
     for (int e0 = beg; e0 < end; e0 += EPW * UNROLL) {
         int src[UNROLL];
         bool ok[UNROLL];
@@ -141,25 +198,61 @@ __global__ void __launch_bounds__(kBlock)
             for (int i = 0; i < VE; i++) acc[t][i] = slot_reduce<G>(acc[t][i]);
         }
     }
-    if (sub == 0) {
-        Vec16 *ov = reinterpret_cast<Vec16 *>(out) + (size_t)row * ROW_VECS + gl;
+    if (seg >= 0) {      // partial sums of the segment: acc in row layout, then Z per head
+        if (sub == 0) {
+            float *rec = sg.part + (size_t)seg * fwd_record(heads, ROW_VECS * VE);
+#pragma unroll
+            for (int t = 0; t < VPL; t++) {
+#pragma unroll
+                for (int i = 0; i < VE; i += 4)
+                    *reinterpret_cast<float4 *>(rec + (gl + G * t) * VE + i) =
+                        make_float4(acc[t][i], acc[t][i + 1], acc[t][i + 2], acc[t][i + 3]);
+                if ((gl % HEAD_VECS) == 0) rec[ROW_VECS * VE + (gl + G * t) / HEAD_VECS] = zs[t];
+            }
+        }
+        return;
+    }
+    fwd_finish<T, HEAD_VECS, ROW_VECS>(row, heads, acc, zs, out, z, node_scores, ns_len);
+}
+
+// One warp per heavy row (the warp of its first segment): adds the row's segment partials in
+// segment order and finishes the row.
+template <typename T, int HEAD_VECS, int ROW_VECS>
+__global__ void __launch_bounds__(kBlock)
+    spattn_fwd_seg_finish(int heads, const int *__restrict__ rowptr, T *__restrict__ out, float *__restrict__ z,
+                          float *__restrict__ node_scores, int ns_len, SegView sg) {
+    using L = VecLayout<T, HEAD_VECS, ROW_VECS>;
+    constexpr int G = L::G, VPL = L::VPL, VE = L::VE;
+    const int seg = blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
+    if (seg >= sg.nseg) return;
+    const int row = __ldg(sg.row + seg);
+    if (seg != __ldg(sg.first + row)) return;
+    const int gl = lane_id() % G;
+    const int cnt = (__ldg(rowptr + row + 1) - __ldg(rowptr + row) + sg.edges - 1) / sg.edges;
+    const int rs = fwd_record(heads, ROW_VECS * VE);
+    float acc[VPL][VE], zs[VPL];
+#pragma unroll
+    for (int t = 0; t < VPL; t++) {
+        zs[t] = 0.f;
+#pragma unroll
+        for (int i = 0; i < VE; i++) acc[t][i] = 0.f;
+    }
+    for (int j = 0; j < cnt; j++) {
+        const float *rec = sg.part + (size_t)(seg + j) * rs;
 #pragma unroll
         for (int t = 0; t < VPL; t++) {
-            const float inv = 1.0f / (zs[t] + kEps);
-            float o[VE];
 #pragma unroll
-            for (int i = 0; i < VE; i++) o[i] = acc[t][i] * inv;
-            st16(ov + G * t, Elem<T>::pack(o));
-            if (z != nullptr && (gl % HEAD_VECS) == 0) z[(size_t)row * heads + (gl + G * t) / HEAD_VECS] = zs[t];
+            for (int i = 0; i < VE; i += 4) {
+                const float4 a = __ldg(reinterpret_cast<const float4 *>(rec + (gl + G * t) * VE + i));
+                acc[t][i] += a.x;
+                acc[t][i + 1] += a.y;
+                acc[t][i + 2] += a.z;
+                acc[t][i + 3] += a.w;
+            }
+            zs[t] += __ldg(rec + ROW_VECS * VE + (gl + G * t) / HEAD_VECS);
         }
     }
-    // node score: head mean of Z (one lane per head contributes through the xor tree)
-    float hs = 0.f;
-#pragma unroll
-    for (int t = 0; t < VPL; t++) hs += zs[t];
-#pragma unroll
-    for (int off = HEAD_VECS; off < G; off <<= 1) hs += __shfl_xor_sync(0xffffffffu, hs, off);
-    if (lane == 0 && row < ns_len) node_scores[row] = hs / (float)heads;
+    fwd_finish<T, HEAD_VECS, ROW_VECS>(row, heads, acc, zs, out, z, node_scores, ns_len);
 }
 
 // ------------------------------------------------------------------------------------
@@ -201,15 +294,39 @@ __global__ void __launch_bounds__(kBlock)
                    const int *__restrict__ src_rowptr, const int *__restrict__ src_dst,
                    const int *__restrict__ src_to_dst_slot, const float *__restrict__ bias,
                    T *__restrict__ dq, T *__restrict__ dk, T *__restrict__ dv,
-                   float *__restrict__ dbias) {
+                   float *__restrict__ dbias, SegView sgd, SegView sgs) {
     using L = VecLayout<T, HEAD_VECS, ROW_VECS>;
     constexpr int G = L::G, VPL = L::VPL, EPW = L::EPW, VE = L::VE, UNROLL = L::UNROLL;
     const int lane = lane_id();
     const int sub = lane / G;
     const int gl = lane % G;
-    const bool role_a = blockIdx.x < blocks_a;
-    const int row = (role_a ? blockIdx.x : blockIdx.x - blocks_a) * kWarpsPerBlock + (threadIdx.x >> 5);
-    if (row >= n) return;
+    const int wid = threadIdx.x >> 5;
+    const int b = blockIdx.x;
+    // blocks: [0, blocks_a) destination rows, [blocks_a, 2 blocks_a) source rows, then the
+    // destination-view segments and the source-view segments of heavy rows
+    const int seg_blocks_d = (sgd.nseg + kWarpsPerBlock - 1) / kWarpsPerBlock;
+    bool role_a;
+    int row, beg, end, seg = -1;
+    if (b < 2 * blocks_a) {
+        role_a = b < blocks_a;
+        row = (role_a ? b : b - blocks_a) * kWarpsPerBlock + wid;
+        if (row >= n) return;
+        const int32_t *first = role_a ? sgd.first : sgs.first;
+        if (first != nullptr && __ldg(first + row) >= 0) return;   // done by its segments
+        const int *rp = role_a ? dst_rowptr : src_rowptr;
+        beg = __ldg(rp + row);
+        end = __ldg(rp + row + 1);
+    } else {
+        const int sb = b - 2 * blocks_a;
+        role_a = sb < seg_blocks_d;
+        seg = (role_a ? sb : sb - seg_blocks_d) * kWarpsPerBlock + wid;
+        if (seg >= (role_a ? sgd.nseg : sgs.nseg)) return;
+        row = __ldg((role_a ? sgd.row : sgs.row) + seg);
+        const int *rp = role_a ? dst_rowptr : src_rowptr;
+        const int edges = role_a ? sgd.edges : sgs.edges;
+        beg = __ldg(rp + row) + (seg - __ldg((role_a ? sgd.first : sgs.first) + row)) * edges;
+        end = min(__ldg(rp + row + 1), beg + edges);
+    }
     const Vec16 *Q = reinterpret_cast<const Vec16 *>(q) + gl;
     const Vec16 *K = reinterpret_cast<const Vec16 *>(k) + gl;
     const Vec16 *V = reinterpret_cast<const Vec16 *>(v) + gl;
@@ -231,7 +348,6 @@ __global__ void __launch_bounds__(kBlock)
 #pragma unroll
             for (int i = 0; i < VE; i++) acc[t][i] = 0.f;
         }
-        const int beg = __ldg(dst_rowptr + row), end = __ldg(dst_rowptr + row + 1);
         for (int e0 = beg; e0 < end; e0 += EPW * UNROLL) {
             int src[UNROLL];
             bool ok[UNROLL];
@@ -284,6 +400,18 @@ __global__ void __launch_bounds__(kBlock)
 #pragma unroll
                 for (int i = 0; i < VE; i++) acc[t][i] = slot_reduce<G>(acc[t][i]);
         }
+        if (seg >= 0) {   // segment partial of dq (before the 1/sqrt(D) scale)
+            if (sub == 0) {
+                float *rec = sgd.part + (size_t)seg * ROW_VECS * VE;
+#pragma unroll
+                for (int t = 0; t < VPL; t++)
+#pragma unroll
+                    for (int i = 0; i < VE; i += 4)
+                        *reinterpret_cast<float4 *>(rec + (gl + G * t) * VE + i) =
+                            make_float4(acc[t][i], acc[t][i + 1], acc[t][i + 2], acc[t][i + 3]);
+            }
+            return;
+        }
         if (sub == 0) {
             Vec16 *o = reinterpret_cast<Vec16 *>(dq) + rbase + gl;
 #pragma unroll
@@ -304,7 +432,6 @@ __global__ void __launch_bounds__(kBlock)
 #pragma unroll
             for (int i = 0; i < VE; i++) ak[t][i] = av[t][i] = 0.f;
         }
-        const int beg = __ldg(src_rowptr + row), end = __ldg(src_rowptr + row + 1);
         for (int e0 = beg; e0 < end; e0 += EPW * UNROLL) {
             int dst[UNROLL];
             bool ok[UNROLL];
@@ -368,6 +495,21 @@ __global__ void __launch_bounds__(kBlock)
                     av[t][i] = slot_reduce<G>(av[t][i]);
                 }
         }
+        if (seg >= 0) {   // segment partials of dk (unscaled) and dv
+            if (sub == 0) {
+                float *rec = sgs.part + (size_t)seg * 2 * ROW_VECS * VE;
+#pragma unroll
+                for (int t = 0; t < VPL; t++)
+#pragma unroll
+                    for (int i = 0; i < VE; i += 4) {
+                        *reinterpret_cast<float4 *>(rec + (gl + G * t) * VE + i) =
+                            make_float4(ak[t][i], ak[t][i + 1], ak[t][i + 2], ak[t][i + 3]);
+                        *reinterpret_cast<float4 *>(rec + ROW_VECS * VE + (gl + G * t) * VE + i) =
+                            make_float4(av[t][i], av[t][i + 1], av[t][i + 2], av[t][i + 3]);
+                    }
+            }
+            return;
+        }
         if (sub == 0) {
             Vec16 *ok_ = reinterpret_cast<Vec16 *>(dk) + rbase + gl;
             Vec16 *ov = reinterpret_cast<Vec16 *>(dv) + rbase + gl;
@@ -379,6 +521,67 @@ __global__ void __launch_bounds__(kBlock)
                 st16(ok_ + G * t, Elem<T>::pack(r));
                 st16(ov + G * t, Elem<T>::pack(av[t]));
             }
+        }
+    }
+}
+
+// One warp per heavy row and view (the warp of its first segment): adds the segment partials in
+// segment order and writes dq (destination view) or dk, dv (source view).
+template <typename T, int HEAD_VECS, int ROW_VECS>
+__global__ void __launch_bounds__(kBlock)
+    spattn_bwd_seg_finish(float scale_inv, const int *__restrict__ dst_rowptr, const int *__restrict__ src_rowptr,
+                          T *__restrict__ dq, T *__restrict__ dk, T *__restrict__ dv, SegView sgd, SegView sgs) {
+    using L = VecLayout<T, HEAD_VECS, ROW_VECS>;
+    constexpr int G = L::G, VPL = L::VPL, VE = L::VE, RF = ROW_VECS * VE;
+    const int seg_blocks_d = (sgd.nseg + kWarpsPerBlock - 1) / kWarpsPerBlock;
+    const bool role_a = (int)blockIdx.x < seg_blocks_d;
+    const int seg = ((int)blockIdx.x - (role_a ? 0 : seg_blocks_d)) * kWarpsPerBlock + (threadIdx.x >> 5);
+    if (seg >= (role_a ? sgd.nseg : sgs.nseg)) return;
+    const int row = __ldg((role_a ? sgd.row : sgs.row) + seg);
+    if (seg != __ldg((role_a ? sgd.first : sgs.first) + row)) return;
+    const int lane = lane_id(), sub = lane / G, gl = lane % G;
+    const int *rp = role_a ? dst_rowptr : src_rowptr;
+    const int edges = role_a ? sgd.edges : sgs.edges;
+    const int cnt = (__ldg(rp + row + 1) - __ldg(rp + row) + edges - 1) / edges;
+    const int parts = role_a ? 1 : 2;
+    const float *base = (role_a ? sgd.part : sgs.part) + (size_t)seg * parts * RF;
+    float a0[VPL][VE], a1[VPL][VE];
+#pragma unroll
+    for (int t = 0; t < VPL; t++)
+#pragma unroll
+        for (int i = 0; i < VE; i++) a0[t][i] = a1[t][i] = 0.f;
+    for (int j = 0; j < cnt; j++) {
+        const float *rec = base + (size_t)j * parts * RF;
+#pragma unroll
+        for (int t = 0; t < VPL; t++)
+#pragma unroll
+            for (int i = 0; i < VE; i += 4) {
+                const float4 x = __ldg(reinterpret_cast<const float4 *>(rec + (gl + G * t) * VE + i));
+                a0[t][i] += x.x;
+                a0[t][i + 1] += x.y;
+                a0[t][i + 2] += x.z;
+                a0[t][i + 3] += x.w;
+                if (!role_a) {
+                    const float4 y = __ldg(reinterpret_cast<const float4 *>(rec + RF + (gl + G * t) * VE + i));
+                    a1[t][i] += y.x;
+                    a1[t][i + 1] += y.y;
+                    a1[t][i + 2] += y.z;
+                    a1[t][i + 3] += y.w;
+                }
+            }
+    }
+    if (sub != 0) return;
+    const size_t rbase = (size_t)row * ROW_VECS + gl;
+#pragma unroll
+    for (int t = 0; t < VPL; t++) {
+        float r[VE];
+#pragma unroll
+        for (int i = 0; i < VE; i++) r[i] = a0[t][i] * scale_inv;
+        if (role_a) {
+            st16(reinterpret_cast<Vec16 *>(dq) + rbase + G * t, Elem<T>::pack(r));
+        } else {
+            st16(reinterpret_cast<Vec16 *>(dk) + rbase + G * t, Elem<T>::pack(r));
+            st16(reinterpret_cast<Vec16 *>(dv) + rbase + G * t, Elem<T>::pack(a1[t]));
         }
     }
 }
@@ -563,18 +766,23 @@ Shape vec_shape(int heads, int head_dim) {
 template <typename T>
 int forward_t(int64_t n, int heads, int head_dim, const void *q, const void *k, const void *v,
               const int32_t *rowptr, const int32_t *col, const float *bias, void *out, float *z,
-              float *ns, int64_t ns_len, cudaStream_t st) {
+              float *ns, int64_t ns_len, SegView sg, cudaStream_t st) {
     const float scale_inv = 1.0f / sqrtf((float)head_dim);
     const Shape sh = vec_shape<T>(heads, head_dim);
     const bool al = aligned16(q) && aligned16(k) && aligned16(v) && aligned16(out);
     if (n == 0) return NGT_OK;
     if (sh.head_vecs && al) {
-        const int grid = ceil_div_i(n, kWarpsPerBlock);
+        const int row_blocks = ceil_div_i(n, kWarpsPerBlock);
+        const int seg_blocks = ceil_div_i(sg.nseg, kWarpsPerBlock);
 #define NGT_FWD(HV, RV)                                                                          \
     if (sh.head_vecs == HV && sh.row_vecs == RV) {                                               \
-        spattn_fwd_vec<T, HV, RV><<<grid, kBlock, 0, st>>>(                                      \
+        spattn_fwd_vec<T, HV, RV><<<row_blocks + seg_blocks, kBlock, 0, st>>>(                   \
             (int)n, heads, scale_inv, (const T *)q, (const T *)k, (const T *)v, rowptr, col,     \
-            bias, (T *)out, z, ns, (int)ns_len);                                                 \
+            bias, (T *)out, z, ns, (int)ns_len, row_blocks, sg);                                 \
+        NGT_CHECK_LAUNCH();                                                                      \
+        if (sg.nseg > 0)                                                                         \
+            spattn_fwd_seg_finish<T, HV, RV><<<seg_blocks, kBlock, 0, st>>>(heads, rowptr, (T *)out, z, ns, \
+                                                                            (int)ns_len, sg);    \
         NGT_CHECK_LAUNCH();                                                                      \
         return NGT_OK;                                                                           \
     }
@@ -603,7 +811,7 @@ int backward_t(int64_t n, int heads, int head_dim, const void *q, const void *k,
                const void *out, const void *dout, const float *z, const int32_t *dst_rowptr,
                const int32_t *dst_src, const int32_t *src_rowptr, const int32_t *src_dst,
                const int32_t *s2d, const float *bias, float *delta, void *dq, void *dk, void *dv,
-               float *dbias, cudaStream_t st) {
+               float *dbias, SegView sgd, SegView sgs, cudaStream_t st) {
     const float scale_inv = 1.0f / sqrtf((float)head_dim);
     if (n == 0) return NGT_OK;
     const Shape sh = vec_shape<T>(heads, head_dim);
@@ -611,16 +819,21 @@ int backward_t(int64_t n, int heads, int head_dim, const void *q, const void *k,
                     aligned16(dout) && aligned16(dq) && aligned16(dk) && aligned16(dv);
     if (sh.head_vecs && al) {
         const int blocks_a = ceil_div_i(n, kWarpsPerBlock);
+        const int seg_blocks = ceil_div_i(sgd.nseg, kWarpsPerBlock) + ceil_div_i(sgs.nseg, kWarpsPerBlock);
 #define NGT_BWD(HV, RV)                                                                           \
     if (sh.head_vecs == HV && sh.row_vecs == RV) {                                                \
         using Lay = VecLayout<T, HV, RV>;                                                         \
         spattn_delta_vec<T, HV, RV><<<ceil_div_i(n, (int64_t)kWarpsPerBlock * Lay::EPW), kBlock, 0, st>>>( \
             (int)n, heads, (const T *)out, (const T *)dout, delta);                               \
         NGT_CHECK_LAUNCH();                                                                       \
-        spattn_bwd_vec<T, HV, RV><<<2 * blocks_a, kBlock, 0, st>>>(                               \
+        spattn_bwd_vec<T, HV, RV><<<2 * blocks_a + seg_blocks, kBlock, 0, st>>>(                  \
             (int)n, heads, scale_inv, blocks_a, (const T *)q, (const T *)k, (const T *)v,         \
             (const T *)dout, z, delta, dst_rowptr, dst_src, src_rowptr, src_dst, s2d, bias,       \
-            (T *)dq, (T *)dk, (T *)dv, dbias);                                                    \
+            (T *)dq, (T *)dk, (T *)dv, dbias, sgd, sgs);                                          \
+        NGT_CHECK_LAUNCH();                                                                       \
+        if (seg_blocks > 0)                                                                       \
+            spattn_bwd_seg_finish<T, HV, RV><<<seg_blocks, kBlock, 0, st>>>(                      \
+                scale_inv, dst_rowptr, src_rowptr, (T *)dq, (T *)dk, (T *)dv, sgd, sgs);          \
         NGT_CHECK_LAUNCH();                                                                       \
         return NGT_OK;                                                                            \
     }
@@ -670,11 +883,60 @@ extern "C" int ngt_spattn_forward(int dtype, int64_t n, int64_t e, int heads, in
     if (node_scores_len < 0 || node_scores_len > n || (node_scores_len > 0 && !node_scores))
         return NGT_ERR_INVALID_ARGUMENT;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const SegView none{0, nullptr, nullptr, 0, nullptr};
     if (dtype == NGT_F32)
         return forward_t<float>(n, heads, head_dim, q, k, v, dst_rowptr, dst_src, edge_bias, out, z,
-                                node_scores, node_scores_len, st);
+                                node_scores, node_scores_len, none, st);
     return forward_t<__nv_bfloat16>(n, heads, head_dim, q, k, v, dst_rowptr, dst_src, edge_bias, out,
-                                    z, node_scores, node_scores_len, st);
+                                    z, node_scores, node_scores_len, none, st);
+}
+
+namespace {
+// Segment tables of one view as the kernels take them; a view without segments is all null.
+int seg_view(int64_t n, int32_t seg_edges, const int32_t *first, const int32_t *row, int64_t nseg, float *part,
+             SegView *out) {
+    *out = SegView{0, nullptr, nullptr, 0, nullptr};
+    if (nseg < 0) return NGT_ERR_INVALID_ARGUMENT;
+    if (nseg == 0 || n == 0) return NGT_OK;
+    if (seg_edges <= 0 || !first || !row || !part) return NGT_ERR_INVALID_ARGUMENT;
+    if (nseg >= (int64_t)INT32_MAX) return NGT_ERR_TOO_LARGE;
+    if ((reinterpret_cast<uintptr_t>(part) & 15u) != 0) return NGT_ERR_MISALIGNED;
+    *out = SegView{seg_edges, first, row, (int)nseg, part};
+    return NGT_OK;
+}
+}  // namespace
+
+extern "C" int ngt_spattn_seg_part_size(int pass, int heads, int head_dim, int64_t dst_nseg, int64_t src_nseg,
+                                        size_t *bytes) {
+    if (!bytes || heads <= 0 || head_dim <= 0 || dst_nseg < 0 || src_nseg < 0 || (pass != 0 && pass != 1))
+        return NGT_ERR_INVALID_ARGUMENT;
+    const size_t hd = (size_t)heads * head_dim;
+    *bytes = sizeof(float) * (pass == 0 ? (size_t)dst_nseg * fwd_record(heads, (int)hd)
+                                        : (size_t)dst_nseg * hd + (size_t)src_nseg * 2 * hd);
+    return NGT_OK;
+}
+
+extern "C" int ngt_spattn_forward_seg(int dtype, int64_t n, int64_t e, int heads, int head_dim, const void *q,
+                                      const void *k, const void *v, const int32_t *dst_rowptr,
+                                      const int32_t *dst_src, const float *edge_bias, void *out, float *z,
+                                      float *node_scores, int64_t node_scores_len, int32_t seg_edges,
+                                      const int32_t *dst_seg_first, const int32_t *dst_seg_row, int64_t dst_nseg,
+                                      float *seg_part, ngt_stream_t stream) {
+    int rc = check_common(dtype, n, e, heads, head_dim);
+    if (rc != NGT_OK) return rc;
+    if (n > 0 && (!q || !k || !v || !dst_rowptr || !out)) return NGT_ERR_INVALID_ARGUMENT;
+    if (e > 0 && !dst_src) return NGT_ERR_INVALID_ARGUMENT;
+    if (node_scores_len < 0 || node_scores_len > n || (node_scores_len > 0 && !node_scores))
+        return NGT_ERR_INVALID_ARGUMENT;
+    SegView sg;
+    rc = seg_view(n, seg_edges, dst_seg_first, dst_seg_row, dst_nseg, seg_part, &sg);
+    if (rc != NGT_OK) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (dtype == NGT_F32)
+        return forward_t<float>(n, heads, head_dim, q, k, v, dst_rowptr, dst_src, edge_bias, out, z,
+                                node_scores, node_scores_len, sg, st);
+    return forward_t<__nv_bfloat16>(n, heads, head_dim, q, k, v, dst_rowptr, dst_src, edge_bias, out,
+                                    z, node_scores, node_scores_len, sg, st);
 }
 
 extern "C" int ngt_spattn_backward(int dtype, int64_t n, int64_t e, int heads, int head_dim,
@@ -692,13 +954,47 @@ extern "C" int ngt_spattn_backward(int dtype, int64_t n, int64_t e, int heads, i
     if (e > 0 && (!dst_src || !src_dst)) return NGT_ERR_INVALID_ARGUMENT;
     if (edge_bias != nullptr && e > 0 && src_to_dst_slot == nullptr) return NGT_ERR_INVALID_ARGUMENT;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const SegView none{0, nullptr, nullptr, 0, nullptr};
     if (dtype == NGT_F32)
         return backward_t<float>(n, heads, head_dim, q, k, v, out, dout, z, dst_rowptr, dst_src,
                                  src_rowptr, src_dst, src_to_dst_slot, edge_bias, delta, dq, dk, dv,
-                                 dedge_bias, st);
+                                 dedge_bias, none, none, st);
     return backward_t<__nv_bfloat16>(n, heads, head_dim, q, k, v, out, dout, z, dst_rowptr, dst_src,
                                      src_rowptr, src_dst, src_to_dst_slot, edge_bias, delta, dq, dk,
-                                     dv, dedge_bias, st);
+                                     dv, dedge_bias, none, none, st);
+}
+
+extern "C" int ngt_spattn_backward_seg(int dtype, int64_t n, int64_t e, int heads, int head_dim, const void *q,
+                                       const void *k, const void *v, const void *out, const void *dout,
+                                       const float *z, const int32_t *dst_rowptr, const int32_t *dst_src,
+                                       const int32_t *src_rowptr, const int32_t *src_dst,
+                                       const int32_t *src_to_dst_slot, const float *edge_bias, float *delta,
+                                       void *dq, void *dk, void *dv, float *dedge_bias, int32_t seg_edges,
+                                       const int32_t *dst_seg_first, const int32_t *dst_seg_row,
+                                       int64_t dst_nseg, const int32_t *src_seg_first,
+                                       const int32_t *src_seg_row, int64_t src_nseg, float *seg_part,
+                                       ngt_stream_t stream) {
+    int rc = check_common(dtype, n, e, heads, head_dim);
+    if (rc != NGT_OK) return rc;
+    if (n > 0 && (!q || !k || !v || !out || !dout || !z || !dst_rowptr || !src_rowptr || !delta ||
+                  !dq || !dk || !dv))
+        return NGT_ERR_INVALID_ARGUMENT;
+    if (e > 0 && (!dst_src || !src_dst)) return NGT_ERR_INVALID_ARGUMENT;
+    if (edge_bias != nullptr && e > 0 && src_to_dst_slot == nullptr) return NGT_ERR_INVALID_ARGUMENT;
+    SegView sgd, sgs;
+    rc = seg_view(n, seg_edges, dst_seg_first, dst_seg_row, dst_nseg, seg_part, &sgd);
+    if (rc != NGT_OK) return rc;
+    float *src_part = seg_part ? seg_part + (size_t)dst_nseg * heads * head_dim : nullptr;
+    rc = seg_view(n, seg_edges, src_seg_first, src_seg_row, src_nseg, src_part, &sgs);
+    if (rc != NGT_OK) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (dtype == NGT_F32)
+        return backward_t<float>(n, heads, head_dim, q, k, v, out, dout, z, dst_rowptr, dst_src,
+                                 src_rowptr, src_dst, src_to_dst_slot, edge_bias, delta, dq, dk, dv,
+                                 dedge_bias, sgd, sgs, st);
+    return backward_t<__nv_bfloat16>(n, heads, head_dim, q, k, v, out, dout, z, dst_rowptr, dst_src,
+                                     src_rowptr, src_dst, src_to_dst_slot, edge_bias, delta, dq, dk,
+                                     dv, dedge_bias, sgd, sgs, st);
 }
 
 // ------------------------------------------------------------------------------------
