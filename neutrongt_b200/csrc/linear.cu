@@ -32,8 +32,13 @@ constexpr int kTileN = 128;        // output columns per CTA tile
 constexpr int kSlice = 32;         // k columns per staged slice of the row GEMM
 constexpr int kAStride = 36;       // padded row stride (floats) of a staged slice
 constexpr int kStages = 3;         // cp.async ring depth of the row GEMM
-constexpr int kRowThreads = 256;   // row GEMM: 8 warps, 2 per SM sub-partition
-constexpr int kMaxSlots = 18;      // row GEMM: 8-row slots per CTA (9 per warp half)
+// Row GEMM: two groups of 4 warps, so each SM sub-partition runs 2 warps.  (One group with up to
+// 12 rows per lane balances shared-memory and FFMA cycles better on paper, but with one warp per
+// sub-partition nothing hides the operand latency, and 2 CTAs no longer fit for 256-wide outputs;
+// measured slower.)
+constexpr int kHalves = 2;
+constexpr int kRowThreads = 128 * kHalves;
+constexpr int kMaxTR = 9;           // row GEMM: rows per lane
 constexpr int kMaxInner = 256;     // row GEMM: inner dimension kept resident in shared memory
 constexpr int kWgThreads = 256;    // weight grad: 16 x 16 threads, 8 x 8 outputs each
 constexpr int kWgSlab = 16;        // rows per staged slab (weight grad); 2 x 2 x 8 KB static smem
@@ -93,7 +98,7 @@ template <int TRH, bool TRANS>
 __device__ __forceinline__ void load_group(float4 (&a)[TRH], float4 (&w)[8], const float *as, const float *bsrc,
                                            int g, int wst) {
 #pragma unroll
-    for (int i = 0; i < TRH; i++) a[i] = *reinterpret_cast<const float4 *>(as + 16 * i * kAStride + 4 * g);
+    for (int i = 0; i < TRH; i++) a[i] = *reinterpret_cast<const float4 *>(as + 8 * kHalves * i * kAStride + 4 * g);
     if (TRANS) {
 #pragma unroll
         for (int j = 0; j < 8; j++) w[j] = *reinterpret_cast<const float4 *>(bsrc + 4 * j * wst + 4 * g);
@@ -130,8 +135,7 @@ struct RowGemmArgs {
     float *C;
 };
 
-// One row tile for a warp half with TRH row slots (rows r0 + rg + 8 * (half + 2i)).  Every
-// thread of the CTA runs the same slice loop (same barriers), whichever TRH its half has.
+// One row tile; lane rows r0 + rg + 8 * (half + kHalves * i), i < TRH.
 template <int TRH, bool TRANS>
 __device__ __forceinline__ void row_tile(const RowGemmArgs &p, float *Bs, float *As, int64_t r0, int RT, int n0,
                                          bool load_b, int half) {
@@ -204,7 +208,7 @@ __device__ __forceinline__ void row_tile(const RowGemmArgs &p, float *Bs, float 
                 const float bj = p.bias ? __ldg(p.bias + c) : 0.f;
 #pragma unroll
                 for (int i = 0; i < TRH; i++) {
-                    const int64_t row = r0 + rg + 8 * (half + 2 * i);
+                    const int64_t row = r0 + rg + 8 * (half + kHalves * i);
                     if (row < p.M) p.C[row * p.N + c] = acc[i][j] + bj;
                 }
             }
@@ -217,7 +221,7 @@ __device__ __forceinline__ void row_tile(const RowGemmArgs &p, float *Bs, float 
             }
 #pragma unroll
             for (int i = 0; i < TRH; i++) {
-                const int64_t row = r0 + rg + 8 * (half + 2 * i);
+                const int64_t row = r0 + rg + 8 * (half + kHalves * i);
                 if (row >= p.M) continue;
                 float *cr = p.C + row * p.N + c;
                 if (c < p.N)
@@ -231,8 +235,8 @@ __device__ __forceinline__ void row_tile(const RowGemmArgs &p, float *Bs, float 
     }
 }
 
-// A CTA owns RT = 16 * TR rows per row tile; warp half h (warps 4h..4h+3) takes the 8-row slots
-// h, h + 2, ... (TR each, so both halves run one code path).
+// A CTA owns RT = 8 * kHalves * TR rows per row tile; warp group h (warps 4h..4h+3) takes the
+// 8-row slots h, h + kHalves, ... (TR each, so all groups run one code path).
 template <int TR, bool TRANS>
 __global__ void __launch_bounds__(kRowThreads, 1)
     row_gemm_kernel(RowGemmArgs p, int col_tiles, int64_t row_tiles) {
@@ -244,7 +248,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
     const int ct = blockIdx.x % col_tiles;
     const int64_t slot = blockIdx.x / col_tiles, nslots = gridDim.x / col_tiles;
     const int n0 = ct * kTileN;
-    const int RT = 16 * TR;
+    const int RT = 8 * kHalves * TR;
     bool load_b = true;
     for (int64_t t = slot; t < row_tiles; t += nslots) {
         row_tile<TR, TRANS>(p, Bs, As, t * RT, RT, n0, load_b, half);
@@ -383,7 +387,7 @@ int launch_row_gemm_t(int64_t M, int K, int N, const float *A, const float *W, c
     static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
-    const size_t smem = row_gemm_smem<TRANS>(2 * TR, kMaxInner);
+    const size_t smem = row_gemm_smem<TRANS>(kHalves * TR, kMaxInner);
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
         if (cudaFuncSetAttribute(row_gemm_kernel<TR, TRANS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)smem) != cudaSuccess)
@@ -391,14 +395,15 @@ int launch_row_gemm_t(int64_t M, int K, int N, const float *A, const float *W, c
         attr_set[dev] = true;
     }
     const int col_tiles = (N + kTileN - 1) / kTileN;
-    const int64_t rt = 16 * TR;
+    const int64_t rt = 8 * kHalves * TR;
     const int64_t row_tiles = (M + rt - 1) / rt;
     int64_t ctas = sm_count() / col_tiles;
     if (ctas < 1) ctas = 1;
     if (ctas > row_tiles) ctas = row_tiles;
     const unsigned grid = (unsigned)(ctas * col_tiles);
     RowGemmArgs p{M, K, N, A, W, bias, C};
-    row_gemm_kernel<TR, TRANS><<<grid, kRowThreads, row_gemm_smem<TRANS>(2 * TR, K), st>>>(p, col_tiles, row_tiles);
+    row_gemm_kernel<TR, TRANS><<<grid, kRowThreads, row_gemm_smem<TRANS>(kHalves * TR, K), st>>>(p, col_tiles,
+                                                                                              row_tiles);
     NGT_CHECK_LAUNCH();
     return NGT_OK;
 }
@@ -407,13 +412,13 @@ template <bool TRANS>
 int launch_row_gemm(int64_t M, int K, int N, const float *A, const float *W, const float *bias, float *C,
                     cudaStream_t st) {
     // 8-row slots per CTA: spread M over one CTA per SM (col_tiles CTAs share a row range), at
-    // most kMaxSlots (then CTAs loop over row tiles)
+    // most kMaxTR rows per lane (then CTAs loop over row tiles)
     const int col_tiles = (N + kTileN - 1) / kTileN;
     int64_t ctas = sm_count() / col_tiles;
     if (ctas < 1) ctas = 1;
     const int64_t per_cta = (M + ctas - 1) / ctas;
-    int tr = (int)((per_cta + 15) / 16);     // 16-row pairs of slots per CTA
-    tr = tr < 1 ? 1 : tr > kMaxSlots / 2 ? kMaxSlots / 2 : tr;
+    int tr = (int)((per_cta + 8 * kHalves - 1) / (8 * kHalves));     // rows per lane
+    tr = tr < 1 ? 1 : tr > kMaxTR ? kMaxTR : tr;
     switch (tr) {
     case 1: return launch_row_gemm_t<1, TRANS>(M, K, N, A, W, bias, C, st);
     case 2: return launch_row_gemm_t<2, TRANS>(M, K, N, A, W, bias, C, st);
