@@ -59,6 +59,9 @@ def parse_args():
     p.add_argument("--skip-epoch", action="store_true")
     p.add_argument("--skip-dense", action="store_true")
     p.add_argument("--skip-cpu", action="store_true")
+    p.add_argument("--epoch-kernels", action="store_true",
+                   help="print the per-kernel device time of one graph-replayed config-2 GT epoch "
+                        "(torch.profiler over CUPTI) instead of the JSON line")
     return p.parse_args()
 
 
@@ -641,8 +644,46 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def epoch_kernel_table(args):
+    """Kernel composition of one graph-replayed GT epoch (one GPU)."""
+    from torch.profiler import ProfilerActivity, profile
+    from neutrongt_b200 import synthetic
+    from neutrongt_b200.train import GraphedWindowTrainer, build_window_state
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    n = 169343
+    rowptr, col = config2_graph()
+    feature = synthetic.node_features(n, 128, seed=1).to(dev)
+    y = synthetic.node_labels(n, 40, seed=2).to(dev)
+    split = synthetic.split_idx(n, seed=3)
+    parts = synthetic.random_partitions(n, 16, seed=0)
+    ws = build_window_state(rowptr, col, parts, 0, 1, feature, dev, split)
+    model = gt_model(dev)
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-4, weight_decay=0.01, fused=True, capturable=True)
+    trainer = GraphedWindowTrainer(SimpleNamespace(use_cache=1, attn_type="sparse"), model, ws, feature, y, opt, 1,
+                                   dev, split_idx=split)
+    for _ in range(max(3, args.warmup)):
+        trainer.run_epoch()
+    t = trainer.run_epoch()[2]
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        trainer.run_epoch()
+        torch.cuda.synchronize()
+    rows = [(e.key, e.self_device_time_total, e.count) for e in prof.key_averages() if e.self_device_time_total > 0]
+    rows.sort(key=lambda r: -r[1])
+    total = sum(r[1] for r in rows)
+    print(f"graph-replayed epoch: {t * 1e3:.2f} ms (CUDA events); kernels {total / 1e3:.2f} ms")
+    print(f"{'us':>10} {'share':>7} {'calls':>6}  kernel")
+    for key, us, cnt in rows:
+        print(f"{us:10.1f} {100 * us / total:6.2f}% {cnt:6d}  {key[:110]}")
+    trainer.graphs.clear()
+    trainer.dummy = None
+
+
 def main():
     args = parse_args()
+    if args.epoch_kernels:
+        epoch_kernel_table(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:
