@@ -560,6 +560,8 @@ def bench_ppr(args, rank, world, dev):
                        "alpha 0.15, 20 iterations, top-k 8 per iteration and at the end",
            "seeds_per_s": n / t, "seconds": t, "entries": int(allreduce_sum(float(ei.shape[1]), world)),
            "scaling": "strong (seeds split into contiguous source ranges per rank)"}
+    if rank == 0 and world == 1:
+        out["window_build"] = bench_window_build(args, dev, ei, val)
     if rank == 0 and not args.skip_cpu:
         from oracle import ppr as oppr
         threads = os.cpu_count() or 1
@@ -575,6 +577,56 @@ def bench_ppr(args, rank, world, dev):
         touched = st["edges_touched"] / sample
         out["adjacency_entries_per_seed"] = touched
         out["achieved_gbs_adjacency_model"] = touched * n * 4 / t / 1e9
+    return out
+
+
+def bench_window_build(args, dev, ppr_ei, ppr_val, pct=5):
+    """SURVEY next-row 1/2 on the config-2 PPR output: the weighted PPR adjacency
+    (build_adj_fromat), the halo merge of each of the 16 windows at the reference scripts'
+    --related_nodes_topk_rate 5, and the duplicate-first order of the grown windows (two parents
+    of 8).  Windows are the seeded random partitions (pymetis is absent).  Rank-0 preprocessing in
+    the reference; measured at N = 1."""
+    from neutrongt_b200 import synthetic
+    from neutrongt_b200.window import build_adj_format, find_duplicate_nodes_and_rerange, merge_related_nodes
+    n = 169343
+    parts = synthetic.random_partitions(n, 16, seed=0)
+
+    def run():
+        csr, ew, _ = build_adj_format((ppr_ei, ppr_val), device=dev)
+        halos = [merge_related_nodes(p, csr, ew, pct, device=dev) for p in parts]
+        groups, dups = find_duplicate_nodes_and_rerange([halos[:8], halos[8:]])
+        return csr, ew, halos, dups
+
+    run()
+    torch.cuda.synchronize()
+    e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    e0.record()
+    csr, ew, _ = build_adj_format((ppr_ei, ppr_val), device=dev)
+    e1.record()
+    halos = [merge_related_nodes(p, csr, ew, pct, device=dev) for p in parts]
+    _, dups = find_duplicate_nodes_and_rerange([halos[:8], halos[8:]])
+    e2.record()
+    e2.synchronize()
+    t_adj, t_win = e0.elapsed_time(e1) / 1e3, e1.elapsed_time(e2) / 1e3
+    out = {"ppr_entries": int(ppr_ei.shape[1]), "undirected_pairs": int(csr.adjacent.numel()) // 2,
+           "adjacency_s": t_adj, "halo_and_dup_order_s": t_win, "topk_percent": pct,
+           "window_nodes_after_halo_mean": sum(int(h.numel()) for h in halos) / len(halos),
+           "duplicated_nodes": sum(int(d.numel()) for d in dups),
+           "note": "host reads of output sizes included; CUDA events on the launching stream"}
+    if not args.skip_cpu:
+        from oracle import window as ow
+        m_s = min(200000, int(ppr_ei.shape[1]))
+        ei_c, v_c = ppr_ei[:, :m_s].cpu().numpy(), ppr_val[:m_s].cpu().numpy()
+        t0 = time.perf_counter()
+        ow.ppr_adjacency(ei_c, v_c)
+        t_a = (time.perf_counter() - t0) * int(ppr_ei.shape[1]) / m_s
+        x, a, e = (t.cpu().numpy() for t in (csr.adj_starts, csr.adjacent, ew))
+        t0 = time.perf_counter()
+        ow.merge_related_nodes(parts[0], x, a, e, pct)
+        t_h = (time.perf_counter() - t0) * len(parts)
+        out["cpu_baseline"] = {"value": t_a + t_h, "unit": "s (adjacency + 16 halo merges)", "cores": 1,
+                               "kind": "port", "sample": f"adjacency over the first {m_s} PPR entries scaled to all, "
+                                                         "one window's halo merge x 16 (oracle/window.py)"}
     return out
 
 

@@ -316,6 +316,49 @@ NGT_API int ngt_linear_backward_weight(int64_t rows, int in_features, int out_fe
                                        const float *dy, float *dweight, float *dbias, void *workspace,
                                        size_t workspace_bytes, ngt_stream_t stream);
 
+/* ----------------------------------------------------------------------------------
+ * Window construction between PPR and the training windows.
+ *
+ * ngt_ppr_adjacency replaces build_adj_fromat (NeutronGT/core/ppr_preprocess.py:30-71): the PPR
+ * list edge_index int64 [2, m] (row 0 seed, row 1 neighbour) with values fp32 [m] becomes the
+ * symmetric weighted adjacency of n nodes (n = max index + 1 in the reference): each undirected
+ * pair {u, v} once, weight int32(max(sum of its PPR values * 1000, 1)) with the values added in
+ * entry order; xadj int32 [n+1], adjncy / eweights int32 [2m] capacity (2U used).  Rows list the
+ * pairs with u < v first, then u > v, each in key order: the stable form of the reference's
+ * argsort (which does not promise an order inside a row).  info int32 [2] (device): out-of-range
+ * entries, U.
+ *
+ * ngt_halo_degree + ngt_halo_merge replace _merge_related_nodes
+ * (NeutronGT/core/metisPartition.py:397-425): the window part int64 [p] (any order) gets the
+ * topk_percent % (rounded down) of its distinct external neighbours with the largest summed edge
+ * weight, ties in first-encounter order (window order, then CSR order); the result is sorted.
+ * ngt_halo_degree writes the window's summed degree `total` (device int64) that sizes the merge:
+ * workspace from ngt_halo_merge_workspace_size(n, p, total) (ngt_halo_degree needs the size for
+ * total = 0); out int64 [p + total] capacity; counts int64 [3] (device): merged size, selected,
+ * distinct external neighbours.
+ *
+ * ngt_duplicate_rerange replaces _find_duplicate_nodes_and_rerange
+ * (NeutronGT/core/metisPartition.py:333-363; window_state.py:52-73 for a rank's windows): nodes
+ * that occur in two or more of the `parts` windows (nodes int64, window k at
+ * [offsets[k], offsets[k+1])) move to the front of every window that holds them, both groups in
+ * window order; dup_counts int64 [parts] (device) = the length of each front group.  bad int32
+ * (device): node ids outside [0, n).
+ * ---------------------------------------------------------------------------------- */
+NGT_API int ngt_ppr_adjacency_workspace_size(int64_t m, int64_t n, size_t *bytes /* host */);
+NGT_API int ngt_ppr_adjacency(int64_t m, int64_t n, const int64_t *edge_index, const float *values, int32_t *xadj,
+                              int32_t *adjncy, int32_t *eweights, int32_t *info, void *workspace,
+                              size_t workspace_bytes, ngt_stream_t stream);
+NGT_API int ngt_halo_degree(int64_t n, const int32_t *xadj, int64_t p, const int64_t *part, int64_t *total,
+                            void *workspace, size_t workspace_bytes, ngt_stream_t stream);
+NGT_API int ngt_halo_merge_workspace_size(int64_t n, int64_t p, int64_t total, size_t *bytes /* host */);
+NGT_API int ngt_halo_merge(int64_t n, const int32_t *xadj, const int32_t *adjncy, const int32_t *eweights,
+                           int64_t p, const int64_t *part, int64_t total, int32_t topk_percent, int64_t *out,
+                           int64_t *counts, void *workspace, size_t workspace_bytes, ngt_stream_t stream);
+NGT_API int ngt_duplicate_rerange_workspace_size(int64_t n, int64_t total, size_t *bytes /* host */);
+NGT_API int ngt_duplicate_rerange(int64_t n, int32_t parts, const int64_t *offsets, const int64_t *nodes,
+                                  int64_t total, int64_t *out_nodes, int64_t *dup_counts, int32_t *bad,
+                                  void *workspace, size_t workspace_bytes, ngt_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -49,6 +49,13 @@ SIGNATURES = {
     "ngt_ppr_workspace_size": [_i64, _i64, _i64, _i64, _sz_p],
     "ngt_ppr_appnp_topk": [_i64, _p, _p, _p, _p, _dbl, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _p,
                            _p, _p, _p, _p, ctypes.c_size_t, _p],
+    "ngt_ppr_adjacency_workspace_size": [_i64, _i64, _sz_p],
+    "ngt_ppr_adjacency": [_i64, _i64, _p, _p, _p, _p, _p, _p, _p, ctypes.c_size_t, _p],
+    "ngt_halo_degree": [_i64, _p, _i64, _p, _p, _p, ctypes.c_size_t, _p],
+    "ngt_halo_merge_workspace_size": [_i64, _i64, _i64, _sz_p],
+    "ngt_halo_merge": [_i64, _p, _p, _p, _i64, _p, _i64, _i32, _p, _p, _p, ctypes.c_size_t, _p],
+    "ngt_duplicate_rerange_workspace_size": [_i64, _i64, _sz_p],
+    "ngt_duplicate_rerange": [_i64, _i32, _p, _p, _i64, _p, _p, _p, _p, ctypes.c_size_t, _p],
     "ngt_rowops_workspace_size": [_i64, _i32, _sz_p],
     "ngt_layernorm_forward": [_i64, _i32, _p, _p, _p, ctypes.c_float, _p, _p, _p, _p],
     "ngt_layernorm_backward": [_i64, _i32, _p, _p, _p, _p, _p, _p, _p, _p, _p, ctypes.c_size_t, _p],

@@ -5,6 +5,8 @@
 #include "common.cuh"
 
 namespace ngt {
+// internal linkage: every translation unit that sorts gets its own copy of these kernels
+namespace {
 
 // ------------------------------------------------------------------------------------
 // exclusive scan: out[i] = sum_{j<i} in[i]   (in may equal out)
@@ -214,4 +216,5 @@ struct Carver {
     }
 };
 
+}  // namespace
 }  // namespace ngt

@@ -7,12 +7,35 @@
 * `compute_local_duplicate_nodes(local_partitions)` — `window_state.py:52-73`:
   nodes that occur in two or more of a rank's windows move to the front of every
   window (both groups keep their order); returns (reranged windows, dup nodes per window).
+  Computed by `ngt_duplicate_rerange` (`csrc/windows.cu`); results on the input's device.
+* `build_adj_format(sorted_ppr_matrix)` — `NeutronGT/core/ppr_preprocess.py:30-71`
+  (`build_adj_fromat`): the symmetric, integer-weighted PPR adjacency, by `ngt_ppr_adjacency`.
+  Returns (CSRAdjacency(adj_starts, adjacent), eweights, None) with int32 CUDA tensors where the
+  reference returns a pymetis CSRAdjacency of lists and a list.
+* `merge_related_nodes(partition, csr_adjacency, eweights, topk_percent)` —
+  `NeutronGT/core/metisPartition.py:397-425`: the window plus the topk_percent % of its external
+  neighbours with the largest summed edge weight, sorted (`ngt_halo_degree`, `ngt_halo_merge`).
+* `find_duplicate_nodes_and_rerange(child_partitions)` — `metisPartition.py:333-363` over the
+  nested [parent][child] window lists; returns (reranged child_partitions, dup nodes per window).
 """
 from __future__ import annotations
+
+from dataclasses import dataclass
 
 import torch
 
 from . import _lib
+
+
+@dataclass
+class CSRAdjacency:
+    """The fields of pymetis.CSRAdjacency that the window code reads, as int32 device tensors."""
+    adj_starts: torch.Tensor
+    adjacent: torch.Tensor
+
+
+def _cuda(device=None):
+    return torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
 
 
 def subgraph_from_csr(node_set, rowptr, col, device=None):
@@ -45,20 +68,111 @@ def subgraph_from_csr(node_set, rowptr, col, device=None):
     return out
 
 
+def duplicate_rerange(partitions, device=None):
+    """Duplicate-first order of a list of windows on the device: (reranged, dup nodes) per window,
+    as int64 tensors on `device` (default: the current CUDA device)."""
+    dev = _cuda(device)
+    parts = [torch.as_tensor(p, dtype=torch.long).reshape(-1) for p in partitions]
+    if not parts:
+        return [], []
+    lens = torch.tensor([p.numel() for p in parts], dtype=torch.long)
+    offsets = torch.zeros(len(parts) + 1, dtype=torch.long)
+    offsets[1:] = torch.cumsum(lens, 0)
+    total = int(offsets[-1])
+    nodes = torch.cat(parts).to(dev).contiguous() if total else torch.empty(0, dtype=torch.long, device=dev)
+    if total and int(nodes.min()) < 0:
+        raise ValueError("window node ids must be non-negative")
+    n = int(nodes.max()) + 1 if total else 0
+    L = _lib.lib()
+    ws = _lib.workspace(_lib.size_query(L.ngt_duplicate_rerange_workspace_size, n, total), dev)
+    out = torch.empty_like(nodes)
+    dup_counts = torch.empty(len(parts), dtype=torch.long, device=dev)
+    bad = torch.empty(1, dtype=torch.int32, device=dev)
+    off_d = offsets.to(dev)
+    _lib.check(L.ngt_duplicate_rerange(n, len(parts), _lib.ptr(off_d), _lib.ptr(nodes), total, _lib.ptr(out),
+                                       _lib.ptr(dup_counts), _lib.ptr(bad), _lib.ptr(ws), ws.numel(),
+                                       _lib.stream_of(nodes)), "ngt_duplicate_rerange")
+    nd = dup_counts.tolist()
+    reranged, dups = [], []
+    for k in range(len(parts)):
+        a, b = int(offsets[k]), int(offsets[k + 1])
+        reranged.append(out[a:b])
+        dups.append(out[a:a + nd[k]])
+    return reranged, dups
+
+
 def compute_local_duplicate_nodes(local_partitions):
     if not local_partitions:
         return [], []
-    parts = [p.to(torch.long) for p in local_partitions]
-    all_nodes = torch.cat(parts)
-    if all_nodes.numel() == 0:
-        return [p.clone() for p in parts], [p.new_empty(0) for p in parts]
-    uniq, counts = torch.unique(all_nodes, return_counts=True, sorted=True)
-    dup = uniq[counts >= 2]
-    if dup.numel() == 0:
-        return [p.clone() for p in parts], [p.new_empty(0) for p in parts]
-    reranged, dups = [], []
-    for p in parts:
-        m = torch.isin(p, dup)
-        reranged.append(torch.cat([p[m], p[~m]]))
-        dups.append(p[m])
-    return reranged, dups
+    src_dev = torch.as_tensor(local_partitions[0]).device
+    reranged, dups = duplicate_rerange(local_partitions)
+    return [r.to(src_dev) for r in reranged], [d.to(src_dev) for d in dups]
+
+
+def find_duplicate_nodes_and_rerange(child_partitions):
+    """`metisPartition.py:333-363`: duplicate-first order over every child window of every parent.
+    Returns (reranged child_partitions, dup nodes per window in flattened order); with no windows,
+    or no nodes at all, the input and an empty list, as the reference leaves them."""
+    flat = [p for group in child_partitions for p in group]
+    if not flat or sum(torch.as_tensor(p).numel() for p in flat) == 0:
+        return child_partitions, []
+    src_dev = torch.as_tensor(flat[0]).device
+    reranged, dups = duplicate_rerange(flat)
+    it = iter(reranged)
+    groups = [[next(it).to(src_dev) for _ in group] for group in child_partitions]
+    return groups, [d.to(src_dev) for d in dups]
+
+
+def build_adj_format(sorted_ppr_matrix, device=None):
+    edge_index, ppr_val = sorted_ppr_matrix
+    assert edge_index.shape[0] == 2
+    dev = _cuda(device)
+    if edge_index.numel() == 0:
+        return (CSRAdjacency(torch.zeros(1, dtype=torch.int32, device=dev), torch.empty(0, dtype=torch.int32, device=dev)),
+                torch.empty(0, dtype=torch.int32, device=dev), None)
+    if ppr_val.dtype != torch.float32:
+        raise TypeError(f"PPR values must be float32 (the PPR backends' output), got {ppr_val.dtype}")
+    ei = edge_index.to(device=dev, dtype=torch.long).contiguous()
+    val = ppr_val.to(dev).contiguous()
+    m = int(ei.shape[1])
+    n = int(ei.max()) + 1
+    L = _lib.lib()
+    ws = _lib.workspace(_lib.size_query(L.ngt_ppr_adjacency_workspace_size, m, n), dev)
+    i32 = dict(dtype=torch.int32, device=dev)
+    xadj = torch.empty(n + 1, **i32)
+    adjncy = torch.empty(2 * m, **i32)
+    eweights = torch.empty(2 * m, **i32)
+    info = torch.empty(2, **i32)
+    _lib.check(L.ngt_ppr_adjacency(m, n, _lib.ptr(ei), _lib.ptr(val), _lib.ptr(xadj), _lib.ptr(adjncy),
+                                   _lib.ptr(eweights), _lib.ptr(info), _lib.ptr(ws), ws.numel(), _lib.stream_of(ei)),
+               "ngt_ppr_adjacency")
+    bad, u = (int(x) for x in info.tolist())
+    if bad:
+        raise IndexError(f"PPR edge_index holds {bad} negative entries")
+    return CSRAdjacency(xadj, adjncy[:2 * u]), eweights[:2 * u], None
+
+
+def merge_related_nodes(partition, csr_adjacency, eweights, topk_percent, device=None):
+    dev = _cuda(device)
+    xadj = torch.as_tensor(csr_adjacency.adj_starts).to(device=dev, dtype=torch.int32).contiguous()
+    adjncy = torch.as_tensor(csr_adjacency.adjacent).to(device=dev, dtype=torch.int32).contiguous()
+    ew = torch.as_tensor(eweights).to(device=dev, dtype=torch.int32).contiguous()
+    part = torch.as_tensor(partition).to(device=dev, dtype=torch.long).reshape(-1).contiguous()
+    n, p = int(xadj.numel()) - 1, int(part.numel())
+    if p and (int(part.min()) < 0 or int(part.max()) >= n):
+        raise IndexError(f"window node ids must lie in [0, {n})")
+    pct = int(topk_percent)
+    L = _lib.lib()
+    st = _lib.stream_of(xadj)
+    total = torch.zeros(1, dtype=torch.long, device=dev)
+    ws0 = _lib.workspace(_lib.size_query(L.ngt_halo_merge_workspace_size, n, p, 0), dev)
+    _lib.check(L.ngt_halo_degree(n, _lib.ptr(xadj), p, _lib.ptr(part), _lib.ptr(total), _lib.ptr(ws0), ws0.numel(), st),
+               "ngt_halo_degree")
+    t = int(total.item())
+    ws = _lib.workspace(_lib.size_query(L.ngt_halo_merge_workspace_size, n, p, t), dev)
+    out = torch.empty(max(p + t, 1), dtype=torch.long, device=dev)
+    counts = torch.zeros(3, dtype=torch.long, device=dev)
+    _lib.check(L.ngt_halo_merge(n, _lib.ptr(xadj), _lib.ptr(adjncy), _lib.ptr(ew), p, _lib.ptr(part), t, pct,
+                                _lib.ptr(out), _lib.ptr(counts), _lib.ptr(ws), ws.numel(), st), "ngt_halo_merge")
+    merged = int(counts[0].item())
+    return out[:merged]

@@ -14,6 +14,16 @@
   in the window, in global edge order, relabelled to window positions.
 * `stable_csr` builds the destination-major (or source-major) CSR of an edge
   list with ties kept in edge order — the layout the attention kernels read.
+* `ppr_adjacency` follows `build_adj_fromat`, `NeutronGT/core/ppr_preprocess.py:30-71`:
+  undirected keys (min, max) of the PPR list, each key's values summed in entry order
+  (the reference's CPU scatter_add_) in float32, weight int32(max(sum * 1000, 1)); both
+  directions listed and ordered by row with a stable sort (the reference's argsort is not
+  stable, so it fixes no order inside a row; the oracle pins the stable one).
+* `merge_related_nodes` follows `_merge_related_nodes`, `NeutronGT/core/metisPartition.py:397-425`:
+  external neighbours of the window with their summed weights, ordered by weight (descending)
+  with ties in first-encounter order, the first len * percent // 100 added, result sorted.
+* `duplicate_rerange_nested` follows `_find_duplicate_nodes_and_rerange`,
+  `metisPartition.py:333-363`: `duplicate_first` over every child window of every parent.
 """
 from __future__ import annotations
 
@@ -77,3 +87,59 @@ def stable_csr(edge_index, n, by="dst"):
     rowptr = np.zeros(int(n) + 1, dtype=np.int64)
     np.cumsum(counts, out=rowptr[1:])
     return torch.from_numpy(rowptr), torch.from_numpy(other[order]), torch.from_numpy(order.astype(np.int64))
+
+
+def ppr_adjacency(edge_index, values):
+    """Returns (xadj int32 [n+1], adjncy int32 [2U], eweights int32 [2U]), n = max index + 1."""
+    ei = np.asarray(edge_index, dtype=np.int64)
+    val = np.asarray(values, dtype=np.float32)
+    if ei.size == 0:
+        return np.zeros(1, np.int32), np.zeros(0, np.int32), np.zeros(0, np.int32)
+    n = int(ei.max()) + 1
+    u = np.minimum(ei[0], ei[1])
+    v = np.maximum(ei[0], ei[1])
+    key = u * n + v
+    order = np.argsort(key, kind="stable")
+    uniq, first = np.unique(key[order], return_index=True)
+    bounds = list(first) + [len(order)]
+    sums = np.zeros(len(uniq), np.float32)
+    for s in range(len(uniq)):
+        acc = np.float32(0.0)
+        for t in order[bounds[s]:bounds[s + 1]]:
+            acc = np.float32(acc + val[t])
+        sums[s] = acc
+    w = np.maximum(sums * np.float32(1000.0), np.float32(1.0)).astype(np.int32)
+    uu, vv = uniq // n, uniq % n
+    rows = np.concatenate([uu, vv])
+    cols = np.concatenate([vv, uu])
+    ww = np.concatenate([w, w])
+    o = np.argsort(rows, kind="stable")
+    xadj = np.zeros(n + 1, np.int64)
+    xadj[1:] = np.cumsum(np.bincount(rows, minlength=n))
+    return xadj.astype(np.int32), cols[o].astype(np.int32), ww[o].astype(np.int32)
+
+
+def merge_related_nodes(partition, xadj, adjncy, eweights, topk_percent):
+    part = [int(x) for x in np.asarray(partition).reshape(-1)]
+    inside = set(part)
+    total, first = {}, {}
+    pos = 0
+    for x in part:
+        for j in range(int(xadj[x]), int(xadj[x + 1])):
+            nb = int(adjncy[j])
+            if nb not in inside:
+                total[nb] = total.get(nb, 0) + int(eweights[j])
+                first.setdefault(nb, pos)
+            pos += 1
+    ranked = sorted(total, key=lambda nb: (-total[nb], first[nb]))
+    k = len(ranked) * topk_percent // 100 if topk_percent > 0 else 0
+    return torch.tensor(sorted(inside | set(ranked[:k])), dtype=torch.long)
+
+
+def duplicate_rerange_nested(child_partitions):
+    flat = [p for group in child_partitions for p in group]
+    if not flat or sum(len(p) for p in flat) == 0:
+        return child_partitions, []
+    reranged, dups = duplicate_first(flat)
+    it = iter(reranged)
+    return [[next(it) for _ in group] for group in child_partitions], dups

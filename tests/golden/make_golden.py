@@ -20,6 +20,11 @@ with `reference_shims.install()` standing in for packages that are absent here
   `_build_transition_csr_values`, `_cusparse_spgemm_iteration`,
   `_segment_topk_from_csr`), with cuSPARSE's `csr_spgemm` replaced by a CPU
   SciPy SpGEMM in fp32.
+* window_build.pt – `build_adj_fromat` (`core/ppr_preprocess.py:30-71`) on a seeded
+  PPR-shaped list, then `weightMetis_keepParent._merge_related_nodes` and
+  `._find_duplicate_nodes_and_rerange` (`core/metisPartition.py:397-425, 333-363`) called on
+  a stand-in `self` that holds only the attributes those methods read (the class constructor
+  runs METIS, which is absent here).
 * gt_sw_step.pt / graphormer_step.pt – one training step (forward, NLL loss,
   backward) of the reference `GT_SW` and `Graphormer` modules with dropout 0,
   sparse attention, together with their initial state_dicts.
@@ -276,10 +281,62 @@ def _model_step(kind):
                               "config": {k: v for k, v in common.items() if k != "args"}})
 
 
+# --------------------------------------------------------------------------------------
+# window construction: PPR adjacency, halo merge, duplicate-first order
+# --------------------------------------------------------------------------------------
+
+def _ppr_like(n, k, seed):
+    """k neighbours per seed with PPR-like values: a few large, many tiny (weight 1 after the
+    x1000 truncation, so the halo ranking has ties), and some pairs listed in both directions."""
+    g = torch.Generator().manual_seed(seed)
+    src = torch.arange(n).repeat_interleave(k)
+    dst = torch.randint(0, n, (n * k,), generator=g)
+    vals = torch.rand(n * k, generator=g) ** 6 * 0.3
+    mirror = torch.randperm(n * k, generator=g)[: n * k // 5]
+    src = torch.cat([src, dst[mirror]])
+    dst = torch.cat([dst, src[mirror]])
+    vals = torch.cat([vals, torch.rand(mirror.numel(), generator=g) * 0.05]).to(torch.float32)
+    return torch.stack([src, dst]), vals
+
+
+def make_window_build():
+    from core.metisPartition import weightMetis_keepParent
+    from core.ppr_preprocess import build_adj_fromat
+
+    n = 600
+    ppr_ei, ppr_val = _ppr_like(n, 6, seed=21)
+    csr, eweights, _ = build_adj_fromat((ppr_ei, ppr_val))
+    g = torch.Generator().manual_seed(22)
+    perm = torch.randperm(n, generator=g)
+    windows = [torch.sort(c).values for c in torch.tensor_split(perm, 6)]
+    fake = SimpleNamespace(csr_adjacency=csr, eweights=eweights)
+    halos = {}
+    for pct in (0, 7, 30, 100):
+        halos[pct] = [weightMetis_keepParent._merge_related_nodes(fake, w, pct) for w in windows]
+    # duplicate-first order over the halo-grown windows (they overlap), grouped 3 + 3 by parent
+    child = [halos[30][:3], halos[30][3:]]
+    fake2 = SimpleNamespace(child_partitions=[list(grp) for grp in child])
+    dups = weightMetis_keepParent._find_duplicate_nodes_and_rerange(fake2)
+    _save("window_build.pt", {
+        "ppr_edge_index": ppr_ei, "ppr_val": ppr_val,
+        "xadj": torch.tensor(csr.adj_starts, dtype=torch.int32),
+        "adjncy": torch.tensor(csr.adjacent, dtype=torch.int32),
+        "eweights": torch.tensor(eweights, dtype=torch.int32),
+        "windows": windows, "halos": halos,
+        "child_partitions": child, "reranged": fake2.child_partitions, "dup_nodes": dups,
+    })
+
+
 if __name__ == "__main__":
+    # python tests/golden/make_golden.py [section ...]   (default: every section)
     torch.set_num_threads(1)
-    make_attention()
-    make_window()
-    make_appnp()
-    _model_step("gt_sw")
-    _model_step("graphormer")
+    sections = {
+        "attention": make_attention,
+        "window": make_window,
+        "appnp": make_appnp,
+        "gt_sw": lambda: _model_step("gt_sw"),
+        "graphormer": lambda: _model_step("graphormer"),
+        "window_build": make_window_build,
+    }
+    for name in (sys.argv[1:] or list(sections)):
+        sections[name]()

@@ -14,8 +14,10 @@ hot path calls:
 * `torch_geometric.utils.subgraph(subset, edge_index, relabel_nodes=True,
   num_nodes)` (PyG 2.4.0): keep edges with both ends in `subset`, in their
   original order, relabelled to the position of each node in `subset`.
-* `dgl`, `pymetis`, `torch_geometric.utils.ppr` are inert placeholders; nothing
-  on the paths exercised by the fixtures calls them.
+* `pymetis.CSRAdjacency(adj_starts, adjacent)`: the record pymetis builds from the
+  two CSR lists (`build_adj_fromat` constructs one); it keeps both lists as given.
+* `dgl`, the rest of `pymetis` (`part_graph`), `torch_geometric.utils.ppr` are inert
+  placeholders; nothing on the paths exercised by the fixtures calls them.
 """
 from __future__ import annotations
 
@@ -63,6 +65,12 @@ def _subgraph(subset, edge_index, edge_attr=None, relabel_nodes=False, num_nodes
     return out, attr
 
 
+class _CSRAdjacency:
+    def __init__(self, adj_starts, adjacent):
+        self.adj_starts = adj_starts
+        self.adjacent = adjacent
+
+
 def _inert(name):
     mod = types.ModuleType(name)
 
@@ -95,6 +103,9 @@ def install():
     for name in ("dgl", "pymetis"):
         if name not in sys.modules:
             sys.modules[name] = _inert(name)
+    pm = sys.modules["pymetis"]
+    if not isinstance(getattr(pm, "__dict__", {}).get("CSRAdjacency"), type):
+        pm.CSRAdjacency = _CSRAdjacency
     if REFERENCE_ROOT not in sys.path:
         sys.path.insert(0, REFERENCE_ROOT)
     import utils.logger as ref_logger  # noqa: E402  (reference module)
