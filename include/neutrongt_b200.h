@@ -359,6 +359,29 @@ NGT_API int ngt_duplicate_rerange(int64_t n, int32_t parts, const int64_t *offse
                                   int64_t total, int64_t *out_nodes, int64_t *dup_counts, int32_t *bad,
                                   void *workspace, size_t workspace_bytes, ngt_stream_t stream);
 
+/* ----------------------------------------------------------------------------------
+ * Random connections of isolated nodes: replaces add_isolated_connections
+ * (NeutronGT/core/ppr_preprocess.py:94-132).  Nodes of [0, n) that appear in neither edge list
+ * (isolated, ascending) are linked to each appearing node (ascending) with probability
+ * connect_prob; new edges (isolated, appearing) in row-major order of that pair grid, as
+ * torch.where on the reference's dense mask gives them.  The reference draws the mask with
+ * torch.rand on an [isolated x appearing] tensor; here each pair's draw is a counter-based
+ * SplitMix64 hash of (seed, isolated index, appearing index), computed twice (count, fill) and
+ * never stored: same distribution, not the same bits.
+ *   count: counts int64 [3] (device) = isolated, appearing, new edges; bad int32 (device) =
+ *          entries outside [0, n)
+ *   fill:  new_edge_index int64 [2, e_new], e_new = counts[2]; same workspace, untouched between
+ *          the two calls
+ * ---------------------------------------------------------------------------------- */
+NGT_API int ngt_isolated_connections_workspace_size(int64_t n, size_t *bytes /* host */);
+NGT_API int ngt_isolated_connections_count(int64_t n, int64_t m_ppr, const int64_t *ppr_edge_index, int64_t m_graph,
+                                           const int64_t *graph_edge_index, double connect_prob, uint64_t seed,
+                                           int64_t *counts, int32_t *bad, void *workspace, size_t workspace_bytes,
+                                           ngt_stream_t stream);
+NGT_API int ngt_isolated_connections_fill(int64_t n, double connect_prob, uint64_t seed, const int64_t *counts,
+                                          int64_t e_new, int64_t *new_edge_index, void *workspace,
+                                          size_t workspace_bytes, ngt_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -56,6 +56,10 @@ SIGNATURES = {
     "ngt_halo_merge": [_i64, _p, _p, _p, _i64, _p, _i64, _i32, _p, _p, _p, ctypes.c_size_t, _p],
     "ngt_duplicate_rerange_workspace_size": [_i64, _i64, _sz_p],
     "ngt_duplicate_rerange": [_i64, _i32, _p, _p, _i64, _p, _p, _p, _p, ctypes.c_size_t, _p],
+    "ngt_isolated_connections_workspace_size": [_i64, _sz_p],
+    "ngt_isolated_connections_count": [_i64, _i64, _p, _i64, _p, _dbl, ctypes.c_uint64, _p, _p, _p, ctypes.c_size_t,
+                                       _p],
+    "ngt_isolated_connections_fill": [_i64, _dbl, ctypes.c_uint64, _p, _i64, _p, _p, ctypes.c_size_t, _p],
     "ngt_rowops_workspace_size": [_i64, _i32, _sz_p],
     "ngt_layernorm_forward": [_i64, _i32, _p, _p, _p, ctypes.c_float, _p, _p, _p, _p],
     "ngt_layernorm_backward": [_i64, _i32, _p, _p, _p, _p, _p, _p, _p, _p, _p, ctypes.c_size_t, _p],

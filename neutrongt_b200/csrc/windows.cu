@@ -6,6 +6,9 @@
 //   ngt_duplicate_rerange  windows reordered duplicate-nodes-first for the K/V cache
 //                          (NeutronGT/core/metisPartition.py:333-363 and
 //                          core/node_level_pipeline/window_state.py:52-73)
+//   ngt_isolated_connections_*  random links from nodes that appear in neither the PPR list nor
+//                          the graph to the nodes that do (NeutronGT/core/ppr_preprocess.py:94-132,
+//                          add_isolated_connections), without the dense [isolated x others] draw
 //
 // The reference does these in host Python (dict / set loops, torch.unique on the CPU).  Here
 // each is a handful of device passes: stable LSD radix sorts (scan_sort.cuh) stand in for the
@@ -333,6 +336,123 @@ __global__ void dup_place_kernel(int64_t total, int parts, const int64_t *__rest
     out[ok + at] = nodes[i];
 }
 
+// ---------------------------------------------------------------------------------------------
+// random connections of isolated nodes
+// ---------------------------------------------------------------------------------------------
+// SplitMix64 finaliser (Steele, Lea & Flood, "Fast splittable pseudorandom number generators",
+// OOPSLA 2014): a counter-based generator, so pair (a, b) gets the same draw on any thread.
+__host__ __device__ inline uint64_t splitmix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+// Bernoulli draw of pair (isolated index a, other index b): top 32 bits of the hash below the
+// threshold floor(p * 2^32).
+__device__ __forceinline__ bool connect_draw(uint64_t seed, int64_t a, int64_t b, uint64_t threshold) {
+    const uint64_t h = splitmix64(seed ^ splitmix64(((uint64_t)a << 32) ^ (uint64_t)b));
+    return (h >> 32) < threshold;
+}
+
+__global__ void iso_mark_kernel(int64_t m, const int64_t *__restrict__ ei, int64_t n, int32_t *__restrict__ seen,
+                                int32_t *__restrict__ bad) {
+    const int64_t i = (int64_t)blockIdx.x * kT + threadIdx.x;
+    if (i >= 2 * m) return;
+    const int64_t x = ei[i];
+    if (x < 0 || x >= n) {
+        atomicAdd(bad, 1);
+        return;
+    }
+    seen[x] = 1;
+}
+
+__global__ void iso_flags_kernel(int64_t n, const int32_t *__restrict__ seen, int64_t *__restrict__ iso,
+                                 int64_t *__restrict__ non) {
+    const int64_t i = (int64_t)blockIdx.x * kT + threadIdx.x;
+    if (i > n) return;
+    iso[i] = (i < n && !seen[i]) ? 1 : 0;
+    non[i] = (i < n && seen[i]) ? 1 : 0;
+}
+
+// ascending lists of isolated and of appeared nodes (torch.arange(n)[mask] order)
+__global__ void iso_compact_kernel(int64_t n, const int32_t *__restrict__ seen, const int64_t *__restrict__ iso_pos,
+                                   const int64_t *__restrict__ non_pos, int64_t *__restrict__ iso_list,
+                                   int64_t *__restrict__ non_list, int64_t *__restrict__ counts) {
+    const int64_t i = (int64_t)blockIdx.x * kT + threadIdx.x;
+    if (i == 0) {
+        counts[0] = iso_pos[n];
+        counts[1] = non_pos[n];
+    }
+    if (i >= n) return;
+    if (seen[i]) non_list[non_pos[i]] = i;
+    else iso_list[iso_pos[i]] = i;
+}
+
+// one block per isolated node a: how many of the appeared nodes it connects to
+__global__ void __launch_bounds__(kT) iso_row_count_kernel(const int64_t *__restrict__ counts, uint64_t seed,
+                                                           uint64_t threshold, int64_t *__restrict__ rowcnt) {
+    const int64_t ni = counts[0], nn = counts[1];
+    __shared__ int64_t part[kT / 32];
+    for (int64_t a = blockIdx.x; a < ni; a += gridDim.x) {
+        int64_t c = 0;
+        for (int64_t b = threadIdx.x; b < nn; b += kT) c += connect_draw(seed, a, b, threshold) ? 1 : 0;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+        if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = c;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            int64_t t = 0;
+            for (int w = 0; w < kT / 32; w++) t += part[w];
+            rowcnt[a] = t;
+        }
+        __syncthreads();
+    }
+}
+
+__global__ void iso_total_kernel(const int64_t *__restrict__ rowcnt, const int64_t *__restrict__ rowoff,
+                                 int64_t *__restrict__ counts) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) {
+        const int64_t ni = counts[0];
+        counts[2] = ni > 0 ? rowoff[ni - 1] + rowcnt[ni - 1] : 0;
+    }
+}
+
+// row a's pairs in column order (torch.where order on the dense mask)
+__global__ void __launch_bounds__(kT) iso_fill_kernel(const int64_t *__restrict__ counts, uint64_t seed,
+                                                      uint64_t threshold, const int64_t *__restrict__ rowoff,
+                                                      const int64_t *__restrict__ iso_list,
+                                                      const int64_t *__restrict__ non_list, int64_t e_new,
+                                                      int64_t *__restrict__ out) {
+    const int64_t ni = counts[0], nn = counts[1];
+    __shared__ int wsum[kT / 32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int64_t a = blockIdx.x; a < ni; a += gridDim.x) {
+        int64_t base = rowoff[a];
+        for (int64_t b0 = 0; b0 < nn; b0 += kT) {
+            const int64_t b = b0 + threadIdx.x;
+            const bool hit = b < nn && connect_draw(seed, a, b, threshold);
+            const uint32_t bal = __ballot_sync(0xffffffffu, hit);
+            if (lane == 0) wsum[warp] = __popc(bal);
+            __syncthreads();
+            int before = 0, all = 0;
+            for (int w = 0; w < kT / 32; w++) {
+                if (w < warp) before += wsum[w];
+                all += wsum[w];
+            }
+            if (hit) {
+                const int64_t at = base + before + __popc(bal & ((1u << lane) - 1u));
+                if (at < e_new) {
+                    out[at] = iso_list[a];
+                    out[e_new + at] = non_list[b];
+                }
+            }
+            base += all;
+            __syncthreads();
+        }
+    }
+}
+
 }  // namespace
 }  // namespace ngt
 
@@ -533,6 +653,92 @@ extern "C" int ngt_duplicate_rerange(int64_t n, int32_t parts, const int64_t *of
     if (rc) return rc;
     const int64_t g = total > parts ? total : parts;
     dup_place_kernel<<<grid_for(g), kT, 0, st>>>(total, parts, offsets, nodes, flag, fs, out_nodes, dup_counts);
+    NGT_CHECK_LAUNCH();
+    return NGT_OK;
+}
+
+// ---------------------------------------------------------------------------------------------
+namespace {
+struct IsoWs {
+    int32_t *seen, *bad;
+    int64_t *iso, *non, *iso_pos, *non_pos, *partials, *iso_list, *non_list, *rowcnt, *rowoff, *row_partials;
+};
+IsoWs carve_iso(void *base, size_t cap, int64_t n, size_t *used) {
+    Carver c(base, cap);
+    IsoWs w;
+    w.seen = c.take<int32_t>(n + 1);
+    w.bad = c.take<int32_t>(1);
+    w.iso = c.take<int64_t>(n + 1);
+    w.non = c.take<int64_t>(n + 1);
+    w.iso_pos = c.take<int64_t>(n + 1);
+    w.non_pos = c.take<int64_t>(n + 1);
+    w.partials = c.take<int64_t>(scan_partials_count(n + 1) + 1);
+    w.iso_list = c.take<int64_t>(n + 1);
+    w.non_list = c.take<int64_t>(n + 1);
+    w.rowcnt = c.take<int64_t>(n + 1);
+    w.rowoff = c.take<int64_t>(n + 1);
+    w.row_partials = c.take<int64_t>(scan_partials_count(n + 1) + 1);
+    *used = c.used;
+    return w;
+}
+uint64_t prob_threshold(double p) {
+    if (!(p > 0.0)) return 0;
+    if (p >= 1.0) return (uint64_t)1 << 32;
+    return (uint64_t)(p * 4294967296.0);
+}
+}  // namespace
+
+extern "C" int ngt_isolated_connections_workspace_size(int64_t n, size_t *bytes) {
+    if (!bytes || n < 0) return NGT_ERR_INVALID_ARGUMENT;
+    carve_iso(nullptr, 0, n, bytes);
+    return NGT_OK;
+}
+
+extern "C" int ngt_isolated_connections_count(int64_t n, int64_t m_ppr, const int64_t *ppr_edge_index,
+                                              int64_t m_graph, const int64_t *graph_edge_index, double connect_prob,
+                                              uint64_t seed, int64_t *counts, int32_t *bad, void *workspace,
+                                              size_t workspace_bytes, ngt_stream_t stream) {
+    if (n < 0 || m_ppr < 0 || m_graph < 0 || !counts || !bad) return NGT_ERR_INVALID_ARGUMENT;
+    if ((m_ppr > 0 && !ppr_edge_index) || (m_graph > 0 && !graph_edge_index)) return NGT_ERR_INVALID_ARGUMENT;
+    size_t need = 0;
+    IsoWs w = carve_iso(workspace, workspace_bytes, n, &need);
+    if (!workspace || workspace_bytes < need) return NGT_ERR_WORKSPACE;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    cudaMemsetAsync(counts, 0, 3 * sizeof(int64_t), st);
+    cudaMemsetAsync(bad, 0, sizeof(int32_t), st);
+    cudaMemsetAsync(w.seen, 0, sizeof(int32_t) * (size_t)(n + 1), st);
+    if (m_ppr > 0) iso_mark_kernel<<<grid_for(2 * m_ppr), kT, 0, st>>>(m_ppr, ppr_edge_index, n, w.seen, bad);
+    if (m_graph > 0) iso_mark_kernel<<<grid_for(2 * m_graph), kT, 0, st>>>(m_graph, graph_edge_index, n, w.seen, bad);
+    iso_flags_kernel<<<grid_for(n + 1), kT, 0, st>>>(n, w.seen, w.iso, w.non);
+    int rc = exclusive_scan<int64_t>(w.iso, w.iso_pos, n + 1, w.partials, st);
+    if (rc) return rc;
+    rc = exclusive_scan<int64_t>(w.non, w.non_pos, n + 1, w.partials, st);
+    if (rc) return rc;
+    iso_compact_kernel<<<grid_for(n > 0 ? n : 1), kT, 0, st>>>(n, w.seen, w.iso_pos, w.non_pos, w.iso_list, w.non_list,
+                                                              counts);
+    const uint64_t thr = prob_threshold(connect_prob);
+    if (n > 0) {
+        cudaMemsetAsync(w.rowcnt, 0, sizeof(int64_t) * (size_t)(n + 1), st);
+        iso_row_count_kernel<<<1184, kT, 0, st>>>(counts, seed, thr, w.rowcnt);
+        rc = exclusive_scan<int64_t>(w.rowcnt, w.rowoff, n + 1, w.row_partials, st);
+        if (rc) return rc;
+        iso_total_kernel<<<1, 32, 0, st>>>(w.rowcnt, w.rowoff, counts);
+    }
+    NGT_CHECK_LAUNCH();
+    return NGT_OK;
+}
+
+extern "C" int ngt_isolated_connections_fill(int64_t n, double connect_prob, uint64_t seed, const int64_t *counts,
+                                             int64_t e_new, int64_t *new_edge_index, void *workspace,
+                                             size_t workspace_bytes, ngt_stream_t stream) {
+    if (n < 0 || e_new < 0 || !counts || (e_new > 0 && !new_edge_index)) return NGT_ERR_INVALID_ARGUMENT;
+    size_t need = 0;
+    IsoWs w = carve_iso(workspace, workspace_bytes, n, &need);
+    if (!workspace || workspace_bytes < need) return NGT_ERR_WORKSPACE;
+    if (e_new == 0 || n == 0) return NGT_OK;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    iso_fill_kernel<<<1184, kT, 0, st>>>(counts, seed, prob_threshold(connect_prob), w.rowoff, w.iso_list, w.non_list,
+                                         e_new, new_edge_index);
     NGT_CHECK_LAUNCH();
     return NGT_OK;
 }

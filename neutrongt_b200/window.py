@@ -17,6 +17,10 @@
   neighbours with the largest summed edge weight, sorted (`ngt_halo_degree`, `ngt_halo_merge`).
 * `find_duplicate_nodes_and_rerange(child_partitions)` — `metisPartition.py:333-363` over the
   nested [parent][child] window lists; returns (reranged child_partitions, dup nodes per window).
+* `add_isolated_connections(ppr_result, original_edge_index, num_nodes, connect_prob,
+  ppr_fill_value, device, seed)` — `NeutronGT/core/ppr_preprocess.py:94-132`: random links from
+  isolated nodes to appearing ones, by `ngt_isolated_connections_count/_fill`, with a seeded
+  counter-based draw per pair instead of a dense torch.rand matrix.
 """
 from __future__ import annotations
 
@@ -176,3 +180,39 @@ def merge_related_nodes(partition, csr_adjacency, eweights, topk_percent, device
                                 _lib.ptr(out), _lib.ptr(counts), _lib.ptr(ws), ws.numel(), st), "ngt_halo_merge")
     merged = int(counts[0].item())
     return out[:merged]
+
+
+def add_isolated_connections(ppr_result, original_edge_index, num_nodes, connect_prob=0.01, ppr_fill_value=0.001,
+                             device="cuda", seed=0):
+    edge_index, edge_values = ppr_result
+    dev = torch.device(device)
+    if dev.type != "cuda":
+        raise RuntimeError("add_isolated_connections runs on CUDA devices (there is no CPU path)")
+    if dev.index is None:
+        dev = _cuda()
+    edge_index = edge_index.to(dev)
+    edge_values = edge_values.to(dev)
+    ppr = edge_index.to(torch.long).contiguous()
+    orig = original_edge_index.to(device=dev, dtype=torch.long).contiguous()
+    n = int(num_nodes)
+    L = _lib.lib()
+    ws = _lib.workspace(_lib.size_query(L.ngt_isolated_connections_workspace_size, n), dev)
+    counts = torch.zeros(3, dtype=torch.long, device=dev)
+    bad = torch.zeros(1, dtype=torch.int32, device=dev)
+    st = _lib.stream_of(ppr)
+    seed64 = int(seed) & 0xFFFFFFFFFFFFFFFF
+    _lib.check(L.ngt_isolated_connections_count(n, int(ppr.shape[1]), _lib.ptr(ppr), int(orig.shape[1]),
+                                                _lib.ptr(orig), float(connect_prob), seed64, _lib.ptr(counts),
+                                                _lib.ptr(bad), _lib.ptr(ws), ws.numel(), st),
+               "ngt_isolated_connections_count")
+    n_iso, n_app, e_new = (int(x) for x in counts.tolist())
+    if int(bad.item()):
+        raise IndexError(f"edge lists hold node ids outside [0, {n})")
+    if n_iso == 0 or n_app == 0 or e_new == 0:
+        return edge_index, edge_values
+    new_edges = torch.empty((2, e_new), dtype=torch.long, device=dev)
+    _lib.check(L.ngt_isolated_connections_fill(n, float(connect_prob), seed64, _lib.ptr(counts), e_new,
+                                               _lib.ptr(new_edges), _lib.ptr(ws), ws.numel(), st),
+               "ngt_isolated_connections_fill")
+    new_values = torch.full((e_new,), ppr_fill_value, device=dev, dtype=edge_values.dtype)
+    return torch.cat([edge_index, new_edges.to(edge_index.dtype)], dim=1), torch.cat([edge_values, new_values], dim=0)

@@ -24,6 +24,9 @@
   with ties in first-encounter order, the first len * percent // 100 added, result sorted.
 * `duplicate_rerange_nested` follows `_find_duplicate_nodes_and_rerange`,
   `metisPartition.py:333-363`: `duplicate_first` over every child window of every parent.
+* `isolated_connections` follows `add_isolated_connections`, `NeutronGT/core/ppr_preprocess.py:94-132`,
+  with the reference's dense torch.rand mask replaced by the per-pair SplitMix64 draw the device
+  uses (Steele, Lea & Flood 2014), so its new edges are the device's exactly.
 """
 from __future__ import annotations
 
@@ -143,3 +146,37 @@ def duplicate_rerange_nested(child_partitions):
     reranged, dups = duplicate_first(flat)
     it = iter(reranged)
     return [[next(it) for _ in group] for group in child_partitions], dups
+
+
+_M64 = (1 << 64) - 1
+
+
+def splitmix64(z):
+    """Vectorised over uint64 arrays (wrap-around arithmetic)."""
+    z = np.asarray(z, dtype=np.uint64)
+    with np.errstate(over="ignore"):
+        z = z + np.uint64(0x9E3779B97F4A7C15)
+        z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+        z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+    return z ^ (z >> np.uint64(31))
+
+
+def isolated_connections(ppr_edge_index, graph_edge_index, num_nodes, connect_prob, seed):
+    """New edges [2, e_new] (int64): isolated nodes x appearing nodes, row-major, pair (a, b) kept
+    when the top 32 bits of splitmix64(seed ^ splitmix64(a << 32 ^ b)) < floor(p * 2^32)."""
+    seen = np.zeros(num_nodes, bool)
+    for ei in (ppr_edge_index, graph_edge_index):
+        ei = np.asarray(ei, dtype=np.int64).reshape(-1)
+        seen[ei] = True
+    iso = np.nonzero(~seen)[0]
+    app = np.nonzero(seen)[0]
+    if iso.size == 0 or app.size == 0:
+        return np.zeros((2, 0), np.int64)
+    thr = 0 if connect_prob <= 0 else (1 << 32 if connect_prob >= 1 else int(connect_prob * 4294967296.0))
+    a = np.arange(iso.size, dtype=np.uint64)[:, None]
+    b = np.arange(app.size, dtype=np.uint64)[None, :]
+    inner = splitmix64((a << np.uint64(32)) ^ b)
+    h = splitmix64(np.uint64(seed & _M64) ^ inner)
+    mask = (h >> np.uint64(32)) < np.uint64(min(thr, (1 << 64) - 1))
+    i, j = np.nonzero(mask)
+    return np.stack([iso[i], app[j]])

@@ -49,3 +49,19 @@ def test_oracle_edge_cases():
     assert ow.merge_related_nodes([0], x, a, e, 34).tolist() == [0, 3]     # 3 * 34 // 100 = 1
     assert ow.merge_related_nodes([0], x, a, e, 67).tolist() == [0, 1, 3]  # then node 1 (seen first)
     assert ow.merge_related_nodes([0, 1, 2, 3], x, a, e, 100).tolist() == [0, 1, 2, 3]
+
+
+def test_isolated_connections_oracle_properties():
+    # SplitMix64 published first outputs for state 0 and 1 (Steele, Lea & Flood 2014)
+    assert ow.splitmix64(np.array([0, 1], np.uint64)).tolist() == [0xE220A8397B1DCDAF, 0x910A2DEC89025CC1]
+    ppr = np.array([[0, 1, 5], [1, 2, 7]])
+    graph = np.array([[9], [10]])
+    e = ow.isolated_connections(ppr, graph, 3000, 0.02, seed=3)
+    iso = np.setdiff1d(np.arange(3000), [0, 1, 2, 5, 7, 9, 10])
+    assert np.all(np.isin(e[0], iso)) and np.all(np.isin(e[1], [0, 1, 2, 5, 7, 9, 10]))
+    order = e[0] * 3000 + e[1]
+    assert np.all(np.diff(order) > 0)                              # row-major, no repeats
+    expect = iso.size * 7 * 0.02
+    assert abs(e.shape[1] - expect) < 5 * np.sqrt(expect)          # Bernoulli(p) per pair
+    assert ow.isolated_connections(ppr, graph, 11, 0.5, seed=3).shape[1] > 0
+    assert ow.isolated_connections(np.array([[0], [1]]), np.zeros((2, 0), np.int64), 2, 1.0, 0).shape[1] == 0

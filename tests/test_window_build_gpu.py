@@ -97,3 +97,27 @@ def test_duplicate_rerange_reference_and_random(cuda):
     ref = ow.duplicate_first(parts)
     for a, b in zip(ours[0] + ours[1], ref[0] + ref[1]):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("n,p,seed", [(5000, 0.01, 1), (50000, 0.002, 2), (300, 1.0, 3), (300, 0.0, 4)])
+def test_isolated_connections_match_oracle(cuda, n, p, seed):
+    from neutrongt_b200.window import add_isolated_connections
+    g = torch.Generator().manual_seed(seed)
+    appear = torch.randperm(n, generator=g)[: n // 3]
+    ppr = torch.stack([appear[: n // 6], appear[n // 6: 2 * (n // 6)]])
+    graph = torch.stack([appear[:: 2][:50], appear[1:: 2][:50]])
+    vals = torch.rand(ppr.shape[1], generator=g)
+    ei, v = add_isolated_connections((ppr, vals), graph, n, connect_prob=p, ppr_fill_value=0.001, seed=seed)
+    ref = ow.isolated_connections(ppr.numpy(), graph.numpy(), n, p, seed)
+    m = ppr.shape[1]
+    assert torch.equal(ei[:, :m].cpu(), ppr) and torch.equal(v[:m].cpu(), vals)
+    assert np.array_equal(ei[:, m:].cpu().numpy(), ref)
+    assert torch.all(v[m:] == torch.tensor(0.001)) and v.dtype == vals.dtype
+
+
+def test_isolated_connections_none_isolated(cuda):
+    from neutrongt_b200.window import add_isolated_connections
+    ppr = torch.tensor([[0, 1], [1, 2]])
+    vals = torch.tensor([0.5, 0.25])
+    ei, v = add_isolated_connections((ppr, vals), torch.zeros((2, 0), dtype=torch.long), 3)
+    assert torch.equal(ei.cpu(), ppr) and torch.equal(v.cpu(), vals)
