@@ -17,11 +17,64 @@ graphormer_dist_node_level.py:179, 183, 286.
 """
 from __future__ import annotations
 
+import contextlib
+import threading
+
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
 from . import _lib
+
+# ---- weight gradients on a side stream -------------------------------------------------------
+# Inside `overlap_weight_grads()` a Linear layer's weight / bias gradient kernels run on a side
+# stream that forks from the backward's stream and joins it again when the backward pass ends
+# (an autograd end-of-backward callback), so they overlap the input-gradient chain of the layers
+# below.  Only valid when autograd hands the gradient to the parameter without reading it (the
+# parameter's .grad is None, as `optimizer.zero_grad(set_to_none=True)` leaves it); the training
+# loops enter it only then.
+# (Process-wide state: autograd runs CUDA backward functions on its own per-device threads.)
+class _State:
+    overlap = False
+    pending = None
+
+
+_state = _State()
+_side: dict = {}
+_lock = threading.Lock()
+
+
+@contextlib.contextmanager
+def overlap_weight_grads(enabled: bool = True):
+    with _lock:
+        prev = _state.overlap
+        _state.overlap = enabled
+    try:
+        yield
+    finally:
+        with _lock:
+            _state.overlap = prev
+
+
+def _side_stream(device) -> torch.cuda.Stream:
+    key = device.index
+    if key not in _side:
+        _side[key] = torch.cuda.Stream(device=device)
+    return _side[key]
+
+
+def _join_later(cur: torch.cuda.Stream, side: torch.cuda.Stream):
+    if _state.pending is None:
+        _state.pending = {}
+        torch.autograd.Variable._execution_engine.queue_callback(_join_all)
+    _state.pending[(cur, side)] = None
+
+
+def _join_all():
+    pending = _state.pending or {}
+    _state.pending = None
+    for cur, side in pending:
+        cur.wait_stream(side)
 
 
 def _rows_ok(x: torch.Tensor, cols: int) -> bool:
@@ -131,13 +184,24 @@ class _LinearFn(torch.autograd.Function):
                 dx = g2.mm(weight)
             dx = dx.view(ctx.shape)
         if ctx.needs_input_grad[1]:
-            dw = torch.empty(out_f, in_f, dtype=torch.float32, device=g2.device)
-            if ctx.needs_input_grad[2]:
-                db = torch.empty(out_f, dtype=torch.float32, device=g2.device)
-            ws = _linear_ws(rows, in_f, out_f, g2.device)
-            _lib.check(_lib.lib().ngt_linear_backward_weight(rows, in_f, out_f, _lib.ptr(x2), _lib.ptr(g2),
-                                                             _lib.ptr(dw), _lib.ptr(db), _lib.ptr(ws), ws.numel(),
-                                                             _lib.stream_of(g2)), "ngt_linear_backward_weight")
+            overlap = _state.overlap
+            cur = torch.cuda.current_stream(g2.device)
+            side = _side_stream(g2.device) if overlap else cur
+            if overlap:
+                side.wait_stream(cur)                  # x2 and g2 are ready
+            with torch.cuda.stream(side):
+                dw = torch.empty(out_f, in_f, dtype=torch.float32, device=g2.device)
+                if ctx.needs_input_grad[2]:
+                    db = torch.empty(out_f, dtype=torch.float32, device=g2.device)
+                ws = _linear_ws(rows, in_f, out_f, g2.device)
+                _lib.check(_lib.lib().ngt_linear_backward_weight(rows, in_f, out_f, _lib.ptr(x2), _lib.ptr(g2),
+                                                                 _lib.ptr(dw), _lib.ptr(db), _lib.ptr(ws),
+                                                                 ws.numel(), _lib.stream_of(g2)),
+                           "ngt_linear_backward_weight")
+            if overlap:
+                x2.record_stream(side)                 # freed on `cur` later: keep until side is done
+                g2.record_stream(side)
+                _join_later(cur, side)
         elif ctx.needs_input_grad[2]:
             db = column_sum(g2)
         return dx, dw, db

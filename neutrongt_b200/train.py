@@ -33,6 +33,7 @@ import torch
 import torch.distributed as dist
 import torch.nn.functional as F
 
+from .layers import overlap_weight_grads
 from .window import compute_local_duplicate_nodes, subgraph_from_csr
 
 
@@ -177,7 +178,8 @@ def train_epoch(args, model, local_partition_ids, local_partitions, feature, y, 
             m = mask.to(loss_all.dtype)
             loss = (loss_all * m).sum() / m.sum().clamp_min(1.0)
             losses.append(loss.detach())
-            loss.backward()
+            with overlap_weight_grads(world_size == 1):   # gradients are handed over, not added (set_to_none)
+                loss.backward()
         grads.average(world_size, group)
         optimizer.step()
     lr_scheduler.step()
@@ -265,7 +267,8 @@ class GraphedWindowTrainer:
             out, _, score_spe, _ = self.model(x, None, self.edges[i], None, None, None, None, attn_type=self.attn_type)
             loss_all = F.nll_loss(out, w["y"], reduction="none")
             loss = (loss_all * w["m"]).sum() / w["m"].sum().clamp_min(1.0)
-            loss.backward()
+            with overlap_weight_grads(self.world == 1):
+                loss.backward()
             scores = score_spe[-1]
         self.grads.average(self.world, self.group)
         self.opt.step()

@@ -87,3 +87,24 @@ def test_c_abi_without_bias_and_empty_rows(cuda):
     small = _lib.workspace(16, "cuda")
     assert lib.ngt_linear_backward_weight(333, 96, 20, _lib.ptr(x), _lib.ptr(dy), _lib.ptr(dw), None,
                                           _lib.ptr(small), 16, st) == 3
+
+
+def test_weight_grads_on_side_stream_match(cuda):
+    """overlap_weight_grads(): same gradients as the single-stream backward, bit for bit, and they
+    are complete when backward() returns (the side stream joined the backward's stream)."""
+    from neutrongt_b200.layers import Linear, overlap_weight_grads
+    torch.manual_seed(0)
+    net = torch.nn.Sequential(Linear(128, 256), torch.nn.ReLU(), Linear(256, 128), torch.nn.ReLU(),
+                              Linear(128, 64)).cuda()
+    x = torch.randn(10583, 128, device="cuda", requires_grad=True)
+    grads = []
+    for overlap in (False, True, True):
+        net.zero_grad(set_to_none=True)
+        x.grad = None
+        with overlap_weight_grads(overlap):
+            net(x).square().sum().backward()
+        g = [p.grad.clone() for p in net.parameters()] + [x.grad.clone()]   # read right away
+        grads.append(g)
+    for g in grads[1:]:
+        for a, b in zip(g, grads[0]):
+            assert torch.equal(a, b)
