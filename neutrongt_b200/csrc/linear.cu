@@ -59,15 +59,13 @@ __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-__device__ __forceinline__ void fma4(float (&acc)[8], float a, const float4 &b0, const float4 &b1) {
-    acc[0] = fmaf(a, b0.x, acc[0]);
-    acc[1] = fmaf(a, b0.y, acc[1]);
-    acc[2] = fmaf(a, b0.z, acc[2]);
-    acc[3] = fmaf(a, b0.w, acc[3]);
-    acc[4] = fmaf(a, b1.x, acc[4]);
-    acc[5] = fmaf(a, b1.y, acc[5]);
-    acc[6] = fmaf(a, b1.z, acc[6]);
-    acc[7] = fmaf(a, b1.w, acc[7]);
+// acc[0..3] (as pairs) += a * (b0, b1): packed f32x2 FMAs, each lane rounded like fmaf
+__device__ __forceinline__ void fma4x2(float2 (&acc)[4], float a, const float4 &b0, const float4 &b1) {
+    const float2 aa = make_float2(a, a);
+    acc[0] = __ffma2_rn(aa, make_float2(b0.x, b0.y), acc[0]);
+    acc[1] = __ffma2_rn(aa, make_float2(b0.z, b0.w), acc[1]);
+    acc[2] = __ffma2_rn(aa, make_float2(b1.x, b1.y), acc[2]);
+    acc[3] = __ffma2_rn(aa, make_float2(b1.z, b1.w), acc[3]);
 }
 
 __device__ __forceinline__ float comp(const float4 &v, int j) {
@@ -112,19 +110,25 @@ __device__ __forceinline__ void load_group(float4 (&a)[TRH], float4 (&w)[8], con
 }
 
 template <int TRH, bool TRANS>
-__device__ __forceinline__ void fma_group(float (&acc)[TRH][8], const float4 (&a)[TRH], const float4 (&w)[8]) {
+__device__ __forceinline__ void fma_group(float2 (&acc)[TRH][4], const float4 (&a)[TRH], const float4 (&w)[8]) {
+    // acc[i][jp] holds the lane's columns 2jp, 2jp + 1.  The input-grad layout has column pairs
+    // adjacent in w, so it uses packed f32x2 FMAs (each lane rounded like fmaf); the forward's
+    // pairs would need repacking per k, which costs more than it saves, so it stays scalar.
     if (TRANS) {
 #pragma unroll
         for (int kk = 0; kk < 4; kk++)
 #pragma unroll
             for (int i = 0; i < TRH; i++)
 #pragma unroll
-                for (int j = 0; j < 8; j++) acc[i][j] = fmaf(comp(a[i], kk), comp(w[j], kk), acc[i][j]);
+                for (int jp = 0; jp < 4; jp++) {
+                    acc[i][jp].x = fmaf(comp(a[i], kk), comp(w[2 * jp], kk), acc[i][jp].x);
+                    acc[i][jp].y = fmaf(comp(a[i], kk), comp(w[2 * jp + 1], kk), acc[i][jp].y);
+                }
     } else {
 #pragma unroll
         for (int j = 0; j < 4; j++)
 #pragma unroll
-            for (int i = 0; i < TRH; i++) fma4(acc[i], comp(a[i], j), w[2 * j], w[2 * j + 1]);
+            for (int i = 0; i < TRH; i++) fma4x2(acc[i], comp(a[i], j), w[2 * j], w[2 * j + 1]);
     }
 }
 
@@ -176,11 +180,11 @@ __device__ __forceinline__ void row_tile(const RowGemmArgs &p, float *Bs, float 
     };
     issue(0);
     issue(1);
-    float acc[TRH > 0 ? TRH : 1][8];
+    float2 acc[TRH > 0 ? TRH : 1][4];
 #pragma unroll
     for (int i = 0; i < (TRH > 0 ? TRH : 1); i++)
 #pragma unroll
-        for (int j = 0; j < 8; j++) acc[i][j] = 0.f;
+        for (int j = 0; j < 4; j++) acc[i][j] = make_float2(0.f, 0.f);
 
     for (int kb = 0; kb < nk; kb++) {
         issue(kb + 2);
@@ -209,7 +213,7 @@ __device__ __forceinline__ void row_tile(const RowGemmArgs &p, float *Bs, float 
 #pragma unroll
                 for (int i = 0; i < TRH; i++) {
                     const int64_t row = r0 + rg + 8 * (half + kHalves * i);
-                    if (row < p.M) p.C[row * p.N + c] = acc[i][j] + bj;
+                    if (row < p.M) p.C[row * p.N + c] = ((j & 1) ? acc[i][j >> 1].y : acc[i][j >> 1].x) + bj;
                 }
             }
         } else {
@@ -225,11 +229,11 @@ __device__ __forceinline__ void row_tile(const RowGemmArgs &p, float *Bs, float 
                 if (row >= p.M) continue;
                 float *cr = p.C + row * p.N + c;
                 if (c < p.N)
-                    *reinterpret_cast<float4 *>(cr) =
-                        make_float4(acc[i][0] + bb0.x, acc[i][1] + bb0.y, acc[i][2] + bb0.z, acc[i][3] + bb0.w);
+                    *reinterpret_cast<float4 *>(cr) = make_float4(acc[i][0].x + bb0.x, acc[i][0].y + bb0.y,
+                                                                  acc[i][1].x + bb0.z, acc[i][1].y + bb0.w);
                 if (c + 4 < p.N)
-                    *reinterpret_cast<float4 *>(cr + 4) =
-                        make_float4(acc[i][4] + bb1.x, acc[i][5] + bb1.y, acc[i][6] + bb1.z, acc[i][7] + bb1.w);
+                    *reinterpret_cast<float4 *>(cr + 4) = make_float4(acc[i][2].x + bb1.x, acc[i][2].y + bb1.y,
+                                                                      acc[i][3].x + bb1.z, acc[i][3].y + bb1.w);
             }
         }
     }
@@ -296,11 +300,11 @@ __global__ void __launch_bounds__(kWgThreads, kWgCtasPerSm)
         cp_async_commit();
     };
 
-    float acc[8][8];
+    float2 acc[8][4];     // acc[i][jp] = dW entries (i, 2jp) and (i, 2jp + 1) of the thread's 8 x 8 block
 #pragma unroll
     for (int i = 0; i < 8; i++)
 #pragma unroll
-        for (int j = 0; j < 8; j++) acc[i][j] = 0.f;
+        for (int j = 0; j < 4; j++) acc[i][j] = make_float2(0.f, 0.f);
     float dbacc = 0.f;
     const bool db_lane = kt == 0 && tx < 8;
     const int db_col = (tx & 7) < 4 ? 4 * ty + (tx & 7) : 60 + 4 * ty + (tx & 7);   // tx >= 8: a db lane's column
@@ -325,14 +329,14 @@ __global__ void __launch_bounds__(kWgThreads, kWgCtasPerSm)
             gd = Gs[b][r][db_col];
         };
         auto fma_row = [&](const float4 &g0, const float4 &g1, const float4 &x0, const float4 &x1) {
-            fma4(acc[0], g0.x, x0, x1);
-            fma4(acc[1], g0.y, x0, x1);
-            fma4(acc[2], g0.z, x0, x1);
-            fma4(acc[3], g0.w, x0, x1);
-            fma4(acc[4], g1.x, x0, x1);
-            fma4(acc[5], g1.y, x0, x1);
-            fma4(acc[6], g1.z, x0, x1);
-            fma4(acc[7], g1.w, x0, x1);
+            fma4x2(acc[0], g0.x, x0, x1);
+            fma4x2(acc[1], g0.y, x0, x1);
+            fma4x2(acc[2], g0.z, x0, x1);
+            fma4x2(acc[3], g0.w, x0, x1);
+            fma4x2(acc[4], g1.x, x0, x1);
+            fma4x2(acc[5], g1.y, x0, x1);
+            fma4x2(acc[6], g1.z, x0, x1);
+            fma4x2(acc[7], g1.w, x0, x1);
         };
         load_row(0, ga0, ga1, xa0, xa1, gda);
 #pragma unroll 1
@@ -355,9 +359,10 @@ __global__ void __launch_bounds__(kWgThreads, kWgCtasPerSm)
         if (n >= N) continue;
         float *pr = p + (size_t)n * K + k0;
         if (k0 + 4 * tx < K)
-            *reinterpret_cast<float4 *>(pr + 4 * tx) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+            *reinterpret_cast<float4 *>(pr + 4 * tx) = make_float4(acc[i][0].x, acc[i][0].y, acc[i][1].x, acc[i][1].y);
         if (k0 + 64 + 4 * tx < K)
-            *reinterpret_cast<float4 *>(pr + 64 + 4 * tx) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+            *reinterpret_cast<float4 *>(pr + 64 + 4 * tx) =
+                make_float4(acc[i][2].x, acc[i][2].y, acc[i][3].x, acc[i][3].y);
     }
     if (db_lane && n0 + db_col < N) p[(size_t)N * K + n0 + db_col] = dbacc;
 }
