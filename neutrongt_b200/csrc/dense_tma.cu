@@ -3,7 +3,7 @@
 // Same contract as the kernels of dense_attn.cu (which keep head_dim 33..64):
 //   forward   S = (q * scale) k^T, P = softmax(S) (+ dropout), X = P v, lse, and the node-score
 //             column sums sum_i |S_ij| (times score_scale) added into node_scores;
-//   backward  dQ (fp32 partials, atomically added), dK, dV.
+//   backward  dQ (fp32 partials, added by TMA reduce-add), dK, dV.
 // Reference: CoreAttention.full_attention, NeutronGT/models/gt_dist_node_level_single_window.py:56-109.
 //
 // Q, K, V and dO tiles arrive by cp.async.bulk.tensor from a 4-D tensor map over the [s, H, D]
@@ -70,10 +70,6 @@ __device__ __forceinline__ void st16(uint8_t *p, uint32_t a, uint32_t b, uint32_
     *reinterpret_cast<uint4 *>(p) = make_uint4(a, b, c, d);
 }
 
-__device__ __forceinline__ void red_add_v4(float *p, float a, float b, float c, float d) {
-    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
-                 : "memory");
-}
 
 // Abort flag in shared memory plus the device status word.
 struct Abort {
@@ -574,7 +570,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 //   S_b = Q K_b^T, dP_b = dO V_b^T                    (TMEM, lanes = queries)
 //   P = 2^(S * scale * log2e - lse * log2e), dS = P (dP - delta)   (registers -> shared memory)
 //   dV += P^T dO, dK += dS^T Q   (P, dS read MN-major: lanes = keys)
-//   dQ(qb) = dS K                 (TMEM, two buffers) -> fp32 atomics by the epilogue warps
+//   dQ(qb) = dS K                 (TMEM, two buffers) -> shared memory -> one TMA reduce-add of
+//                                 the [128 x D] fp32 partial into dq_acc per query block
 // ------------------------------------------------------------------------------------
 struct BwdL {
     static constexpr int NST = 3;   // Q / dO / lse / delta stages
@@ -584,7 +581,9 @@ struct BwdL {
     static constexpr uint32_t kStageBytes = 2 * kTileBytes + 2 * TILE * 4;   // Q, dO, -lse*log2e, -delta
     static constexpr uint32_t kPS = kStage + NST * kStageBytes;              // 2 x {P, dS} [128 q x 128 keys]
     static constexpr uint32_t kPSBytes = 2 * TILE * TILE * 2;
-    static constexpr uint32_t kBars = kPS + 2 * kPSBytes;
+    static constexpr uint32_t kDQS = kPS + 2 * kPSBytes;                     // dQ partial [128 q x D] fp32
+    static constexpr uint32_t kDQSBytes = TILE * DP * 4;
+    static constexpr uint32_t kBars = kDQS + kDQSBytes;
     enum {
         KVF = 0,
         QF = 1,
@@ -638,7 +637,8 @@ __device__ __forceinline__ void bwd_chunk_fast(const float (&sv)[32], const floa
 
 __global__ void __launch_bounds__(kThreads, 1)
     dense_bwd_tma_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                         const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do, int s,
+                         const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                         const __grid_constant__ CUtensorMap tm_dq, int s,
                          int H, int D, float scale, float drop_p, uint32_t seed, const float *__restrict__ lse,
                          const float *__restrict__ delta, float *__restrict__ dq_acc, __nv_bfloat16 *__restrict__ dk,
                          __nv_bfloat16 *__restrict__ dv, int *__restrict__ status) {
@@ -872,14 +872,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else if (warp >= 12) {
-        // ---------------- dQ reductions (lane = query), then dK / dV (lane = key) ----------------
+        // ---------------- dQ partials (lane = query), then dK / dV (lane = key) ----------------
+        // Per query block the four warps stage the [128 x D] partial in shared memory and thread
+        // 384 adds it to dq_acc with one TMA reduce-add (rows past s are clipped by the tensor
+        // map).  Barrier 1 (these 128 threads) orders the stage's reuse and makes every exit
+        // decision collective, so no warp waits at a barrier that another warp has left.
+        constexpr int kDqBar = 1;
         const int r = tid & 127;
         const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
         const size_t rs = (size_t)H * D;
+        float *stage = reinterpret_cast<float *>(smem + L::kDQS);
         bool ok = true;
         for (int qb = 0; qb < nqb; qb++) {
             const int par = qb & 1;
-            if (ab.set() || !(ok = warp_wait(&bars[L::DQF + par], (qb >> 1) & 1, ab))) {
+            const bool fail = ab.set() || !warp_wait(&bars[L::DQF + par], (qb >> 1) & 1, ab);
+            if (tc::bar_red_or(kDqBar, 128, fail)) {
                 ok = false;
                 break;
             }
@@ -889,14 +896,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc::fence_before_sync();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&bars[L::DQE + par]);
-            const int qi = qb * TILE + r;
-            if (qi < s) {   // dq_acc rows are 16-byte aligned: D % 8 == 0 and fp32
-                float *p = dq_acc + (size_t)qi * rs + (size_t)h * D;
+            if (r == 0) tc::bulk_wait_read_all();   // the previous block's reduce has read the stage
+            tc::bar_sync(kDqBar, 128);
+            float *row = stage + r * D;            // D % 8 == 0: 16-byte aligned rows
 #pragma unroll
-                for (int d = 0; d < DP; d += 4)
-                    if (d < D) red_add_v4(p + d, g[d] * scale, g[d + 1] * scale, g[d + 2] * scale, g[d + 3] * scale);
+            for (int d = 0; d < DP; d += 4)
+                if (d < D)
+                    *reinterpret_cast<float4 *>(row + d) =
+                        make_float4(g[d] * scale, g[d + 1] * scale, g[d + 2] * scale, g[d + 3] * scale);
+            tc::fence_smem_for_async();
+            tc::bar_sync(kDqBar, 128);
+            if (r == 0) {
+                tc::tma_reduce_add_2d(&tm_dq, h * D, qb * TILE, stage);
+                tc::bulk_commit();
             }
         }
+        if (r == 0) tc::bulk_wait_all();
         if (ok && warp_wait(&bars[L::ACC + 2], 0, ab) && !ab.set()) {
             tc::fence_after_sync();
             const int kj = k0 + r;
@@ -959,6 +974,21 @@ int rows_map(CUtensorMap *m, const void *base, int64_t s, int H, int D) {
     return r == CUDA_SUCCESS ? NGT_OK : NGT_ERR_CUDA;
 }
 
+// dq_acc [s, H * D] fp32 as 2-D (H * D columns, s rows); box (D, 128): one head's D columns of a
+// 128-row query block.  Column coordinate h * D: h * D * 4 bytes is a multiple of 16 (D % 8 == 0).
+int dq_map(CUtensorMap *m, float *base, int64_t s, int H, int D) {
+    EncodeTiled enc = encoder();
+    if (!enc) return NGT_ERR_CUDA;
+    const cuuint64_t dims[2] = {(cuuint64_t)H * D, (cuuint64_t)s};
+    const cuuint64_t strides[1] = {(cuuint64_t)H * D * 4};
+    const cuuint32_t box[2] = {(cuuint32_t)D, TILE};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? NGT_OK : NGT_ERR_CUDA;
+}
+
 }  // namespace
 }  // namespace dtma
 
@@ -985,17 +1015,18 @@ int dense_bwd_tma(int64_t s, int heads, int head_dim, float scale, float drop_p,
                   const void *k, const void *v, const void *dout, const float *lse, const float *delta, float *dq_acc,
                   void *dk, void *dv, int *status, cudaStream_t st) {
     using namespace dtma;
-    CUtensorMap mq, mk, mv, mdo;
+    CUtensorMap mq, mk, mv, mdo, mdq;
     int rc;
     if ((rc = rows_map(&mq, q, s, heads, head_dim)) != NGT_OK) return rc;
     if ((rc = rows_map(&mk, k, s, heads, head_dim)) != NGT_OK) return rc;
     if ((rc = rows_map(&mv, v, s, heads, head_dim)) != NGT_OK) return rc;
     if ((rc = rows_map(&mdo, dout, s, heads, head_dim)) != NGT_OK) return rc;
+    if ((rc = dq_map(&mdq, dq_acc, s, heads, head_dim)) != NGT_OK) return rc;
     if (cudaFuncSetAttribute(dense_bwd_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)BwdL::kBytes) !=
         cudaSuccess)
         return NGT_ERR_CUDA;
     dim3 grid((unsigned)((s + TILE - 1) / TILE), (unsigned)heads);
-    dense_bwd_tma_kernel<<<grid, kThreads, BwdL::kBytes, st>>>(mq, mk, mv, mdo, (int)s, heads, head_dim, scale, drop_p,
+    dense_bwd_tma_kernel<<<grid, kThreads, BwdL::kBytes, st>>>(mq, mk, mv, mdo, mdq, (int)s, heads, head_dim, scale, drop_p,
                                                                seed, lse, delta, dq_acc, (__nv_bfloat16 *)dk,
                                                                (__nv_bfloat16 *)dv, status);
     NGT_CHECK_LAUNCH();

@@ -181,5 +181,36 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     return *reinterpret_cast<uint32_t *>(&h);
 }
 
+// 2-D tiled TMA reduce-add shared -> global (the tensor map's element type, here f32), tracked in
+// the issuing thread's bulk async-group.  Coordinates are never negative here.
+__device__ __forceinline__ void tma_reduce_add_2d(const void *tmap, int c0, int c1, const void *src) {
+    asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2}], [%3];"
+                 ::"l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(smem_addr(src))
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// the shared-memory sources of this thread's committed bulk groups have been read
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// this thread's committed bulk groups are complete (writes performed)
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Named barrier over `n` threads (a multiple of 32) of the CTA.
+__device__ __forceinline__ void bar_sync(int id, int n) {
+    asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+// Named barrier that also returns, to every participant, the OR of their predicates.
+__device__ __forceinline__ bool bar_red_or(int id, int n, bool pred) {
+    uint32_t out;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "barrier.red.or.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}\n"
+        : "=r"(out)
+        : "r"((uint32_t)pred), "r"(id), "r"(n)
+        : "memory");
+    return out != 0;
+}
+
 }  // namespace tc
 }  // namespace ngt
