@@ -191,10 +191,30 @@ __global__ void halo_heads_kernel(int64_t t, uint32_t n, const uint32_t *__restr
     head[j] = (j < t && key[j] != n && (j == 0 || key[j] != key[j - 1])) ? 1u : 0u;
 }
 
-// Per external neighbour: total weight (integer sum, order-free) and first-encounter position
-// (the head's position: the sort is stable and positions increase with the input index).
+// Weights in sorted order (0 for members) for a prefix sum, and the end of each external
+// neighbour's run of entries, written by the run's last entry.
+__global__ void halo_runs_kernel(int64_t t, uint32_t n, const uint32_t *__restrict__ key,
+                                 const uint32_t *__restrict__ pos, const int32_t *__restrict__ wpos,
+                                 const uint32_t *__restrict__ head, const uint32_t *__restrict__ seg,
+                                 int64_t *__restrict__ wsorted, uint32_t *__restrict__ seg_end) {
+    const int64_t j = (int64_t)blockIdx.x * kT + threadIdx.x;
+    if (j > t) return;
+    if (j == t) {
+        wsorted[j] = 0;
+        return;
+    }
+    const bool ext = key[j] != n;
+    wsorted[j] = ext ? (int64_t)wpos[pos[j]] : 0;
+    // seg is the exclusive scan of the run heads, so entry j belongs to run seg[j] + head[j] - 1
+    if (ext && (j + 1 == t || key[j + 1] != key[j])) seg_end[seg[j] + head[j] - 1] = (uint32_t)(j + 1);
+}
+
+// Per external neighbour: total weight (integer sum, from the prefix sum of the sorted weights)
+// and first-encounter position (the head's position: the sort is stable and positions increase
+// with the input index).
 __global__ void halo_segments_kernel(int64_t t, uint32_t n, const uint32_t *__restrict__ key,
-                                     const uint32_t *__restrict__ pos, const int32_t *__restrict__ wpos,
+                                     const uint32_t *__restrict__ pos, const int64_t *__restrict__ wscan,
+                                     const uint32_t *__restrict__ seg_end,
                                      const uint32_t *__restrict__ head, const uint32_t *__restrict__ seg,
                                      uint32_t *__restrict__ seg_nb, uint32_t *__restrict__ first_key,
                                      uint32_t *__restrict__ invw_key, uint32_t *__restrict__ sidx) {
@@ -208,9 +228,8 @@ __global__ void halo_segments_kernel(int64_t t, uint32_t n, const uint32_t *__re
         sidx[j] = (uint32_t)j;
     }
     if (!head[j]) return;
-    int64_t w = 0;
-    for (int64_t q = j; q < t && key[q] == key[j]; q++) w += wpos[pos[q]];
     const uint32_t s = seg[j];
+    const int64_t w = wscan[seg_end[s]] - wscan[j];
     seg_nb[s] = key[j];
     first_key[s] = pos[j];
     invw_key[s] = 0xFFFFFFFEu - (uint32_t)(w < 0 ? 0 : (w > 0xFFFFFFFEll ? 0xFFFFFFFEll : w));
@@ -256,8 +275,8 @@ __global__ void halo_out_kernel(int64_t cap, const uint32_t *__restrict__ key, c
 
 struct HaloWs {
     int32_t *member, *bad, *wpos;
-    int64_t *deg, *off, *off_partials, *total;
-    uint32_t *ka, *kb, *va, *vb, *head, *seg, *seg_nb, *fk, *wk, *hist, *partials;
+    int64_t *deg, *off, *off_partials, *total, *wsorted, *wscan, *w_partials;
+    uint32_t *ka, *kb, *va, *vb, *head, *seg, *seg_nb, *seg_end, *fk, *wk, *hist, *partials;
 };
 
 HaloWs carve_halo(void *base, size_t cap, int64_t n, int64_t p, int64_t t, size_t *used) {
@@ -278,6 +297,10 @@ HaloWs carve_halo(void *base, size_t cap, int64_t n, int64_t p, int64_t t, size_
     w.head = c.take<uint32_t>(t + 1);
     w.seg = c.take<uint32_t>(t + 1);
     w.seg_nb = c.take<uint32_t>(t + 1);
+    w.seg_end = c.take<uint32_t>(t + 1);
+    w.wsorted = c.take<int64_t>(t + 1);
+    w.wscan = c.take<int64_t>(t + 1);
+    w.w_partials = c.take<int64_t>(scan_partials_count(t + 1) + 1);
     w.fk = c.take<uint32_t>(t + 1);
     w.wk = c.take<uint32_t>(t + 1);
     const int64_t hist_n = 256 * radix_tiles(big);
@@ -576,8 +599,12 @@ extern "C" int ngt_halo_merge(int64_t n, const int32_t *xadj, const int32_t *adj
         if (rc) return rc;
         // free buffers for the segment sort: the one not holding (skey, spos)
         uint32_t *ska = where ? w.ka : w.kb, *sva = where ? w.va : w.vb;
-        halo_segments_kernel<<<grid_for(total), kT, 0, st>>>(total, un, skey, spos, w.wpos, w.head, w.seg, w.seg_nb,
-                                                              w.fk, w.wk, sva);
+        halo_runs_kernel<<<grid_for(total + 1), kT, 0, st>>>(total, un, skey, spos, w.wpos, w.head, w.seg,
+                                                              w.wsorted, w.seg_end);
+        rc = exclusive_scan<int64_t>(w.wsorted, w.wscan, total + 1, w.w_partials, st);
+        if (rc) return rc;
+        halo_segments_kernel<<<grid_for(total), kT, 0, st>>>(total, un, skey, spos, w.wscan, w.seg_end, w.head, w.seg,
+                                                              w.seg_nb, w.fk, w.wk, sva);
         halo_select_kernel<<<1, 32, 0, st>>>(total, p, topk_percent, w.head, w.seg, counts);
         // order the externals by (weight desc, first encounter asc): stable sort by position, then
         // stable sort by inverted weight (the other key buffers are free now)
