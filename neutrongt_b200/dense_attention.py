@@ -14,6 +14,11 @@ counter-based hash of (seed, head, query, key), regenerated in the backward; it 
 torch's dropout in distribution, not bit for bit.  The optional dense attn_bias / mask /
 pruning_mask tensors ([b, H, s, s]) are not supported: NeutronGT's training loop passes
 None for all three.
+
+A kernel whose bounded wait runs out returns early and sets a device status word; the host
+learns of it without a stall (`_StatusWord`): the next call on the device raises, and
+`check_dense_status()` waits and raises at once.  Nothing in the forward or backward blocks the
+host, so the Ulysses layer enqueues its exchanges while the kernels run.
 """
 from __future__ import annotations
 
@@ -24,9 +29,53 @@ import torch
 from . import _lib
 
 
-def _check_status(status):
-    if int(status.item()) != 0:
-        raise RuntimeError("dense attention kernel timed out waiting for the tensor core")
+class _StatusWord:
+    """Timeout reports of the dense kernels, read without stalling the host.
+
+    Every bounded wait in the forward and backward kernels that runs out sets the int32 status
+    word to 1 (no kernel ever clears it).  One persistent word per device collects every launch;
+    after a launch with checking on, the word is copied to pinned host memory on the launching
+    stream, so the host never waits for the kernel: the timeout is raised by the next dense
+    attention call on that device, or by `check_dense_status`, which waits for the copies.  The
+    word only goes 0 -> 1, so every value the host reads is a valid snapshot.
+    """
+
+    _by_device: dict = {}
+
+    def __init__(self, dev):
+        self.word = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        self.event = torch.cuda.Event()
+
+    @classmethod
+    def of(cls, dev):
+        key = torch.device(dev).index if torch.device(dev).index is not None else torch.cuda.current_device()
+        sw = cls._by_device.get(key)
+        if sw is None:
+            sw = cls._by_device[key] = cls(torch.device("cuda", key))
+        return sw
+
+    def raise_if_set(self):
+        if int(self.host[0]) != 0:
+            self.event.synchronize()       # every copy in flight has landed before the reset
+            self.word.zero_()
+            torch.cuda.current_stream(self.word.device).synchronize()
+            self.host.zero_()
+            raise RuntimeError("dense attention kernel timed out waiting for the tensor core")
+
+    def publish(self):
+        if torch.cuda.is_current_stream_capturing():
+            return                         # a captured launch is checked by the next eager one
+        self.host.copy_(self.word, non_blocking=True)
+        self.event.record()
+
+
+def check_dense_status(device=None):
+    """Waits for the status copies of the dense kernels on `device` and raises if any wait of
+    theirs timed out since the last report."""
+    sw = _StatusWord.of(torch.cuda.current_device() if device is None else device)
+    sw.event.synchronize()
+    sw.raise_if_set()
 
 
 class _DenseAttention(torch.autograd.Function):
@@ -36,14 +85,16 @@ class _DenseAttention(torch.autograd.Function):
         out = torch.empty_like(q)
         lse = torch.empty(heads, s, dtype=torch.float32, device=q.device)
         ns = torch.zeros(s, dtype=torch.float32, device=q.device)
-        status = torch.zeros(1, dtype=torch.int32, device=q.device)
+        sw = _StatusWord.of(q.device)
+        if check:
+            sw.raise_if_set()
         _lib.check(_lib.lib().ngt_dense_attn_forward(s, heads, dim, float(scale), 1.0 / score_heads,
                                                      float(dropout_p), int(seed), _lib.ptr(q), _lib.ptr(k),
                                                      _lib.ptr(v), _lib.ptr(out), _lib.ptr(lse), _lib.ptr(ns),
-                                                     _lib.ptr(status), _lib.stream_of(q)),
+                                                     _lib.ptr(sw.word), _lib.stream_of(q)),
                    "ngt_dense_attn_forward")
         if check:
-            _check_status(status)
+            sw.publish()
         ctx.save_for_backward(q, k, v, out, lse)
         ctx.args = (scale, dropout_p, seed, check)
         ctx.mark_non_differentiable(ns)
@@ -58,15 +109,17 @@ class _DenseAttention(torch.autograd.Function):
         delta = torch.empty(heads, s, dtype=torch.float32, device=q.device)
         dq_acc = torch.empty(s, heads, dim, dtype=torch.float32, device=q.device)
         dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-        status = torch.zeros(1, dtype=torch.int32, device=q.device)
+        sw = _StatusWord.of(q.device)
+        if check:
+            sw.raise_if_set()
         _lib.check(_lib.lib().ngt_dense_attn_backward(s, heads, dim, float(scale), float(dropout_p), int(seed),
                                                       _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(out),
                                                       _lib.ptr(dout), _lib.ptr(lse), _lib.ptr(delta), _lib.ptr(dq_acc),
-                                                      _lib.ptr(dq), _lib.ptr(dk), _lib.ptr(dv), _lib.ptr(status),
+                                                      _lib.ptr(dq), _lib.ptr(dk), _lib.ptr(dv), _lib.ptr(sw.word),
                                                       _lib.stream_of(q)),
                    "ngt_dense_attn_backward")
         if check:
-            _check_status(status)
+            sw.publish()
         return dq, dk, dv, None, None, None, None, None
 
 

@@ -102,3 +102,23 @@ def test_full_attention_contract(cuda):
     assert x.shape == (1, s, H * D)
     assert rel_err(x.reshape(s, H, D), rx) < BF16_TOL
     assert rel_err(score, rns) < BF16_TOL
+
+
+def test_status_word_reports_a_timeout_without_a_host_wait(cuda):
+    """A timeout recorded in the device status word (set here from the host: no wait is made
+    to run out) is raised by `check_dense_status` once, and cleared after the report."""
+    from neutrongt_b200.dense_attention import _StatusWord, check_dense_status, dense_attention
+    s, H, D = 256, 2, 24
+    q, k, v, dout = _inputs(s, H, D, 11)
+    check_dense_status()
+    sw = _StatusWord.of(q.device)
+    sw.word.fill_(1)
+    qd = q.clone().requires_grad_(True)
+    x, _ = dense_attention(qd, k, v, math.sqrt(D))     # launches and publishes the word
+    with pytest.raises(RuntimeError, match="timed out"):
+        check_dense_status()
+    check_dense_status()                                  # reported once, then clear
+    x, _ = dense_attention(qd, k, v, math.sqrt(D))
+    x.backward(dout)
+    check_dense_status()
+    assert int(sw.word.item()) == 0
