@@ -298,7 +298,10 @@ NGT_API int ngt_column_sum(int64_t rows, int cols, const float *x, float *out, v
  * 235-237, 313-318, 361; graphormer_dist_node_level.py:179, 183, 286).  All tensors row-major fp32,
  * 16-byte aligned: x / dx [rows, in_features], y / dy [rows, out_features], weight / dweight
  * [out_features, in_features], bias / dbias [out_features] (bias and dbias may be NULL).
- * in_features and out_features are multiples of 4.  CUDA-core FFMA, no TF32.
+ * in_features and out_features are multiples of 4.  fp32 precision throughout: with both
+ * dimensions <= 256 the forward and input grad run on the tcgen05 tensor cores with split TF32
+ * operands (three TF32 products per pair: hi*hi + hi*lo + lo*hi, fp32 accumulation), otherwise
+ * on CUDA-core FFMA; the weight grad is FFMA.
  *   ngt_linear_forward         y = x W^T + b          in_features  <= 256 (else NGT_ERR_UNSUPPORTED)
  *   ngt_linear_backward_input  dx = dy W              out_features <= 256 (else NGT_ERR_UNSUPPORTED)
  *   ngt_linear_backward_weight dW = dy^T x, db = column sums of dy; any size; summed in a fixed
@@ -315,6 +318,9 @@ NGT_API int ngt_linear_weight_workspace_size(int64_t rows, int in_features, int 
 NGT_API int ngt_linear_backward_weight(int64_t rows, int in_features, int out_features, const float *x,
                                        const float *dy, float *dweight, float *dbias, void *workspace,
                                        size_t workspace_bytes, ngt_stream_t stream);
+/* Number of tensor-core Linear CTAs whose bounded waits ran out (they store nothing) since the
+ * library was loaded; synchronous.  No counterpart in the reference (torch's GEMMs do not wait). */
+NGT_API int ngt_linear_status(int32_t *timeouts /* host */);
 
 /* ----------------------------------------------------------------------------------
  * Window construction between PPR and the training windows.

@@ -68,6 +68,7 @@ SIGNATURES = {
     "ngt_linear_backward_input": [_i64, _i32, _i32, _p, _p, _p, _p],
     "ngt_linear_weight_workspace_size": [_i64, _i32, _i32, _sz_p],
     "ngt_linear_backward_weight": [_i64, _i32, _i32, _p, _p, _p, _p, _p, ctypes.c_size_t, _p],
+    "ngt_linear_status": [_p],
 }
 
 NGT_F32 = 0

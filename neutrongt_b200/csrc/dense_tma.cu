@@ -960,8 +960,16 @@ EncodeTiled encoder() {
     return fn;
 }
 
+// The encoder is a driver call: it needs the device's primary context current in the calling
+// thread, which a thread that has only made runtime calls (autograd's device threads) may lack.
+void bind_primary_context() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaSetDevice(dev);
+}
+
 // [s, H, D] bf16 rows viewed as (8 elements, s rows, D / 8 chunks, H heads); box (8, 128, 4, 1).
 int rows_map(CUtensorMap *m, const void *base, int64_t s, int H, int D) {
+    bind_primary_context();
     EncodeTiled enc = encoder();
     if (!enc) return NGT_ERR_CUDA;
     const cuuint64_t dims[4] = {8, (cuuint64_t)s, (cuuint64_t)(D / 8), (cuuint64_t)H};
@@ -977,6 +985,7 @@ int rows_map(CUtensorMap *m, const void *base, int64_t s, int H, int D) {
 // dq_acc [s, H * D] fp32 as 2-D (H * D columns, s rows); box (D, 128): one head's D columns of a
 // 128-row query block.  Column coordinate h * D: h * D * 4 bytes is a multiple of 16 (D % 8 == 0).
 int dq_map(CUtensorMap *m, float *base, int64_t s, int H, int D) {
+    bind_primary_context();
     EncodeTiled enc = encoder();
     if (!enc) return NGT_ERR_CUDA;
     const cuuint64_t dims[2] = {(cuuint64_t)H * D, (cuuint64_t)s};

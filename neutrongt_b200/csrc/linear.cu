@@ -19,11 +19,14 @@
 //    2-stage cp.async ring of 16-row slabs), and a share of db.  Per-chunk partials are summed in chunk order by
 //    a second kernel, so dW and db are bitwise reproducible.
 //
-// fp32 FFMA throughout (no TF32), the precision of torch's fp32 Linear.  Reference layers: the
+// fp32 FFMA throughout (no TF32), the precision of torch's fp32 Linear.  The forward and input
+// grad with both dimensions <= 256 go to the split-TF32 tensor-core kernel of linear_tc.cu (same
+// precision); the row GEMM keeps the wider outputs.  Reference layers: the
 // models' nn.Linear (NeutronGT/models/gt_dist_node_level_single_window.py:235-237, 313-318, 361;
 // graphormer_dist_node_level.py:179, 183, 286).
 #include "chunk_sum.cuh"
 #include "common.cuh"
+#include "linear_tc.h"
 
 namespace ngt {
 namespace {
@@ -474,6 +477,9 @@ extern "C" int ngt_linear_forward(int64_t rows, int in_features, int out_feature
     if (rows == 0) return NGT_OK;
     if (!x || !weight || !y) return NGT_ERR_INVALID_ARGUMENT;
     if (!aligned16(x) || !aligned16(weight) || !aligned16(y) || (bias && !aligned16(bias))) return NGT_ERR_MISALIGNED;
+    if (linear_tc_supported(in_features, out_features))
+        return launch_linear_tc(rows, in_features, out_features, x, weight, false, bias, y,
+                                reinterpret_cast<cudaStream_t>(stream));
     return launch_row_gemm<true>(rows, in_features, out_features, x, weight, bias, y,
                                  reinterpret_cast<cudaStream_t>(stream));
 }
@@ -485,6 +491,9 @@ extern "C" int ngt_linear_backward_input(int64_t rows, int in_features, int out_
     if (rows == 0) return NGT_OK;
     if (!dy || !weight || !dx) return NGT_ERR_INVALID_ARGUMENT;
     if (!aligned16(dy) || !aligned16(weight) || !aligned16(dx)) return NGT_ERR_MISALIGNED;
+    if (linear_tc_supported(out_features, in_features))
+        return launch_linear_tc(rows, out_features, in_features, dy, weight, true, nullptr, dx,
+                                reinterpret_cast<cudaStream_t>(stream));
     return launch_row_gemm<false>(rows, out_features, in_features, dy, weight, nullptr, dx,
                                   reinterpret_cast<cudaStream_t>(stream));
 }
@@ -522,4 +531,12 @@ extern "C" int ngt_linear_backward_weight(int64_t rows, int in_features, int out
     launch_chunk_sum((int)p.chunks, nk, nk + out_features, part, dweight, dbias, st);
     NGT_CHECK_LAUNCH();
     return NGT_OK;
+}
+
+extern "C" int ngt_linear_status(int32_t *timeouts) {
+    if (!timeouts) return NGT_ERR_INVALID_ARGUMENT;
+    int n = 0;
+    const int rc = linear_tc_timeouts(&n);
+    *timeouts = n;
+    return rc;
 }

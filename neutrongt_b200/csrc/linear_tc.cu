@@ -1,0 +1,387 @@
+// fp32 Linear GEMMs (forward y = x W^T + b, input grad dx = dy W) on the tcgen05 tensor cores
+// with split TF32 operands.
+//
+// Every fp32 operand element a is split into hi = tf32_rn(a) and lo = tf32_rn(a - hi) (a - hi is
+// exact in fp32); a b is then hi_a hi_b + hi_a lo_b + lo_a hi_b, three kind::tf32 MMAs per k-step
+// into one fp32 TMEM accumulator.  The dropped lo_a lo_b and the rounding of lo leave a relative
+// error per product near 2^-21, the size of fp32's own rounding in a sum of 10^2 products, so the
+// result keeps the precision of torch's fp32 Linear (no TF32 loss), at tensor-core speed.
+//
+// Tiling: one CTA = 128 rows (the 128 TMEM lanes, MMA M = 128) x `ncta` output columns (MMA N,
+// padded to a multiple of 16, <= 256), the reduction dimension streamed in slices of 16 elements.
+// Thread 0 keeps STAGES - 1 slices in flight with TMA: A through a 3-D tensor map (4 elements,
+// rows, 16-byte chunks) whose box lands in the no-swizzle K-major core-matrix layout (row r,
+// chunk c at c * rows * 16 + r * 16); the forward's weight the same way; the input grad's weight
+// (W [out, in], reduced over `out`) as plain row-major [16 k][np n] tiles, transposed by the
+// threads.  All 256 threads split a landed slice into hi / lo operand buffers (two, alternating)
+// in the same core-matrix layout; thread 0 issues the slice's 6 MMAs and commits them to the
+// buffer's mbarrier.  TMA writes through the async proxy, so the threads' proxy fence before the
+// MMAs waits only for their own split stores, never for loads in flight.  The epilogue reads the
+// accumulator with tcgen05.ld (warp w: lanes 32 (w % 4).., column groups alternating between
+// w < 4 and w >= 4), adds the bias and stores fp32 rows.
+//
+// Every wait is bounded; a timeout is counted in a device word (ngt_linear_status), the CTA waits
+// (bounded) for its MMAs in flight, frees its TMEM and returns without storing.
+//
+// Reference layers: the models' nn.Linear (NeutronGT/models/gt_dist_node_level_single_window.py:
+// 235-237, 313-318, 361; graphormer_dist_node_level.py:179, 183, 286).
+#include <cuda.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "linear_tc.h"
+#include "tc.cuh"
+
+namespace ngt {
+
+__device__ int g_linear_tc_timeouts = 0;
+
+namespace {
+
+constexpr int kM = 128;                        // rows per CTA = TMEM lanes = MMA M
+constexpr int kKS = 16;                        // reduction elements per slice (4 chunks of 16 B)
+constexpr int kThreads = 256;
+constexpr uint32_t kARaw = kM * kKS * 4;       // bytes of one A slice (raw, hi or lo): 8 KiB
+constexpr uint32_t kPolls = 1u << 26;
+constexpr int kMaxN = 256;
+constexpr uint32_t kSmemPerSm = 233472;        // 228 KiB per SM, 1 KiB of it reserved per CTA
+
+struct TcArgs {
+    int64_t M;
+    int K, N;          // reduction length, output columns (row stride of C)
+    int ncta, np;      // columns per CTA, padded to the MMA N
+    uint32_t tmem_cols;
+    int trans;         // 0: B(n, k) = W[n * K + k];  1: B(n, k) = W[k * N + n]
+    const float *bias;
+    float *C;
+};
+
+// Shared memory: STAGES raw slices (A, then B), two operand buffers (A hi, A lo, B hi, B lo),
+// then the mbarriers (STAGES "slice landed", 2 "MMAs done") and the TMEM address.
+__host__ __device__ constexpr uint32_t raw_bytes(int np) { return kARaw + (uint32_t)np * 64u; }
+__host__ __device__ constexpr uint32_t op_bytes(int np) { return 2 * kARaw + 2 * (uint32_t)np * 64u; }
+__host__ __device__ constexpr uint32_t smem_bytes(int np, int stages) {
+    return (uint32_t)stages * raw_bytes(np) + 2 * op_bytes(np) + 8 * (uint32_t)stages + 32;
+}
+
+// hi = x rounded to the nearest tf32 (ties away from zero; 10 mantissa bits), lo = x - hi (exact);
+// the tensor core reads lo as tf32 too, which costs at most 2^-11 of |lo| <= 2^-22 |x|.
+// Non-finite x: hi = x, lo = 0.
+__device__ __forceinline__ void split1(float x, uint32_t &hi, float &lo) {
+    const uint32_t b = __float_as_uint(x);
+    const bool fin = (b & 0x7F800000u) != 0x7F800000u;
+    hi = fin ? ((b + 0x1000u) & 0xFFFFE000u) : b;
+    lo = fin ? x - __uint_as_float(hi) : 0.f;
+}
+__device__ __forceinline__ void split_store(float4 v, uint8_t *hi, uint8_t *lo) {
+    uint4 h;
+    float4 l;
+    split1(v.x, h.x, l.x);
+    split1(v.y, h.y, l.y);
+    split1(v.z, h.z, l.z);
+    split1(v.w, h.w, l.w);
+    *reinterpret_cast<uint4 *>(hi) = h;
+    *reinterpret_cast<float4 *>(lo) = l;
+}
+
+// Splits a landed slice into operand buffer `op`.  Chunk (row r, 16-byte chunk c) sits at
+// c * rows * 16 + r * 16 in raw and operand tiles alike; consecutive threads take consecutive
+// rows, so every access is conflict-free.
+__device__ __forceinline__ void split_slice(const TcArgs &p, const uint8_t *raw, uint8_t *op) {
+    const int tid = threadIdx.x;
+    const uint8_t *rb = raw + kARaw;
+    uint8_t *a_hi = op, *a_lo = op + kARaw, *b_hi = op + 2 * kARaw, *b_lo = b_hi + (uint32_t)p.np * 64u;
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        const uint32_t o = (uint32_t)(tid + i * kThreads) * 16u;   // (c, r) = (idx / 128, idx % 128)
+        split_store(*reinterpret_cast<const float4 *>(raw + o), a_hi + o, a_lo + o);
+    }
+    const int items = p.np * 4;
+    for (int idx = tid; idx < items; idx += kThreads) {
+        const uint32_t o = (uint32_t)idx * 16u;                    // (c, n) = (idx / np, idx % np)
+        float4 v;
+        if (!p.trans) {
+            v = *reinterpret_cast<const float4 *>(rb + o);
+        } else {   // raw row-major [16 k][np n]: column n, rows 4c .. 4c + 3
+            const int n = idx % p.np, c = idx / p.np;
+            const float *col = reinterpret_cast<const float *>(rb) + (4 * c) * p.np + n;
+            v = make_float4(col[0], col[p.np], col[2 * p.np], col[3 * p.np]);
+        }
+        split_store(v, b_hi + o, b_lo + o);
+    }
+}
+
+template <int STAGES>
+__global__ void __launch_bounds__(kThreads, 2)
+    linear_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
+                     const TcArgs p) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t m0 = (int64_t)blockIdx.x * kM;
+    const int n0 = blockIdx.y * p.ncta;
+    const uint32_t rawb = raw_bytes(p.np), opb = op_bytes(p.np);
+    uint8_t *ops = smem + STAGES * rawb;
+    uint64_t *full = reinterpret_cast<uint64_t *>(ops + 2 * opb);
+    uint64_t *done = full + STAGES;
+    uint32_t *slot = reinterpret_cast<uint32_t *>(done + 2);
+    const int ns = (p.K + kKS - 1) / kKS;
+
+    auto load = [&](int j) {   // thread 0: slice j into stage j % STAGES
+        uint8_t *raw = smem + (j % STAGES) * rawb;
+        uint64_t *bar = &full[j % STAGES];
+        tc::mbar_arrive_expect_tx(bar, rawb);
+        tc::tma_load_3d(raw, &tm_a, 0, (int)m0, j * (kKS / 4), bar);
+        if (!p.trans)
+            tc::tma_load_3d(raw + kARaw, &tm_w, 0, n0, j * (kKS / 4), bar);
+        else
+            tc::tma_load_2d(raw + kARaw, &tm_w, n0, j * kKS, bar);
+    };
+
+    if (tid == 0) {
+        for (int st = 0; st < STAGES; st++) tc::mbar_init(&full[st], 1);
+        tc::mbar_init(&done[0], 1);
+        tc::mbar_init(&done[1], 1);
+        tc::mbar_init_fence();
+        for (int j = 0; j < STAGES - 1 && j < ns; j++) load(j);
+    }
+    if (warp == 0) tc::tmem_alloc(slot, p.tmem_cols);
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *slot;
+
+    const uint32_t idesc = tc::idesc_tf32(kM, p.np);
+    const uint32_t b_lbo = (uint32_t)p.np * 16u;
+    bool ok = true;
+    int issued = 0, loaded = ns < STAGES - 1 ? ns : STAGES - 1, landed = 0;
+    for (int s = 0; s < ns; s++) {
+        // the stage of slice s - 1 was read by every thread before the last barrier
+        if (tid == 0 && s + STAGES - 1 < ns) load(s + STAGES - 1);
+        loaded = s + STAGES - 1 < ns ? s + STAGES : loaded;
+        const int b = s & 1;
+        bool w = tc::mbar_wait_bounded(&full[s % STAGES], (uint32_t)(s / STAGES) & 1u, kPolls);
+        if (w && s >= 2)   // operand buffer b was last read by the MMAs of slice s - 2
+            w = tc::mbar_wait_bounded(&done[b], ((s - 2) >> 1) & 1, kPolls);
+        if (__syncthreads_or(!w)) {
+            ok = false;
+            break;
+        }
+        landed = s + 1;
+        uint8_t *op = ops + b * opb;
+        split_slice(p, smem + (s % STAGES) * rawb, op);
+        tc::fence_smem_for_async();
+        __syncthreads();
+        if (tid == 0) {
+            tc::fence_after_sync();
+            const uint32_t a_hi = tc::smem_addr(op), a_lo = a_hi + kARaw, b_hi = a_hi + 2 * kARaw,
+                           b_lo = b_hi + (uint32_t)p.np * 64u;
+#pragma unroll
+            for (int kk = 0; kk < kKS / 8; kk++) {   // K = 8 tf32 = two 16-byte chunks per MMA
+                const uint32_t oa = (uint32_t)kk * 2u * 2048u, ob = (uint32_t)kk * 2u * b_lbo;
+                const uint64_t dah = tc::smem_desc(a_hi + oa, 2048, 128), dal = tc::smem_desc(a_lo + oa, 2048, 128);
+                const uint64_t dbh = tc::smem_desc(b_hi + ob, b_lbo, 128), dbl = tc::smem_desc(b_lo + ob, b_lbo, 128);
+                tc::mma_tf32(tmem, dal, dbh, idesc, (s > 0 || kk > 0) ? 1u : 0u);
+                tc::mma_tf32(tmem, dah, dbl, idesc, 1u);
+                tc::mma_tf32(tmem, dah, dbh, idesc, 1u);
+            }
+            tc::commit(&done[b]);
+        }
+        issued = s + 1;
+    }
+    if (ok) {
+        const int last = ns - 1;
+        const bool w = tc::mbar_wait_bounded(&done[last & 1], (last >> 1) & 1, kPolls);
+        ok = !__syncthreads_or(!w);
+    }
+    if (!ok) {
+        if (tid == 0) {
+            atomicAdd(&g_linear_tc_timeouts, 1);
+            for (int j = landed; j < loaded; j++)   // TMA loads in flight land before the CTA exits
+                tc::mbar_wait_bounded(&full[j % STAGES], (uint32_t)(j / STAGES) & 1u, kPolls);
+            if (issued > 0)   // and the MMAs in flight end before the TMEM is freed (bounded)
+                tc::mbar_wait_bounded(&done[(issued - 1) & 1], ((issued - 1) >> 1) & 1, kPolls);
+        }
+        tc::fence_before_sync();
+        __syncthreads();
+        tc::fence_after_sync();
+        if (warp == 0) tc::tmem_dealloc(tmem, p.tmem_cols);
+        return;
+    }
+    tc::fence_after_sync();
+
+    const int q = warp & 3;
+    const int64_t row = m0 + q * 32 + lane;
+    const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
+    const int nv = min(p.ncta, p.N - n0);
+    for (int g = warp >> 2; g * 32 < nv; g += 2) {
+        float v[32];
+        tc::ld32(taddr + (uint32_t)(g * 32), v);
+        if (row < p.M) {
+            const int c0 = g * 32;
+            const int cnt = min(32, nv - c0);
+            float *dst = p.C + row * p.N + n0 + c0;
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+                if (j < cnt) {
+                    float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                    if (p.bias) {
+                        const float4 bb = __ldg(reinterpret_cast<const float4 *>(p.bias + n0 + c0 + j));
+                        o.x += bb.x;
+                        o.y += bb.y;
+                        o.z += bb.z;
+                        o.w += bb.w;
+                    }
+                    *reinterpret_cast<float4 *>(dst + j) = o;
+                }
+            }
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    if (warp == 0) tc::tmem_dealloc(tmem, p.tmem_cols);
+}
+
+// ------------------------------------------------------------------------------------
+// Host side
+// ------------------------------------------------------------------------------------
+using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encoder() {
+    static EncodeTiled fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(p);
+    });
+    return fn;
+}
+
+// The encoder is a driver call: it needs the device's primary context current in the calling
+// thread, which a thread that has only made runtime calls (autograd's device threads) may lack.
+void bind_primary_context() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaSetDevice(dev);
+}
+
+// Row-major fp32 [rows, cols] (cols % 4 == 0) as (4 elements, rows, cols / 4 chunks); box
+// (4, box_rows, 4): 16 columns of box_rows rows, landing chunk-major (core-matrix layout).
+int chunk_map(CUtensorMap *m, const float *base, int64_t rows, int cols, int box_rows) {
+    EncodeTiled enc = encoder();
+    if (!enc) return NGT_ERR_CUDA;
+    const cuuint64_t dims[3] = {4, (cuuint64_t)rows, (cuuint64_t)(cols / 4)};
+    const cuuint64_t strides[2] = {(cuuint64_t)cols * 4, 16};
+    const cuuint32_t box[3] = {4, (cuuint32_t)box_rows, (cuuint32_t)(kKS / 4)};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? NGT_OK : NGT_ERR_CUDA;
+}
+
+// Row-major fp32 [rows, cols] as a plain 2-D map; box (box_cols, 16 rows).
+int plain_map(CUtensorMap *m, const float *base, int64_t rows, int cols, int box_cols) {
+    EncodeTiled enc = encoder();
+    if (!enc) return NGT_ERR_CUDA;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * 4};
+    const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)kKS};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? NGT_OK : NGT_ERR_CUDA;
+}
+
+int sm_count_tc() {
+    static int cached[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && cached[dev] > 0) return cached[dev];
+    int n = 148;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+    if (dev >= 0 && dev < 64) cached[dev] = n;
+    return n;
+}
+
+uint32_t tmem_cols_for(int np) {
+    uint32_t c = 32;
+    while (c < (uint32_t)np) c <<= 1;
+    return c;
+}
+
+struct TcPlan {
+    int split, stages;
+};
+
+// Column split and raw-stage depth: all CTAs resident in one wave where possible (two CTAs per
+// SM need <= 113 KiB of shared memory each), deeper staging first.
+TcPlan tc_plan(int64_t gm, int N, int sms) {
+    const int splits[2] = {(N >= 64 && N % 32 == 0 && gm < sms) ? 2 : 1, 1};
+    for (int split : splits) {
+        const int np = ((N + split - 1) / split + 15) / 16 * 16;
+        for (int stages = 4; stages >= 3; stages--) {
+            const uint32_t per_sm = kSmemPerSm / (smem_bytes(np, stages) + 1024);
+            if (per_sm >= 1 && gm * split <= (int64_t)sms * (per_sm > 2 ? 2 : per_sm)) return {split, stages};
+        }
+    }
+    return {1, 3};
+}
+
+template <int STAGES>
+int launch_stages(const CUtensorMap &ma, const CUtensorMap &mw, const TcArgs &p, dim3 grid, cudaStream_t st) {
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+        if (cudaFuncSetAttribute(linear_tc_kernel<STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem_bytes(kMaxN, STAGES)) != cudaSuccess)
+            return NGT_ERR_CUDA;
+        attr_set[dev] = true;
+    }
+    linear_tc_kernel<STAGES><<<grid, kThreads, smem_bytes(p.np, STAGES), st>>>(ma, mw, p);
+    NGT_CHECK_LAUNCH();
+    return NGT_OK;
+}
+
+}  // namespace
+
+bool linear_tc_supported(int K, int N) { return K > 0 && N > 0 && N <= kMaxN && K % 4 == 0 && N % 4 == 0; }
+
+int launch_linear_tc(int64_t M, int K, int N, const float *A, const float *W, bool trans_w, const float *bias,
+                     float *C, cudaStream_t st) {
+    const int64_t gm = (M + kM - 1) / kM;
+    if (M > 0x7fffffffLL - kM) return NGT_ERR_UNSUPPORTED;   // TMA row coordinates are 32-bit signed
+    const TcPlan plan = tc_plan(gm, N, sm_count_tc());
+    TcArgs p;
+    p.M = M;
+    p.K = K;
+    p.N = N;
+    p.ncta = (N + plan.split - 1) / plan.split;
+    p.np = (p.ncta + 15) / 16 * 16;
+    p.tmem_cols = tmem_cols_for(p.np);
+    p.trans = trans_w ? 1 : 0;
+    p.bias = bias;
+    p.C = C;
+    CUtensorMap ma, mw;
+    bind_primary_context();
+    int rc = chunk_map(&ma, A, M, K, kM);
+    if (rc == NGT_OK) rc = trans_w ? plain_map(&mw, W, K, N, p.np) : chunk_map(&mw, W, N, K, p.np);
+    if (rc != NGT_OK) return rc;
+    const dim3 grid((unsigned)gm, (unsigned)plan.split);
+    return plan.stages == 4 ? launch_stages<4>(ma, mw, p, grid, st) : launch_stages<3>(ma, mw, p, grid, st);
+}
+
+int linear_tc_timeouts(int *count) {
+    if (cudaMemcpyFromSymbol(count, g_linear_tc_timeouts, sizeof(int)) != cudaSuccess) return NGT_ERR_CUDA;
+    return NGT_OK;
+}
+
+}  // namespace ngt

@@ -108,3 +108,17 @@ def test_weight_grads_on_side_stream_match(cuda):
     for g in grads[1:]:
         for a, b in zip(g, grads[0]):
             assert torch.equal(a, b)
+
+
+def test_tensor_core_path_reports_no_timeouts(cuda):
+    """The split-TF32 tcgen05 kernel (both dimensions <= 256) bounds its waits and counts any that
+    run out; a normal forward + backward leaves the count at zero."""
+    from neutrongt_b200 import _lib
+    from neutrongt_b200.layers import Linear
+    lin = Linear(128, 40).cuda()
+    x = torch.randn(777, 128, device="cuda", requires_grad=True)
+    lin(x).sum().backward()
+    torch.cuda.synchronize()
+    n = ctypes.c_int32(-1)
+    assert _lib.lib().ngt_linear_status(ctypes.byref(n)) == 0
+    assert n.value == 0
