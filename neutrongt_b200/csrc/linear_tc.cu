@@ -18,7 +18,7 @@
 // buffer's mbarrier.  TMA writes through the async proxy, so the threads' proxy fence before the
 // MMAs waits only for their own split stores, never for loads in flight.  The epilogue reads the
 // accumulator with tcgen05.ld (warp w: lanes 32 (w % 4).., column groups alternating between
-// w < 4 and w >= 4), adds the bias and stores fp32 rows.
+// w < 4 and w >= 4) into a shared-memory tile, then stores whole rows (coalesced) with the bias.
 //
 // Every wait is bounded; a timeout is counted in a device word (ngt_linear_status), the CTA waits
 // (bounded) for its MMAs in flight, frees its TMEM and returns without storing.
@@ -210,32 +210,37 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     tc::fence_after_sync();
 
+    // Epilogue: accumulator -> shared tile [128 rows][ldt floats] (the raw stages and operand
+    // buffers are all consumed; ldt = 32 k + 4, so rows sit 16 bytes apart modulo 128 and a
+    // quarter-warp's 16-byte stores hit distinct banks), then coalesced row stores with the bias.
     const int q = warp & 3;
-    const int64_t row = m0 + q * 32 + lane;
-    const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
     const int nv = min(p.ncta, p.N - n0);
-    for (int g = warp >> 2; g * 32 < nv; g += 2) {
+    const int ngrp = (nv + 31) / 32;
+    const int ldt = ngrp * 32 + 4;
+    float *tile = reinterpret_cast<float *>(smem);
+    const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
+    for (int g = warp >> 2; g < ngrp; g += 2) {
         float v[32];
         tc::ld32(taddr + (uint32_t)(g * 32), v);
-        if (row < p.M) {
-            const int c0 = g * 32;
-            const int cnt = min(32, nv - c0);
-            float *dst = p.C + row * p.N + n0 + c0;
+        float4 *dst = reinterpret_cast<float4 *>(tile + (q * 32 + lane) * ldt + g * 32);
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-                if (j < cnt) {
-                    float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-                    if (p.bias) {
-                        const float4 bb = __ldg(reinterpret_cast<const float4 *>(p.bias + n0 + c0 + j));
-                        o.x += bb.x;
-                        o.y += bb.y;
-                        o.z += bb.z;
-                        o.w += bb.w;
-                    }
-                    *reinterpret_cast<float4 *>(dst + j) = o;
-                }
-            }
+        for (int j = 0; j < 8; j++) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    const int vpr = nv / 4;   // 16-byte vectors per output row (N % 4 == 0)
+    const int rows_here = (int)(p.M - m0 < kM ? p.M - m0 : kM);
+    for (int i = tid; i < rows_here * vpr; i += kThreads) {
+        const int rr = i / vpr, c = (i - rr * vpr) * 4;
+        float4 o = *reinterpret_cast<const float4 *>(tile + rr * ldt + c);
+        if (p.bias) {
+            const float4 bb = __ldg(reinterpret_cast<const float4 *>(p.bias + n0 + c));
+            o.x += bb.x;
+            o.y += bb.y;
+            o.z += bb.z;
+            o.w += bb.w;
         }
+        *reinterpret_cast<float4 *>(p.C + (m0 + rr) * p.N + n0 + c) = o;
     }
     tc::fence_before_sync();
     __syncthreads();
@@ -321,13 +326,13 @@ struct TcPlan {
     int split, stages;
 };
 
-// Column split and raw-stage depth: all CTAs resident in one wave where possible (two CTAs per
-// SM need <= 113 KiB of shared memory each), deeper staging first.
+// Column split and raw-stage depth (3..5 slices; STAGES - 1 in flight): all CTAs resident in one
+// wave where possible (two CTAs per SM need <= 113 KiB of shared memory each), deeper first.
 TcPlan tc_plan(int64_t gm, int N, int sms) {
     const int splits[2] = {(N >= 64 && N % 32 == 0 && gm < sms) ? 2 : 1, 1};
     for (int split : splits) {
         const int np = ((N + split - 1) / split + 15) / 16 * 16;
-        for (int stages = 4; stages >= 3; stages--) {
+        for (int stages = 5; stages >= 3; stages--) {
             const uint32_t per_sm = kSmemPerSm / (smem_bytes(np, stages) + 1024);
             if (per_sm >= 1 && gm * split <= (int64_t)sms * (per_sm > 2 ? 2 : per_sm)) return {split, stages};
         }
@@ -376,6 +381,10 @@ int launch_linear_tc(int64_t M, int K, int N, const float *A, const float *W, bo
     if (rc == NGT_OK) rc = trans_w ? plain_map(&mw, W, K, N, p.np) : chunk_map(&mw, W, N, K, p.np);
     if (rc != NGT_OK) return rc;
     const dim3 grid((unsigned)gm, (unsigned)plan.split);
+    // the epilogue's output tile reuses the stages and operand buffers
+    if ((size_t)kM * (((p.ncta + 31) / 32) * 32 + 4) * 4 > (size_t)plan.stages * raw_bytes(p.np) + 2 * op_bytes(p.np))
+        return NGT_ERR_UNSUPPORTED;
+    if (plan.stages == 5) return launch_stages<5>(ma, mw, p, grid, st);
     return plan.stages == 4 ? launch_stages<4>(ma, mw, p, grid, st) : launch_stages<3>(ma, mw, p, grid, st);
 }
 
