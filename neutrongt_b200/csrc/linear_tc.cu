@@ -9,13 +9,13 @@
 //
 // Tiling: one CTA = 128 rows (the 128 TMEM lanes, MMA M = 128) x `ncta` output columns (MMA N,
 // padded to a multiple of 16, <= 256), the reduction dimension streamed in slices of 16 elements.
-// Thread 0 keeps STAGES - 1 slices in flight with TMA: A through a 3-D tensor map (4 elements,
-// rows, 16-byte chunks) whose box lands in the no-swizzle K-major core-matrix layout (row r,
-// chunk c at c * rows * 16 + r * 16); the forward's weight the same way; the input grad's weight
-// (W [out, in], reduced over `out`) as plain row-major [16 k][np n] tiles, transposed by the
-// threads.  All 256 threads split a landed slice into hi / lo operand buffers (two, alternating)
-// in the same core-matrix layout; thread 0 issues the slice's 6 MMAs and commits them to the
-// buffer's mbarrier.  TMA writes through the async proxy, so the threads' proxy fence before the
+// Thread 0 keeps STAGES - 1 slices in flight with 2-D TMA boxes of 64-byte rows: A as [128 rows]
+// [16], the forward's weight as [np rows][16], the input grad's weight (W [out, in], reduced over
+// `out`) as [16 k][np n], transposed by the threads.  All 256 threads split a landed slice into
+// hi / lo operand buffers (two, alternating) in the no-swizzle K-major core-matrix layout: row r,
+// 16-byte chunk c at c * LBO + r * 16 with LBO = rows * 16 + 32, so the eight 16-byte stores of a
+// quarter-warp (two rows x four chunks) hit distinct banks.  Thread 0 issues the slice's 6 MMAs
+// and commits them to the buffer's mbarrier.  TMA writes through the async proxy, so the threads' proxy fence before the
 // MMAs waits only for their own split stores, never for loads in flight.  The epilogue reads the
 // accumulator with tcgen05.ld (warp w: lanes 32 (w % 4).., column groups alternating between
 // w < 4 and w >= 4) into a shared-memory tile, then stores whole rows (coalesced) with the bias.
@@ -60,7 +60,10 @@ struct TcArgs {
 // Shared memory: STAGES raw slices (A, then B), two operand buffers (A hi, A lo, B hi, B lo),
 // then the mbarriers (STAGES "slice landed", 2 "MMAs done") and the TMEM address.
 __host__ __device__ constexpr uint32_t raw_bytes(int np) { return kARaw + (uint32_t)np * 64u; }
-__host__ __device__ constexpr uint32_t op_bytes(int np) { return 2 * kARaw + 2 * (uint32_t)np * 64u; }
+// Operand tiles: K-chunk stride (LBO) rows * 16 + 32 bytes; a tile spans 3 LBO + rows * 16 bytes.
+__host__ __device__ constexpr uint32_t op_lbo(int rows) { return (uint32_t)rows * 16u + 32u; }
+__host__ __device__ constexpr uint32_t op_tile(int rows) { return 3 * op_lbo(rows) + (uint32_t)rows * 16u; }
+__host__ __device__ constexpr uint32_t op_bytes(int np) { return 2 * op_tile(kM) + 2 * op_tile(np); }
 __host__ __device__ constexpr uint32_t smem_bytes(int np, int stages) {
     return (uint32_t)stages * raw_bytes(np) + 2 * op_bytes(np) + 8 * (uint32_t)stages + 32;
 }
@@ -85,28 +88,32 @@ __device__ __forceinline__ void split_store(float4 v, uint8_t *hi, uint8_t *lo) 
     *reinterpret_cast<float4 *>(lo) = l;
 }
 
-// Splits a landed slice into operand buffer `op`.  Chunk (row r, 16-byte chunk c) sits at
-// c * rows * 16 + r * 16 in raw and operand tiles alike; consecutive threads take consecutive
-// rows, so every access is conflict-free.
+// Splits a landed slice into operand buffer `op`.  Raw rows are 64 bytes (item idx = row idx / 4,
+// chunk idx % 4, at idx * 16: consecutive threads read consecutive bytes); operand chunk (r, c)
+// goes to c * LBO + r * 16.
 __device__ __forceinline__ void split_slice(const TcArgs &p, const uint8_t *raw, uint8_t *op) {
     const int tid = threadIdx.x;
     const uint8_t *rb = raw + kARaw;
-    uint8_t *a_hi = op, *a_lo = op + kARaw, *b_hi = op + 2 * kARaw, *b_lo = b_hi + (uint32_t)p.np * 64u;
+    const uint32_t lba = op_lbo(kM), lbb = op_lbo(p.np);
+    uint8_t *a_hi = op, *a_lo = op + op_tile(kM), *b_hi = op + 2 * op_tile(kM), *b_lo = b_hi + op_tile(p.np);
 #pragma unroll
     for (int i = 0; i < 2; i++) {
-        const uint32_t o = (uint32_t)(tid + i * kThreads) * 16u;   // (c, r) = (idx / 128, idx % 128)
-        split_store(*reinterpret_cast<const float4 *>(raw + o), a_hi + o, a_lo + o);
+        const int idx = tid + i * kThreads;
+        const uint32_t o = (uint32_t)(idx & 3) * lba + (uint32_t)(idx >> 2) * 16u;
+        split_store(*reinterpret_cast<const float4 *>(raw + idx * 16), a_hi + o, a_lo + o);
     }
     const int items = p.np * 4;
     for (int idx = tid; idx < items; idx += kThreads) {
-        const uint32_t o = (uint32_t)idx * 16u;                    // (c, n) = (idx / np, idx % np)
         float4 v;
+        uint32_t o;
         if (!p.trans) {
-            v = *reinterpret_cast<const float4 *>(rb + o);
+            v = *reinterpret_cast<const float4 *>(rb + idx * 16);
+            o = (uint32_t)(idx & 3) * lbb + (uint32_t)(idx >> 2) * 16u;
         } else {   // raw row-major [16 k][np n]: column n, rows 4c .. 4c + 3
             const int n = idx % p.np, c = idx / p.np;
             const float *col = reinterpret_cast<const float *>(rb) + (4 * c) * p.np + n;
             v = make_float4(col[0], col[p.np], col[2 * p.np], col[3 * p.np]);
+            o = (uint32_t)c * lbb + (uint32_t)n * 16u;
         }
         split_store(v, b_hi + o, b_lo + o);
     }
@@ -131,9 +138,9 @@ __global__ void __launch_bounds__(kThreads, 2)
         uint8_t *raw = smem + (j % STAGES) * rawb;
         uint64_t *bar = &full[j % STAGES];
         tc::mbar_arrive_expect_tx(bar, rawb);
-        tc::tma_load_3d(raw, &tm_a, 0, (int)m0, j * (kKS / 4), bar);
+        tc::tma_load_2d(raw, &tm_a, j * kKS, (int)m0, bar);
         if (!p.trans)
-            tc::tma_load_3d(raw + kARaw, &tm_w, 0, n0, j * (kKS / 4), bar);
+            tc::tma_load_2d(raw + kARaw, &tm_w, j * kKS, n0, bar);
         else
             tc::tma_load_2d(raw + kARaw, &tm_w, n0, j * kKS, bar);
     };
@@ -152,7 +159,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     const uint32_t tmem = *slot;
 
     const uint32_t idesc = tc::idesc_tf32(kM, p.np);
-    const uint32_t b_lbo = (uint32_t)p.np * 16u;
+    const uint32_t a_lbo = op_lbo(kM), b_lbo = op_lbo(p.np);
     bool ok = true;
     int issued = 0, loaded = ns < STAGES - 1 ? ns : STAGES - 1, landed = 0;
     for (int s = 0; s < ns; s++) {
@@ -174,12 +181,12 @@ __global__ void __launch_bounds__(kThreads, 2)
         __syncthreads();
         if (tid == 0) {
             tc::fence_after_sync();
-            const uint32_t a_hi = tc::smem_addr(op), a_lo = a_hi + kARaw, b_hi = a_hi + 2 * kARaw,
-                           b_lo = b_hi + (uint32_t)p.np * 64u;
+            const uint32_t a_hi = tc::smem_addr(op), a_lo = a_hi + op_tile(kM), b_hi = a_hi + 2 * op_tile(kM),
+                           b_lo = b_hi + op_tile(p.np);
 #pragma unroll
             for (int kk = 0; kk < kKS / 8; kk++) {   // K = 8 tf32 = two 16-byte chunks per MMA
-                const uint32_t oa = (uint32_t)kk * 2u * 2048u, ob = (uint32_t)kk * 2u * b_lbo;
-                const uint64_t dah = tc::smem_desc(a_hi + oa, 2048, 128), dal = tc::smem_desc(a_lo + oa, 2048, 128);
+                const uint32_t oa = (uint32_t)kk * 2u * a_lbo, ob = (uint32_t)kk * 2u * b_lbo;
+                const uint64_t dah = tc::smem_desc(a_hi + oa, a_lbo, 128), dal = tc::smem_desc(a_lo + oa, a_lbo, 128);
                 const uint64_t dbh = tc::smem_desc(b_hi + ob, b_lbo, 128), dbl = tc::smem_desc(b_lo + ob, b_lbo, 128);
                 tc::mma_tf32(tmem, dal, dbh, idesc, (s > 0 || kk > 0) ? 1u : 0u);
                 tc::mma_tf32(tmem, dah, dbl, idesc, 1u);
@@ -275,28 +282,13 @@ void bind_primary_context() {
     if (cudaGetDevice(&dev) == cudaSuccess) cudaSetDevice(dev);
 }
 
-// Row-major fp32 [rows, cols] (cols % 4 == 0) as (4 elements, rows, cols / 4 chunks); box
-// (4, box_rows, 4): 16 columns of box_rows rows, landing chunk-major (core-matrix layout).
-int chunk_map(CUtensorMap *m, const float *base, int64_t rows, int cols, int box_rows) {
-    EncodeTiled enc = encoder();
-    if (!enc) return NGT_ERR_CUDA;
-    const cuuint64_t dims[3] = {4, (cuuint64_t)rows, (cuuint64_t)(cols / 4)};
-    const cuuint64_t strides[2] = {(cuuint64_t)cols * 4, 16};
-    const cuuint32_t box[3] = {4, (cuuint32_t)box_rows, (cuuint32_t)(kKS / 4)};
-    const cuuint32_t estr[3] = {1, 1, 1};
-    const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims, strides, box, estr,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                           CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS ? NGT_OK : NGT_ERR_CUDA;
-}
-
-// Row-major fp32 [rows, cols] as a plain 2-D map; box (box_cols, 16 rows).
-int plain_map(CUtensorMap *m, const float *base, int64_t rows, int cols, int box_cols) {
+// Row-major fp32 [rows, cols] (cols % 4 == 0) as a 2-D map with box (box_cols, box_rows).
+int map2d(CUtensorMap *m, const float *base, int64_t rows, int cols, int box_cols, int box_rows) {
     EncodeTiled enc = encoder();
     if (!enc) return NGT_ERR_CUDA;
     const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)cols * 4};
-    const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)kKS};
+    const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -377,8 +369,9 @@ int launch_linear_tc(int64_t M, int K, int N, const float *A, const float *W, bo
     p.C = C;
     CUtensorMap ma, mw;
     bind_primary_context();
-    int rc = chunk_map(&ma, A, M, K, kM);
-    if (rc == NGT_OK) rc = trans_w ? plain_map(&mw, W, K, N, p.np) : chunk_map(&mw, W, N, K, p.np);
+    int rc = map2d(&ma, A, M, K, kKS, kM);                     // [128 rows][16] boxes
+    if (rc == NGT_OK)                                            // [16 k][np n] or [np rows][16]
+        rc = trans_w ? map2d(&mw, W, K, N, p.np, kKS) : map2d(&mw, W, N, K, kKS, p.np);
     if (rc != NGT_OK) return rc;
     const dim3 grid((unsigned)gm, (unsigned)plan.split);
     // the epilogue's output tile reuses the stages and operand buffers
