@@ -41,7 +41,8 @@ namespace {
 
 constexpr int kM = 128;                        // rows per CTA = TMEM lanes = MMA M
 constexpr int kKS = 16;                        // reduction elements per slice (4 chunks of 16 B)
-constexpr int kThreads = 256;
+constexpr int kThreads = 256;                  // splitter / epilogue threads (warps 0-7)
+constexpr int kThreadsAll = kThreads + 32;     // + warp 8: lane 0 issues the TMA loads and MMAs
 constexpr uint32_t kARaw = kM * kKS * 4;       // bytes of one A slice (raw, hi or lo): 8 KiB
 constexpr uint32_t kPolls = 1u << 26;
 constexpr int kMaxN = 256;
@@ -58,14 +59,14 @@ struct TcArgs {
 };
 
 // Shared memory: STAGES raw slices (A, then B), two operand buffers (A hi, A lo, B hi, B lo),
-// then the mbarriers (STAGES "slice landed", 2 "MMAs done") and the TMEM address.
+// then the mbarriers (STAGES "slice landed", 2 "MMAs done", 2 "operands split") and the TMEM address.
 __host__ __device__ constexpr uint32_t raw_bytes(int np) { return kARaw + (uint32_t)np * 64u; }
 // Operand tiles: K-chunk stride (LBO) rows * 16 + 32 bytes; a tile spans 3 LBO + rows * 16 bytes.
 __host__ __device__ constexpr uint32_t op_lbo(int rows) { return (uint32_t)rows * 16u + 32u; }
 __host__ __device__ constexpr uint32_t op_tile(int rows) { return 3 * op_lbo(rows) + (uint32_t)rows * 16u; }
 __host__ __device__ constexpr uint32_t op_bytes(int np) { return 2 * op_tile(kM) + 2 * op_tile(np); }
 __host__ __device__ constexpr uint32_t smem_bytes(int np, int stages) {
-    return (uint32_t)stages * raw_bytes(np) + 2 * op_bytes(np) + 8 * (uint32_t)stages + 32;
+    return (uint32_t)stages * raw_bytes(np) + 2 * op_bytes(np) + 8 * (uint32_t)stages + 48;
 }
 
 // hi = x rounded to the nearest tf32 (ties away from zero; 10 mantissa bits), lo = x - hi (exact);
@@ -120,7 +121,7 @@ __device__ __forceinline__ void split_slice(const TcArgs &p, const uint8_t *raw,
 }
 
 template <int STAGES>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreadsAll, 2)
     linear_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
                      const TcArgs p) {
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -129,12 +130,14 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int n0 = blockIdx.y * p.ncta;
     const uint32_t rawb = raw_bytes(p.np), opb = op_bytes(p.np);
     uint8_t *ops = smem + STAGES * rawb;
-    uint64_t *full = reinterpret_cast<uint64_t *>(ops + 2 * opb);
-    uint64_t *done = full + STAGES;
-    uint32_t *slot = reinterpret_cast<uint32_t *>(done + 2);
+    uint64_t *full = reinterpret_cast<uint64_t *>(ops + 2 * opb);   // [STAGES] slice landed (TMA bytes)
+    uint64_t *done = full + STAGES;                                  // [2] MMAs of an operand buffer done
+    uint64_t *ready = done + 2;                                      // [2] operand buffer split (256 arrivals)
+    uint32_t *slot = reinterpret_cast<uint32_t *>(ready + 2);
     const int ns = (p.K + kKS - 1) / kKS;
+    const bool producer = tid == kThreads;                           // warp 8, lane 0
 
-    auto load = [&](int j) {   // thread 0: slice j into stage j % STAGES
+    auto load = [&](int j) {   // slice j into stage j % STAGES
         uint8_t *raw = smem + (j % STAGES) * rawb;
         uint64_t *bar = &full[j % STAGES];
         tc::mbar_arrive_expect_tx(bar, rawb);
@@ -145,12 +148,15 @@ __global__ void __launch_bounds__(kThreads, 2)
             tc::tma_load_2d(raw + kARaw, &tm_w, n0, j * kKS, bar);
     };
 
-    if (tid == 0) {
+    int loaded = 0, issued = 0;   // producer's counts
+    if (producer) {
         for (int st = 0; st < STAGES; st++) tc::mbar_init(&full[st], 1);
-        tc::mbar_init(&done[0], 1);
-        tc::mbar_init(&done[1], 1);
+        for (int b = 0; b < 2; b++) {
+            tc::mbar_init(&done[b], 1);
+            tc::mbar_init(&ready[b], kThreads);
+        }
         tc::mbar_init_fence();
-        for (int j = 0; j < STAGES - 1 && j < ns; j++) load(j);
+        for (; loaded < STAGES - 1 && loaded < ns; loaded++) load(loaded);
     }
     if (warp == 0) tc::tmem_alloc(slot, p.tmem_cols);
     tc::fence_before_sync();
@@ -158,31 +164,21 @@ __global__ void __launch_bounds__(kThreads, 2)
     tc::fence_after_sync();
     const uint32_t tmem = *slot;
 
-    const uint32_t idesc = tc::idesc_tf32(kM, p.np);
-    const uint32_t a_lbo = op_lbo(kM), b_lbo = op_lbo(p.np);
     bool ok = true;
-    int issued = 0, loaded = ns < STAGES - 1 ? ns : STAGES - 1, landed = 0;
-    for (int s = 0; s < ns; s++) {
-        // the stage of slice s - 1 was read by every thread before the last barrier
-        if (tid == 0 && s + STAGES - 1 < ns) load(s + STAGES - 1);
-        loaded = s + STAGES - 1 < ns ? s + STAGES : loaded;
-        const int b = s & 1;
-        bool w = tc::mbar_wait_bounded(&full[s % STAGES], (uint32_t)(s / STAGES) & 1u, kPolls);
-        if (w && s >= 2)   // operand buffer b was last read by the MMAs of slice s - 2
-            w = tc::mbar_wait_bounded(&done[b], ((s - 2) >> 1) & 1, kPolls);
-        if (__syncthreads_or(!w)) {
-            ok = false;
-            break;
-        }
-        landed = s + 1;
-        uint8_t *op = ops + b * opb;
-        split_slice(p, smem + (s % STAGES) * rawb, op);
-        tc::fence_smem_for_async();
-        __syncthreads();
-        if (tid == 0) {
+    if (producer) {
+        // Slice s - 1's stage is free once every splitter arrived on ready for slice s - 1 (waited
+        // below in the previous iteration), so slice s + STAGES - 1 can take it.
+        const uint32_t idesc = tc::idesc_tf32(kM, p.np);
+        const uint32_t a_lbo = op_lbo(kM), b_lbo = op_lbo(p.np);
+        for (int s = 0; s < ns; s++) {
+            if (loaded < ns) load(loaded++);
+            if (!tc::mbar_wait_bounded(&ready[s & 1], (uint32_t)(s >> 1) & 1u, kPolls)) {
+                ok = false;
+                break;
+            }
             tc::fence_after_sync();
-            const uint32_t a_hi = tc::smem_addr(op), a_lo = a_hi + op_tile(kM), b_hi = a_hi + 2 * op_tile(kM),
-                           b_lo = b_hi + op_tile(p.np);
+            const uint32_t a_hi = tc::smem_addr(ops + (s & 1) * opb), a_lo = a_hi + op_tile(kM),
+                           b_hi = a_hi + 2 * op_tile(kM), b_lo = b_hi + op_tile(p.np);
 #pragma unroll
             for (int kk = 0; kk < kKS / 8; kk++) {   // K = 8 tf32 = two 16-byte chunks per MMA
                 const uint32_t oa = (uint32_t)kk * 2u * a_lbo, ob = (uint32_t)kk * 2u * b_lbo;
@@ -192,22 +188,36 @@ __global__ void __launch_bounds__(kThreads, 2)
                 tc::mma_tf32(tmem, dah, dbl, idesc, 1u);
                 tc::mma_tf32(tmem, dah, dbh, idesc, 1u);
             }
-            tc::commit(&done[b]);
+            tc::commit(&done[s & 1]);
+            issued = s + 1;
         }
-        issued = s + 1;
+    } else if (tid < kThreads) {   // splitters: no CTA-wide barrier per slice
+        for (int s = 0; s < ns; s++) {
+            const int b = s & 1;
+            bool w = tc::mbar_wait_bounded(&full[s % STAGES], (uint32_t)(s / STAGES) & 1u, kPolls);
+            if (w && s >= 2)   // operand buffer b was last read by the MMAs of slice s - 2
+                w = tc::mbar_wait_bounded(&done[b], (uint32_t)((s - 2) >> 1) & 1u, kPolls);
+            if (!w) {
+                ok = false;
+                break;
+            }
+            split_slice(p, smem + (s % STAGES) * rawb, ops + b * opb);
+            tc::fence_smem_for_async();
+            tc::mbar_arrive(&ready[b]);
+        }
     }
-    if (ok) {
+    {
         const int last = ns - 1;
-        const bool w = tc::mbar_wait_bounded(&done[last & 1], (last >> 1) & 1, kPolls);
+        const bool w = ok && tc::mbar_wait_bounded(&done[last & 1], (uint32_t)(last >> 1) & 1u, kPolls);
         ok = !__syncthreads_or(!w);
     }
     if (!ok) {
-        if (tid == 0) {
+        if (producer) {
             atomicAdd(&g_linear_tc_timeouts, 1);
-            for (int j = landed; j < loaded; j++)   // TMA loads in flight land before the CTA exits
-                tc::mbar_wait_bounded(&full[j % STAGES], (uint32_t)(j / STAGES) & 1u, kPolls);
+            for (int j = loaded - (STAGES - 1) < 0 ? 0 : loaded - (STAGES - 1); j < loaded; j++)
+                tc::mbar_wait_bounded(&full[j % STAGES], (uint32_t)(j / STAGES) & 1u, kPolls);   // TMA in flight
             if (issued > 0)   // and the MMAs in flight end before the TMEM is freed (bounded)
-                tc::mbar_wait_bounded(&done[(issued - 1) & 1], ((issued - 1) >> 1) & 1, kPolls);
+                tc::mbar_wait_bounded(&done[(issued - 1) & 1], (uint32_t)((issued - 1) >> 1) & 1u, kPolls);
         }
         tc::fence_before_sync();
         __syncthreads();
@@ -226,7 +236,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int ldt = ngrp * 32 + 4;
     float *tile = reinterpret_cast<float *>(smem);
     const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
-    for (int g = warp >> 2; g < ngrp; g += 2) {
+    for (int g = warp >> 2; warp < kThreads / 32 && g < ngrp; g += 2) {
         float v[32];
         tc::ld32(taddr + (uint32_t)(g * 32), v);
         float4 *dst = reinterpret_cast<float4 *>(tile + (q * 32 + lane) * ldt + g * 32);
@@ -237,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     __syncthreads();
     const int vpr = nv / 4;   // 16-byte vectors per output row (N % 4 == 0)
     const int rows_here = (int)(p.M - m0 < kM ? p.M - m0 : kM);
-    for (int i = tid; i < rows_here * vpr; i += kThreads) {
+    for (int i = tid; i < rows_here * vpr; i += kThreadsAll) {
         const int rr = i / vpr, c = (i - rr * vpr) * 4;
         float4 o = *reinterpret_cast<const float4 *>(tile + rr * ldt + c);
         if (p.bias) {
@@ -343,7 +353,7 @@ int launch_stages(const CUtensorMap &ma, const CUtensorMap &mw, const TcArgs &p,
             return NGT_ERR_CUDA;
         attr_set[dev] = true;
     }
-    linear_tc_kernel<STAGES><<<grid, kThreads, smem_bytes(p.np, STAGES), st>>>(ma, mw, p);
+    linear_tc_kernel<STAGES><<<grid, kThreadsAll, smem_bytes(p.np, STAGES), st>>>(ma, mw, p);
     NGT_CHECK_LAUNCH();
     return NGT_OK;
 }
