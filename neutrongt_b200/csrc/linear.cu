@@ -1,4 +1,4 @@
-// fp32 Linear layers of the GT / Graphormer models on the CUDA cores (sm_100a):
+// fp32 Linear layers of the GT / Graphormer models: entry points, and the CUDA-core kernels (sm_100a):
 //   forward       y  = x W^T + b               x [rows, in], W [out, in], y [rows, out]
 //   input grad    dx = dy W                    dy [rows, out], dx [rows, in]
 //   weight grad   dW = dy^T x, db = sum dy     dW [out, in], db [out]

@@ -7,7 +7,9 @@
   sums of the weight / bias gradients in a fixed order);
 * `Linear` runs `ngt_linear_forward` (y = x W^T + b), `ngt_linear_backward_input` (dx = dy W) and
   `ngt_linear_backward_weight` (dW = dy^T x and db = column sums of dy, one pass, fixed-order
-  reduction): fp32 FFMA GEMMs sized to the SM count for the windows' thin shapes.
+  reduction).  With both dimensions <= 256 the forward and input grad run on the tcgen05 tensor
+  cores with split TF32 operands (fp32 precision, `csrc/linear_tc.cu`); the weight grad and wider
+  outputs are fp32 FFMA GEMMs sized to the SM count for the windows' thin shapes.
 
 torch's kernels for these ops take 15-60 us per call on the models' [~10^4, 32..256] fp32
 windows; these take a few.  Other devices, dtypes or shapes (features not a multiple of 4, a

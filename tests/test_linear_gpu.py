@@ -1,7 +1,9 @@
-"""fp32 Linear layers on csrc/linear.cu (forward, input grad, weight + bias grad) against torch.
+"""fp32 Linear layers (forward, input grad, weight + bias grad) against torch.
 
-Tolerance: relative (max|a-b| / max|b|) against an fp64 torch restatement, 1e-5 -- fp32 FFMA in a
-different summation order than cuBLAS; torch's own fp32 result is held to the same bound.
+Shapes with both dimensions <= 256 run the forward and input grad on the tensor cores with split
+TF32 operands (csrc/linear_tc.cu), the others on fp32 FFMA (csrc/linear.cu); the weight grad is FFMA.
+Tolerance: relative (max|a-b| / max|b|) against an fp64 torch restatement, 1e-5 -- fp32 precision
+in a different summation order than cuBLAS; torch's own fp32 result is held to the same bound.
 """
 import ctypes
 
