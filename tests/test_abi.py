@@ -62,6 +62,7 @@ def test_invalid_arguments_are_rejected_without_a_gpu():
     assert lib.ngt_linear_backward_input(4, 8, 260, *([None] * 3), None) == 2
     assert lib.ngt_linear_forward(4, 6, 8, *([None] * 4), None) == 1           # features % 4 != 0
     assert lib.ngt_linear_forward(0, 8, 8, *([None] * 4), None) == 0
+    assert lib.ngt_linear_status(None) == 1                                     # null output pointer
     # window construction: size queries; invalid arguments are refused before any launch
     assert _lib.size_query(lib.ngt_ppr_adjacency_workspace_size, 1000, 100) > 1000 * 4
     assert _lib.size_query(lib.ngt_halo_merge_workspace_size, 1000, 10, 50) >= 1000 * 4
