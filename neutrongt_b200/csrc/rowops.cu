@@ -17,7 +17,7 @@ namespace {
 
 constexpr int kRowThreads = 256;             // 8 warps, one row per warp
 constexpr int kColThreads = 256;             // column-sum blocks
-constexpr int kRowsPerPartial = 64;          // rows summed by one block of the column-sum kernels
+constexpr int kRowsPerPartial = 32;          // rows summed by one block of the column-sum kernels
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
