@@ -328,16 +328,16 @@ struct TcPlan {
     int split, stages;
 };
 
-// Column split and raw-stage depth (3..5 slices; STAGES - 1 in flight): all CTAs resident in one
-// wave where possible (two CTAs per SM need <= 113 KiB of shared memory each), deeper first.
+// Raw-stage depth (3..5 slices; STAGES - 1 in flight): all CTAs resident in one wave where possible
+// (two CTAs per SM need <= 113 KiB of shared memory each), deeper first.  One CTA covers all N
+// columns of its 128 rows: splitting the columns over two CTAs (so that 10^4-row windows fill more
+// SMs) measured equal or slower for every model shape — the block scheduler packs the halves two
+// per SM, and each half loads and splits the whole A tile again.
 TcPlan tc_plan(int64_t gm, int N, int sms) {
-    const int splits[2] = {(N >= 64 && N % 32 == 0 && gm < sms) ? 2 : 1, 1};
-    for (int split : splits) {
-        const int np = ((N + split - 1) / split + 15) / 16 * 16;
-        for (int stages = 5; stages >= 3; stages--) {
-            const uint32_t per_sm = kSmemPerSm / (smem_bytes(np, stages) + 1024);
-            if (per_sm >= 1 && gm * split <= (int64_t)sms * (per_sm > 2 ? 2 : per_sm)) return {split, stages};
-        }
+    const int np = (N + 15) / 16 * 16;
+    for (int stages = 5; stages >= 3; stages--) {
+        const uint32_t per_sm = kSmemPerSm / (smem_bytes(np, stages) + 1024);
+        if (per_sm >= 1 && gm <= (int64_t)sms * (per_sm > 2 ? 2 : per_sm)) return {1, stages};
     }
     return {1, 3};
 }
