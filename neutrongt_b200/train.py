@@ -50,6 +50,39 @@ class WindowState:
     local_spatial_pos_by_pid: list = field(default_factory=list)
 
 
+def broadcast_partitions(partitions, src: int = 0, group=None, device=None) -> list:
+    """The window node lists of rank `src` on every rank, by collective instead of files.
+
+    The reference's rank 0 writes one bundle file per rank (`window_state.py:296-311`:
+    `torch.save` of each rank's windows, a barrier, every rank `torch.load`s its own, a barrier,
+    rank 0 deletes the files).  Here the node lists travel in three broadcasts (window count,
+    lengths, the concatenated ids as int64) over the process group's backend, NCCL between GPUs
+    (`device` then a CUDA device) or gloo on the host; every rank then takes its own windows
+    (pid mod world_size) in `build_window_state`.  `partitions` is only read on `src`.
+    Returns CPU int64 tensors, in the source's order."""
+    import torch.distributed as dist
+    dev = torch.device("cpu") if device is None else torch.device(device)
+    rank = dist.get_rank(group)
+    count = torch.zeros(1, dtype=torch.long, device=dev)
+    if rank == src:
+        count.fill_(len(partitions))
+    dist.broadcast(count, src=src, group=group)
+    n = int(count.item())
+    lengths = torch.zeros(n, dtype=torch.long, device=dev)
+    if rank == src and n:
+        lengths.copy_(torch.tensor([int(p.numel()) for p in partitions], dtype=torch.long))
+    if n:
+        dist.broadcast(lengths, src=src, group=group)
+    sizes = lengths.cpu().tolist()
+    total = sum(sizes)
+    flat = torch.empty(total, dtype=torch.long, device=dev)
+    if rank == src and total:
+        flat.copy_(torch.cat([p.reshape(-1).to(torch.long).cpu() for p in partitions]))
+    if total:
+        dist.broadcast(flat, src=src, group=group)
+    return list(torch.split(flat.cpu(), sizes)) if n else []
+
+
 def build_window_state(rowptr, col, partitions, rank, world_size, feature, device, split_idx=None,
                        use_cache=True) -> WindowState:
     ids = list(range(rank, len(partitions), world_size))

@@ -80,3 +80,36 @@ def test_flat_gradients_are_views():
     assert all(p.grad.data_ptr() >= fg.flat.data_ptr() for p in model.parameters())
     fg.zero()
     assert all(float(p.grad.abs().sum()) == 0 for p in model.parameters())
+
+
+def _partitions():
+    g = torch.Generator().manual_seed(3)
+    return [torch.randperm(100, generator=g)[: 5 + 3 * i] for i in range(7)] + [torch.empty(0, dtype=torch.long)]
+
+
+def _bcast_worker(rank, world, port, results):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from neutrongt_b200.train import broadcast_partitions
+    got = broadcast_partitions(_partitions() if rank == 0 else None)
+    results[rank] = ([p.clone() for p in got], list(range(rank, len(got), world)))
+    results[f"empty{rank}"] = len(broadcast_partitions([] if rank == 0 else None))
+    dist.destroy_process_group()
+
+
+def test_window_node_lists_broadcast_from_rank_zero():
+    """The collective replacement of the reference's per-rank bundle files: every rank receives
+    rank 0's window node lists (order, lengths and ids, an empty window included) and owns
+    windows pid mod world_size of them."""
+    port = _free_port()
+    with mp.get_context("spawn").Manager() as m:
+        results = m.dict()
+        mp.spawn(_bcast_worker, args=(2, port, results), nprocs=2, join=True)
+        out = {k: results[k] for k in results.keys()}
+    expected = _partitions()
+    for r in range(2):
+        got, owned = out[r]
+        assert len(got) == len(expected)
+        assert all(torch.equal(a, b) and a.dtype == torch.long for a, b in zip(got, expected))
+        assert owned == list(range(r, 8, 2))
+        assert out[f"empty{r}"] == 0
