@@ -47,6 +47,8 @@ constexpr uint32_t kARaw = kM * kKS * 4;       // bytes of one A slice (raw, hi 
 constexpr uint32_t kPolls = 1u << 26;
 constexpr int kMaxN = 256;
 constexpr uint32_t kSmemPerSm = 233472;        // 228 KiB per SM, 1 KiB of it reserved per CTA
+constexpr uint32_t kSmemPerCta = 232448;       // 227 KiB: the most one CTA may request
+constexpr int kMaxStages = 8;
 
 struct TcArgs {
     int64_t M;
@@ -328,14 +330,14 @@ struct TcPlan {
     int split, stages;
 };
 
-// Raw-stage depth (3..5 slices; STAGES - 1 in flight): all CTAs resident in one wave where possible
+// Raw-stage depth (3..8 slices; STAGES - 1 in flight): all CTAs resident in one wave where possible
 // (two CTAs per SM need <= 113 KiB of shared memory each), deeper first.  One CTA covers all N
 // columns of its 128 rows: splitting the columns over two CTAs (so that 10^4-row windows fill more
 // SMs) measured equal or slower for every model shape — the block scheduler packs the halves two
 // per SM, and each half loads and splits the whole A tile again.
 TcPlan tc_plan(int64_t gm, int N, int sms) {
     const int np = (N + 15) / 16 * 16;
-    for (int stages = 5; stages >= 3; stages--) {
+    for (int stages = kMaxStages; stages >= 3; stages--) {
         const uint32_t per_sm = kSmemPerSm / (smem_bytes(np, stages) + 1024);
         if (per_sm >= 1 && gm <= (int64_t)sms * (per_sm > 2 ? 2 : per_sm)) return {1, stages};
     }
@@ -344,16 +346,18 @@ TcPlan tc_plan(int64_t gm, int N, int sms) {
 
 template <int STAGES>
 int launch_stages(const CUtensorMap &ma, const CUtensorMap &mw, const TcArgs &p, dim3 grid, cudaStream_t st) {
-    static bool attr_set[64] = {false};
+    static uint32_t attr_bytes[64] = {0};   // dynamic shared memory allowed so far, per device
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        if (cudaFuncSetAttribute(linear_tc_kernel<STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)smem_bytes(kMaxN, STAGES)) != cudaSuccess)
+    const uint32_t need = smem_bytes(p.np, STAGES);
+    if (need > kSmemPerCta) return NGT_ERR_UNSUPPORTED;
+    if (dev < 0 || dev >= 64 || attr_bytes[dev] < need) {
+        if (cudaFuncSetAttribute(linear_tc_kernel<STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need) !=
+            cudaSuccess)
             return NGT_ERR_CUDA;
-        attr_set[dev] = true;
+        if (dev >= 0 && dev < 64) attr_bytes[dev] = need;
     }
-    linear_tc_kernel<STAGES><<<grid, kThreadsAll, smem_bytes(p.np, STAGES), st>>>(ma, mw, p);
+    linear_tc_kernel<STAGES><<<grid, kThreadsAll, need, st>>>(ma, mw, p);
     NGT_CHECK_LAUNCH();
     return NGT_OK;
 }
@@ -387,8 +391,14 @@ int launch_linear_tc(int64_t M, int K, int N, const float *A, const float *W, bo
     // the epilogue's output tile reuses the stages and operand buffers
     if ((size_t)kM * (((p.ncta + 31) / 32) * 32 + 4) * 4 > (size_t)plan.stages * raw_bytes(p.np) + 2 * op_bytes(p.np))
         return NGT_ERR_UNSUPPORTED;
-    if (plan.stages == 5) return launch_stages<5>(ma, mw, p, grid, st);
-    return plan.stages == 4 ? launch_stages<4>(ma, mw, p, grid, st) : launch_stages<3>(ma, mw, p, grid, st);
+    switch (plan.stages) {
+    case 8: return launch_stages<8>(ma, mw, p, grid, st);
+    case 7: return launch_stages<7>(ma, mw, p, grid, st);
+    case 6: return launch_stages<6>(ma, mw, p, grid, st);
+    case 5: return launch_stages<5>(ma, mw, p, grid, st);
+    case 4: return launch_stages<4>(ma, mw, p, grid, st);
+    default: return launch_stages<3>(ma, mw, p, grid, st);
+    }
 }
 
 int linear_tc_timeouts(int *count) {
