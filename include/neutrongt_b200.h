@@ -5,8 +5,10 @@
  * asynchronously on that stream, allocates nothing, and returns an int status
  * (NGT_OK = 0).  No exception crosses the ABI.  Pointers are device pointers unless a
  * parameter says "host".  Workspaces are caller-owned; their size comes from the
- * matching *_workspace_size query.  Entry points are reentrant: they keep no state
- * between calls.
+ * matching *_workspace_size query.  Entry points keep no state between calls, with two
+ * exceptions: ngt_spattn_backward_noalloc uses one fixed scratch array per device (shared
+ * by all its calls; see its comment), and ngt_linear_status reads a per-device counter of
+ * the Linear kernels' bounded-wait timeouts.
  *
  * Element layout of attention tensors: row-major [n, heads, head_dim] (the reference's
  * [1, s, H, D] with b == 1, viewed as [s, H, D] at
@@ -130,26 +132,6 @@ NGT_API int ngt_spattn_backward(int dtype, int64_t n, int64_t e, int heads, int 
                         void *dq, void *dk, void *dv, float *dedge_bias, ngt_stream_t stream);
 
 /* ------------------------------------------------------------------------------------
- * Graph-sparse window attention, backward, allocating nothing.  No counterpart in the
- * reference: an extra entry point of this library.
- *
- * Same arguments and results as ngt_spattn_backward minus `delta`: the n * heads floats of
- * per-row scratch come from a fixed array inside the library (NGT_NOALLOC_MAX_ROWS_X_HEADS
- * floats = 8 MiB, reserved on every GPU that loads the library until the process exits).
- * For callers that cannot allocate device memory where they run the backward — e.g. code
- * running inside a fixed memory budget with no allocator handle, or host runtimes that do
- * not own a CUDA allocator and may not call cudaMalloc mid-step.  The caller still passes
- * every input and output buffer.
- *
- *   - n * heads above NGT_NOALLOC_MAX_ROWS_X_HEADS returns NGT_ERR_TOO_LARGE, before any work.
- *   - The first call on a device looks up the array's device address with that device
- *     current (the current device must be the one the pointers live on); make that first
- *     call before any stream capture.
- *   - Every call shares the one array.  Each call writes all the scratch it reads, so no
- *     clearing is needed, but calls that overlap on the GPU (other streams, other threads)
- *     race on it: serialise them.
- * ---------------------------------------------------------------------------------- */
-/* ------------------------------------------------------------------------------------
  * Sparse attention with heavy rows split into segments (tables from ngt_edge_csr_segments;
  * same results as ngt_spattn_forward / ngt_spattn_backward up to fp32 summation order).
  *   seg_edges, *_seg_first, *_seg_row, *_nseg: one view's tables (nseg == 0: none)
@@ -175,6 +157,26 @@ NGT_API int ngt_spattn_backward_seg(int dtype, int64_t n, int64_t e, int heads, 
                                     const int32_t *src_seg_first, const int32_t *src_seg_row, int64_t src_nseg,
                                     float *seg_part, ngt_stream_t stream);
 
+/* ------------------------------------------------------------------------------------
+ * Graph-sparse window attention, backward, allocating nothing.  No counterpart in the
+ * reference: an extra entry point of this library.
+ *
+ * Same arguments and results as ngt_spattn_backward minus `delta`: the n * heads floats of
+ * per-row scratch come from a fixed array inside the library (NGT_NOALLOC_MAX_ROWS_X_HEADS
+ * floats = 8 MiB, reserved on every GPU that loads the library until the process exits).
+ * For callers that cannot allocate device memory where they run the backward — e.g. code
+ * running inside a fixed memory budget with no allocator handle, or host runtimes that do
+ * not own a CUDA allocator and may not call cudaMalloc mid-step.  The caller still passes
+ * every input and output buffer.
+ *
+ *   - n * heads above NGT_NOALLOC_MAX_ROWS_X_HEADS returns NGT_ERR_TOO_LARGE, before any work.
+ *   - The first call on a device looks up the array's device address with that device
+ *     current (the current device must be the one the pointers live on); make that first
+ *     call before any stream capture.
+ *   - Every call shares the one array.  Each call writes all the scratch it reads, so no
+ *     clearing is needed, but calls that overlap on the GPU (other streams, other threads)
+ *     race on it: serialise them.
+ * ---------------------------------------------------------------------------------- */
 #define NGT_NOALLOC_MAX_ROWS_X_HEADS 2097152
 NGT_API int ngt_spattn_backward_noalloc(int dtype, int64_t n, int64_t e, int heads, int head_dim,
                                         const void *q, const void *k, const void *v,

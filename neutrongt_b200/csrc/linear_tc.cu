@@ -73,11 +73,14 @@ __host__ __device__ constexpr uint32_t smem_bytes(int np, int stages) {
 
 // hi = x rounded to the nearest tf32 (ties away from zero; 10 mantissa bits), lo = x - hi (exact);
 // the tensor core reads lo as tf32 too, which costs at most 2^-11 of |lo| <= 2^-22 |x|.
-// Non-finite x: hi = x, lo = 0.
+// Within 2^-11 of FLT_MAX the rounding would carry into the exponent (hi = inf, lo = -inf, a NaN
+// product); there hi is truncated instead, and lo stays exact.  Non-finite x: hi = x, lo = 0.
 __device__ __forceinline__ void split1(float x, uint32_t &hi, float &lo) {
     const uint32_t b = __float_as_uint(x);
     const bool fin = (b & 0x7F800000u) != 0x7F800000u;
-    hi = fin ? ((b + 0x1000u) & 0xFFFFE000u) : b;
+    uint32_t r = (b + 0x1000u) & 0xFFFFE000u;
+    if ((r & 0x7F800000u) == 0x7F800000u) r = b & 0xFFFFE000u;
+    hi = fin ? r : b;
     lo = fin ? x - __uint_as_float(hi) : 0.f;
 }
 __device__ __forceinline__ void split_store(float4 v, uint8_t *hi, uint8_t *lo) {
@@ -216,7 +219,9 @@ __global__ void __launch_bounds__(kThreadsAll, 2)
     if (!ok) {
         if (producer) {
             atomicAdd(&g_linear_tc_timeouts, 1);
-            for (int j = loaded - (STAGES - 1) < 0 ? 0 : loaded - (STAGES - 1); j < loaded; j++)
+            // slices loaded - STAGES .. loaded - 1 may still be landing: slice s's stage was only
+            // known free (its splitters arrived on ready) up to slice s - 1 when the loop stopped
+            for (int j = loaded - STAGES < 0 ? 0 : loaded - STAGES; j < loaded; j++)
                 tc::mbar_wait_bounded(&full[j % STAGES], (uint32_t)(j / STAGES) & 1u, kPolls);   // TMA in flight
             if (issued > 0)   // and the MMAs in flight end before the TMEM is freed (bounded)
                 tc::mbar_wait_bounded(&done[(issued - 1) & 1], (uint32_t)((issued - 1) >> 1) & 1u, kPolls);
@@ -346,16 +351,23 @@ TcPlan tc_plan(int64_t gm, int N, int sms) {
 
 template <int STAGES>
 int launch_stages(const CUtensorMap &ma, const CUtensorMap &mw, const TcArgs &p, dim3 grid, cudaStream_t st) {
-    static uint32_t attr_bytes[64] = {0};   // dynamic shared memory allowed so far, per device
+    // The attribute is set once per device to the largest size this instantiation can take, under a
+    // lock, so concurrent host threads never leave it below what a later launch needs.
+    static std::mutex mu;
+    static bool attr_set[64] = {};
     int dev = 0;
-    cudaGetDevice(&dev);
+    if (cudaGetDevice(&dev) != cudaSuccess) return NGT_ERR_CUDA;
     const uint32_t need = smem_bytes(p.np, STAGES);
     if (need > kSmemPerCta) return NGT_ERR_UNSUPPORTED;
-    if (dev < 0 || dev >= 64 || attr_bytes[dev] < need) {
-        if (cudaFuncSetAttribute(linear_tc_kernel<STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)need) !=
-            cudaSuccess)
-            return NGT_ERR_CUDA;
-        if (dev >= 0 && dev < 64) attr_bytes[dev] = need;
+    {
+        const uint32_t most = smem_bytes(kMaxN, STAGES) < kSmemPerCta ? smem_bytes(kMaxN, STAGES) : kSmemPerCta;
+        std::lock_guard<std::mutex> lock(mu);
+        if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+            if (cudaFuncSetAttribute(linear_tc_kernel<STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)most) != cudaSuccess)
+                return NGT_ERR_CUDA;
+            if (dev >= 0 && dev < 64) attr_set[dev] = true;
+        }
     }
     linear_tc_kernel<STAGES><<<grid, kThreadsAll, need, st>>>(ma, mw, p);
     NGT_CHECK_LAUNCH();

@@ -61,17 +61,44 @@ def window_state_from_preprocess_cache(payload_or_path, rank: int, world_size: i
 
 _CHECKPOINT_KEYS = ("epoch", "start_epoch", "model_state_dict", "optimizer_state_dict", "lr_scheduler_state_dict",
                     "args_snapshot", "loss_mean_list", "window_state_version", "best_val", "best_test")
+# run arguments a checkpoint records and a resume must agree with (checkpoint.py:10-20)
+CHECKPOINT_COMPAT_KEYS = ("dataset", "model", "n_layers", "hidden_dim", "num_heads", "attn_type", "n_parts",
+                          "related_nodes_topk_rate", "ppr_topk")
 
 
-def build_checkpoint_payload(args_snapshot: dict, model, optimizer, lr_scheduler, epoch: int, loss_mean_list,
+def checkpoint_args_snapshot(args) -> dict:
+    """The `args_snapshot` record of a checkpoint: each compatibility key read from `args`
+    (an argparse namespace or any object with those attributes; a dict is read by key), None
+    where absent, as `checkpoint.py:126` builds it."""
+    if isinstance(args, dict):
+        return {key: args.get(key) for key in CHECKPOINT_COMPAT_KEYS}
+    return {key: getattr(args, key, None) for key in CHECKPOINT_COMPAT_KEYS}
+
+
+def validate_checkpoint_compatibility(args, args_snapshot: dict) -> None:
+    """Raises ValueError when a run argument differs from the checkpoint's snapshot; keys the
+    snapshot does not hold (or holds as None) are skipped (`checkpoint.py:77-90`)."""
+    if not args_snapshot:
+        return
+    current = checkpoint_args_snapshot(args)
+    mismatches = [f"{key}: current={current[key]}, checkpoint={args_snapshot.get(key)}"
+                  for key in CHECKPOINT_COMPAT_KEYS
+                  if args_snapshot.get(key) is not None and current[key] != args_snapshot.get(key)]
+    if mismatches:
+        raise ValueError("Checkpoint is incompatible with current run arguments: " + "; ".join(mismatches))
+
+
+def build_checkpoint_payload(args, model, optimizer, lr_scheduler, epoch: int, loss_mean_list,
                              window_state_version: int, best_val: float, best_test: float) -> dict[str, Any]:
+    """The reference's checkpoint payload (`checkpoint.py:118-131`), same keys and types; `args`
+    is the run's argument namespace (its compatibility keys become `args_snapshot`)."""
     return {
         "epoch": epoch,
         "start_epoch": epoch + 1,
         "model_state_dict": model.state_dict(),
         "optimizer_state_dict": optimizer.state_dict(),
         "lr_scheduler_state_dict": lr_scheduler.state_dict(),
-        "args_snapshot": dict(args_snapshot),
+        "args_snapshot": checkpoint_args_snapshot(args),
         "loss_mean_list": list(loss_mean_list),
         "window_state_version": int(window_state_version),
         "best_val": float(best_val),
@@ -79,14 +106,18 @@ def build_checkpoint_payload(args_snapshot: dict, model, optimizer, lr_scheduler
     }
 
 
-def load_checkpoint(path_or_payload, model, optimizer=None, lr_scheduler=None, map_location="cpu"):
+def load_checkpoint(path_or_payload, model, optimizer=None, lr_scheduler=None, map_location="cpu", args=None):
     """Restores model (strict), optimizer and scheduler state from a reference-format checkpoint;
-    returns the resume fields (start_epoch, loss_mean_list, best_val, best_test, ...)."""
+    returns the resume fields (start_epoch, loss_mean_list, best_val, best_test, ...).  With
+    `args`, the checkpoint's `args_snapshot` is checked against them first and a mismatch raises
+    ValueError before any state is loaded (`checkpoint.py:93-103`)."""
     ck = torch.load(path_or_payload, map_location=map_location, weights_only=False) \
         if isinstance(path_or_payload, (str, os.PathLike)) else path_or_payload
     missing = [k for k in ("model_state_dict",) if k not in ck]
     if missing:
         raise KeyError(f"checkpoint lacks {missing}")
+    if args is not None:
+        validate_checkpoint_compatibility(args, ck.get("args_snapshot", {}))
     model.load_state_dict(ck["model_state_dict"], strict=True)
     if optimizer is not None and "optimizer_state_dict" in ck:
         optimizer.load_state_dict(ck["optimizer_state_dict"])

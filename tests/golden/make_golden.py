@@ -1,8 +1,8 @@
 """Generate the golden fixtures under tests/golden/ by running the reference itself.
 
-Run in the build container (the reference checkout must be importable):
+Run where the reference checkout exists, naming its NeutronGT/ directory:
 
-    python tests/golden/make_golden.py
+    NEUTRONGT_REFERENCE=<checkout>/NeutronGT python tests/golden/make_golden.py [section ...]
 
 Every output below comes from the reference's own Python, imported unmodified,
 with `reference_shims.install()` standing in for packages that are absent here
@@ -11,6 +11,11 @@ with `reference_shims.install()` standing in for packages that are absent here
 * attention_*.pt  – `CoreAttention.sparse_attention_bias` and `CoreAttention.forward`
   (`models/gt_dist_node_level_single_window.py:112-179, 198-227`) forward in fp32
   and fp64, backward through torch autograd in fp64.
+* dense_attention.pt – `CoreAttention.full_attention` and `CoreAttention.forward(attn_type="full")`
+  (`models/gt_dist_node_level_single_window.py:56-109, 198-227`), dropout 0, on bf16-representable
+  inputs: forward and fp64 autograd backward (dq, dk, dv and, where given, the gradients of
+  attn_bias and pruning_mask); cases with attn_bias, an additive pruning_mask holding -inf entries,
+  and a boolean mask with one fully masked row.
 * window_subgraph.pt – `_subgraph_from_csr` and `_compute_local_duplicate_nodes`
   (`core/node_level_pipeline/window_state.py:92-119, 52-73`).
 * appnp_*.pt – APPNP top-k PPR.  `personal_pagerank_appnp` refuses CPU devices
@@ -120,6 +125,60 @@ def make_attention():
     _attention_case("bias_h4", s, 4, 8, torch.stack([src, dst]), seed=3, with_bias=True)
     # D: empty edge list.
     _attention_case("empty", 16, 8, 8, torch.empty(2, 0, dtype=torch.long), seed=4)
+
+
+# --------------------------------------------------------------------------------------
+# dense full attention
+# --------------------------------------------------------------------------------------
+
+def _dense_case(s, H, D, seed, bias=False, pruning=False, mask=False):
+    from models.gt_dist_node_level_single_window import CoreAttention
+
+    g = torch.Generator().manual_seed(seed)
+    # bf16-representable inputs: the kernels compute in bf16, so the comparison measures the
+    # kernels' arithmetic, not the input rounding
+    mk = lambda: (torch.randn(1, s, H, D, generator=g) * 0.5).to(torch.bfloat16).double()  # noqa: E731
+    q, k, v, dout = mk(), mk(), mk(), mk()
+    attn_bias = torch.randn(1, H, s, s, generator=g).double() if bias else None   # fp32 values, exact in fp64
+    pruning_mask = None
+    if pruning:
+        u = torch.rand(1, 1, s, s, generator=g)
+        pruning_mask = torch.where(u < 0.1, torch.tensor(float("-inf")),
+                                   torch.where(u < 0.3, torch.tensor(-3.0), torch.tensor(0.0))).double()
+    mask_t = None
+    if mask:
+        mask_t = torch.rand(s, s, generator=g) < 0.15
+        mask_t[5] = True                        # one fully masked query row: uniform softmax
+    attn = CoreAttention(H * D, 0.0, H).eval()
+    leaves = [t.clone().requires_grad_(True) for t in (q, k, v)]
+    b_leaf = attn_bias.clone().requires_grad_(True) if bias else None
+    p_leaf = pruning_mask.clone().requires_grad_(True) if pruning else None
+    x, ns = attn.full_attention(leaves[1], leaves[0], leaves[2], b_leaf, mask=mask_t, pruning_mask=p_leaf)
+    (x * dout).sum().backward()
+    xf, sf = attn.forward(q.float(), k.float(), v.float(), None if attn_bias is None else attn_bias.float(), None,
+                          "full", mask=mask_t, pruning_mask=None if pruning_mask is None else pruning_mask.float())
+    # stored compactly: inputs as bf16 / fp32 (exact), the fp64 results rounded to fp32
+    f32 = lambda t: None if t is None else t.detach().float()  # noqa: E731
+    return {"s": s, "H": H, "D": D, "q": q.to(torch.bfloat16), "k": k.to(torch.bfloat16),
+            "v": v.to(torch.bfloat16), "dout": dout.to(torch.bfloat16),
+            "attn_bias": f32(attn_bias), "pruning_mask": f32(pruning_mask), "mask": mask_t,
+            "x": f32(x), "node_scores": f32(ns), "dq": f32(leaves[0].grad), "dk": f32(leaves[1].grad),
+            "dv": f32(leaves[2].grad), "dbias": f32(b_leaf.grad) if bias else None,
+            "dpruning": f32(p_leaf.grad) if pruning else None, "forward_x": xf, "forward_score": sf}
+
+
+def make_dense():
+    cases = {
+        "d24_h4": _dense_case(160, 4, 24, seed=31),       # the GPH_Large head shape (768 / 32)
+        "d16_h2": _dense_case(300, 2, 16, seed=32),
+        "d8_h3": _dense_case(96, 3, 8, seed=33),
+        "d64_h2": _dense_case(130, 2, 64, seed=34),
+        "d40_h1": _dense_case(200, 1, 40, seed=35),
+        "bias_d16": _dense_case(144, 2, 16, seed=36, bias=True),
+        "bias_pruning_mask_d24": _dense_case(136, 2, 24, seed=37, bias=True, pruning=True, mask=True),
+        "mask_d64": _dense_case(150, 2, 64, seed=38, mask=True),
+    }
+    _save("dense_attention.pt", cases)
 
 
 # --------------------------------------------------------------------------------------
@@ -332,6 +391,7 @@ if __name__ == "__main__":
     torch.set_num_threads(1)
     sections = {
         "attention": make_attention,
+        "dense": make_dense,
         "window": make_window,
         "appnp": make_appnp,
         "gt_sw": lambda: _model_step("gt_sw"),

@@ -21,12 +21,15 @@ hot path calls:
 """
 from __future__ import annotations
 
+import os
 import sys
 import types
 
 import torch
 
-REFERENCE_ROOT = "/root/reference/NeutronGT"
+# The reference checkout's NeutronGT/ directory (the one holding models/, core/, gt_sp/), named by
+# the NEUTRONGT_REFERENCE environment variable.
+REFERENCE_ROOT = os.environ.get("NEUTRONGT_REFERENCE", "")
 
 
 def _scatter(src, index, dim=-1, out=None, dim_size=None, reduce="sum"):
@@ -106,6 +109,8 @@ def install():
     pm = sys.modules["pymetis"]
     if not isinstance(getattr(pm, "__dict__", {}).get("CSRAdjacency"), type):
         pm.CSRAdjacency = _CSRAdjacency
+    if not REFERENCE_ROOT or not os.path.isdir(REFERENCE_ROOT):
+        raise RuntimeError("set NEUTRONGT_REFERENCE to the reference checkout's NeutronGT directory")
     if REFERENCE_ROOT not in sys.path:
         sys.path.insert(0, REFERENCE_ROOT)
     import utils.logger as ref_logger  # noqa: E402  (reference module)

@@ -3,7 +3,6 @@
 Tolerances (from the build's parity contract): outputs and gradients within 1e-5
 relative error in float32 and 2e-2 in bfloat16, measured as max|a-b| / max|b|.
 """
-import math
 
 import pytest
 import torch
@@ -160,7 +159,7 @@ def test_core_attention_forward_shape(cuda):
     assert rel_err(x.reshape(50, 8, 8), rx) < F32_TOL
 
 
-# ---------------- full-size window: size-independent properties ----------------
+# ---------------- full-size window: 65,536 tokens, Poisson(32) in-degrees, H=8, D=16, bf16 ----------------
 
 def _config3(device):
     from neutrongt_b200 import synthetic
@@ -172,37 +171,23 @@ def _config3(device):
     return mk(), mk(), mk(), mk(), ei.to(device)
 
 
-def test_config3_properties(cuda):
+def test_config3_full_window_elementwise(cuda):
+    """Every output of the isolated-kernel workload (65,536 tokens, E ~ 2.09 M) element by element:
+    x, node_scores, dq, dk and dv against the fp64 restatement run over the whole window on the
+    GPU (the oracle is plain torch; ~2 GB per fp64 [E, H, D] temporary), bf16 tolerance 2e-2."""
     from neutrongt_b200 import sparse_attention_bias
     q, k, v, dout, ei = _config3(cuda)
     qd, kd, vd = (t.clone().requires_grad_(True) for t in (q, k, v))
     x, ns = sparse_attention_bias(qd, kd, vd, ei, None)
     x.backward(dout)
-    # 1) forward + dq on 256 random destination rows: their in-edges fully determine them
-    rows = torch.randperm(65536, generator=torch.Generator().manual_seed(1))[:256].to(cuda)
-    keep = torch.isin(ei[1], rows)
-    sub = ei[:, keep].cpu()
-    rx, rns, _, _ = oatt.sparse_attention_forward(q.double().cpu(), k.double().cpu(), v.double().cpu(), sub)
-    rdq, _, _, _ = oatt.sparse_attention_backward(q.double().cpu(), k.double().cpu(), v.double().cpu(), sub,
-                                                  dout.double().cpu())
-    r = rows.cpu()
-    assert rel_err(x[rows], rx[r]) < BF16_TOL
-    assert rel_err(ns[rows], rns[r]) < BF16_TOL
-    assert rel_err(qd.grad[rows], rdq[r]) < BF16_TOL
-    # 2) checksum identities that tie the dst-major and src-major passes together:
-    #    sum_j dv_j = sum_d Z_d/(Z_d+eps) dO_d   and   sum_d <dq_d,q_d> = sum_j <dk_j,k_j> (per head)
-    from neutrongt_b200.edge_csr import edge_csr_for
-    csr = edge_csr_for(ei, 65536)
-    z = torch.zeros(65536, 8, dtype=torch.float64, device=cuda)
-    src, dst = ei[0], ei[1]
-    s_raw = (k[src].double() * q[dst].double()).sum(-1) / math.sqrt(16)
-    p = torch.exp(s_raw.clamp(-5, 5))
-    z.index_add_(0, dst, p)
-    w = z / (z + 1e-6)
-    lhs = vd.grad.double().sum(0)
-    rhs = (w.unsqueeze(-1) * dout.double()).sum(0)
-    assert rel_err(lhs, rhs) < BF16_TOL
-    a = (qd.grad.double() * q.double()).sum(-1).sum(0)
-    b = (kd.grad.double() * k.double()).sum(-1).sum(0)
-    assert rel_err(a, b) < BF16_TOL
-    assert csr.e == ei.shape[1]
+    got = {"x": x.detach(), "node_scores": ns, "dq": qd.grad, "dk": kd.grad, "dv": vd.grad}
+    del qd, kd, vd, x
+    q64, k64, v64, g64 = (t.double() for t in (q, k, v, dout))
+    rx, rns, _, _ = oatt.sparse_attention_forward(q64, k64, v64, ei)
+    errs = {"x": rel_err(got["x"], rx), "node_scores": rel_err(got["node_scores"], rns)}
+    del rx, rns
+    torch.cuda.empty_cache()
+    rdq, rdk, rdv, _ = oatt.sparse_attention_backward(q64, k64, v64, ei, g64)
+    errs.update(dq=rel_err(got["dq"], rdq), dk=rel_err(got["dk"], rdk), dv=rel_err(got["dv"], rdv))
+    bad = {name: e for name, e in errs.items() if not e < BF16_TOL}
+    assert not bad, bad

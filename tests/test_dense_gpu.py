@@ -1,13 +1,18 @@
-"""Dense full-attention window (tcgen05 kernels) against an fp32 torch restatement of
-`CoreAttention.full_attention` (`…single_window.py:56-109`) on the same bf16 inputs, forward
-and backward.  bf16 tolerance: 2e-2 relative (max|a-b| / max|b|)."""
+"""Dense full-attention window (tcgen05 kernels), forward and backward:
+
+* against the reference's own `CoreAttention.full_attention` outputs (tests/golden/dense_attention.pt,
+  fp64 autograd of the reference module on bf16-representable inputs);
+* against `oracle/dense.py` (the restatement pinned to those outputs) in fp32 on the GPU, at shapes
+  up to the GPH_Large per-rank window (32,768 tokens, 4 heads, head_dim 24), element by element.
+
+bf16 tolerance: 2e-2 relative (max|a-b| / max|b|)."""
 import math
 
 import numpy as np
 import pytest
 import torch
 
-from conftest import rel_err
+from conftest import golden, rel_err
 
 pytestmark = pytest.mark.gpu
 BF16_TOL = 2e-2
@@ -38,15 +43,40 @@ def keep_mask(seed, s, heads, p):
 
 
 def _reference(q, k, v, scale, keep=None, p=0.0):
-    """fp32 restatement; returns (x, node_scores) with autograd through q, k, v."""
-    qf, kf, vf = (t.float().transpose(0, 1) for t in (q, k, v))      # [H, s, D]
-    score = torch.matmul(qf * scale, kf.transpose(1, 2))              # [H, s, s]
-    prob = torch.softmax(score, dim=-1)
-    if keep is not None:
-        prob = prob * keep.to(prob.device, prob.dtype) / (1.0 - p)
-    x = torch.matmul(prob, vf).transpose(0, 1)                        # [s, H, D]
-    ns = score.detach().abs().mean(dim=0).sum(dim=0)
-    return x, ns
+    """fp32 oracle; returns (x [s, H, D], node_scores) with autograd through q, k, v."""
+    from oracle import dense as odense
+    return odense.full_attention(k.float(), q.float(), v.float(), scale=scale, keep=keep, dropout_p=p)
+
+
+@pytest.mark.parametrize("case", ["d24_h4", "d16_h2", "d8_h3", "d64_h2", "d40_h1"])
+def test_matches_reference_fixture(cuda, case):
+    """The public `full_attention(k, q, v, ...)` against the reference module's own fp64 results."""
+    from neutrongt_b200.dense_attention import full_attention
+    c = golden("dense_attention.pt")[case]
+    q, k, v, g = (c[n].to(cuda) for n in ("q", "k", "v", "dout"))
+    qd, kd, vd = (t.clone().requires_grad_(True) for t in (q, k, v))
+    x, ns = full_attention(kd, qd, vd, None, None, None)
+    x.backward(g)
+    assert x.shape == c["x"].shape
+    errs = {"x": rel_err(x, c["x"]), "node_scores": rel_err(ns, c["node_scores"]), "dq": rel_err(qd.grad, c["dq"]),
+            "dk": rel_err(kd.grad, c["dk"]), "dv": rel_err(vd.grad, c["dv"])}
+    assert all(e < BF16_TOL for e in errs.values()), errs
+
+
+def test_gph_large_window_elementwise(cuda):
+    """The GPH_Large per-rank dense window: 32,768 tokens, 4 heads, head_dim 24, dropout 0.  Every
+    element of x, node_scores, dq, dk and dv against the chunked fp32 oracle on the GPU."""
+    from neutrongt_b200.dense_attention import dense_attention
+    from oracle import dense as odense
+    s, H, D = 32768, 4, 24
+    q, k, v, dout = _inputs(s, H, D, 2024)
+    qd, kd, vd = (t.clone().requires_grad_(True) for t in (q, k, v))
+    x, ns = dense_attention(qd, kd, vd, math.sqrt(D))
+    x.backward(dout)
+    rx, rns, rdq, rdk, rdv = odense.full_attention_chunked(q, k, v, dout)
+    errs = {"x": rel_err(x, rx), "node_scores": rel_err(ns, rns), "dq": rel_err(qd.grad, rdq),
+            "dk": rel_err(kd.grad, rdk), "dv": rel_err(vd.grad, rdv)}
+    assert all(e < BF16_TOL for e in errs.values()), errs
 
 
 def _inputs(s, H, D, seed):

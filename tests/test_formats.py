@@ -42,7 +42,12 @@ def test_checkpoint_round_trip(tmp_path):
         p.grad = torch.ones_like(p)
     opt.step()
     sched = torch.optim.lr_scheduler.LambdaLR(opt, lambda e: 0.5)
-    payload = build_checkpoint_payload({"model": "gt"}, m, opt, sched, 4, [1.0, 0.5], 2, 0.7, 0.6)
+    run_args = SimpleNamespace(dataset="ogbn-arxiv", model="gt", n_layers=1, hidden_dim=8, num_heads=2,
+                               attn_type="sparse", n_parts=16, related_nodes_topk_rate=5, ppr_topk=8, seed=0)
+    payload = build_checkpoint_payload(run_args, m, opt, sched, 4, [1.0, 0.5], 2, 0.7, 0.6)
+    assert payload["args_snapshot"] == {"dataset": "ogbn-arxiv", "model": "gt", "n_layers": 1, "hidden_dim": 8,
+                                        "num_heads": 2, "attn_type": "sparse", "n_parts": 16,
+                                        "related_nodes_topk_rate": 5, "ppr_topk": 8}
     assert set(payload) == {"epoch", "start_epoch", "model_state_dict", "optimizer_state_dict",
                             "lr_scheduler_state_dict", "args_snapshot", "loss_mean_list", "window_state_version",
                             "best_val", "best_test"}
@@ -51,11 +56,29 @@ def test_checkpoint_round_trip(tmp_path):
     m2 = _small_gt()
     opt2 = torch.optim.AdamW(m2.parameters(), lr=1e-3)
     sched2 = torch.optim.lr_scheduler.LambdaLR(opt2, lambda e: 0.5)
-    info = load_checkpoint(str(path), m2, opt2, sched2)
+    info = load_checkpoint(str(path), m2, opt2, sched2, args=run_args)
     assert info["start_epoch"] == 5 and info["loss_mean_list"] == [1.0, 0.5] and info["best_test"] == 0.6
     for a, b in zip(m.state_dict().values(), m2.state_dict().values()):
         assert torch.equal(a, b)
     assert opt2.state_dict()["state"][0]["step"] == opt.state_dict()["state"][0]["step"]
+
+
+def test_checkpoint_rejects_incompatible_run_arguments():
+    """A resume with other model arguments raises before any state is loaded
+    (`checkpoint.py:77-90`); keys the snapshot does not hold are skipped."""
+    from neutrongt_b200.formats import load_checkpoint
+    m = _small_gt()
+    before = {k: v.clone() for k, v in m.state_dict().items()}
+    other = _small_gt()
+    with torch.no_grad():
+        for p in other.parameters():
+            p.add_(1.0)
+    ck = {"model_state_dict": other.state_dict(), "args_snapshot": {"model": "gt", "hidden_dim": 8, "n_parts": 16}}
+    with pytest.raises(ValueError, match="hidden_dim: current=16, checkpoint=8"):
+        load_checkpoint(ck, m, args=SimpleNamespace(model="gt", hidden_dim=16, n_parts=16))
+    for k, v in m.state_dict().items():
+        assert torch.equal(v, before[k])
+    load_checkpoint(ck, m, args={"model": "gt", "hidden_dim": 8, "n_parts": 16, "dataset": "x"})
 
 
 def test_reference_state_dict_loads_through_checkpoint(tmp_path):

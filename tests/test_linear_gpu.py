@@ -18,9 +18,11 @@ TOL = 1e-5
 
 # (rows, in, out): the GT / Graphormer window shapes, ragged and tiny row counts, the largest
 # inner dimension kept on chip (256), several column tiles, many row tiles per CTA
+# (30000, 128, 32) and (30000, 64, 40) are the row counts and narrow outputs for which the
+# tensor-core Linear picks a 7- and a 6-slice TMA ring (149-296 row tiles, two CTAs per SM).
 SHAPES = [(10583, 128, 128), (10583, 128, 256), (10583, 256, 128), (10583, 128, 64), (10583, 64, 32),
           (10583, 32, 40), (1, 4, 4), (5, 8, 12), (100, 64, 64), (1001, 256, 512), (200000, 128, 128),
-          (3, 300, 8)]
+          (3, 300, 8), (30000, 128, 32), (30000, 64, 40)]
 
 
 def _ref(x, w, b, dy):
@@ -124,3 +126,19 @@ def test_tensor_core_path_reports_no_timeouts(cuda):
     n = ctypes.c_int32(-1)
     assert _lib.lib().ngt_linear_status(ctypes.byref(n)) == 0
     assert n.value == 0
+
+
+def test_inputs_near_flt_max_stay_finite(cuda):
+    """Operands within 2^-11 of FLT_MAX split without carrying into the exponent, so the tensor-core
+    forward stays finite and fp32-accurate where a naive round-up would give inf - inf = NaN."""
+    from neutrongt_b200.layers import Linear
+    x = torch.randn(300, 64, device="cuda") * 1e-3
+    big = torch.tensor([0x7F7FF000, 0x7F7FFFFF, -0x00800800], dtype=torch.int32).view(torch.float32)
+    x[:3, 5] = big.to("cuda")
+    lin = Linear(64, 16).cuda()
+    with torch.no_grad():
+        lin.weight.mul_(1e-3)
+    y = lin(x.unsqueeze(0))[0]
+    ry = x.double() @ lin.weight.detach().double().t() + lin.bias.detach().double()
+    assert bool(torch.isfinite(y).all())
+    assert rel_err(y, ry) < TOL

@@ -136,3 +136,37 @@ def test_appnp_source_range_and_empty():
     ei, val = oppr.personal_pagerank_appnp(None, 0.5, topk=2, csr_data={"rowptr": rowptr, "col": col},
                                            source_start=1, source_end=1)
     assert ei.shape == (2, 0) and val.numel() == 0
+
+
+# ---------------- dense full attention (oracle/dense.py) against the reference's outputs ----------------
+
+@pytest.mark.parametrize("case", ["d24_h4", "d16_h2", "d8_h3", "d64_h2", "d40_h1", "bias_d16",
+                                  "bias_pruning_mask_d24", "mask_d64"])
+def test_dense_oracle_matches_reference(case):
+    from oracle import dense as odense
+    c = golden("dense_attention.pt")[case]
+    q, k, v, g = (c[n].double().requires_grad_(n != "dout") for n in ("q", "k", "v", "dout"))
+    b = c["attn_bias"].double().requires_grad_(True) if c["attn_bias"] is not None else None
+    pm = c["pruning_mask"].double().requires_grad_(True) if c["pruning_mask"] is not None else None
+    x, ns = odense.full_attention(k, q, v, b, c["mask"], pm)
+    (x * g).sum().backward()
+    tol = 1e-6     # the fixture holds fp64 results rounded to fp32
+    assert rel_err(x, c["x"]) < tol and rel_err(ns, c["node_scores"]) < tol
+    assert rel_err(q.grad, c["dq"]) < tol and rel_err(k.grad, c["dk"]) < tol and rel_err(v.grad, c["dv"]) < tol
+    if b is not None:
+        assert rel_err(b.grad, c["dbias"]) < tol
+    if pm is not None:
+        assert rel_err(pm.grad, c["dpruning"]) < tol
+    if c["attn_bias"] is None and c["mask"] is None:      # the chunked form (no bias / mask)
+        out, ns2, dq, dk, dv = odense.full_attention_chunked(q[0].detach(), k[0].detach(), v[0].detach(),
+                                                             g[0].detach(), rows=37)
+        assert rel_err(out, c["x"][0]) < tol and rel_err(ns2, c["node_scores"]) < tol
+        assert rel_err(dq, c["dq"][0]) < tol and rel_err(dk, c["dk"][0]) < tol and rel_err(dv, c["dv"][0]) < tol
+
+
+def test_dense_reference_dispatch_matches_full_attention():
+    """`CoreAttention.forward(attn_type="full")` reshapes the full_attention output to [b, s, H*D]."""
+    c = golden("dense_attention.pt")["d24_h4"]
+    assert c["forward_x"].shape == (1, c["s"], c["H"] * c["D"])
+    assert rel_err(c["forward_x"].reshape(c["x"].shape), c["x"]) < 1e-5
+    assert rel_err(c["forward_score"], c["node_scores"]) < 1e-5

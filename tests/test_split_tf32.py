@@ -16,7 +16,9 @@ import pytest
 def _tf32_round(x):
     b = x.astype(np.float32).view(np.uint32)
     finite = (b & 0x7F800000) != 0x7F800000
-    r = np.where(finite, (b + np.uint32(0x1000)) & np.uint32(0xFFFFE000), b)
+    r = (b + np.uint32(0x1000)) & np.uint32(0xFFFFE000)
+    r = np.where((r & 0x7F800000) == 0x7F800000, b & np.uint32(0xFFFFE000), r)   # no carry into inf
+    r = np.where(finite, r, b)
     return r.astype(np.uint32).view(np.float32)
 
 
@@ -50,6 +52,20 @@ def test_rounding_matches_the_definition():
     assert np.all(np.abs(x - hi) <= np.abs(x) * 2.0 ** -11 + 1e-45)
     inf = np.array([np.inf, -np.inf], dtype=np.float32)
     assert np.array_equal(_tf32_round(inf), inf)                          # non-finite kept
+
+
+def test_split_near_flt_max_stays_finite():
+    """Within 2^-11 of FLT_MAX, rounding up would carry into the exponent (hi = inf, lo = -inf,
+    so hi * w + lo * w is NaN); the split truncates there and hi + lo is still exactly x."""
+    big = np.array([0x7F7FF000, 0x7F7FFFFF, 0xFF7FF800, 0x7F7FE000], dtype=np.uint32).view(np.float32)
+    hi = _tf32_round(big)
+    assert np.isfinite(hi).all()
+    lo = (big - hi).astype(np.float32)
+    assert np.array_equal((hi.astype(np.float64) + lo.astype(np.float64)).astype(np.float32), big)
+    w = np.full((1, 4), 1e-3, dtype=np.float32)
+    y = _split_gemm(big[None, :], w)
+    assert np.isfinite(y).all()
+    assert _rel(y, big[None, :].astype(np.float64) @ w.astype(np.float64).T) < 1e-5
 
 
 @pytest.mark.parametrize("rows,fin,fout", [(2048, 128, 128), (1024, 256, 128), (1024, 128, 256), (777, 100, 40)])
