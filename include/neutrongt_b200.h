@@ -222,6 +222,28 @@ NGT_API int ngt_dense_attn_backward(int64_t s, int heads, int head_dim, float sc
                                     ngt_stream_t stream);
 
 /* ------------------------------------------------------------------------------------
+ * Dense full-attention window with an additive bias: the attn_bias / pruning_mask / mask arguments
+ * of `CoreAttention.full_attention` (NeutronGT/models/gt_dist_node_level_single_window.py:78-99).
+ * Same arguments and results as ngt_dense_attn_forward / ngt_dense_attn_backward, plus
+ *   bias              float: X = S + bias[h, i, j] before the softmax, element (h, i, j) at
+ *                     h * bias_head_stride + i * s + j; bias_head_stride 0 (one [s, s] matrix for
+ *                     every head) or s * s ([heads, s, s]).  -inf entries (masked keys) get no weight;
+ *                     a row with no finite entry gets lse = -inf and an output of 0.
+ *   dbias (backward)  float [heads, s, s] (nullable): dX = P (dP - delta), 0 at -inf entries.
+ * Any head_dim <= 64 that is a multiple of 8 (single-role tcgen05 kernels, head_dim padded to 32
+ * or 64); node scores are those of the raw S, as the reference computes them before the bias.
+ * ---------------------------------------------------------------------------------- */
+NGT_API int ngt_dense_attn_forward_bias(int64_t s, int heads, int head_dim, float scale, float score_scale,
+                                        float dropout_p, uint64_t seed, const void *q, const void *k, const void *v,
+                                        const float *bias, int64_t bias_head_stride, void *out, float *lse,
+                                        float *node_scores, int32_t *status, ngt_stream_t stream);
+NGT_API int ngt_dense_attn_backward_bias(int64_t s, int heads, int head_dim, float scale, float dropout_p,
+                                         uint64_t seed, const void *q, const void *k, const void *v, const void *out,
+                                         const void *dout, const float *lse, const float *bias,
+                                         int64_t bias_head_stride, float *delta, float *dq_accum, void *dq, void *dk,
+                                         void *dv, float *dbias, int32_t *status, ngt_stream_t stream);
+
+/* ------------------------------------------------------------------------------------
  * Window subgraph (the window's edge list from the global CSR).
  *
  * Replaces `_subgraph_from_csr` (NeutronGT/core/node_level_pipeline/window_state.py:92-119):
@@ -320,9 +342,84 @@ NGT_API int ngt_linear_weight_workspace_size(int64_t rows, int in_features, int 
 NGT_API int ngt_linear_backward_weight(int64_t rows, int in_features, int out_features, const float *x,
                                        const float *dy, float *dweight, float *dbias, void *workspace,
                                        size_t workspace_bytes, ngt_stream_t stream);
-/* Number of tensor-core Linear CTAs whose bounded waits ran out (they store nothing) since the
- * library was loaded; synchronous.  No counterpart in the reference (torch's GEMMs do not wait). */
+/* ------------------------------------------------------------------------------------
+ * bf16 Linear layers (the large model's projections) on the tcgen05 tensor cores.
+ *
+ * Replace torch's bf16 Linear GEMMs in GPH_Large's QKV, output and FFN projections
+ * (NeutronGT/models/gt_dist_node_level_single_window.py:235-237, 313-318;
+ * graphormer_dist_node_level.py:139, 179, 183) with the same contract as the fp32 entry points
+ * above, on bf16 tensors: x / dx [rows, in_features], y / dy [rows, out_features], weight /
+ * dweight [out_features, in_features], bias / dbias [out_features] (nullable), all bf16,
+ * row-major, 16-byte aligned; in_features and out_features multiples of 8.  fp32 accumulation;
+ * results rounded to bf16 once.
+ *   ngt_linear_bf16_forward          y = x W^T + b
+ *   ngt_linear_bf16_backward_input   dx = dy W
+ *   ngt_linear_bf16_backward_weight  dW = dy^T x and db = column sums of dy, each summed in a
+ *                                    fixed order (bitwise reproducible); fp32 workspace of
+ *                                    ngt_linear_bf16_weight_workspace_size bytes (depends on the
+ *                                    current device's SM count)
+ * ---------------------------------------------------------------------------------- */
+NGT_API int ngt_linear_bf16_forward(int64_t rows, int in_features, int out_features, const void *x,
+                                    const void *weight, const void *bias, void *y, ngt_stream_t stream);
+NGT_API int ngt_linear_bf16_backward_input(int64_t rows, int in_features, int out_features, const void *dy,
+                                           const void *weight, void *dx, ngt_stream_t stream);
+NGT_API int ngt_linear_bf16_weight_workspace_size(int64_t rows, int in_features, int out_features,
+                                                  size_t *bytes /* host */);
+NGT_API int ngt_linear_bf16_backward_weight(int64_t rows, int in_features, int out_features, const void *x,
+                                            const void *dy, void *dweight, void *dbias, void *workspace,
+                                            size_t workspace_bytes, ngt_stream_t stream);
+/* Number of tensor-core Linear CTAs (fp32 and bf16 kernels) whose bounded waits ran out (they store
+ * nothing) since the library was loaded; synchronous.  No counterpart in the reference (torch's
+ * GEMMs do not wait). */
 NGT_API int ngt_linear_status(int32_t *timeouts /* host */);
+
+/* ------------------------------------------------------------------------------------
+ * Push-based approximate personalised PageRank + per-seed top-k.
+ *
+ * Replaces the reference's default backend, personal_pagerank_torch_geometric
+ * (NeutronGT/core/ppr_backends/torch_geometric_backend.py:5-30: PyG get_ppr(edge_index, alpha, eps),
+ * then a per-source top-k loop).  Per seed s in [seed_start, seed_end): the push method with a LIFO
+ * stack (p = {s: 0}, r = {s: alpha}; pop u: p[u] += r[u], r[u] = 0, r[v] += (1 - alpha) r[u] /
+ * deg(u) for v in adj(u) in CSR order, push v when r[v] >= alpha * eps * deg(v) and v is not on the
+ * stack), fp64, each operation one IEEE rounding.  Kept: p in insertion order when it has at most
+ * topk entries, else the topk largest by (value desc, node asc).
+ *   rowptr int64 [n+1], col int32 [E] (columns ascending within a row, as PyG sorts them)
+ *   slots        concurrent seeds (one warp each); workspace from ngt_ppr_push_workspace_size(n, slots)
+ *                (about 29 bytes x n per slot; zeroed by the call)
+ *   out_idx / out_val / out_val64 (nullable) [(seed_end - seed_start) * topk], out_cnt [seeds]
+ *   info         int32 [1]: seeds stopped by the termination guard (0 in practice)
+ * ngt_ppr_push_stats reads the last call's push and adjacency-read totals from its workspace
+ * (synchronous).  alpha in (0, 1], eps > 0.
+ * ---------------------------------------------------------------------------------- */
+NGT_API int ngt_ppr_push_workspace_size(int64_t n, int64_t slots, size_t *bytes /* host */);
+NGT_API int ngt_ppr_push_topk(int64_t n, const int64_t *rowptr, const int32_t *col, double alpha, double eps,
+                              int64_t seed_start, int64_t seed_end, int64_t topk, int64_t slots, int64_t *out_idx,
+                              float *out_val, double *out_val64, int32_t *out_cnt, int32_t *info, void *workspace,
+                              size_t workspace_bytes, ngt_stream_t stream);
+NGT_API int ngt_ppr_push_stats(const void *workspace, int64_t n, int64_t slots, int64_t *pushes_and_reads /* host [2] */,
+                               ngt_stream_t stream);
+
+/* ------------------------------------------------------------------------------------
+ * Sparse x sparse product C = A B of fp32 CSR matrices.
+ *
+ * Replaces csr_spgemm (NeutronGT/core/ppr_backends/cusparse_ops.py:97-114; cuSPARSE SpGEMM in
+ * csrc/cusparse_spgemm.cu:65-267): A [m x n], B [n x n], C [m x n] holding every structural entry
+ * of the product (entries that cancel to 0 stay, as cuSPARSE keeps them), columns ascending per
+ * row, each value the fp32 sum of its products in A's entry order.  Two calls on one workspace:
+ *   ngt_csr_spgemm_symbolic  writes rowptr_c int64 [m+1] (rowptr_c[m] = nnz(C)); zeroes the workspace
+ *   ngt_csr_spgemm_numeric   fills col_c int64 [nnz], val_c float [nnz] (after the symbolic call)
+ *   rowptr_a / rowptr_b int64, col_a / col_b int32 (in [0, n)), val_a / val_b float
+ *   slots    concurrent rows (one warp each); workspace from ngt_csr_spgemm_workspace_size
+ *            (about 9 bytes x n per slot plus a power-of-two sort buffer)
+ * ---------------------------------------------------------------------------------- */
+NGT_API int ngt_csr_spgemm_workspace_size(int64_t m, int64_t n, int64_t slots, size_t *bytes /* host */);
+NGT_API int ngt_csr_spgemm_symbolic(int64_t m, int64_t n, const int64_t *rowptr_a, const int32_t *col_a,
+                                    const int64_t *rowptr_b, const int32_t *col_b, int64_t slots, int64_t *rowptr_c,
+                                    void *workspace, size_t workspace_bytes, ngt_stream_t stream);
+NGT_API int ngt_csr_spgemm_numeric(int64_t m, int64_t n, const int64_t *rowptr_a, const int32_t *col_a,
+                                   const float *val_a, const int64_t *rowptr_b, const int32_t *col_b,
+                                   const float *val_b, int64_t slots, const int64_t *rowptr_c, int64_t *col_c,
+                                   float *val_c, void *workspace, size_t workspace_bytes, ngt_stream_t stream);
 
 /* ----------------------------------------------------------------------------------
  * Window construction between PPR and the training windows.

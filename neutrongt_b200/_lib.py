@@ -43,6 +43,10 @@ SIGNATURES = {
                                _p, _p, _p, _p, _p, _p, _p, _p],
     "ngt_dense_attn_backward": [_i64, _i32, _i32, ctypes.c_float, ctypes.c_float, ctypes.c_uint64, _p, _p, _p, _p,
                                 _p, _p, _p, _p, _p, _p, _p, _p, _p],
+    "ngt_dense_attn_forward_bias": [_i64, _i32, _i32, ctypes.c_float, ctypes.c_float, ctypes.c_float,
+                                    ctypes.c_uint64, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _p],
+    "ngt_dense_attn_backward_bias": [_i64, _i32, _i32, ctypes.c_float, ctypes.c_float, ctypes.c_uint64, _p, _p, _p, _p,
+                                     _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _p],
     "ngt_window_subgraph_workspace_size": [_i64, _i64, _sz_p],
     "ngt_window_subgraph_count": [_i64, _p, _p, _p, _i64, _p, _p, _p, ctypes.c_size_t, _p],
     "ngt_window_subgraph_fill": [_i64, _p, _p, _p, _i64, _p, _p, _i64, _p, ctypes.c_size_t, _p],
@@ -68,7 +72,18 @@ SIGNATURES = {
     "ngt_linear_backward_input": [_i64, _i32, _i32, _p, _p, _p, _p],
     "ngt_linear_weight_workspace_size": [_i64, _i32, _i32, _sz_p],
     "ngt_linear_backward_weight": [_i64, _i32, _i32, _p, _p, _p, _p, _p, ctypes.c_size_t, _p],
+    "ngt_linear_bf16_forward": [_i64, _i32, _i32, _p, _p, _p, _p, _p],
+    "ngt_linear_bf16_backward_input": [_i64, _i32, _i32, _p, _p, _p, _p],
+    "ngt_linear_bf16_weight_workspace_size": [_i64, _i32, _i32, _sz_p],
+    "ngt_linear_bf16_backward_weight": [_i64, _i32, _i32, _p, _p, _p, _p, _p, ctypes.c_size_t, _p],
     "ngt_linear_status": [_p],
+    "ngt_ppr_push_workspace_size": [_i64, _i64, _sz_p],
+    "ngt_ppr_push_topk": [_i64, _p, _p, _dbl, _dbl, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, ctypes.c_size_t,
+                          _p],
+    "ngt_ppr_push_stats": [_p, _i64, _i64, _p, _p],
+    "ngt_csr_spgemm_workspace_size": [_i64, _i64, _i64, _sz_p],
+    "ngt_csr_spgemm_symbolic": [_i64, _i64, _p, _p, _p, _p, _i64, _p, _p, ctypes.c_size_t, _p],
+    "ngt_csr_spgemm_numeric": [_i64, _i64, _p, _p, _p, _p, _p, _p, _i64, _p, _p, _p, _p, ctypes.c_size_t, _p],
 }
 
 NGT_F32 = 0

@@ -70,12 +70,16 @@ struct FwdSmem {
 
 // Two CTAs share an SM (<= 113 KiB shared memory and 256 TMEM columns each), so one CTA's
 // softmax overlaps the other's tensor-core work.
-template <int DP>
+// BIAS: an additive fp32 bias joins the scores before the softmax, X = S + bias[h, i, j] (bias
+// element (h, i, j) at h * bias_hs + i * s + j; bias_hs = 0 shares one [s, s] matrix over the
+// heads); -inf entries (masked keys) take no weight.  The node scores stay those of the raw S.
+template <int DP, bool BIAS = false>
 __global__ void __launch_bounds__(kThreads, 2)
     dense_fwd_kernel(int s, int H, int D, float scale, float score_scale, float drop_p, uint32_t seed,
                      const __nv_bfloat16 *__restrict__ q, const __nv_bfloat16 *__restrict__ k,
                      const __nv_bfloat16 *__restrict__ v, __nv_bfloat16 *__restrict__ out,
-                     float *__restrict__ lse, float *__restrict__ node_scores, int *__restrict__ status) {
+                     float *__restrict__ lse, float *__restrict__ node_scores, int *__restrict__ status,
+                     const float *__restrict__ bias, int64_t bias_hs) {
     using L = FwdSmem<DP>;
     constexpr int CH = L::CH;
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -169,13 +173,22 @@ __global__ void __launch_bounds__(kThreads, 2)
         tc::fence_after_sync();
 
         const bool full_block = k0 + BN <= s;   // every key of the block is real
-        // pass 1: row max of the raw scores (scale > 0, so the max commutes with scaling)
-        float mraw = -INFINITY;
+        // the row's bias for this key block (BIAS only; rows past s read none)
+        const float *brow = BIAS && row_ok ? bias + (size_t)h * bias_hs + (size_t)qi * s + k0 : nullptr;
+        // pass 1: row max of the raw scores (scale > 0, so the max commutes with scaling); with a
+        // bias, the max of the biased scores in log2 units
+        float mraw = -INFINITY, mb2 = -INFINITY;
 #pragma unroll 1
         for (int c4 = 0; c4 < BN / 32; c4++) {
             float t[32];
             tc::ld32(tS + lane_off + c4 * 32, t);
-            if (full_block) {
+            if constexpr (BIAS) {
+                if (row_ok) {
+#pragma unroll
+                    for (int i = 0; i < 32; i++)
+                        if (k0 + c4 * 32 + i < s) mb2 = fmaxf(mb2, fmaf(t[i], sl2, brow[c4 * 32 + i] * kLog2e));
+                }
+            } else if (full_block) {
 #pragma unroll
                 for (int i = 0; i < 32; i++) mraw = fmaxf(mraw, t[i]);
             } else {
@@ -184,7 +197,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                     if (k0 + c4 * 32 + i < s) mraw = fmaxf(mraw, t[i]);
             }
         }
-        const float m_new = fmaxf(m2, mraw * sl2);
+        const float m_new = fmaxf(m2, BIAS ? mb2 : mraw * sl2);
         const float alpha = (m_new == -INFINITY) ? 1.f : tc::ex2(m2 - m_new);
         l *= alpha;
         m2 = m_new;
@@ -197,7 +210,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
             for (int c = 0; c < 4; c++) {
                 uint32_t pw[4], aw[4];
-                if (full_block && row_ok && !drop_threshold) {   // common case: no checks per element
+                if (!BIAS && full_block && row_ok && !drop_threshold) {   // common case: no checks per element
 #pragma unroll
                     for (int e = 0; e < 8; e += 2) {
                         const float p0 = tc::ex2(fmaf(t[c * 8 + e], sl2, -m_new));
@@ -215,7 +228,14 @@ __global__ void __launch_bounds__(kThreads, 2)
                             const int jj = c * 8 + e + u;
                             const int key = k0 + c4 * 32 + jj;
                             const bool ok = key < s;
-                            const float p = ok ? tc::ex2(fmaf(t[jj], sl2, -m_new)) : 0.f;
+                            float p;
+                            if constexpr (BIAS) {
+                                // a key whose biased score is -inf (or a row with none finite yet) takes no weight
+                                const float x2 = ok && row_ok ? fmaf(t[jj], sl2, brow[c4 * 32 + jj] * kLog2e) : -INFINITY;
+                                p = (x2 == -INFINITY || m_new == -INFINITY) ? 0.f : tc::ex2(x2 - m_new);
+                            } else {
+                                p = ok ? tc::ex2(fmaf(t[jj], sl2, -m_new)) : 0.f;
+                            }
                             l += p;
                             float pd = p;
                             if (drop_threshold) pd = keep_elem(seed, h, qi, key, drop_threshold) ? p * keep_scale : 0.f;
@@ -301,18 +321,19 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (warp == 0) tc::tmem_dealloc(tmem, kTmemCols);
 }
 
-template <int DP>
+template <int DP, bool BIAS = false>
 int launch_fwd(int64_t s, int heads, int head_dim, float scale, float score_scale, float drop_p, uint32_t seed,
                const void *q, const void *k, const void *v, void *out, float *lse, float *ns, int *status,
-               cudaStream_t st) {
+               cudaStream_t st, const float *bias = nullptr, int64_t bias_hs = 0) {
     using L = FwdSmem<DP>;
-    auto fn = dense_fwd_kernel<DP>;
+    auto fn = dense_fwd_kernel<DP, BIAS>;
     if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kBytes) != cudaSuccess)
         return NGT_ERR_CUDA;
     dim3 grid((unsigned)((s + BM - 1) / BM), (unsigned)heads);
     fn<<<grid, kThreads, L::kBytes, st>>>((int)s, heads, head_dim, scale, score_scale, drop_p, seed,
                                           (const __nv_bfloat16 *)q, (const __nv_bfloat16 *)k,
-                                          (const __nv_bfloat16 *)v, (__nv_bfloat16 *)out, lse, ns, status);
+                                          (const __nv_bfloat16 *)v, (__nv_bfloat16 *)out, lse, ns, status, bias,
+                                          bias_hs);
     NGT_CHECK_LAUNCH();
     return NGT_OK;
 }
@@ -388,14 +409,18 @@ __device__ __forceinline__ void stage_rows(uint8_t *dst, const __nv_bfloat16 *sr
     }
 }
 
-template <int DP>
+// BIAS: the forward's additive bias (same layout) is added to the recomputed scores, and the
+// gradient of the biased scores, dX = P (dP - delta) (zero at -inf entries), is written to
+// dbias [H, s, s] when it is not null.
+template <int DP, bool BIAS = false>
 __global__ void __launch_bounds__(kThreads, 2)
     dense_bwd_kernel(int s, int H, int D, float scale, float drop_p, uint32_t seed,
                      const __nv_bfloat16 *__restrict__ q, const __nv_bfloat16 *__restrict__ k,
                      const __nv_bfloat16 *__restrict__ v, const __nv_bfloat16 *__restrict__ dout,
                      const float *__restrict__ lse, const float *__restrict__ delta,
                      float *__restrict__ dq_acc, __nv_bfloat16 *__restrict__ dk, __nv_bfloat16 *__restrict__ dv,
-                     int *__restrict__ status) {
+                     int *__restrict__ status, const float *__restrict__ bias, int64_t bias_hs,
+                     float *__restrict__ dbias) {
     using L = BwdSmem<DP>;
     constexpr int CH = L::CH;
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -503,7 +528,17 @@ __global__ void __launch_bounds__(kThreads, 2)
                         for (int u = 0; u < 2; u++) {
                             const int j = c * 8 + e + u;                   // query within the 32-chunk
                             const int qq = half * QH + c4 * 32 + j;        // query within the block
-                            const float p = key_ok ? tc::ex2(fmaf(sv[j], sl2, -s_lse[qq])) : 0.f;
+                            float p;
+                            if constexpr (BIAS) {
+                                const int qg = q0 + qq;
+                                const float l2 = s_lse[qq];
+                                const float x2 = key_ok && qg < s
+                                                     ? fmaf(sv[j], sl2, bias[(size_t)h * bias_hs + (size_t)qg * s + kj] * kLog2e)
+                                                     : -INFINITY;
+                                p = (x2 == -INFINITY || l2 == -INFINITY) ? 0.f : tc::ex2(x2 - l2);
+                            } else {
+                                p = key_ok ? tc::ex2(fmaf(sv[j], sl2, -s_lse[qq])) : 0.f;
+                            }
                             float g = dp[j];
                             float pd = p;
                             if (drop_threshold) {
@@ -513,6 +548,8 @@ __global__ void __launch_bounds__(kThreads, 2)
                             }
                             pv[u] = pd;
                             dv2[u] = p * (g - s_delta[qq]);
+                            if (BIAS && dbias != nullptr && key_ok && q0 + qq < s)
+                                dbias[(size_t)h * s * s + (size_t)(q0 + qq) * s + kj] = dv2[u];
                         }
                         pw[e / 2] = tc::pack_bf16(pv[0], pv[1]);
                         dw[e / 2] = tc::pack_bf16(dv2[0], dv2[1]);
@@ -640,7 +677,7 @@ int launch_bwd(int64_t s, int heads, int head_dim, float scale, float drop_p, ui
         fn<<<grid, kThreads, L::kBytes, st>>>((int)s, heads, head_dim, scale, drop_p, seed, (const __nv_bfloat16 *)q,
                                               (const __nv_bfloat16 *)k, (const __nv_bfloat16 *)v,
                                               (const __nv_bfloat16 *)dout, lse, delta, dq_acc, (__nv_bfloat16 *)dk,
-                                              (__nv_bfloat16 *)dv, status);
+                                              (__nv_bfloat16 *)dv, status, nullptr, 0, nullptr);
     }
     dense_dq_cast_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(n, dq_acc, (__nv_bfloat16 *)dq);
     NGT_CHECK_LAUNCH();
@@ -670,4 +707,90 @@ extern "C" int ngt_dense_attn_backward(int64_t s, int heads, int head_dim, float
                               dk, dv, status, st);
     return launch_bwd<64>(s, heads, head_dim, scale, dropout_p, sd, q, k, v, out, dout, lse, delta, dq_accum, dq, dk,
                           dv, status, st);
+}
+
+// ------------------------------------------------------------------------------------
+// Dense attention with an additive bias (attn_bias + pruning_mask, masked keys at -inf): the
+// single-role kernels above with BIAS set, for any head_dim <= 64 (padded to 32 or 64).
+// ------------------------------------------------------------------------------------
+namespace ngt {
+namespace {
+
+template <int DP>
+int launch_bwd_bias(int64_t s, int heads, int head_dim, float scale, float drop_p, uint32_t seed, const void *q,
+                    const void *k, const void *v, const void *out, const void *dout, const float *lse,
+                    const float *bias, int64_t bias_hs, float *delta, float *dq_acc, void *dq, void *dk, void *dv,
+                    float *dbias, int *status, cudaStream_t st) {
+    using L = BwdSmem<DP>;
+    const int64_t n = s * heads * head_dim;
+    if (cudaMemsetAsync(dq_acc, 0, sizeof(float) * (size_t)n, st) != cudaSuccess) return NGT_ERR_CUDA;
+    dense_delta_kernel<<<(unsigned)((s * heads + 255) / 256), 256, 0, st>>>(
+        (int)s, heads, head_dim, (const __nv_bfloat16 *)out, (const __nv_bfloat16 *)dout, delta);
+    auto fn = dense_bwd_kernel<DP, true>;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kBytes) != cudaSuccess)
+        return NGT_ERR_CUDA;
+    dim3 grid((unsigned)((s + BN - 1) / BN), (unsigned)heads);
+    fn<<<grid, kThreads, L::kBytes, st>>>((int)s, heads, head_dim, scale, drop_p, seed, (const __nv_bfloat16 *)q,
+                                          (const __nv_bfloat16 *)k, (const __nv_bfloat16 *)v,
+                                          (const __nv_bfloat16 *)dout, lse, delta, dq_acc, (__nv_bfloat16 *)dk,
+                                          (__nv_bfloat16 *)dv, status, bias, bias_hs, dbias);
+    dense_dq_cast_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(n, dq_acc, (__nv_bfloat16 *)dq);
+    NGT_CHECK_LAUNCH();
+    return NGT_OK;
+}
+
+int check_bias_args(int64_t s, int heads, int64_t bias_hs, const float *bias) {
+    if (!bias) return NGT_ERR_INVALID_ARGUMENT;
+    if (bias_hs != 0 && bias_hs != s * s) return NGT_ERR_INVALID_ARGUMENT;
+    if (s * s * (int64_t)heads >= ((int64_t)1 << 40)) return NGT_ERR_TOO_LARGE;
+    return NGT_OK;
+}
+
+}  // namespace
+}  // namespace ngt
+
+extern "C" int ngt_dense_attn_forward_bias(int64_t s, int heads, int head_dim, float scale, float score_scale,
+                                           float dropout_p, uint64_t seed, const void *q, const void *k, const void *v,
+                                           const float *bias, int64_t bias_head_stride, void *out, float *lse,
+                                           float *node_scores, int32_t *status, ngt_stream_t stream) {
+    if (s < 0 || heads <= 0 || head_dim <= 0 || !status) return NGT_ERR_INVALID_ARGUMENT;
+    if (s > 0 && (!q || !k || !v || !out || !lse || !node_scores)) return NGT_ERR_INVALID_ARGUMENT;
+    if (head_dim % 8 != 0 || head_dim > 64) return NGT_ERR_UNSUPPORTED;
+    if (!(dropout_p >= 0.f && dropout_p < 1.f) || !(scale > 0.f)) return NGT_ERR_INVALID_ARGUMENT;
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)) return NGT_ERR_MISALIGNED;
+    if (s * (int64_t)heads * head_dim >= (int64_t)INT32_MAX) return NGT_ERR_TOO_LARGE;
+    if (s == 0) return NGT_OK;
+    int rc = check_bias_args(s, heads, bias_head_stride, bias);
+    if (rc != NGT_OK) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const uint32_t sd = (uint32_t)(seed ^ (seed >> 32));
+    if (head_dim <= 32)
+        return launch_fwd<32, true>(s, heads, head_dim, scale, score_scale, dropout_p, sd, q, k, v, out, lse,
+                                    node_scores, status, st, bias, bias_head_stride);
+    return launch_fwd<64, true>(s, heads, head_dim, scale, score_scale, dropout_p, sd, q, k, v, out, lse, node_scores,
+                                status, st, bias, bias_head_stride);
+}
+
+extern "C" int ngt_dense_attn_backward_bias(int64_t s, int heads, int head_dim, float scale, float dropout_p,
+                                            uint64_t seed, const void *q, const void *k, const void *v, const void *out,
+                                            const void *dout, const float *lse, const float *bias,
+                                            int64_t bias_head_stride, float *delta, float *dq_accum, void *dq, void *dk,
+                                            void *dv, float *dbias, int32_t *status, ngt_stream_t stream) {
+    if (s < 0 || heads <= 0 || head_dim <= 0 || !status) return NGT_ERR_INVALID_ARGUMENT;
+    if (s > 0 && (!q || !k || !v || !out || !dout || !lse || !delta || !dq_accum || !dq || !dk || !dv))
+        return NGT_ERR_INVALID_ARGUMENT;
+    if (head_dim % 8 != 0 || head_dim > 64) return NGT_ERR_UNSUPPORTED;
+    if (!(dropout_p >= 0.f && dropout_p < 1.f)) return NGT_ERR_INVALID_ARGUMENT;
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(dk) || !aligned16(dv)) return NGT_ERR_MISALIGNED;
+    if (s * (int64_t)heads * head_dim >= (int64_t)INT32_MAX) return NGT_ERR_TOO_LARGE;
+    if (s == 0) return NGT_OK;
+    int rc = check_bias_args(s, heads, bias_head_stride, bias);
+    if (rc != NGT_OK) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const uint32_t sd = (uint32_t)(seed ^ (seed >> 32));
+    if (head_dim <= 32)
+        return launch_bwd_bias<32>(s, heads, head_dim, scale, dropout_p, sd, q, k, v, out, dout, lse, bias,
+                                   bias_head_stride, delta, dq_accum, dq, dk, dv, dbias, status, st);
+    return launch_bwd_bias<64>(s, heads, head_dim, scale, dropout_p, sd, q, k, v, out, dout, lse, bias,
+                               bias_head_stride, delta, dq_accum, dq, dk, dv, dbias, status, st);
 }

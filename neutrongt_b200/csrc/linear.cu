@@ -26,6 +26,7 @@
 // graphormer_dist_node_level.py:179, 183, 286).
 #include "chunk_sum.cuh"
 #include "common.cuh"
+#include "gemm_bf16.h"
 #include "linear_tc.h"
 
 namespace ngt {
@@ -535,8 +536,9 @@ extern "C" int ngt_linear_backward_weight(int64_t rows, int in_features, int out
 
 extern "C" int ngt_linear_status(int32_t *timeouts) {
     if (!timeouts) return NGT_ERR_INVALID_ARGUMENT;
-    int n = 0;
-    const int rc = linear_tc_timeouts(&n);
-    *timeouts = n;
+    int n = 0, m = 0;
+    int rc = linear_tc_timeouts(&n);
+    if (rc == NGT_OK) rc = gemm_bf16_timeouts(&m);
+    *timeouts = n + m;
     return rc;
 }

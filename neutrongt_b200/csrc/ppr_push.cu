@@ -1,0 +1,300 @@
+// Push-based approximate personalised PageRank with per-seed top-k (sm_100a).
+//
+// Replaces the reference's default PPR backend, `personal_pagerank_torch_geometric`
+// (NeutronGT/core/ppr_backends/torch_geometric_backend.py:5-30): PyG's `get_ppr(edge_index,
+// alpha, eps)` followed by a per-source top-k loop in Python.  PyG's function implements the
+// published push method (Andersen, Chung & Lang 2006; the variant of Bojchevski et al., PPRGo
+// 2020), run per seed s over the row-stochastic walk of the CSR graph:
+//
+//   p = {s: 0}, r = {s: alpha}, stack = [s]
+//   while stack:  u = pop()
+//       res = r[u];  p[u] += res (an entry is created at u's first pop);  r[u] = 0
+//       for v in adj(u) in CSR order:
+//           r[v] += ((1 - alpha) * res) / deg(u)
+//           if r[v] >= (alpha * eps) * deg(v) and v is not on the stack:  push(v)
+//
+// then keeps, for a seed with more than topk entries, the topk largest (ties: smaller node
+// first), emitted by (value desc, node asc); a seed with at most topk entries keeps p in
+// insertion order (seed first, then first-pop order).
+//
+// One warp per seed, persistent warps taking seeds from a counter.  Each warp owns a slot of
+// dense per-node arrays in the workspace (r, p values, flags) plus its stack, p list and the list
+// of touched nodes, which resets exactly what the seed wrote.  A push spreads one adjacency row
+// over the lanes, 32 neighbours per step: the neighbours of a row are distinct (columns ascend,
+// so a repeated edge shows as equal neighbouring lanes; such a step runs on lane 0 alone), so
+// their updates commute, and the stack appends are placed with a ballot in lane (= CSR) order.
+// Every operation is a separate IEEE fp64 rounding (__dmul_rn / __ddiv_rn / __dadd_rn) in the
+// method's own order, so the result is bit-identical to the sequential method (the CPU
+// restatement in oracle/push_oracle.c).
+#include "common.cuh"
+
+namespace ngt {
+namespace {
+
+constexpr int kPushThreads = 256;
+constexpr int kPushWarps = kPushThreads / 32;
+
+struct PushWs {
+    double *r, *pv;
+    uint8_t *fl;
+    int32_t *stack, *plist, *touched;
+    unsigned long long *counter;   // [0] next seed, [1] pushes, [2] adjacency entries read
+    size_t used;
+};
+
+// Slot-major layout: slot k's arrays at k * n.  256-byte aligned pieces.
+PushWs carve_push(void *base, int64_t n, int64_t slots) {
+    PushWs w;
+    char *p = static_cast<char *>(base);
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        off = (off + 255) & ~size_t(255);
+        char *q = p ? p + off : nullptr;
+        off += bytes;
+        return q;
+    };
+    const size_t ns = (size_t)n * (size_t)slots;
+    w.counter = reinterpret_cast<unsigned long long *>(take(4 * sizeof(unsigned long long)));
+    w.r = reinterpret_cast<double *>(take(ns * sizeof(double)));
+    w.pv = reinterpret_cast<double *>(take(ns * sizeof(double)));
+    w.stack = reinterpret_cast<int32_t *>(take(ns * sizeof(int32_t)));
+    w.plist = reinterpret_cast<int32_t *>(take(ns * sizeof(int32_t)));
+    w.touched = reinterpret_cast<int32_t *>(take(ns * sizeof(int32_t)));
+    w.fl = reinterpret_cast<uint8_t *>(take(ns));
+    w.used = off;
+    return w;
+}
+
+constexpr uint8_t kTouched = 1, kInP = 2, kOnStack = 4;
+
+// One neighbour update of the method in its sequential form (lane 0, for a step that holds a
+// repeated neighbour).
+__device__ __forceinline__ void relax_one(int32_t v, double val, double alpha_eps, const int64_t *__restrict__ rowptr,
+                                          double *r, uint8_t *fl, int32_t *stack, int32_t *touched, int &sp, int &nt) {
+    const uint8_t f = fl[v];
+    const double rv = (f & kTouched) ? __dadd_rn(r[v], val) : val;
+    r[v] = rv;
+    uint8_t g = f | kTouched;
+    if (!(f & kTouched)) touched[nt++] = v;
+    const double thr = __dmul_rn(alpha_eps, (double)(rowptr[v + 1] - rowptr[v]));
+    if (rv >= thr && !(f & kOnStack)) {
+        g |= kOnStack;
+        stack[sp++] = v;
+    }
+    fl[v] = g;
+}
+
+__global__ void __launch_bounds__(kPushThreads)
+    ppr_push_kernel(int n, const int64_t *__restrict__ rowptr, const int32_t *__restrict__ col, double alpha,
+                    double eps, int s0, int s1, int topk, int slots, int64_t *__restrict__ out_idx,
+                    float *__restrict__ out_val, double *__restrict__ out_val64, int32_t *__restrict__ out_cnt,
+                    int32_t *__restrict__ info, PushWs w, long long max_pushes) {
+    const int lane = threadIdx.x & 31;
+    const int slot = blockIdx.x * kPushWarps + (threadIdx.x >> 5);
+    if (slot >= slots) return;
+    const size_t base = (size_t)slot * (size_t)n;
+    double *r = w.r + base, *pv = w.pv + base;
+    uint8_t *fl = w.fl + base;
+    int32_t *stack = w.stack + base, *plist = w.plist + base, *touched = w.touched + base;
+    const double keep = 1.0 - alpha;
+    const double alpha_eps = __dmul_rn(alpha, eps);
+    const unsigned full = 0xffffffffu;
+    const unsigned lt = (1u << lane) - 1u;
+    unsigned long long pushes = 0, read = 0;
+
+    for (;;) {
+        int s = 0;
+        if (lane == 0) s = (int)atomicAdd(w.counter, 1ull) + s0;
+        s = __shfl_sync(full, s, 0);
+        if (s >= s1) break;
+        int sp = 1, np = 1, nt = 1;
+        if (lane == 0) {
+            r[s] = alpha;
+            pv[s] = 0.0;
+            fl[s] = kTouched | kInP | kOnStack;
+            touched[0] = s;
+            plist[0] = s;
+            stack[0] = s;
+        }
+        __syncwarp();
+        long long count = 0;
+        bool capped = false;
+        while (sp > 0) {
+            if (++count > max_pushes) {
+                capped = true;
+                break;
+            }
+            const int u = stack[--sp];
+            double res = 0.0;
+            int added = 0;
+            if (lane == 0) {
+                const uint8_t f = fl[u];
+                res = r[u];
+                if (f & kInP) {
+                    pv[u] = __dadd_rn(pv[u], res);
+                } else {
+                    pv[u] = res;
+                    plist[np] = u;
+                    added = 1;
+                }
+                fl[u] = (uint8_t)((f | kInP) & ~kOnStack);
+                r[u] = 0.0;
+            }
+            res = __shfl_sync(full, res, 0);
+            np += __shfl_sync(full, added, 0);
+            __syncwarp();
+            pushes++;
+            const int64_t b = rowptr[u], e = rowptr[u + 1];
+            if (e == b) continue;
+            read += (unsigned long long)(e - b);
+            const double val = __ddiv_rn(__dmul_rn(keep, res), (double)(e - b));
+            for (int64_t q0 = b; q0 < e; q0 += 32) {
+                const int64_t q = q0 + lane;
+                const bool act = q < e;
+                const int32_t v = act ? col[q] : -1;
+                const int32_t prev = __shfl_up_sync(full, v, 1);
+                const bool dup = __any_sync(full, act && lane > 0 && v == prev);
+                if (!dup) {
+                    bool fresh = false, push = false;
+                    if (act) {
+                        const uint8_t f = fl[v];
+                        const double rv = (f & kTouched) ? __dadd_rn(r[v], val) : val;
+                        r[v] = rv;
+                        fresh = !(f & kTouched);
+                        const double thr = __dmul_rn(alpha_eps, (double)(rowptr[v + 1] - rowptr[v]));
+                        push = rv >= thr && !(f & kOnStack);
+                        fl[v] = (uint8_t)(f | kTouched | (push ? kOnStack : 0));
+                    }
+                    const unsigned bf = __ballot_sync(full, fresh), bp = __ballot_sync(full, push);
+                    if (fresh) touched[nt + __popc(bf & lt)] = v;
+                    if (push) stack[sp + __popc(bp & lt)] = v;
+                    nt += __popc(bf);
+                    sp += __popc(bp);
+                } else {
+                    __syncwarp();
+                    int sp2 = sp, nt2 = nt;
+                    if (lane == 0)
+                        for (int64_t qq = q0; qq < e && qq < q0 + 32; qq++)
+                            relax_one(col[qq], val, alpha_eps, rowptr, r, fl, stack, touched, sp2, nt2);
+                    sp = __shfl_sync(full, sp2, 0);
+                    nt = __shfl_sync(full, nt2, 0);
+                }
+                __syncwarp();
+            }
+        }
+        if (capped && lane == 0) atomicAdd(info, 1);
+        // ---- selection ----
+        const int o = s - s0;
+        if (np <= topk) {
+            for (int i = lane; i < np; i += 32) {
+                const int c = plist[i];
+                const double x = pv[c];
+                out_idx[(int64_t)o * topk + i] = c;
+                out_val[(int64_t)o * topk + i] = __double2float_rn(x);
+                if (out_val64) out_val64[(int64_t)o * topk + i] = x;
+            }
+            if (lane == 0) out_cnt[o] = np;
+        } else {
+            for (int t = 0; t < topk; t++) {
+                double bv = -1.0;
+                int bc = -1, bi = -1;
+                for (int i = lane; i < np; i += 32) {
+                    const int c = plist[i];
+                    if (c < 0) continue;
+                    const double x = pv[c];
+                    if (bi < 0 || x > bv || (x == bv && c < bc)) {
+                        bv = x;
+                        bc = c;
+                        bi = i;
+                    }
+                }
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) {
+                    const double ov = __shfl_xor_sync(full, bv, off);
+                    const int oc = __shfl_xor_sync(full, bc, off), oi = __shfl_xor_sync(full, bi, off);
+                    const bool take = oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oc < bc));
+                    if (take) {
+                        bv = ov;
+                        bc = oc;
+                        bi = oi;
+                    }
+                }
+                if (lane == 0) {
+                    out_idx[(int64_t)o * topk + t] = bc;
+                    out_val[(int64_t)o * topk + t] = __double2float_rn(bv);
+                    if (out_val64) out_val64[(int64_t)o * topk + t] = bv;
+                    plist[bi] = -1;
+                }
+                __syncwarp();
+            }
+            if (lane == 0) out_cnt[o] = topk;
+        }
+        // ---- reset what this seed wrote ----
+        for (int i = lane; i < nt; i += 32) {
+            const int v = touched[i];
+            r[v] = 0.0;
+            pv[v] = 0.0;
+            fl[v] = 0;
+        }
+        __syncwarp();
+    }
+    if (lane == 0) {
+        atomicAdd(w.counter + 1, pushes);
+        atomicAdd(w.counter + 2, read);
+    }
+}
+
+}  // namespace
+}  // namespace ngt
+
+using namespace ngt;
+
+extern "C" int ngt_ppr_push_workspace_size(int64_t n, int64_t slots, size_t *bytes) {
+    if (n < 0 || slots <= 0 || !bytes) return NGT_ERR_INVALID_ARGUMENT;
+    *bytes = carve_push(nullptr, n, slots).used;
+    return NGT_OK;
+}
+
+extern "C" int ngt_ppr_push_topk(int64_t n, const int64_t *rowptr, const int32_t *col, double alpha, double eps,
+                                 int64_t seed_start, int64_t seed_end, int64_t topk, int64_t slots,
+                                 int64_t *out_idx, float *out_val, double *out_val64, int32_t *out_cnt,
+                                 int32_t *info, void *workspace, size_t workspace_bytes, ngt_stream_t stream) {
+    if (n < 0 || seed_start < 0 || seed_end > n || seed_start > seed_end || topk <= 0 || slots <= 0 || !info)
+        return NGT_ERR_INVALID_ARGUMENT;
+    if (!(alpha > 0.0 && alpha <= 1.0) || !(eps > 0.0)) return NGT_ERR_INVALID_ARGUMENT;
+    if (n >= (int64_t)INT32_MAX || topk >= (int64_t)INT32_MAX || slots >= (int64_t)INT32_MAX)
+        return NGT_ERR_TOO_LARGE;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (cudaMemsetAsync(info, 0, sizeof(int32_t), st) != cudaSuccess) return NGT_ERR_CUDA;
+    if (seed_start == seed_end) return NGT_OK;
+    if (!rowptr || !col || !out_idx || !out_val || !out_cnt) return NGT_ERR_INVALID_ARGUMENT;
+    PushWs w = carve_push(workspace, n, slots);
+    if (!workspace || workspace_bytes < w.used) return NGT_ERR_WORKSPACE;
+    // the slot arrays start (and must stay) zero: cleared here once, and every seed resets what it wrote
+    if (cudaMemsetAsync(workspace, 0, w.used, st) != cudaSuccess) return NGT_ERR_CUDA;
+    // Termination guard only: a pop of a node with neighbours removes alpha * res >= alpha^2 eps of the
+    // residual mass (alpha to start), so there are at most 1 + 1 / (alpha eps) of those; a node without
+    // neighbours enters the stack only through an edge relaxation.  Past this bound a seed stops and
+    // counts in *info.
+    const double bound = 1.0 / (alpha * alpha * eps) + 4294967296.0;
+    const long long max_pushes = bound > 9.0e18 ? (long long)9.0e18 : (long long)bound;
+    const int blocks = (int)((slots + kPushWarps - 1) / kPushWarps);
+    ppr_push_kernel<<<blocks, kPushThreads, 0, st>>>((int)n, rowptr, col, alpha, eps, (int)seed_start, (int)seed_end,
+                                                    (int)topk, (int)slots, out_idx, out_val, out_val64, out_cnt,
+                                                    info, w, max_pushes);
+    NGT_CHECK_LAUNCH();
+    return NGT_OK;
+}
+
+extern "C" int ngt_ppr_push_stats(const void *workspace, int64_t n, int64_t slots, int64_t *pushes_and_reads,
+                                  ngt_stream_t stream) {
+    if (!workspace || !pushes_and_reads || n < 0 || slots <= 0) return NGT_ERR_INVALID_ARGUMENT;
+    unsigned long long c[3];
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (cudaMemcpyAsync(c, workspace, sizeof(c), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return NGT_ERR_CUDA;
+    pushes_and_reads[0] = (int64_t)c[1];
+    pushes_and_reads[1] = (int64_t)c[2];
+    return NGT_OK;
+}

@@ -11,9 +11,15 @@
   cores with split TF32 operands (fp32 precision, `csrc/linear_tc.cu`); the weight grad and wider
   outputs are fp32 FFMA GEMMs sized to the SM count for the windows' thin shapes.
 
+On CUDA bf16 inputs with a bf16 weight (the large model trained in bf16), `Linear` runs the bf16
+tcgen05 GEMMs of `csrc/gemm_bf16.cu`: `ngt_linear_bf16_forward`, `ngt_linear_bf16_backward_input`
+and `ngt_linear_bf16_backward_weight` (fp32 accumulation in TMEM, TMA-fed 128-byte-swizzled
+tiles, any size with both feature counts multiples of 8).
+
 torch's kernels for these ops take 15-60 us per call on the models' [~10^4, 32..256] fp32
-windows; these take a few.  Other devices, dtypes or shapes (features not a multiple of 4, a
-LayerNorm wider than 1024, a Linear inner dimension above 256) use the torch operators.  Reference
+windows; these take a few.  Other devices, dtypes or shapes (features not a multiple of 4 (fp32)
+or 8 (bf16), a LayerNorm wider than 1024, an fp32 Linear inner dimension above 256) use the torch
+operators.  Reference
 layers: NeutronGT/models/gt_dist_node_level_single_window.py:235-241, 311-325, 360-361, 537, 565;
 graphormer_dist_node_level.py:179, 183, 286.
 """
@@ -209,6 +215,79 @@ class _LinearFn(torch.autograd.Function):
         return dx, dw, db
 
 
+_WSB: dict = {}
+
+
+def _linear_bf16_ws(rows: int, in_f: int, out_f: int, device) -> torch.Tensor:
+    key = (rows, in_f, out_f, device.index)
+    nbytes = _WSB.get(key)
+    if nbytes is None:
+        nbytes = _WSB[key] = _lib.size_query(_lib.lib().ngt_linear_bf16_weight_workspace_size, rows, in_f, out_f)
+    return _lib.workspace(nbytes, device)
+
+
+class _LinearBf16Fn(torch.autograd.Function):
+    """bf16 y = x W^T + b on the tcgen05 tensor cores (fp32 accumulation, one bf16 rounding)."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias):
+        shape = x.shape
+        out_f, in_f = weight.shape
+        x2 = x.reshape(-1, in_f).contiguous()
+        rows = x2.shape[0]
+        y = torch.empty(rows, out_f, dtype=torch.bfloat16, device=x.device)
+        _lib.check(_lib.lib().ngt_linear_bf16_forward(rows, in_f, out_f, _lib.ptr(x2), _lib.ptr(weight),
+                                                      _lib.ptr(bias), _lib.ptr(y), _lib.stream_of(x2)),
+                   "ngt_linear_bf16_forward")
+        ctx.save_for_backward(x2, weight)
+        ctx.shape = shape
+        ctx.has_bias = bias is not None
+        return y.view(*shape[:-1], out_f)
+
+    @staticmethod
+    def backward(ctx, g):
+        x2, weight = ctx.saved_tensors
+        out_f, in_f = weight.shape
+        g2 = g.reshape(-1, out_f).to(torch.bfloat16).contiguous()
+        rows = g2.shape[0]
+        dx = dw = db = None
+        if ctx.needs_input_grad[0]:
+            dx = torch.empty(rows, in_f, dtype=torch.bfloat16, device=g2.device)
+            _lib.check(_lib.lib().ngt_linear_bf16_backward_input(rows, in_f, out_f, _lib.ptr(g2), _lib.ptr(weight),
+                                                                 _lib.ptr(dx), _lib.stream_of(g2)),
+                       "ngt_linear_bf16_backward_input")
+            dx = dx.view(ctx.shape)
+        want_db = ctx.has_bias and ctx.needs_input_grad[2]
+        if ctx.needs_input_grad[1] or want_db:
+            overlap = _state.overlap
+            cur = torch.cuda.current_stream(g2.device)
+            side = _side_stream(g2.device) if overlap else cur
+            if overlap:
+                side.wait_stream(cur)
+            with torch.cuda.stream(side):
+                dw = torch.empty(out_f, in_f, dtype=torch.bfloat16, device=g2.device)
+                if want_db:
+                    db = torch.empty(out_f, dtype=torch.bfloat16, device=g2.device)
+                ws = _linear_bf16_ws(rows, in_f, out_f, g2.device)
+                _lib.check(_lib.lib().ngt_linear_bf16_backward_weight(rows, in_f, out_f, _lib.ptr(x2), _lib.ptr(g2),
+                                                                      _lib.ptr(dw), _lib.ptr(db), _lib.ptr(ws),
+                                                                      ws.numel(), _lib.stream_of(g2)),
+                           "ngt_linear_bf16_backward_weight")
+            if overlap:
+                x2.record_stream(side)
+                g2.record_stream(side)
+                _join_later(cur, side)
+            if not ctx.needs_input_grad[1]:
+                dw = None
+        return dx, dw, db
+
+
+def _bf16_linear_ok(x: torch.Tensor, weight: torch.Tensor, bias) -> bool:
+    return (x.is_cuda and x.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16 and x.numel() > 0
+            and (bias is None or bias.dtype == torch.bfloat16)
+            and weight.shape[0] % 8 == 0 and weight.shape[1] % 8 == 0)
+
+
 class LayerNorm(nn.LayerNorm):
     def forward(self, x):
         if (self.elementwise_affine and self.bias is not None and len(self.normalized_shape) == 1
@@ -222,4 +301,6 @@ class Linear(nn.Linear):
         if (self.bias is not None and _rows_ok(x, 4) and self.weight.dtype == torch.float32 and x.numel() > 0
                 and self.in_features % 4 == 0 and self.out_features % 4 == 0):
             return _LinearFn.apply(x, self.weight, self.bias)
+        if _bf16_linear_ok(x, self.weight, self.bias):
+            return _LinearBf16Fn.apply(x, self.weight, self.bias)
         return F.linear(x, self.weight, self.bias)

@@ -69,3 +69,15 @@ def test_invalid_arguments_are_rejected_without_a_gpu():
     assert _lib.size_query(lib.ngt_duplicate_rerange_workspace_size, 1000, 50) >= 1000 * 4
     assert lib.ngt_halo_merge(10, None, None, None, 1, None, 0, 5, None, None, None, 0, None) == 1
     assert lib.ngt_duplicate_rerange(10, 1, None, None, 0, None, None, None, None, 0, None) == 1
+
+
+def test_bf16_linear_shape_checks_without_a_gpu():
+    import ctypes
+
+    from neutrongt_b200 import _lib
+    lib = _lib.lib()
+    out = ctypes.c_size_t(0)
+    assert lib.ngt_linear_bf16_weight_workspace_size(1000, 30, 16, ctypes.byref(out)) == 1   # 30 % 8 != 0
+    assert lib.ngt_linear_bf16_weight_workspace_size(32768, 768, 768, ctypes.byref(out)) == 0
+    assert out.value >= 768 * 768 * 4
+    assert lib.ngt_linear_bf16_forward(10, 64, 12, None, None, None, None, None) == 1        # 12 % 8 != 0

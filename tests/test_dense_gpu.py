@@ -152,3 +152,68 @@ def test_status_word_reports_a_timeout_without_a_host_wait(cuda):
     x.backward(dout)
     check_dense_status()
     assert int(sw.word.item()) == 0
+
+
+# ---------------- attn_bias / pruning_mask / mask (`…single_window.py:78-99`) ----------------
+
+@pytest.mark.parametrize("case", ["bias_d16", "bias_pruning_mask_d24", "mask_d64"])
+def test_bias_and_masks_match_reference_fixture(cuda, case):
+    """attn_bias and pruning_mask added to the scores, masked entries filled with -1e9 (one query row
+    entirely masked): outputs and the gradients of q, k, v, attn_bias and pruning_mask against the
+    reference module's own fp64 results."""
+    from neutrongt_b200.dense_attention import full_attention
+    c = golden("dense_attention.pt")[case]
+    q, k, v, g = (c[n].to(cuda) for n in ("q", "k", "v", "dout"))
+    qd, kd, vd = (t.clone().requires_grad_(True) for t in (q, k, v))
+    b = c["attn_bias"].to(cuda).requires_grad_(True) if c["attn_bias"] is not None else None
+    pm = c["pruning_mask"].to(cuda).requires_grad_(True) if c["pruning_mask"] is not None else None
+    mask = c["mask"].to(cuda) if c["mask"] is not None else None
+    x, ns = full_attention(kd, qd, vd, b, mask=mask, pruning_mask=pm)
+    x.backward(g)
+    errs = {"x": rel_err(x, c["x"]), "node_scores": rel_err(ns, c["node_scores"]), "dq": rel_err(qd.grad, c["dq"]),
+            "dk": rel_err(kd.grad, c["dk"]), "dv": rel_err(vd.grad, c["dv"])}
+    if b is not None:
+        errs["dbias"] = rel_err(b.grad, c["dbias"])
+    if pm is not None:
+        errs["dpruning"] = rel_err(pm.grad, c["dpruning"])
+    assert all(e < BF16_TOL for e in errs.values()), errs
+    assert torch.isfinite(x).all()
+
+
+@pytest.mark.parametrize("s,H,D,shared", [(1000, 4, 24, False), (777, 2, 64, True), (300, 3, 16, False)])
+def test_bias_against_oracle(cuda, s, H, D, shared):
+    from neutrongt_b200.dense_attention import full_attention
+    from oracle import dense as odense
+    q, k, v, dout = _inputs(s, H, D, s + D)
+    g = torch.Generator(device="cuda").manual_seed(s)
+    bias = torch.randn(1, 1 if shared else H, s, s, generator=g, device="cuda")
+    mask = torch.rand(s, s, generator=g, device="cuda") < 0.2
+    qd, kd, vd = (t.clone().unsqueeze(0).requires_grad_(True) for t in (q, k, v))
+    bd = bias.clone().requires_grad_(True)
+    x, ns = full_attention(kd, qd, vd, bd, mask=mask)
+    x.backward(dout.unsqueeze(0))
+    qr, kr, vr = (t.float().unsqueeze(0).clone().requires_grad_(True) for t in (q, k, v))
+    br = bias.clone().requires_grad_(True)
+    rx, rns = odense.full_attention(kr, qr, vr, br, mask=mask)
+    rx.backward(dout.float().unsqueeze(0))
+    errs = {"x": rel_err(x, rx), "ns": rel_err(ns, rns), "dq": rel_err(qd.grad, qr.grad), "dk": rel_err(kd.grad, kr.grad),
+            "dv": rel_err(vd.grad, vr.grad), "dbias": rel_err(bd.grad, br.grad)}
+    assert all(e < BF16_TOL for e in errs.values()), errs
+
+
+def test_bias_with_dropout_matches_mask_restatement(cuda):
+    from neutrongt_b200.dense_attention import full_attention
+    from oracle import dense as odense
+    s, H, D, p, seed = 256, 2, 24, 0.3, 987654321
+    q, k, v, dout = _inputs(s, H, D, 17)
+    bias = torch.randn(1, H, s, s, device="cuda")
+    qd, kd, vd = (t.clone().unsqueeze(0).requires_grad_(True) for t in (q, k, v))
+    x, _ = full_attention(kd, qd, vd, bias, dropout_p=p, seed=seed)
+    x.backward(dout.unsqueeze(0))
+    keep = keep_mask(seed, s, H, p)
+    qr, kr, vr = (t.float().unsqueeze(0).clone().requires_grad_(True) for t in (q, k, v))
+    rx, _ = odense.full_attention(kr, qr, vr, bias, keep=keep, dropout_p=p)
+    rx.backward(dout.float().unsqueeze(0))
+    assert rel_err(x, rx) < BF16_TOL
+    assert rel_err(qd.grad, qr.grad) < BF16_TOL and rel_err(kd.grad, kr.grad) < BF16_TOL
+    assert rel_err(vd.grad, vr.grad) < BF16_TOL

@@ -170,3 +170,107 @@ def test_dense_reference_dispatch_matches_full_attention():
     assert c["forward_x"].shape == (1, c["s"], c["H"] * c["D"])
     assert rel_err(c["forward_x"].reshape(c["x"].shape), c["x"]) < 1e-5
     assert rel_err(c["forward_score"], c["node_scores"]) < 1e-5
+
+
+# ---------------- push PPR (oracle/push_oracle.c): the published method and its guarantee ----------------
+
+def _push_python(rowptr, col, alpha, eps, seed):
+    """The push method written with Python dicts and a list stack, line by line as the published
+    algorithm states it (PPRGo variant of Andersen, Chung & Lang); returns p in insertion order."""
+    deg = [rowptr[i + 1] - rowptr[i] for i in range(len(rowptr) - 1)]
+    p, r, q = {seed: 0.0}, {seed: alpha}, [seed]
+    while q:
+        u = q.pop()
+        res = r.get(u, 0.0)
+        p[u] = p[u] + res if u in p else res
+        r[u] = 0.0
+        for v in col[rowptr[u]:rowptr[u + 1]]:
+            val = (1 - alpha) * res / deg[u]
+            r[v] = r[v] + val if v in r else val
+            if r[v] >= alpha * eps * deg[v] and v not in q:
+                q.append(v)
+    return list(p.items())
+
+
+@pytest.mark.parametrize("alpha,eps", [(0.15, 1e-3), (0.85, 1e-4), (0.2, 1e-5)])
+def test_push_oracle_matches_the_python_statement(alpha, eps):
+    import numpy as np
+    from neutrongt_b200 import synthetic
+    rowptr, col = synthetic.chung_lu_graph(120, 500, seed=17)
+    rp, cl = rowptr.tolist(), col.tolist()
+    big = 10 ** 6
+    ei, v = oppr.personal_pagerank_push(None, alpha, topk=big, eps=eps, csr_data={"rowptr": rowptr, "col": col},
+                                        return_fp64=True)
+    for seed in (0, 1, 7, 63, 119):
+        want = _push_python(rp, cl, alpha, eps, seed)
+        sel = (ei[0] == seed).nonzero().flatten()
+        got = list(zip(ei[1, sel].tolist(), v[sel].tolist()))
+        assert got == want                     # same entries, same insertion order, same bits
+    # top-k: (value desc, node asc) when a seed has more entries than topk
+    ei5, v5 = oppr.personal_pagerank_push(None, alpha, topk=5, eps=eps, csr_data={"rowptr": rowptr, "col": col},
+                                          return_fp64=True)
+    for seed in (0, 7):
+        want = sorted(_push_python(rp, cl, alpha, eps, seed), key=lambda t: (-t[1], t[0]))[:5]
+        sel = (ei5[0] == seed).nonzero().flatten()
+        assert list(zip(ei5[1, sel].tolist(), v5[sel].tolist())) == want
+    assert np.all(np.diff(ei5[0].numpy()) >= 0)
+
+
+@pytest.mark.parametrize("n,m,alpha,eps", [(200, 900, 0.15, 1e-4), (150, 2000, 0.85, 1e-3), (400, 1200, 0.3, 1e-5)])
+def test_push_oracle_meets_the_error_guarantee(n, m, alpha, eps):
+    """Undirected graph: 0 <= pi_s(v) - p_s(v) < eps * deg(v) for every seed s and node v, with pi_s the
+    exact PPR (teleport alpha) from a dense solve."""
+    import numpy as np
+    from neutrongt_b200 import synthetic
+    rowptr, col = synthetic.chung_lu_graph(n, m, seed=n + m)
+    ei, v = oppr.personal_pagerank_push(None, alpha, topk=n, eps=eps, csr_data={"rowptr": rowptr, "col": col},
+                                        return_fp64=True, nthreads=4)
+    A = np.zeros((n, n))
+    rp, cl = rowptr.numpy(), col.numpy()
+    for u in range(n):
+        np.add.at(A[u], cl[rp[u]:rp[u + 1]], 1.0)
+    assert np.array_equal(A, A.T)
+    deg = A.sum(1)
+    P = A / np.maximum(deg, 1.0)[:, None]
+    pi = alpha * np.linalg.inv(np.eye(n) - (1 - alpha) * P)
+    got = np.zeros((n, n))
+    got[ei[0].numpy(), ei[1].numpy()] = v.numpy()
+    diff = pi - got
+    assert diff.min() > -1e-12
+    assert (diff < eps * deg[None, :] + 1e-12).all()
+
+
+# ---------------- sparse product (oracle/spgemm.py) against SciPy's row-wise product ----------------
+
+def _rand_csr(rows, cols, nnz, seed, positive=True):
+    import numpy as np
+    import scipy.sparse as sp
+    g = np.random.default_rng(seed)
+    r = g.integers(0, rows, nnz)
+    c = g.integers(0, cols, nnz)
+    v = (g.random(nnz) + 0.1 if positive else g.standard_normal(nnz)).astype(np.float32)
+    mat = sp.csr_matrix((v, (r, c)), shape=(rows, cols))
+    mat.sum_duplicates()
+    mat.sort_indices()
+    return mat
+
+
+@pytest.mark.parametrize("m,n,nnz_a,nnz_b,seed", [(40, 60, 200, 500, 1), (1, 30, 5, 100, 2), (25, 25, 0, 100, 3),
+                                                  (80, 50, 600, 900, 4)])
+def test_spgemm_oracle_matches_scipy(m, n, nnz_a, nnz_b, seed):
+    import numpy as np
+    from oracle import spgemm as osg
+    a = _rand_csr(m, n, nnz_a, seed)
+    b = _rand_csr(n, n, nnz_b, seed + 100)
+    c = (a @ b).tocsr()
+    c.sort_indices()
+    rp, cl, vl = osg.csr_spgemm(a.indptr, a.indices, a.data, b.indptr, b.indices, b.data)
+    assert np.array_equal(rp, c.indptr) and np.array_equal(cl, c.indices)
+    assert np.array_equal(vl.view(np.uint32), c.data.astype(np.float32).view(np.uint32))   # bit for bit
+
+
+def test_spgemm_oracle_keeps_cancelled_entries():
+    """A row whose two products cancel: SciPy drops the entry, cuSPARSE (and this) keeps it as 0."""
+    from oracle import spgemm as osg
+    rp, cl, vl = osg.csr_spgemm([0, 2], [0, 1], [1.0, -1.0], [0, 1, 2], [0, 0], [2.0, 2.0])
+    assert rp.tolist() == [0, 1] and cl.tolist() == [0] and vl.tolist() == [0.0]
