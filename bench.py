@@ -3,20 +3,29 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Headline (`value`): graph-sparse window attention, forward + backward, in edges/s —
-one 65,536-token window per GPU, in-degree ~ Poisson(32) with uniform
-sources (E ~ 2.09M), 8 heads x head_dim 16, bf16, inputs resident in HBM, L2 flushed
-(256 MiB write) between steps.  A step is one fwd+bwd of the rank's window; with N GPUs
-each rank owns its own window (weak scaling) and value = all ranks' edges x K / the
-slowest rank's device time.
+Headline (`value`): graph-sparse window attention, forward + backward, in edges/s, on the
+isolated-kernel workload: one 65,536-token window per GPU, in-degree ~ Poisson(32) with uniform
+sources (E ~ 2.09M), 8 heads x head_dim 16, bf16, inputs resident in HBM, L2 flushed (256 MiB
+write) between steps.  A step is one fwd+bwd of the rank's window; with N GPUs each rank owns its
+own window (weak scaling) and value = all ranks' edges x K / the slowest rank's device time.
 
 The same JSON line carries:
   e2e          the same metric through the public API (`sparse_attention_bias` + autograd)
                with pinned host buffers: inputs copied in and outputs/grads copied out
                every step, CSR build included;
-  roofline     the dominant kernel (backward) against the measured HBM copy bandwidth;
+  roofline     the dominant kernel (backward) against the measured HBM copy bandwidth, plus an
+               `l2` object against an L2 copy bandwidth measured in this run;
   cpu_baseline the reference algorithm on the host cores (CPU restatement), bounded sample;
-  ppr          APPNP PPR + top-k over every seed of the config-2 graph (169,343 nodes);
+  gt_epoch     GT (4 layers, hidden 128, 8 heads, fp32) epochs on the 169,343-node graph, windows
+               built by the preprocessing pipeline (PPR, adjacency, 5 % halo merge, duplicate-first
+               order); the seeded random windows without halos as a second figure;
+  dense        GPH_Large dense windows (32,768 tokens, head_dim 24, bf16): the per-rank attention
+               share, and one whole GPH_Large encoder layer (bf16 projections on the tensor cores,
+               dense attention over 32 heads, FFN) forward + backward;
+  ppr          APPNP PPR + top-k over every seed of the 169,343-node graph (seed ranges balanced
+               by degree across ranks), push PPR (eps 1e-4, top-10) on the 232,965-node graph with
+               114.6 M directed edges, APPNP top-4 on the 2,449,029-node graph with 123.7 M
+               directed edges;
   clocks       nvidia-smi samples taken during the timed region.
 
 `--impl reference` times the reference's CPU algorithm for the same metric instead
@@ -59,6 +68,9 @@ def parse_args():
     p.add_argument("--skip-epoch", action="store_true")
     p.add_argument("--skip-dense", action="store_true")
     p.add_argument("--skip-cpu", action="store_true")
+    p.add_argument("--skip-layer", action="store_true")
+    p.add_argument("--skip-large-ppr", action="store_true",
+                   help="skip the PPR runs on the 232,965- and 2,449,029-node graphs")
     p.add_argument("--epoch-kernels", action="store_true",
                    help="print the per-kernel device time of one graph-replayed config-2 GT epoch "
                         "(torch.profiler over CUPTI) instead of the JSON line")
@@ -170,6 +182,22 @@ def measured_hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
+def measured_l2_gbs(dev, mib=24, reps=50):
+    """Copy bandwidth with source and destination both resident in L2 (24 MiB each of the 126 MB),
+    read + write bytes over CUDA-event time: the denominator of the L2 roofline."""
+    a = torch.empty(mib << 20, dtype=torch.uint8, device=dev)
+    b = torch.empty_like(a)
+    for _ in range(5):
+        b.copy_(a)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        b.copy_(a)
+    e1.record()
+    e1.synchronize()
+    return 2.0 * (mib << 20) * reps / (e0.elapsed_time(e1) / 1e3) / 1e9
+
+
 def ncu_traffic():
     """Per-launch DRAM bytes from the committed ncu summary (null when absent)."""
     path = os.path.join(ROOT, "profiles", "ncu_traffic.json")
@@ -181,7 +209,7 @@ def ncu_traffic():
 
 
 # ------------------------------------------------------------------------------------
-# workload (config 3)
+# workload: the isolated-kernel window
 # ------------------------------------------------------------------------------------
 def make_window(seed: int):
     from neutrongt_b200 import synthetic
@@ -276,9 +304,18 @@ def bench_attention(args, rank, world, dev):
                         "traffic": traffic.get("fwd")},
                 "bwd": {"ms": avg_bwd * 1e3, "achieved": bwd_bytes / avg_bwd / 1e9, "frac": bwd_bytes / avg_bwd / 1e9 / peak,
                         "traffic": traffic.get("bwd")},
+                "l2": None,
                 "compulsory_bytes": {"fwd": 4 * n * HEADS * HEAD_DIM * 2 + 4 * (n + 1 + e) + 4 * n * HEADS + 4 * n,
                                      "note": "Q,K,V,O once + CSR + Z + node scores; K/V (33.5 MB) can stay in L2, "
                                              "so the no-reuse algorithmic bytes and these bracket the DRAM traffic"}}
+
+    # L2-side roofline of the backward: its L2 traffic (lts__t_bytes of one ncu capture of this launch,
+    # profiles/ncu_traffic.json) over its time, against an L2-resident copy measured here
+    l2_peak = measured_l2_gbs(dev)
+    lts = traffic.get("bwd_lts")
+    roofline["l2"] = {"peak": l2_peak, "unit": "GB/s", "peak_kind": "measured here: L2-resident copy (24 MiB)",
+                      "traffic": lts, "achieved": (lts / avg_bwd / 1e9) if lts else None,
+                      "frac": (lts / avg_bwd / 1e9 / l2_peak) if lts else None}
 
     # e2e through the public API with pinned host buffers.  Every step copies its own inputs in and
     # its results out.  Pipelined: two CUDA streams with their own pinned buffers, and step i + 1's
@@ -358,11 +395,31 @@ _GRAPH = {}
 
 
 def config2_graph():
-    """BASELINE config 2 graph: Chung-Lu, 169,343 nodes, 1,166,243 undirected edges (seed 0)."""
+    """The 169,343-node graph: Chung-Lu, 1,166,243 undirected edges (seed 0)."""
     if "g" not in _GRAPH:
         from neutrongt_b200 import synthetic
         _GRAPH["g"] = synthetic.chung_lu_graph(169343, 1166243, seed=0)
     return _GRAPH["g"]
+
+
+PPR2 = dict(alpha=0.15, topk=8, num_iterations=20, iter_topk=8)
+
+
+def config2_windows(dev, pct=5):
+    """Windows as the reference's preprocessing builds them (rank 0 in the reference, every rank
+    here): APPNP PPR top-8 of every node, the weighted PPR adjacency (build_adj_fromat), 16 seeded
+    random parts (METIS is absent) each grown by its top 5 % PPR neighbours (the scripts'
+    --related_nodes_topk_rate 5).  Cached per process."""
+    if "windows" not in _GRAPH:
+        from neutrongt_b200 import personal_pagerank_appnp, synthetic
+        from neutrongt_b200.window import build_adj_format, merge_related_nodes
+        rowptr, col = config2_graph()
+        csr = {"rowptr": rowptr.to(dev), "col": col.to(dev)}
+        ei, val = personal_pagerank_appnp(None, csr_data=csr, device=dev, **PPR2)
+        adj, ew, _ = build_adj_format((ei, val), device=dev)
+        parts = synthetic.random_partitions(169343, 16, seed=0)
+        _GRAPH["windows"] = [merge_related_nodes(p, adj, ew, pct, device=dev).cpu() for p in parts]
+    return _GRAPH["windows"]
 
 
 def gt_model(dev):
@@ -374,8 +431,33 @@ def gt_model(dev):
                  num_edges=512, max_dist=5, edge_dim=64).to(dev)
 
 
-def bench_gt_epoch(args, rank, world, dev, warm=2, epochs=5):
-    """GT (4 layers, hidden 128, 8 heads, fp32) training epochs over 16 windows."""
+def attention_time_per_epoch(ws, dev, heads=8, dim=16, layers=4, reps=3):
+    """Device time of the sparse-attention kernels one epoch runs (every local window, every layer,
+    forward + backward), timed on their own with the epoch's window shapes (fp32)."""
+    from neutrongt_b200.attention import WindowAttentionBuffers
+    from neutrongt_b200.edge_csr import edge_csr_for
+    bufs = []
+    for p, ei in zip(ws.local_partitions, ws.local_sub_edge_index_for_partition_results):
+        n = int(p.numel())
+        q, k, v, g = (torch.randn(n, heads, dim, device=dev) for _ in range(4))
+        bufs.append((WindowAttentionBuffers(q, k, v, edge_csr_for(ei, n)), g))
+    for b, g in bufs:
+        b.forward()
+        b.backward(g)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        for b, g in bufs:
+            for _ in range(layers):
+                b.forward()
+                b.backward(g)
+    e1.record()
+    e1.synchronize()
+    return e0.elapsed_time(e1) / 1e3 / reps
+
+
+def bench_gt_epoch(args, rank, world, dev, windows, label, warm=2, epochs=5, with_cpu=True):
+    """GT (4 layers, hidden 128, 8 heads, fp32) training epochs over the given 16 windows."""
     from neutrongt_b200 import synthetic
     from neutrongt_b200.train import FlatGradients, build_window_state, train_epoch
     n = 169343
@@ -383,14 +465,13 @@ def bench_gt_epoch(args, rank, world, dev, warm=2, epochs=5):
     feature = synthetic.node_features(n, 128, seed=1)
     y = synthetic.node_labels(n, 40, seed=2)
     split = synthetic.split_idx(n, seed=3)
-    parts = synthetic.random_partitions(n, 16, seed=0)
     model = gt_model(dev)
     grads = FlatGradients(model)
     opt = torch.optim.AdamW(model.parameters(), lr=1e-4, weight_decay=0.01, fused=True)
     sched = torch.optim.lr_scheduler.LambdaLR(opt, lambda e: 1.0)
     a = SimpleNamespace(use_cache=1, attn_type="sparse")
     feat_dev = feature.to(dev)
-    ws = build_window_state(rowptr, col, parts, rank, world, feat_dev, dev, split)
+    ws = build_window_state(rowptr, col, windows, rank, world, feat_dev, dev, split)
 
     def run(feat, k):
         out = []
@@ -420,27 +501,31 @@ def bench_gt_epoch(args, rank, world, dev, warm=2, epochs=5):
     trainer.dummy = None
     del trainer
     torch.cuda.synchronize()
-    run(feature, 1)
-    timed_h = run(feature, epochs)
-    t_host = allreduce_max(statistics.mean(t for t, _ in timed_h), world)
+    t_attn = allreduce_max(attention_time_per_epoch(ws, dev), world)
     e_local = sum(int(e.shape[1]) for e in ws.local_sub_edge_index_for_partition_results)
     n_local = sum(int(p.numel()) for p in ws.local_partitions)
     edges_epoch = allreduce_sum(float(e_local), world)
-    out = {"workload": "BASELINE config 2: GT 4L/128/8H fp32, Chung-Lu 169,343 nodes / 1,166,243 undirected "
-                       "edges, 16 seeded random windows (pymetis absent), features N(0,1) dim 128, 40 classes",
+    out = {"workload": f"GT 4L/128/8H fp32 on the Chung-Lu 169,343-node / 1,166,243-edge graph, {label}; "
+                       "features N(0,1) dim 128, 40 classes",
            "epoch_time_s": t_graph, "unit": "s", "higher_is_better": False,
            "epoch_time_eager_s": t_dev,
            "loss_graph_last_epoch": gt[-1][0],
            "scaling": "strong (16 windows split round-robin over ranks)",
-           "epoch_time_host_features_s": t_host,
-           "loss_last_epoch": timed[-1][1], "windows": len(parts), "window_nodes_mean": n_local / max(1, len(ws.local_partitions)),
+           "loss_last_epoch": timed[-1][1], "windows": len(windows),
+           "window_nodes_mean": n_local / max(1, len(ws.local_partitions)),
            "attention_edges_per_epoch": edges_epoch,
-           "note": "epoch_time_s: one captured CUDA graph per window (gather, forward, loss, backward, "
-                   "gradient all-reduce, AdamW) replayed per epoch; epoch_time_eager_s: the same loop eagerly "
-                   "with device-resident features; epoch_time_host_features_s: eager, each window's features "
-                   "gathered on the host and copied through pinned memory, as the reference does per window"}
-    if rank == 0 and not args.skip_cpu:
-        out["cpu_baseline"] = gt_epoch_cpu_baseline(model, ws, feature, y, split, len(parts))
+           "attention_kernels_s_per_epoch": t_attn,
+           "attention_share": t_attn / t_graph if t_graph > 0 else None,
+           "note": "epoch_time_s: one captured CUDA graph per window (gather, forward, loss, backward, gradient "
+                   "all-reduce, AdamW) replayed per epoch; epoch_time_eager_s: the same loop eagerly; "
+                   "attention_kernels_s_per_epoch: the epoch's sparse-attention launches (4 layers x windows, "
+                   "fwd+bwd) timed alone"}
+    if with_cpu:
+        run(feature, 1)
+        timed_h = run(feature, epochs)
+        out["epoch_time_host_features_s"] = allreduce_max(statistics.mean(t for t, _ in timed_h), world)
+    if with_cpu and rank == 0 and not args.skip_cpu:
+        out["cpu_baseline"] = gt_epoch_cpu_baseline(model, ws, feature, y, split, len(windows))
     return out
 
 
@@ -479,17 +564,17 @@ def gt_epoch_cpu_baseline(model_gpu, ws, feature, y, split, n_windows, sample=2)
             "kind": "port", "sample": f"{len(times)} windows fwd+bwd+AdamW on the host, scaled to {n_windows} windows"}
 
 
-def measured_bf16_peak():
+def measured_bf16_peak(sustained=False):
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
         with open(path) as f:
-            return float(json.load(f)["bf16_tflops"]), "measured"
+            return float(json.load(f)["bf16_tflops_sustained" if sustained else "bf16_tflops"]), "measured"
     except Exception:
-        return 1590.0, "fallback"
+        return (1400.0 if sustained else 1590.0), "fallback"
 
 
 def bench_dense(args, rank, world, dev, steps=5, warm=2):
-    """Dense attention windows (per-rank share): S = 32,768 tokens of one window,
+    """GPH_Large dense attention windows, per-rank share: S = 32,768 tokens of one window,
     the rank's 4 of 32 heads after the Ulysses exchange (head_dim 24), bf16, fwd + bwd.  With N > 1
     the step is the reference's `DistributedAttentionNodeLevel` layer: the exchange (NCCL
     all_to_all_single) of q, k, v and the output is inside the timed step.  It is timed as the
@@ -547,7 +632,7 @@ def bench_dense(args, rank, world, dev, steps=5, warm=2):
     flops = fwd_flops * 3.5            # forward + backward (recompute S, dP, dV, dK, dQ)
     peak, kind = measured_bf16_peak()
     achieved = flops / t / 1e12
-    return {"workload": "BASELINE config 4 per-rank share: one window of 32,768 tokens, 4 heads of 32 "
+    return {"workload": "GPH_Large dense window, per-rank share: one window of 32,768 tokens, 4 heads of 32 "
                         "(after the Ulysses exchange), head_dim 24, bf16, dense attention fwd+bwd",
             "ms_per_step": t * 1e3, "tflops_algorithmic": achieved,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
@@ -559,25 +644,42 @@ def bench_dense(args, rank, world, dev, steps=5, warm=2):
             "ms_per_step_by_head_chunks": {str(c): v * 1e3 for c, v in per_chunks.items()} if world > 1 else None}
 
 
-def bench_ppr(args, rank, world, dev):
-    from neutrongt_b200 import personal_pagerank_appnp
-    rowptr, col = config2_graph()
-    n = 169343
-    s0, s1 = (n * rank) // world, (n * (rank + 1)) // world
-    csr = {"rowptr": rowptr.to(dev), "col": col.to(dev)}
-    params = dict(alpha=0.15, topk=8, num_iterations=20, iter_topk=8)
-    personal_pagerank_appnp(None, csr_data=csr, device=dev, source_start=s0, source_end=min(s1, s0 + 2000), **params)
+def balanced_ranges(weights, world):
+    """Contiguous seed ranges [s_r, s_{r+1}) cut at equal prefix sums of a per-seed cost, so ranks get
+    equal work while the concatenation in rank order keeps the seeds ascending (the gathered output
+    is the single-rank output, bit for bit)."""
+    c = torch.cumsum(weights.double(), 0)
+    total = float(c[-1])
+    cuts = [0] + [int(torch.searchsorted(c, total * r / world).item()) for r in range(1, world)] + [weights.numel()]
+    return [(cuts[r], max(cuts[r], cuts[r + 1])) for r in range(world)]
+
+
+def _timed_call(fn, world):
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    ei, val = personal_pagerank_appnp(None, csr_data=csr, device=dev, source_start=s0, source_end=s1, **params)
+    out = fn()
     e1.record()
     barrier(world)
-    t = allreduce_max(e0.elapsed_time(e1) / 1e3, world)
-    out = {"workload": "config 2 graph (Chung-Lu, 169,343 nodes, 2,332,486 directed edges), every node a seed, "
+    return out, allreduce_max(e0.elapsed_time(e1) / 1e3, world)
+
+
+def bench_ppr(args, rank, world, dev):
+    """APPNP PPR + top-8 over every seed of the 169,343-node graph (seeds sharded over ranks in
+    degree-balanced contiguous ranges)."""
+    from neutrongt_b200 import personal_pagerank_appnp
+    rowptr, col = config2_graph()
+    n = 169343
+    deg = (rowptr[1:] - rowptr[:-1]).to(torch.float64)
+    s0, s1 = balanced_ranges(deg + 8.0, world)[rank]
+    csr = {"rowptr": rowptr.to(dev), "col": col.to(dev)}
+    personal_pagerank_appnp(None, csr_data=csr, device=dev, source_start=s0, source_end=min(s1, s0 + 2000), **PPR2)
+    (ei, val), t = _timed_call(lambda: personal_pagerank_appnp(None, csr_data=csr, device=dev, source_start=s0,
+                                                                source_end=s1, **PPR2), world)
+    out = {"workload": "169,343-node Chung-Lu graph (2,332,486 directed edges), every node a seed, "
                        "alpha 0.15, 20 iterations, top-k 8 per iteration and at the end",
            "seeds_per_s": n / t, "seconds": t, "entries": int(allreduce_sum(float(ei.shape[1]), world)),
-           "scaling": "strong (seeds split into contiguous source ranges per rank)"}
+           "scaling": "strong (seeds split into contiguous ranges of equal degree + 8 sums per rank)"}
     if rank == 0 and world == 1:
         out["window_build"] = bench_window_build(args, dev, ei, val)
     if rank == 0 and not args.skip_cpu:
@@ -587,19 +689,134 @@ def bench_ppr(args, rank, world, dev):
         st = {}
         t0 = time.perf_counter()
         oppr.personal_pagerank_appnp(None, csr_data={"rowptr": rowptr, "col": col}, source_start=0,
-                                     source_end=sample, nthreads=threads, stats=st, **params)
+                                     source_end=sample, nthreads=threads, stats=st, **PPR2)
         tc = time.perf_counter() - t0
         out["cpu_baseline"] = {"value": sample / tc, "unit": "seeds/s", "cores": threads, "kind": "port",
                                "sample": f"seeds 0..{sample - 1}, canonical fp64 restatement in C (oracle/appnp_oracle.c)"}
-        # expansions per seed-iteration measured on the sample, for the bytes model
         touched = st["edges_touched"] / sample
         out["adjacency_entries_per_seed"] = touched
         out["achieved_gbs_adjacency_model"] = touched * n * 4 / t / 1e9
     return out
 
 
+def bench_ppr_large(args, rank, world, dev):
+    """PPR on the two large graphs, seeds sharded over ranks in degree-balanced ranges:
+    push PPR (the reference's default backend) with eps 1e-4, alpha 0.15, top-10 on 232,965 nodes /
+    57,307,946 undirected edges (mean degree ~492), and APPNP (alpha 0.15, 20 iterations, top-4) on
+    2,449,029 nodes / 61,859,140 undirected edges.  Graphs are sampled on the device."""
+    from neutrongt_b200 import personal_pagerank_appnp, personal_pagerank_torch_geometric, synthetic
+    peak, peak_kind = measured_hbm_peak()
+    res = {}
+    # ---- push PPR, 232,965 nodes ----
+    n5 = 232965
+    rp, col = synthetic.chung_lu_graph_device(n5, 114615892 // 2, seed=5, device=dev)
+    deg = (rp[1:] - rp[:-1]).double()
+    s0, s1 = balanced_ranges(deg.cpu() + 64.0, world)[rank]
+    csr = {"rowptr": rp, "col": col}
+    personal_pagerank_torch_geometric(None, 0.15, topk=10, eps=1e-4, device=dev, csr_data=csr, source_start=s0,
+                                      source_end=min(s1, s0 + 500))
+    st = {}
+    (ei, _), t = _timed_call(lambda: personal_pagerank_torch_geometric(None, 0.15, topk=10, eps=1e-4, device=dev,
+                                                                      csr_data=csr, source_start=s0, source_end=s1,
+                                                                      stats=st), world)
+    reads = allreduce_sum(float(st["edges_touched"]), world)
+    pushes = allreduce_sum(float(st["pushes"]), world)
+    # bytes per adjacency entry read in a push: column index 4, residual read + write 16, flags 2,
+    # the neighbour's degree (two row pointers) 16
+    gbs = reads * 38 / t / 1e9
+    push = {"workload": "push PPR (torch_geometric backend), alpha 0.15, eps 1e-4, top-10, every node a seed; "
+                        "232,965-node Chung-Lu graph with 114,615,892 directed edges",
+            "seconds": t, "seeds_per_s": n5 / t, "pushes": pushes, "adjacency_entries_read": reads,
+            "entries": int(allreduce_sum(float(ei.shape[1]), world)),
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                         "peak_kind": f"{peak_kind} hbm_gbs",
+                         "note": "38 algorithmic bytes per adjacency entry read (column 4, residual 8+8, flags 2, "
+                                 "neighbour degree 16); random 8-byte residual accesses"}}
+    if rank == 0 and not args.skip_cpu:
+        from oracle import ppr as oppr
+        threads = os.cpu_count() or 1
+        cpu_csr = {"rowptr": rp.cpu(), "col": col.cpu()}
+        sample = 1000
+        t0 = time.perf_counter()
+        oppr.personal_pagerank_push(None, 0.15, topk=10, eps=1e-4, csr_data=cpu_csr, source_start=0,
+                                    source_end=sample, nthreads=threads)
+        tc = time.perf_counter() - t0
+        push["cpu_baseline"] = {"value": sample / tc, "unit": "seeds/s", "cores": threads, "kind": "port",
+                                "sample": f"seeds 0..{sample - 1} (the hubs), the push method restated in C "
+                                          "(oracle/push_oracle.c)"}
+    res["push_232965"] = push
+    del rp, col, csr, deg, ei
+    torch.cuda.empty_cache()
+    # ---- APPNP top-4, 2,449,029 nodes ----
+    n4 = 2449029
+    rp, col = synthetic.chung_lu_graph_device(n4, 61859140, seed=4, device=dev)
+    deg = (rp[1:] - rp[:-1]).double()
+    s0, s1 = balanced_ranges(deg.cpu() + 8.0, world)[rank]
+    csr = {"rowptr": rp, "col": col}
+    prm = dict(alpha=0.15, topk=4, num_iterations=20, iter_topk=4)
+    personal_pagerank_appnp(None, csr_data=csr, device=dev, source_start=s0, source_end=min(s1, s0 + 2000), **prm)
+    (ei, _), t = _timed_call(lambda: personal_pagerank_appnp(None, csr_data=csr, device=dev, source_start=s0,
+                                                              source_end=s1, **prm), world)
+    appnp = {"workload": "APPNP PPR, alpha 0.15, 20 iterations, top-4 per iteration and at the end, every node a "
+                         "seed; 2,449,029-node Chung-Lu graph with 123,718,280 directed edges",
+             "seconds": t, "seeds_per_s": n4 / t, "entries": int(allreduce_sum(float(ei.shape[1]), world))}
+    if rank == 0 and not args.skip_cpu:
+        from oracle import ppr as oppr
+        threads = os.cpu_count() or 1
+        sample = 2000
+        t0 = time.perf_counter()
+        oppr.personal_pagerank_appnp(None, csr_data={"rowptr": rp.cpu(), "col": col.cpu()}, source_start=0,
+                                     source_end=sample, nthreads=threads, **prm)
+        tc = time.perf_counter() - t0
+        appnp["cpu_baseline"] = {"value": sample / tc, "unit": "seeds/s", "cores": threads, "kind": "port",
+                                 "sample": f"seeds 0..{sample - 1} (the hubs), canonical fp64 restatement in C "
+                                           "(oracle/appnp_oracle.c)"}
+    res["appnp_2449029"] = appnp
+    return res
+
+
+def bench_gph_large_layer(args, dev, steps=3, warm=2):
+    """One GPH_Large (Graphormer) encoder layer, bf16: 32,768 tokens, hidden 768, ffn 768, 32 heads of
+    24, full attention; forward + backward.  The projections run on the bf16 tcgen05 GEMMs, the
+    attention on the dense tcgen05 kernels."""
+    from neutrongt_b200.models import GraphormerEncoderLayer
+    S, hid, heads = 32768, 768, 32
+    torch.manual_seed(0)
+    layer = GraphormerEncoderLayer(hid, hid, 0.0, 0.0, heads).to(dev).to(torch.bfloat16).train()
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(1, S, hid, generator=g, device=dev).to(torch.bfloat16).requires_grad_(True)
+    dy = torch.randn(1, S, hid, generator=g, device=dev).to(torch.bfloat16)
+
+    def step():
+        layer.zero_grad(set_to_none=True)
+        x.grad = None
+        y, _, _ = layer(x, attn_type="full")
+        y.backward(dy)
+
+    for _ in range(warm):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    e1.synchronize()
+    t = e0.elapsed_time(e1) / 1e3 / steps
+    proj = 2.0 * S * 6 * hid * hid * 3          # QKV, output, FFN in and out: forward + two backward GEMMs
+    attn = 4.0 * S * S * hid * 3.5              # 4 S^2 H D forward, 2.5x that backward
+    peak, kind = measured_bf16_peak(sustained=True)
+    achieved = (proj + attn) / t / 1e12
+    return {"workload": "one GPH_Large (Graphormer) encoder layer, bf16, 32,768 tokens, hidden 768, ffn 768, "
+                        "32 heads of 24, full attention, forward + backward, one GPU",
+            "ms_per_step": t * 1e3, "tflops_algorithmic": achieved,
+            "flops": {"projections": proj, "attention": attn},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "peak_kind": f"{kind} bf16_tflops_sustained", "frac": achieved / peak}}
+
+
 def bench_window_build(args, dev, ppr_ei, ppr_val, pct=5):
-    """SURVEY next-row 1/2 on the config-2 PPR output: the weighted PPR adjacency
+    """Window construction on the 169,343-node graph's PPR output: the weighted PPR adjacency
     (build_adj_fromat), the halo merge of each of the 16 windows at the reference scripts'
     --related_nodes_topk_rate 5, and the duplicate-first order of the grown windows (two parents
     of 8).  Windows are the seeded random partitions (pymetis is absent).  Rank-0 preprocessing in
@@ -653,20 +870,33 @@ def run_ours(args):
     dev = torch.device("cuda", local)
     res = bench_attention(args, rank, world, dev)
     ppr = None if args.skip_ppr else bench_ppr(args, rank, world, dev)
-    epoch = None if args.skip_epoch else bench_gt_epoch(args, rank, world, dev)
+    if ppr is not None and not args.skip_large_ppr:
+        ppr.update(bench_ppr_large(args, rank, world, dev))
+    epoch = None
+    if not args.skip_epoch:
+        epoch = bench_gt_epoch(args, rank, world, dev, config2_windows(dev),
+                               "16 windows from the preprocessing pipeline (APPNP PPR top-8, PPR adjacency, seeded "
+                               "random parts as METIS stand-in, 5 % halo merge, duplicate-first order)")
+        from neutrongt_b200 import synthetic
+        epoch["random_windows"] = bench_gt_epoch(args, rank, world, dev, synthetic.random_partitions(169343, 16, seed=0),
+                                                 "16 seeded random windows without halo growth", epochs=3,
+                                                 with_cpu=False)
     dense = None if args.skip_dense else bench_dense(args, rank, world, dev)
+    if dense is not None and world == 1 and not args.skip_layer:
+        dense["gph_large_layer"] = bench_gph_large_layer(args, dev)
     cpu = None
     if rank == 0 and not args.skip_cpu:
         q, k, v, g, ei = res["host"]
         cpu = cpu_baseline_sample(q, k, v, g, ei)
     if rank == 0:
         line = {
-            "metric": "sparse-attn edges/s (fwd+bwd; BASELINE 'GT epoch time (s) & sparse-attn edges/s')",
+            "metric": "sparse-attn edges/s (graph-sparse window attention fwd+bwd; the GT epoch time is reported "
+                      "in gt_epoch)",
             "value": res["value"], "unit": "edges/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": res["ms_per_step"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "BASELINE config 3: isolated graph-sparse attention fwd+bwd, one 65,536-token "
-                                   "window per GPU, in-degree ~ Poisson(32), uniform sources",
+            "config": {"workload": "isolated graph-sparse attention fwd+bwd, one 65,536-token window per GPU, "
+                                   "in-degree ~ Poisson(32), uniform sources",
                        "tokens": N_TOKENS, "edges_per_window": res["edges"], "heads": HEADS, "head_dim": HEAD_DIM,
                        "l2": "flushed between steps (256 MiB write outside the timed events)",
                        "parallelism": f"independent windows, dp{world}"},
@@ -700,11 +930,13 @@ def run_reference(args):
     t = sum(times)
     value = sub.shape[1] * args.steps / t
     threads = os.cpu_count() or 1
-    line = {"impl": "reference", "metric": "sparse-attn edges/s (fwd+bwd; BASELINE 'GT epoch time (s) & sparse-attn edges/s')",
+    line = {"impl": "reference", "metric": "sparse-attn edges/s (graph-sparse window attention fwd+bwd; the GT epoch "
+                                           "time is reported in gt_epoch)",
             "value": value, "unit": "edges/s", "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": t / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "BASELINE config 3 window, bounded sample: the in-edges of the lowest "
+            "config": {"workload": "isolated-kernel window (65,536 tokens, Poisson(32) in-degrees), bounded sample: the "
+                                   "in-edges of the lowest "
                                    f"{rows} destination rows ({sub.shape[1]} edges) per step",
                        "tokens": N_TOKENS, "heads": HEADS, "head_dim": HEAD_DIM},
             "cpu_baseline": {"value": value, "unit": "edges/s", "cores": threads, "kind": "port",
@@ -715,7 +947,7 @@ def run_reference(args):
 
 
 def epoch_kernel_table(args):
-    """Kernel composition of one graph-replayed GT epoch (one GPU)."""
+    """Kernel composition of one graph-replayed GT epoch (the 169,343-node graph's pipeline windows, one GPU)."""
     from torch.profiler import ProfilerActivity, profile
     from neutrongt_b200 import synthetic
     from neutrongt_b200.train import GraphedWindowTrainer, build_window_state
@@ -726,8 +958,7 @@ def epoch_kernel_table(args):
     feature = synthetic.node_features(n, 128, seed=1).to(dev)
     y = synthetic.node_labels(n, 40, seed=2).to(dev)
     split = synthetic.split_idx(n, seed=3)
-    parts = synthetic.random_partitions(n, 16, seed=0)
-    ws = build_window_state(rowptr, col, parts, 0, 1, feature, dev, split)
+    ws = build_window_state(rowptr, col, config2_windows(dev), 0, 1, feature, dev, split)
     model = gt_model(dev)
     opt = torch.optim.AdamW(model.parameters(), lr=1e-4, weight_decay=0.01, fused=True, capturable=True)
     trainer = GraphedWindowTrainer(SimpleNamespace(use_cache=1, attn_type="sparse"), model, ws, feature, y, opt, 1,

@@ -9,6 +9,8 @@ a seed instead:
 * `chung_lu_graph` – undirected power-law graph (Chung-Lu model), symmetrised and
   stored as an int64 CSR `{rowptr, col}` with each row's columns ascending, the
   layout `utils/trans2csr.py:24-37` writes.
+* `chung_lu_graph_device` – the same model sampled on the GPU (torch's CUDA generator), for the
+  graphs with 10^7..10^8 edges; same degree distribution, different draws than the host version.
 * `poisson_window_csr` – one attention window whose in-degree per destination row
   is Poisson distributed with uniform random sources (the isolated-kernel case).
 * `random_partitions` – contiguous chunks of a seeded permutation, each sorted,
@@ -71,6 +73,49 @@ def chung_lu_graph(num_nodes: int, num_undirected_edges: int, exponent: float = 
     rowptr = np.zeros(n + 1, dtype=np.int64)
     np.cumsum(counts, out=rowptr[1:])
     return torch.from_numpy(rowptr), torch.from_numpy(dst.astype(np.int64))
+
+
+def chung_lu_graph_device(num_nodes: int, num_undirected_edges: int, exponent: float = 2.5, seed: int = 0,
+                          device="cuda") -> tuple[torch.Tensor, torch.Tensor]:
+    """`chung_lu_graph` sampled on the device: candidate pairs drawn with torch's seeded CUDA
+    generator, self loops dropped, the distinct pairs deduplicated, `num_undirected_edges` of them
+    kept by a seeded permutation.  Returns (rowptr int64, col int64) on `device`, both directions,
+    rows ascending."""
+    n, m = int(num_nodes), int(num_undirected_edges)
+    dev = torch.device(device)
+    if n <= 1 or m <= 0:
+        return torch.zeros(n + 1, dtype=torch.long, device=dev), torch.empty(0, dtype=torch.long, device=dev)
+    if m > n * (n - 1) // 2:
+        raise ValueError(f"{m} undirected edges do not fit in a simple graph on {n} nodes")
+    g = torch.Generator(device=dev).manual_seed(seed)
+    w = torch.arange(1, n + 1, dtype=torch.float64, device=dev) ** (-1.0 / (exponent - 1.0))
+    cdf = torch.cumsum(w, 0)
+    cdf /= cdf[-1].clone()
+    keys = torch.empty(0, dtype=torch.long, device=dev)
+    draw = int(m * 1.25) + 4096
+    for _ in range(256):
+        if keys.numel() >= m:
+            break
+        u = torch.searchsorted(cdf, torch.rand(draw, generator=g, device=dev, dtype=torch.float64), right=True)
+        v = torch.searchsorted(cdf, torch.rand(draw, generator=g, device=dev, dtype=torch.float64), right=True)
+        u.clamp_(max=n - 1)
+        v.clamp_(max=n - 1)
+        keep = u != v
+        lo, hi = torch.minimum(u[keep], v[keep]), torch.maximum(u[keep], v[keep])
+        keys = torch.unique(torch.cat([keys, lo * n + hi]))
+        draw = int((m - keys.numel()) * 2.0) + 4096
+    if keys.numel() < m:
+        raise RuntimeError(f"could not draw {m} distinct edges (the weights concentrate on too few pairs)")
+    keys = keys[torch.randperm(keys.numel(), generator=g, device=dev)[:m]]
+    lo, hi = keys // n, keys % n
+    src = torch.cat([lo, hi])
+    dst = torch.cat([hi, lo])
+    del keys, lo, hi
+    order = torch.argsort(src * n + dst)
+    src, dst = src[order], dst[order]
+    rowptr = torch.zeros(n + 1, dtype=torch.long, device=dev)
+    rowptr[1:] = torch.cumsum(torch.bincount(src, minlength=n), 0)
+    return rowptr, dst
 
 
 def poisson_window_csr(num_tokens: int, mean_degree: float, seed: int = 0) -> tuple[torch.Tensor, torch.Tensor]:

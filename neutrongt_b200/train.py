@@ -15,7 +15,9 @@ Changes of mechanism (not of results):
 * features are gathered on the device when the feature matrix lives there; a host feature
   matrix is gathered on the host and copied through a pinned staging buffer;
 * gradients live in one flat buffer (each parameter's .grad is a view of it), so the
-  average over ranks is one NCCL all-reduce per step instead of one per parameter;
+  average over ranks is a few NCCL all-reduces per step instead of one per parameter; in the
+  eager loop the buffer is cut into 4 MiB buckets that are all-reduced from post-accumulate
+  hooks while backward still runs (the graph-replayed loop keeps one all-reduce per step);
 * the window losses stay on the device and are read once per epoch, and the per-stage
   `torch.cuda.synchronize()` calls used for wall-clock timing are replaced by CUDA events.
 
@@ -117,12 +119,71 @@ class FlatGradients:
     the reference gives every parameter a gradient (zeros where none was produced) and
     all-reduces them (train_eval.py:289-295): `zero()` keeps the flat views for that."""
 
-    def __init__(self, model: torch.nn.Module):
+    def __init__(self, model: torch.nn.Module, bucket_bytes: int | None = None, group=None):
         self.params = [p for p in model.parameters() if p.requires_grad]
         total = sum(p.numel() for p in self.params)
         dev = self.params[0].device
         self.flat = torch.zeros(total, dtype=self.params[0].dtype, device=dev)
         self._bind()
+        self.group = group
+        self.buckets = None
+        if bucket_bytes is not None and dist.is_available() and dist.is_initialized() \
+                and dist.get_world_size(group) > 1:
+            self._make_buckets(int(bucket_bytes))
+
+    # ---- all-reduce overlapped with backward -------------------------------------------------
+    # With `bucket_bytes`, the flat buffer is cut into buckets of whole parameters, last parameter
+    # first (backward produces the last layers' gradients first).  A post-accumulate hook on each
+    # parameter counts its bucket down; a bucket whose gradients are all in is all-reduced at once,
+    # asynchronously on NCCL's stream, while backward continues with the layers below.  Buckets go
+    # out strictly in bucket order (a ready bucket waits for the ones before it), so every rank
+    # issues the same collectives in the same order; `average()` sends the rest and waits.
+    def _make_buckets(self, bucket_bytes):
+        offs, off = [], 0
+        for p in self.params:
+            offs.append(off)
+            off += p.numel()
+        esize = self.flat.element_size()
+        buckets, cur, cur_bytes = [], [], 0
+        for i in reversed(range(len(self.params))):
+            cur.append(i)
+            cur_bytes += self.params[i].numel() * esize
+            if cur_bytes >= bucket_bytes:
+                buckets.append(cur)
+                cur, cur_bytes = [], 0
+        if cur:
+            buckets.append(cur)
+        self.buckets = []
+        self.bucket_of = {}
+        for b, idx in enumerate(buckets):
+            lo = min(offs[i] for i in idx)
+            hi = max(offs[i] + self.params[i].numel() for i in idx)
+            self.buckets.append((lo, hi, len(idx)))
+            for i in idx:
+                self.bucket_of[i] = b
+        self._reset_buckets()
+        for i, p in enumerate(self.params):
+            p.register_post_accumulate_grad_hook(lambda _p, i=i: self._grad_ready(i))
+
+    def _reset_buckets(self):
+        self.pending = [n for _, _, n in self.buckets]
+        self.handles = []
+        self.next_bucket = 0
+
+    def _launch_ready(self, force=False):
+        while self.next_bucket < len(self.buckets) and (force or self.pending[self.next_bucket] == 0):
+            lo, hi, _ = self.buckets[self.next_bucket]
+            self.handles.append(dist.all_reduce(self.flat[lo:hi], op=dist.ReduceOp.SUM, group=self.group,
+                                                async_op=True))
+            self.next_bucket += 1
+
+    def _grad_ready(self, i):
+        if not self.bound:
+            return
+        b = self.bucket_of[i]
+        self.pending[b] -= 1
+        if self.pending[b] == 0:
+            self._launch_ready()
 
     def _bind(self):
         off = 0
@@ -140,11 +201,21 @@ class FlatGradients:
         if not self.bound:
             self._bind()
         self.flat.zero_()
+        if self.buckets is not None:
+            self._reset_buckets()
 
     def average(self, world_size: int, group=None):
-        if world_size > 1:
+        if world_size <= 1:
+            return
+        if self.buckets is not None and self.bound:
+            self._launch_ready(force=True)     # buckets with unused parameters go now, in order
+            for h in self.handles:
+                h.wait()
             self.flat.div_(world_size)
-            dist.all_reduce(self.flat, op=dist.ReduceOp.SUM, group=group)
+            self._reset_buckets()
+            return
+        self.flat.div_(world_size)
+        dist.all_reduce(self.flat, op=dist.ReduceOp.SUM, group=group)
 
 
 def _window_features(feature, idx_i, dup_index_i, dup_cache, device, staging=None):
@@ -175,7 +246,8 @@ def train_epoch(args, model, local_partition_ids, local_partitions, feature, y, 
     masks = getattr(structInfo, "local_train_masks", None) or []
     use_cache = bool(getattr(args, "use_cache", 1))
     if grads is None:
-        grads = FlatGradients(model)
+        # with several ranks, 4 MiB buckets are all-reduced while backward is still running
+        grads = FlatGradients(model, bucket_bytes=4 << 20 if world_size > 1 else None, group=group)
     local_count = len(local_partitions)
     max_steps = local_count
     if world_size > 1:

@@ -113,3 +113,45 @@ def test_window_node_lists_broadcast_from_rank_zero():
         assert all(torch.equal(a, b) and a.dtype == torch.long for a, b in zip(got, expected))
         assert owned == list(range(r, 8, 2))
         assert out[f"empty{r}"] == 0
+
+
+def _bucket_worker(rank, world, port, results):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from neutrongt_b200.train import FlatGradients
+    torch.manual_seed(0)
+    model = torch.nn.Sequential(torch.nn.Linear(16, 32), torch.nn.ReLU(), torch.nn.Linear(32, 32), torch.nn.ReLU(),
+                                torch.nn.Linear(32, 4))
+    unused = torch.nn.Linear(4, 4)          # a parameter without a gradient: its bucket goes in average()
+    model.add_module("unused", unused)
+    out = {}
+    for mode in ("plain", "buckets"):
+        grads = FlatGradients(model, bucket_bytes=600 if mode == "buckets" else None)
+        if mode == "buckets":
+            assert len(grads.buckets) >= 3
+        per_step = []
+        for step in range(3):
+            grads.zero()
+            g = torch.Generator().manual_seed(100 * step + rank)
+            x = torch.randn(8, 16, generator=g)
+            model(x).square().sum().backward()
+            grads.average(world)
+            per_step.append(grads.flat.clone())
+        out[mode] = per_step
+    results[rank] = out
+    dist.destroy_process_group()
+
+
+def test_bucketed_allreduce_overlapped_with_backward_matches_one_flat_allreduce():
+    """Gradient buckets all-reduced from post-accumulate hooks while backward runs give the same
+    averaged gradients, bit for bit, as one all-reduce after backward (two gloo ranks)."""
+    port = _free_port()
+    with mp.get_context("spawn").Manager() as m:     # no fork of the test process
+        results = m.dict()
+        mp.spawn(_bucket_worker, args=(2, port, results), nprocs=2, join=True)
+        results = dict(results)
+    for r in range(2):
+        for a, b in zip(results[r]["plain"], results[r]["buckets"]):
+            assert torch.equal(a, b)
+    for a, b in zip(results[0]["buckets"], results[1]["buckets"]):
+        assert torch.equal(a, b)
