@@ -29,23 +29,6 @@ namespace {
 
 constexpr float kClamp = 5.0f;
 constexpr float kEps = 1e-6f;
-constexpr float kLog2e = 1.44269504088896341f;
-
-// e^s of a clamped edge score (|s| <= 5 plus any bias) as 2^(s log2 e) on the MUFU unit
-// (ex2.approx: relative error ~2^-22, plus ~2^-21 from rounding s log2 e, far inside the fp32
-// parity tolerance of 1e-5).  Used by the vector kernels, forward and backward alike, so both
-// see the same p_e.
-__device__ __forceinline__ float edge_exp(float s) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(s * kLog2e));
-    return y;
-}
-// 1 / x on the MUFU unit (rcp.approx: <= 1 ulp for the normal x here, Z + 1e-6 >= 1e-6).
-__device__ __forceinline__ float fast_rcp(float x) {
-    float y;
-    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
 constexpr int kBlock = 256;
 constexpr int kWarpsPerBlock = kBlock / kWarp;
 
@@ -199,7 +182,7 @@ __global__ void __launch_bounds__(kBlock)
                 d = head_reduce<HEAD_VECS>(d);
                 float s = fminf(fmaxf(d * scale_inv, -kClamp), kClamp);
                 if (bias != nullptr && ok[u]) s += __ldg(bias + (size_t)e * heads + (gl + G * t) / HEAD_VECS);
-                const float p = ok[u] ? edge_exp(s) : 0.f;
+                const float p = ok[u] ? expf(s) : 0.f;
                 zs[t] += p;
                 Elem<T>::unpack(vr[u][t], vf);
 #pragma unroll
@@ -302,10 +285,8 @@ __global__ void __launch_bounds__(kBlock)
 
 // Blocks [0, blocks_a) : one warp per destination row -> dq.
 // Blocks [blocks_a, .) : one warp per source row      -> dk, dv.
-// MINB: resident blocks per SM the register allocation must allow; UNR: edge batches in flight
-// per lane group (0: the layout's default).
-template <typename T, int HEAD_VECS, int ROW_VECS, int MINB = 2, int UNR = 0>
-__global__ void __launch_bounds__(kBlock, MINB)
+template <typename T, int HEAD_VECS, int ROW_VECS>
+__global__ void __launch_bounds__(kBlock)
     spattn_bwd_vec(int n, int heads, float scale_inv, int blocks_a, const T *__restrict__ q,
                    const T *__restrict__ k, const T *__restrict__ v, const T *__restrict__ dout,
                    const float *__restrict__ z, const float *__restrict__ delta,
@@ -315,7 +296,7 @@ __global__ void __launch_bounds__(kBlock, MINB)
                    T *__restrict__ dq, T *__restrict__ dk, T *__restrict__ dv,
                    float *__restrict__ dbias, SegView sgd, SegView sgs) {
     using L = VecLayout<T, HEAD_VECS, ROW_VECS>;
-    constexpr int G = L::G, VPL = L::VPL, EPW = L::EPW, VE = L::VE, UNROLL = UNR > 0 ? UNR : L::UNROLL;
+    constexpr int G = L::G, VPL = L::VPL, EPW = L::EPW, VE = L::VE, UNROLL = L::UNROLL;
     const int lane = lane_id();
     const int sub = lane / G;
     const int gl = lane % G;
@@ -404,7 +385,7 @@ __global__ void __launch_bounds__(kBlock, MINB)
                     const bool inside = s >= -kClamp && s <= kClamp;
                     float sc = fminf(fmaxf(s, -kClamp), kClamp);
                     if (bias != nullptr && ok[u]) sc += __ldg(bias + (size_t)e * heads + head[t]);
-                    const float p = edge_exp(sc);
+                    const float p = expf(sc);
                     const float dpre = (dgv - dl[t]) * inv[t] * p;
                     const float ds = (ok[u] && inside) ? dpre : 0.f;
                     if (dbias != nullptr && ok[u] && (gl % HEAD_VECS) == 0) dbias[(size_t)e * heads + head[t]] = dpre;
@@ -492,8 +473,270 @@ __global__ void __launch_bounds__(kBlock, MINB)
                     float sc = fminf(fmaxf(s, -kClamp), kClamp);
                     if (bias != nullptr && ok[u])
                         sc += __ldg(bias + (size_t)__ldg(src_to_dst_slot + e) * heads + head[t]);
-                    const float p = ok[u] ? edge_exp(sc) : 0.f;
-                    const float inv = fast_rcp(zr[u][t] + kEps);
+                    const float p = ok[u] ? expf(sc) : 0.f;
+                    const float inv = 1.0f / (zr[u][t] + kEps);
+                    const float a = p * inv;
+                    const float dpre = (dgv - dr[u][t]) * inv * p;
+                    const float ds = inside ? dpre : 0.f;
+#pragma unroll
+                    for (int i = 0; i < VE; i++) {
+                        av[t][i] = fmaf(a, gf[i], av[t][i]);
+                        ak[t][i] = fmaf(ds, qf[i], ak[t][i]);
+                    }
+                }
+            }
+        }
+        if (EPW > 1) {
+#pragma unroll
+            for (int t = 0; t < VPL; t++)
+#pragma unroll
+                for (int i = 0; i < VE; i++) {
+                    ak[t][i] = slot_reduce<G>(ak[t][i]);
+                    av[t][i] = slot_reduce<G>(av[t][i]);
+                }
+        }
+        if (seg >= 0) {   // segment partials of dk (unscaled) and dv
+            if (sub == 0) {
+                float *rec = sgs.part + (size_t)seg * 2 * ROW_VECS * VE;
+#pragma unroll
+                for (int t = 0; t < VPL; t++)
+#pragma unroll
+                    for (int i = 0; i < VE; i += 4) {
+                        *reinterpret_cast<float4 *>(rec + (gl + G * t) * VE + i) =
+                            make_float4(ak[t][i], ak[t][i + 1], ak[t][i + 2], ak[t][i + 3]);
+                        *reinterpret_cast<float4 *>(rec + ROW_VECS * VE + (gl + G * t) * VE + i) =
+                            make_float4(av[t][i], av[t][i + 1], av[t][i + 2], av[t][i + 3]);
+                    }
+            }
+            return;
+        }
+        if (sub == 0) {
+            Vec16 *ok_ = reinterpret_cast<Vec16 *>(dk) + rbase + gl;
+            Vec16 *ov = reinterpret_cast<Vec16 *>(dv) + rbase + gl;
+#pragma unroll
+            for (int t = 0; t < VPL; t++) {
+                float r[VE];
+#pragma unroll
+                for (int i = 0; i < VE; i++) r[i] = ak[t][i] * scale_inv;
+                st16(ok_ + G * t, Elem<T>::pack(r));
+                st16(ov + G * t, Elem<T>::pack(av[t]));
+            }
+        }
+    }
+}
+
+// e^s of a clamped edge score as 2^(s log2 e) on the MUFU unit (ex2.approx: relative error
+// ~2^-22, plus ~2^-21 from rounding s log2 e), and 1 / x as rcp.approx (<= 1 ulp for the normal
+// x = Z + 1e-6 here): both far inside the parity tolerances.
+constexpr float kLog2e = 1.44269504088896341f;
+__device__ __forceinline__ float mufu_exp(float s) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(s * kLog2e));
+    return y;
+}
+__device__ __forceinline__ float mufu_rcp(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// The backward above specialised for the 65,536-token workload's shape (bf16, 16 vectors per row,
+// H * D = 128): exponentials and the source role's reciprocal on the MUFU unit, two edge batches
+// in flight per lane group, and four resident blocks per SM (64 registers); 0.33 ms against 0.45
+// for the general kernel at that shape.  A separate kernel (the general one is left as it is)
+// because its code generation is sensitive: variants of these kernels with other register budgets
+// and fast-math forms have stopped with a misaligned address on some shapes; this one has passed
+// every test of its shape.
+template <typename T, int HEAD_VECS, int ROW_VECS>
+__global__ void __launch_bounds__(kBlock, 4)
+    spattn_bwd_vec_narrow(int n, int heads, float scale_inv, int blocks_a, const T *__restrict__ q,
+                   const T *__restrict__ k, const T *__restrict__ v, const T *__restrict__ dout,
+                   const float *__restrict__ z, const float *__restrict__ delta,
+                   const int *__restrict__ dst_rowptr, const int *__restrict__ dst_src,
+                   const int *__restrict__ src_rowptr, const int *__restrict__ src_dst,
+                   const int *__restrict__ src_to_dst_slot, const float *__restrict__ bias,
+                   T *__restrict__ dq, T *__restrict__ dk, T *__restrict__ dv,
+                   float *__restrict__ dbias, SegView sgd, SegView sgs) {
+    using L = VecLayout<T, HEAD_VECS, ROW_VECS>;
+    constexpr int G = L::G, VPL = L::VPL, EPW = L::EPW, VE = L::VE, UNROLL = 2;
+    const int lane = lane_id();
+    const int sub = lane / G;
+    const int gl = lane % G;
+    const int wid = threadIdx.x >> 5;
+    const int b = blockIdx.x;
+    // blocks: [0, blocks_a) destination rows, [blocks_a, 2 blocks_a) source rows, then the
+    // destination-view segments and the source-view segments of heavy rows
+    const int seg_blocks_d = (sgd.nseg + kWarpsPerBlock - 1) / kWarpsPerBlock;
+    bool role_a;
+    int row, beg, end, seg = -1;
+    if (b < 2 * blocks_a) {
+        role_a = b < blocks_a;
+        row = (role_a ? b : b - blocks_a) * kWarpsPerBlock + wid;
+        if (row >= n) return;
+        const int32_t *first = role_a ? sgd.first : sgs.first;
+        if (first != nullptr && __ldg(first + row) >= 0) return;   // done by its segments
+        const int *rp = role_a ? dst_rowptr : src_rowptr;
+        beg = __ldg(rp + row);
+        end = __ldg(rp + row + 1);
+    } else {
+        const int sb = b - 2 * blocks_a;
+        role_a = sb < seg_blocks_d;
+        seg = (role_a ? sb : sb - seg_blocks_d) * kWarpsPerBlock + wid;
+        if (seg >= (role_a ? sgd.nseg : sgs.nseg)) return;
+        row = __ldg((role_a ? sgd.row : sgs.row) + seg);
+        const int *rp = role_a ? dst_rowptr : src_rowptr;
+        const int edges = role_a ? sgd.edges : sgs.edges;
+        beg = __ldg(rp + row) + (seg - __ldg((role_a ? sgd.first : sgs.first) + row)) * edges;
+        end = min(__ldg(rp + row + 1), beg + edges);
+    }
+    const Vec16 *Q = reinterpret_cast<const Vec16 *>(q) + gl;
+    const Vec16 *K = reinterpret_cast<const Vec16 *>(k) + gl;
+    const Vec16 *V = reinterpret_cast<const Vec16 *>(v) + gl;
+    const Vec16 *DO = reinterpret_cast<const Vec16 *>(dout) + gl;
+    const size_t rbase = (size_t)row * ROW_VECS;
+    int head[VPL];
+#pragma unroll
+    for (int t = 0; t < VPL; t++) head[t] = (gl + G * t) / HEAD_VECS;
+
+    if (role_a) {
+        // ---- dq for destination row `row` ----
+        float qf[VPL][VE], gf[VPL][VE], inv[VPL], dl[VPL], acc[VPL][VE];
+#pragma unroll
+        for (int t = 0; t < VPL; t++) {
+            Elem<T>::unpack(ldg16(Q + rbase + G * t), qf[t]);
+            Elem<T>::unpack(ldg16(DO + rbase + G * t), gf[t]);
+            inv[t] = 1.0f / (__ldg(z + (size_t)row * heads + head[t]) + kEps);
+            dl[t] = __ldg(delta + (size_t)row * heads + head[t]);
+#pragma unroll
+            for (int i = 0; i < VE; i++) acc[t][i] = 0.f;
+        }
+        for (int e0 = beg; e0 < end; e0 += EPW * UNROLL) {
+            int src[UNROLL];
+            bool ok[UNROLL];
+#pragma unroll
+            for (int u = 0; u < UNROLL; u++) {
+                const int e = e0 + sub + EPW * u;
+                ok[u] = e < end;
+                src[u] = ok[u] ? __ldg(dst_src + e) : 0;
+            }
+            Vec16 kr[UNROLL][VPL], vr[UNROLL][VPL];
+#pragma unroll
+            for (int u = 0; u < UNROLL; u++)
+#pragma unroll
+                for (int t = 0; t < VPL; t++) {
+                    kr[u][t] = ldg16(K + (size_t)src[u] * ROW_VECS + G * t);
+                    vr[u][t] = ldg16(V + (size_t)src[u] * ROW_VECS + G * t);
+                }
+#pragma unroll
+            for (int u = 0; u < UNROLL; u++) {
+                const int e = e0 + sub + EPW * u;
+#pragma unroll
+                for (int t = 0; t < VPL; t++) {
+                    float kf[VE], vf[VE];
+                    Elem<T>::unpack(kr[u][t], kf);
+                    Elem<T>::unpack(vr[u][t], vf);
+                    float dqk = 0.f, dgv = 0.f;
+#pragma unroll
+                    for (int i = 0; i < VE; i++) {
+                        dqk = fmaf(kf[i], qf[t][i], dqk);
+                        dgv = fmaf(gf[t][i], vf[i], dgv);
+                    }
+                    dqk = head_reduce<HEAD_VECS>(dqk);
+                    dgv = head_reduce<HEAD_VECS>(dgv);
+                    const float s = dqk * scale_inv;
+                    const bool inside = s >= -kClamp && s <= kClamp;
+                    float sc = fminf(fmaxf(s, -kClamp), kClamp);
+                    if (bias != nullptr && ok[u]) sc += __ldg(bias + (size_t)e * heads + head[t]);
+                    const float p = mufu_exp(sc);
+                    const float dpre = (dgv - dl[t]) * inv[t] * p;
+                    const float ds = (ok[u] && inside) ? dpre : 0.f;
+                    if (dbias != nullptr && ok[u] && (gl % HEAD_VECS) == 0) dbias[(size_t)e * heads + head[t]] = dpre;
+#pragma unroll
+                    for (int i = 0; i < VE; i++) acc[t][i] = fmaf(ds, kf[i], acc[t][i]);
+                }
+            }
+        }
+        if (EPW > 1) {
+#pragma unroll
+            for (int t = 0; t < VPL; t++)
+#pragma unroll
+                for (int i = 0; i < VE; i++) acc[t][i] = slot_reduce<G>(acc[t][i]);
+        }
+        if (seg >= 0) {   // segment partial of dq (before the 1/sqrt(D) scale)
+            if (sub == 0) {
+                float *rec = sgd.part + (size_t)seg * ROW_VECS * VE;
+#pragma unroll
+                for (int t = 0; t < VPL; t++)
+#pragma unroll
+                    for (int i = 0; i < VE; i += 4)
+                        *reinterpret_cast<float4 *>(rec + (gl + G * t) * VE + i) =
+                            make_float4(acc[t][i], acc[t][i + 1], acc[t][i + 2], acc[t][i + 3]);
+            }
+            return;
+        }
+        if (sub == 0) {
+            Vec16 *o = reinterpret_cast<Vec16 *>(dq) + rbase + gl;
+#pragma unroll
+            for (int t = 0; t < VPL; t++) {
+                float r[VE];
+#pragma unroll
+                for (int i = 0; i < VE; i++) r[i] = acc[t][i] * scale_inv;
+                st16(o + G * t, Elem<T>::pack(r));
+            }
+        }
+    } else {
+        // ---- dk, dv for source row `row` ----
+        float kf[VPL][VE], vf[VPL][VE], ak[VPL][VE], av[VPL][VE];
+#pragma unroll
+        for (int t = 0; t < VPL; t++) {
+            Elem<T>::unpack(ldg16(K + rbase + G * t), kf[t]);
+            Elem<T>::unpack(ldg16(V + rbase + G * t), vf[t]);
+#pragma unroll
+            for (int i = 0; i < VE; i++) ak[t][i] = av[t][i] = 0.f;
+        }
+        for (int e0 = beg; e0 < end; e0 += EPW * UNROLL) {
+            int dst[UNROLL];
+            bool ok[UNROLL];
+#pragma unroll
+            for (int u = 0; u < UNROLL; u++) {
+                const int e = e0 + sub + EPW * u;
+                ok[u] = e < end;
+                dst[u] = ok[u] ? __ldg(src_dst + e) : 0;
+            }
+            Vec16 qr[UNROLL][VPL], gr[UNROLL][VPL];
+            float zr[UNROLL][VPL], dr[UNROLL][VPL];
+#pragma unroll
+            for (int u = 0; u < UNROLL; u++)
+#pragma unroll
+                for (int t = 0; t < VPL; t++) {
+                    qr[u][t] = ldg16(Q + (size_t)dst[u] * ROW_VECS + G * t);
+                    gr[u][t] = ldg16(DO + (size_t)dst[u] * ROW_VECS + G * t);
+                    zr[u][t] = __ldg(z + (size_t)dst[u] * heads + head[t]);
+                    dr[u][t] = __ldg(delta + (size_t)dst[u] * heads + head[t]);
+                }
+#pragma unroll
+            for (int u = 0; u < UNROLL; u++) {
+                const int e = e0 + sub + EPW * u;
+#pragma unroll
+                for (int t = 0; t < VPL; t++) {
+                    float qf[VE], gf[VE];
+                    Elem<T>::unpack(qr[u][t], qf);
+                    Elem<T>::unpack(gr[u][t], gf);
+                    float dqk = 0.f, dgv = 0.f;
+#pragma unroll
+                    for (int i = 0; i < VE; i++) {
+                        dqk = fmaf(kf[t][i], qf[i], dqk);
+                        dgv = fmaf(gf[i], vf[t][i], dgv);
+                    }
+                    dqk = head_reduce<HEAD_VECS>(dqk);
+                    dgv = head_reduce<HEAD_VECS>(dgv);
+                    const float s = dqk * scale_inv;
+                    const bool inside = s >= -kClamp && s <= kClamp;
+                    float sc = fminf(fmaxf(s, -kClamp), kClamp);
+                    if (bias != nullptr && ok[u])
+                        sc += __ldg(bias + (size_t)__ldg(src_to_dst_slot + e) * heads + head[t]);
+                    const float p = ok[u] ? mufu_exp(sc) : 0.f;
+                    const float inv = mufu_rcp(zr[u][t] + kEps);
                     const float a = p * inv;
                     const float dpre = (dgv - dr[u][t]) * inv * p;
                     const float ds = inside ? dpre : 0.f;
@@ -825,17 +1068,6 @@ int forward_t(int64_t n, int heads, int head_dim, const void *q, const void *k, 
     return NGT_ERR_UNSUPPORTED;
 }
 
-// Register budget of the backward: for bf16 rows of 16 vectors (H*D = 128, the 65,536-token
-// workload's shape) four resident blocks per SM with two edge batches in flight per lane group
-// measured fastest (0.331 vs 0.388 ms at two blocks and four batches); other shapes keep two
-// blocks and the layout's default depth.
-template <typename T, int RV>
-struct BwdTune {
-    static constexpr bool kNarrowBf16 = sizeof(T) == 2 && RV == 16;
-    static constexpr int kMinBlocks = kNarrowBf16 ? 4 : 2;
-    static constexpr int kUnroll = kNarrowBf16 ? 2 : 0;
-};
-
 template <typename T>
 int backward_t(int64_t n, int heads, int head_dim, const void *q, const void *k, const void *v,
                const void *out, const void *dout, const float *z, const int32_t *dst_rowptr,
@@ -856,11 +1088,16 @@ int backward_t(int64_t n, int heads, int head_dim, const void *q, const void *k,
         spattn_delta_vec<T, HV, RV><<<ceil_div_i(n, (int64_t)kWarpsPerBlock * Lay::EPW), kBlock, 0, st>>>( \
             (int)n, heads, (const T *)out, (const T *)dout, delta);                               \
         NGT_CHECK_LAUNCH();                                                                       \
-        spattn_bwd_vec<T, HV, RV, BwdTune<T, RV>::kMinBlocks, BwdTune<T, RV>::kUnroll>            \
-            <<<2 * blocks_a + seg_blocks, kBlock, 0, st>>>(                                       \
-            (int)n, heads, scale_inv, blocks_a, (const T *)q, (const T *)k, (const T *)v,         \
-            (const T *)dout, z, delta, dst_rowptr, dst_src, src_rowptr, src_dst, s2d, bias,       \
-            (T *)dq, (T *)dk, (T *)dv, dbias, sgd, sgs);                                          \
+        if (sizeof(T) == 2 && HV == 2 && RV == 16)                                                \
+            spattn_bwd_vec_narrow<T, 2, 16><<<2 * blocks_a + seg_blocks, kBlock, 0, st>>>(        \
+                (int)n, heads, scale_inv, blocks_a, (const T *)q, (const T *)k, (const T *)v,     \
+                (const T *)dout, z, delta, dst_rowptr, dst_src, src_rowptr, src_dst, s2d, bias,   \
+                (T *)dq, (T *)dk, (T *)dv, dbias, sgd, sgs);                                      \
+        else                                                                                      \
+            spattn_bwd_vec<T, HV, RV><<<2 * blocks_a + seg_blocks, kBlock, 0, st>>>(              \
+                (int)n, heads, scale_inv, blocks_a, (const T *)q, (const T *)k, (const T *)v,     \
+                (const T *)dout, z, delta, dst_rowptr, dst_src, src_rowptr, src_dst, s2d, bias,   \
+                (T *)dq, (T *)dk, (T *)dv, dbias, sgd, sgs);                                      \
         NGT_CHECK_LAUNCH();                                                                       \
         if (seg_blocks > 0)                                                                       \
             spattn_bwd_seg_finish<T, HV, RV><<<seg_blocks, kBlock, 0, st>>>(                      \
