@@ -71,6 +71,10 @@ def parse_args():
     p.add_argument("--skip-layer", action="store_true")
     p.add_argument("--skip-large-ppr", action="store_true",
                    help="skip the PPR runs on the 232,965- and 2,449,029-node graphs")
+    p.add_argument("--profile-case", choices=["spattn", "gemm", "push"], default=None,
+                   help="run one small workload for an ncu capture (no JSON line): the 65,536-token window "
+                        "fwd+bwd x3 with L2 flushes, the bf16 Linear 32768x768->768 fwd+bwd x3, or push PPR "
+                        "(eps 1e-5) on a 40,000-node graph x2")
     p.add_argument("--epoch-kernels", action="store_true",
                    help="print the per-kernel device time of one graph-replayed config-2 GT epoch "
                         "(torch.profiler over CUPTI) instead of the JSON line")
@@ -182,20 +186,19 @@ def measured_hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def measured_l2_gbs(dev, mib=24, reps=50):
-    """Copy bandwidth with source and destination both resident in L2 (24 MiB each of the 126 MB),
-    read + write bytes over CUDA-event time: the denominator of the L2 roofline."""
-    a = torch.empty(mib << 20, dtype=torch.uint8, device=dev)
-    b = torch.empty_like(a)
+def measured_l2_gbs(dev, mib=32, reps=50):
+    """Read bandwidth of L2-resident data (a 32 MiB fp32 buffer, summed repeatedly) over CUDA-event
+    time: the denominator of the L2 roofline (the sparse backward's L2 traffic is gathers)."""
+    a = torch.ones((mib << 20) // 4, dtype=torch.float32, device=dev)
     for _ in range(5):
-        b.copy_(a)
+        a.sum()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(reps):
-        b.copy_(a)
+        a.sum()
     e1.record()
     e1.synchronize()
-    return 2.0 * (mib << 20) * reps / (e0.elapsed_time(e1) / 1e3) / 1e9
+    return float(mib << 20) * reps / (e0.elapsed_time(e1) / 1e3) / 1e9
 
 
 def ncu_traffic():
@@ -313,7 +316,7 @@ def bench_attention(args, rank, world, dev):
     # profiles/ncu_traffic.json) over its time, against an L2-resident copy measured here
     l2_peak = measured_l2_gbs(dev)
     lts = traffic.get("bwd_lts")
-    roofline["l2"] = {"peak": l2_peak, "unit": "GB/s", "peak_kind": "measured here: L2-resident copy (24 MiB)",
+    roofline["l2"] = {"peak": l2_peak, "unit": "GB/s", "peak_kind": "measured here: reads of an L2-resident 32 MiB buffer",
                       "traffic": lts, "achieved": (lts / avg_bwd / 1e9) if lts else None,
                       "frac": (lts / avg_bwd / 1e9 / l2_peak) if lts else None}
 
@@ -980,8 +983,44 @@ def epoch_kernel_table(args):
     trainer.dummy = None
 
 
+def profile_case(case):
+    """Small, fixed workloads for one-kernel ncu captures (profiles/*.md give the commands)."""
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    if case == "spattn":
+        from neutrongt_b200.attention import WindowAttentionBuffers
+        from neutrongt_b200.edge_csr import build_edge_csr
+        q, k, v, dout, ei = (t.to(dev) for t in make_window(seed=0))
+        buf = WindowAttentionBuffers(q, k, v, build_edge_csr(ei, N_TOKENS))
+        flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+        for i in range(3):
+            flush.fill_(i)
+            buf.forward()
+            buf.backward(dout)
+    elif case == "gemm":
+        from neutrongt_b200.layers import Linear
+        x = torch.randn(32768, 768, device=dev).to(torch.bfloat16).requires_grad_(True)
+        lin = Linear(768, 768).to(dev).to(torch.bfloat16)
+        dy = torch.randn(32768, 768, device=dev).to(torch.bfloat16)
+        for _ in range(3):
+            lin.zero_grad(set_to_none=True)
+            lin(x).backward(dy)
+    else:
+        from neutrongt_b200 import synthetic
+        from neutrongt_b200.ppr import personal_pagerank_torch_geometric
+        rp, col = synthetic.chung_lu_graph_device(40000, 2000000, seed=5, device=dev)
+        for _ in range(2):
+            personal_pagerank_torch_geometric(None, 0.15, topk=10, eps=1e-5, device=dev,
+                                              csr_data={"rowptr": rp, "col": col}, source_start=10000,
+                                              source_end=14000)
+    torch.cuda.synchronize()
+
+
 def main():
     args = parse_args()
+    if args.profile_case:
+        profile_case(args.profile_case)
+        return
     if args.epoch_kernels:
         epoch_kernel_table(args)
         return
