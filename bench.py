@@ -186,21 +186,6 @@ def measured_hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def measured_l2_gbs(dev, mib=32, reps=50):
-    """Read bandwidth of L2-resident data (a 32 MiB fp32 buffer, summed repeatedly) over CUDA-event
-    time: the denominator of the L2 roofline (the sparse backward's L2 traffic is gathers)."""
-    a = torch.ones((mib << 20) // 4, dtype=torch.float32, device=dev)
-    for _ in range(5):
-        a.sum()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(reps):
-        a.sum()
-    e1.record()
-    e1.synchronize()
-    return float(mib << 20) * reps / (e0.elapsed_time(e1) / 1e3) / 1e9
-
-
 def ncu_traffic():
     """Per-launch DRAM bytes from the committed ncu summary (null when absent)."""
     path = os.path.join(ROOT, "profiles", "ncu_traffic.json")
@@ -312,13 +297,17 @@ def bench_attention(args, rank, world, dev):
                                      "note": "Q,K,V,O once + CSR + Z + node scores; K/V (33.5 MB) can stay in L2, "
                                              "so the no-reuse algorithmic bytes and these bracket the DRAM traffic"}}
 
-    # L2-side roofline of the backward: its L2 traffic (lts__t_bytes of one ncu capture of this launch,
-    # profiles/ncu_traffic.json) over its time, against an L2-resident copy measured here
-    l2_peak = measured_l2_gbs(dev)
-    lts = traffic.get("bwd_lts")
-    roofline["l2"] = {"peak": l2_peak, "unit": "GB/s", "peak_kind": "measured here: reads of an L2-resident 32 MiB buffer",
-                      "traffic": lts, "achieved": (lts / avg_bwd / 1e9) if lts else None,
-                      "frac": (lts / avg_bwd / 1e9 / l2_peak) if lts else None}
+    # L2-side roofline of the backward, from the committed one-kernel ncu capture of this launch
+    # (profiles/ncu_traffic.json): its L2 traffic (lts__t_sectors x 32 B) over the time measured
+    # here, and ncu's lts__throughput percentage as the fraction of the L2's sustained peak
+    lts, pct, ncu_us = traffic.get("bwd_lts"), traffic.get("bwd_lts_pct"), traffic.get("bwd_ncu_us")
+    l2_achieved = lts / avg_bwd / 1e9 if lts else None
+    l2_peak = lts / (ncu_us * 1e-6) / (pct / 100.0) / 1e9 if (lts and pct and ncu_us) else None
+    roofline["l2"] = {"traffic": lts, "achieved": l2_achieved, "unit": "GB/s", "peak": l2_peak,
+                      "frac": l2_achieved / l2_peak if l2_peak else None,
+                      "peak_kind": "L2 sustained peak implied by the committed capture (its lts__t_sectors over "
+                                   "its duration, divided by its lts__throughput percent of peak; "
+                                   "profiles/spattn_bwd_narrow_config3.md)"}
 
     # e2e through the public API with pinned host buffers.  Every step copies its own inputs in and
     # its results out.  Pipelined: two CUDA streams with their own pinned buffers, and step i + 1's
