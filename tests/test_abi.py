@@ -81,3 +81,30 @@ def test_bf16_linear_shape_checks_without_a_gpu():
     assert lib.ngt_linear_bf16_weight_workspace_size(32768, 768, 768, ctypes.byref(out)) == 0
     assert out.value >= 768 * 768 * 4
     assert lib.ngt_linear_bf16_forward(10, 64, 12, None, None, None, None, None) == 1        # 12 % 8 != 0
+
+
+def test_new_entry_points_reject_bad_arguments_without_a_gpu():
+    """Argument checks of the push PPR, SpGEMM and biased dense attention entry points run before any
+    CUDA call (NGT_ERR_INVALID_ARGUMENT = 1, NGT_ERR_UNSUPPORTED = 2)."""
+    import ctypes
+
+    from neutrongt_b200 import _lib
+    lib = _lib.lib()
+    out = ctypes.c_size_t(0)
+    assert lib.ngt_ppr_push_workspace_size(100, 0, ctypes.byref(out)) == 1
+    assert lib.ngt_ppr_push_workspace_size(100, 4, ctypes.byref(out)) == 0 and out.value >= 4 * 100 * 29
+    info = ctypes.c_void_p(16)      # never dereferenced: the checks fail first
+    for alpha, eps in ((0.0, 1e-4), (1.5, 1e-4), (0.15, 0.0), (0.15, -1.0)):
+        assert lib.ngt_ppr_push_topk(10, None, None, alpha, eps, 0, 10, 4, 1, None, None, None, None, info, None, 0,
+                                     None) == 1
+    assert lib.ngt_ppr_push_topk(10, None, None, 0.15, 1e-4, 5, 3, 4, 1, None, None, None, None, info, None, 0,
+                                 None) == 1
+    assert lib.ngt_csr_spgemm_workspace_size(-1, 10, 1, ctypes.byref(out)) == 1
+    assert lib.ngt_csr_spgemm_workspace_size(10, 10, 2, ctypes.byref(out)) == 0 and out.value > 0
+    assert lib.ngt_csr_spgemm_symbolic(4, 4, None, None, None, None, 1, None, None, 0, None) == 1
+    st = ctypes.c_int32(0)
+    dummy = ctypes.c_void_p(256)
+    assert lib.ngt_dense_attn_forward_bias(64, 2, 72, 1.0, 0.5, 0.0, 0, dummy, dummy, dummy, dummy, 0, dummy, dummy,
+                                           dummy, ctypes.byref(st), None) == 2          # head_dim > 64
+    assert lib.ngt_dense_attn_forward_bias(64, 2, 16, 1.0, 0.5, 0.0, 0, dummy, dummy, dummy, dummy, 7, dummy, dummy,
+                                           dummy, ctypes.byref(st), None) == 1          # bad head stride
