@@ -385,7 +385,7 @@ NGT_API int ngt_linear_status(int32_t *timeouts /* host */);
  * topk entries, else the topk largest by (value desc, node asc).
  *   rowptr int64 [n+1], col int32 [E] (columns ascending within a row, as PyG sorts them)
  *   slots        concurrent seeds (one warp each); workspace from ngt_ppr_push_workspace_size(n, slots)
- *                (about 29 bytes x n per slot; zeroed by the call)
+ *                (about 29 bytes x n per slot; its flags are cleared by the call)
  *   out_idx / out_val / out_val64 (nullable) [(seed_end - seed_start) * topk], out_cnt [seeds]
  *   info         int32 [1]: seeds stopped by the termination guard (0 in practice)
  * ngt_ppr_push_stats reads the last call's push and adjacency-read totals from its workspace

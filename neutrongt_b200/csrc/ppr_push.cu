@@ -19,7 +19,8 @@
 //
 // One warp per seed, persistent warps taking seeds from a counter.  Each warp owns a slot of
 // dense per-node arrays in the workspace (r, p values, flags) plus its stack, p list and the list
-// of touched nodes, which resets exactly what the seed wrote.  A push spreads one adjacency row
+// of touched nodes, through which the seed clears the flags it set (a value is only read when its
+// flag says it was written, so only the flags need clearing).  A push spreads one adjacency row
 // over the lanes, 32 neighbours per step: the neighbours of a row are distinct (columns ascend,
 // so a repeated edge shows as equal neighbouring lanes; such a step runs on lane 0 alone), so
 // their updates commute, and the stack appends are placed with a ballot in lane (= CSR) order.
@@ -229,13 +230,8 @@ __global__ void __launch_bounds__(kPushThreads)
             }
             if (lane == 0) out_cnt[o] = topk;
         }
-        // ---- reset what this seed wrote ----
-        for (int i = lane; i < nt; i += 32) {
-            const int v = touched[i];
-            r[v] = 0.0;
-            pv[v] = 0.0;
-            fl[v] = 0;
-        }
+        // ---- clear the flags this seed set (residuals and p values are dead once their flags are) ----
+        for (int i = lane; i < nt; i += 32) fl[touched[i]] = 0;
         __syncwarp();
     }
     if (lane == 0) {
@@ -270,8 +266,12 @@ extern "C" int ngt_ppr_push_topk(int64_t n, const int64_t *rowptr, const int32_t
     if (!rowptr || !col || !out_idx || !out_val || !out_cnt) return NGT_ERR_INVALID_ARGUMENT;
     PushWs w = carve_push(workspace, n, slots);
     if (!workspace || workspace_bytes < w.used) return NGT_ERR_WORKSPACE;
-    // the slot arrays start (and must stay) zero: cleared here once, and every seed resets what it wrote
-    if (cudaMemsetAsync(workspace, 0, w.used, st) != cudaSuccess) return NGT_ERR_CUDA;
+    // Only the flags must start at zero (a residual or p value is read only when its flag says it was
+    // written, and the lists are written before they are read): the counters and flags are cleared
+    // here, and every seed clears the flags it set.
+    if (cudaMemsetAsync(w.counter, 0, 4 * sizeof(unsigned long long), st) != cudaSuccess ||
+        cudaMemsetAsync(w.fl, 0, (size_t)n * (size_t)slots, st) != cudaSuccess)
+        return NGT_ERR_CUDA;
     // Termination guard only: a pop of a node with neighbours removes alpha * res >= alpha^2 eps of the
     // residual mass (alpha to start), so there are at most 1 + 1 / (alpha eps) of those; a node without
     // neighbours enters the stack only through an edge relaxation.  Past this bound a seed stops and

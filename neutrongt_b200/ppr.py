@@ -158,16 +158,16 @@ def _sorted_rows(rowptr, col, n):
 
 
 def _push_slots(n, nseeds, device, slots=None):
-    """Concurrent seeds (one warp and ~29 n bytes of workspace each): up to 32 warps per SM, so the
-    dependent push chains of many seeds hide each other's memory latency, capped at a quarter of
-    the free device memory (16 GiB at most)."""
+    """Concurrent seeds (one warp and ~29 n bytes of workspace each): eight warps per SM (more slots
+    measured slower: their scattered per-node arrays thrash the L2), capped at a quarter of the free
+    device memory (16 GiB at most)."""
     if slots is not None:
         return max(1, min(int(slots), nseeds))
     sms = torch.cuda.get_device_properties(device).multi_processor_count
     free, _ = torch.cuda.mem_get_info(device)
     per = _lib.size_query(_lib.lib().ngt_ppr_push_workspace_size, n, 1)
     cap = max(1, int(min(free // 4, 16 << 30) // max(per, 1)))
-    return max(1, min(nseeds, 32 * sms, cap))
+    return max(1, min(nseeds, 8 * sms, cap))
 
 
 def personal_pagerank_torch_geometric(edge_index, alpha, topk=100, eps: float = 1e-6, device="cuda", csr_data=None,
