@@ -310,45 +310,59 @@ def bench_attention(args, rank, world, dev):
                                    "profiles/spattn_bwd_narrow_config3.md)"}
 
     # e2e through the public API with pinned host buffers.  Every step copies its own inputs in and
-    # its results out.  Pipelined: two CUDA streams with their own pinned buffers, and step i + 1's
-    # host-to-device copy is enqueued before step i's API call, so the copy engine streams inputs
-    # while the host waits on step i's edge-list validation and the GPU computes and copies step i
-    # back (the copy engines are full duplex).  The same steps one after another on one stream are
-    # reported beside it.
-    pins = [[t.pin_memory() for t in (q_h, k_h, v_h, g_h, ei_h)] for _ in range(2)]
+    # its results out.  Pipelined: one stream per engine — host-to-device copies, the API call, and
+    # device-to-host copies — joined by events, with the inputs of steps i + 1 and i + 2 in flight
+    # while step i runs, so the two copy directions (full duplex) and the kernels overlap and the
+    # host's wait inside the call (the edge-list validation) never holds back the next input copy.
+    # The same steps one after another on one stream are reported beside it.
+    pins = [t.pin_memory() for t in (q_h, k_h, v_h, g_h, ei_h)]
     outs = [[torch.empty((n, HEADS, HEAD_DIM), dtype=torch.bfloat16).pin_memory() for _ in range(4)]
             for _ in range(2)]
     ns_h = [torch.empty(n, dtype=torch.float32).pin_memory() for _ in range(2)]
-    side = [torch.cuda.Stream(dev), torch.cuda.Stream(dev)]
+    s_in, s_comp, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     staged = {}
 
     def e2e_copy_in(i, s):
         with torch.cuda.stream(s):
-            staged[i] = [t.to(dev, non_blocking=True) for t in pins[i % 2]]
+            staged[i] = ([t.to(dev, non_blocking=True) for t in pins], torch.cuda.Event())
+            staged[i][1].record(s)
 
-    def e2e_compute(i, s):
+    def e2e_compute(i, s, s_copy_out):
+        tensors, ready = staged.pop(i)
         with torch.cuda.stream(s):
-            qd, kd, vd, gd, eid = staged.pop(i)
+            s.wait_event(ready)
+            for t in tensors:
+                t.record_stream(s)
+            qd, kd, vd, gd, eid = tensors
             qd.requires_grad_(True)
             kd.requires_grad_(True)
             vd.requires_grad_(True)
             x, ns = sparse_attention_bias(qd, kd, vd, eid, None)
             x.backward(gd)
-            for h, d in zip(outs[i % 2], (x.detach(), qd.grad, kd.grad, vd.grad)):
+            results = (x.detach(), qd.grad, kd.grad, vd.grad, ns)
+            done = torch.cuda.Event()
+            done.record(s)
+        with torch.cuda.stream(s_copy_out):
+            s_copy_out.wait_event(done)
+            for d in results:
+                d.record_stream(s_copy_out)
+            for h, d in zip(outs[i % 2], results[:4]):
                 h.copy_(d, non_blocking=True)
             ns_h[i % 2][:ns.numel()].copy_(ns, non_blocking=True)
 
     def run_steps(count, streams):
-        pipelined = len(streams) > 1
-        if pipelined:
-            e2e_copy_in(0, streams[0])
+        if len(streams) == 1:                       # one stream: copy in, call, copy out, in turn
+            for i in range(count):
+                e2e_copy_in(i, streams[0])
+                e2e_compute(i, streams[0], streams[0])
+            return
+        s_i, s_c, s_o = streams
+        for i in range(min(2, count)):
+            e2e_copy_in(i, s_i)
         for i in range(count):
-            s = streams[i % len(streams)]
-            if pipelined and i + 1 < count:
-                e2e_copy_in(i + 1, streams[(i + 1) % len(streams)])
-            if not pipelined:
-                e2e_copy_in(i, s)
-            e2e_compute(i, s)
+            e2e_compute(i, s_c, s_o)
+            if i + 2 < count:
+                e2e_copy_in(i + 2, s_i)
 
     def timed(streams):
         run_steps(max(2, args.warmup), streams)
@@ -367,17 +381,17 @@ def bench_attention(args, rank, world, dev):
         return allreduce_max(e0.elapsed_time(e1) / 1e3, world)
 
     t_serial = timed([st])
-    t_e2e = timed(side)
-    h2d = sum(t.numel() * t.element_size() for t in pins[0])
+    t_e2e = timed([s_in, s_comp, s_out])
+    h2d = sum(t.numel() * t.element_size() for t in pins)
     d2h = sum(t.numel() * t.element_size() for t in outs[0]) + 4 * (csr.node_scores_len)
     e2e = {"value": edges_all * args.steps / t_e2e, "unit": "edges/s", "h2d_bytes_per_step": h2d,
            "d2h_bytes_per_step": d2h, "ms_per_step": t_e2e / args.steps * 1e3,
            "serial_ms_per_step": t_serial / args.steps * 1e3,
            "serial_value": edges_all * args.steps / t_serial,
            "path": "neutrongt_b200.sparse_attention_bias + autograd backward, pinned host buffers, CSR built "
-                   "from the copied edge_index every step; value: two streams, step i+1's input copy enqueued "
-                   "before step i's call so it streams while step i computes and copies out; serial_*: the same "
-                   "steps on one stream"}
+                   "from the copied edge_index every step; value: input copies, calls and output copies on "
+                   "three streams joined by events, two steps' inputs in flight; serial_*: the same steps on "
+                   "one stream"}
     return {"value": value, "ms_per_step": t_max / args.steps * 1e3, "edges": e, "roofline": roofline,
             "e2e": e2e, "clocks": clocks, "gpu_launches": 3 * args.steps,
             "host": (q_h, k_h, v_h, g_h, ei_h)}
