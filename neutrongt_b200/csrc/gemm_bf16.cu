@@ -37,7 +37,6 @@ namespace {
 
 constexpr int BM = 128;                      // tile rows = TMEM lanes = MMA M
 constexpr int BK = 64;                       // reduction elements per stage (one swizzle row)
-constexpr int kStages = 4;
 constexpr int kThreads = 192;
 constexpr uint32_t kPolls = 1u << 26;
 constexpr uint32_t kAtom = 1024;             // 8 rows x 128 bytes: one swizzle atom
@@ -69,7 +68,7 @@ __device__ __forceinline__ void st_v4(void *p, uint32_t a, uint32_t b, uint32_t 
     asm volatile("st.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
 
-template <int BN>
+template <int BN, int kStages>
 struct Smem {
     static constexpr uint32_t kA = BM * BK * 2;            // 16 KiB
     static constexpr uint32_t kB = BN * BK * 2;
@@ -94,11 +93,11 @@ __device__ __forceinline__ void raise_abort(volatile int *abort) {
     if (atomicExch(const_cast<int *>(abort), 1) == 0) atomicAdd(&g_gemm_bf16_timeouts, 1);
 }
 
-template <int BN>
+template <int BN, int kStages>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                      const GemmArgs p) {
-    using L = Smem<BN>;
+    using L = Smem<BN, kStages>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L::kBars);
@@ -390,7 +389,7 @@ int sm_count() {
     return n;
 }
 
-template <int BN>
+template <int BN, int kStages>
 int launch(const CUtensorMap &ma, const CUtensorMap &mb, const GemmArgs &p, cudaStream_t st) {
     static std::mutex mu;
     static bool attr_set[64] = {};
@@ -399,15 +398,15 @@ int launch(const CUtensorMap &ma, const CUtensorMap &mb, const GemmArgs &p, cuda
     {
         std::lock_guard<std::mutex> lock(mu);
         if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-            if (cudaFuncSetAttribute(gemm_bf16_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)Smem<BN>::kBytes) != cudaSuccess)
+            if (cudaFuncSetAttribute(gemm_bf16_kernel<BN, kStages>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)Smem<BN, kStages>::kBytes) != cudaSuccess)
                 return NGT_ERR_CUDA;
             if (dev >= 0 && dev < 64) attr_set[dev] = true;
         }
     }
     const int tiles = p.tiles_m * p.tiles_n * p.splits;
     const int grid = tiles < sm_count() ? tiles : sm_count();
-    gemm_bf16_kernel<BN><<<grid, kThreads, Smem<BN>::kBytes, st>>>(ma, mb, p);
+    gemm_bf16_kernel<BN, kStages><<<grid, kThreads, Smem<BN, kStages>::kBytes, st>>>(ma, mb, p);
     NGT_CHECK_LAUNCH();
     return NGT_OK;
 }
@@ -422,7 +421,7 @@ int run(GemmArgs p, const void *a, int64_t a_rows, int64_t a_cols, const void *b
     int rc = map_bf16(&ma, a, a_rows, a_cols, p.a_mn ? BK : BM);
     if (rc == NGT_OK) rc = map_bf16(&mb, b, b_rows, b_cols, p.b_mn ? BK : bn);
     if (rc != NGT_OK) return rc;
-    return bn == 128 ? launch<128>(ma, mb, p, st) : launch<256>(ma, mb, p, st);
+    return bn == 128 ? launch<128, 4>(ma, mb, p, st) : launch<256, 4>(ma, mb, p, st);
 }
 
 bool shape_ok(int64_t rows, int in_f, int out_f) {

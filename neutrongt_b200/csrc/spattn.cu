@@ -19,7 +19,8 @@
 // Lane layout of the vector path: a row of H*D elements is ROW_VECS 16-byte vectors.  A
 // group of G = min(ROW_VECS, 32) lanes cooperates on one edge (lane gl owns vectors
 // gl + G*t), so a warp keeps 32/G edges of the same row in flight, times UNROLL.  A head
-// spans HEAD_VECS consecutive lanes; its dot product is reduced with xor shuffles.
+// spans HEAD_VECS consecutive lanes; its dot product is reduced with xor shuffles.  bf16 rows of
+// 128 elements (the 65,536-token workload) run separate packed-math kernels (spattn_*_r128).
 #include <mutex>
 
 #include "common.cuh"
@@ -540,25 +541,179 @@ __device__ __forceinline__ float mufu_rcp(float x) {
     return y;
 }
 
-// The backward above specialised for the 65,536-token workload's shape (bf16, 16 vectors per row,
-// H * D = 128): exponentials and the source role's reciprocal on the MUFU unit, two edge batches
-// in flight per lane group, and four resident blocks per SM (64 registers); 0.33 ms against 0.45
-// for the general kernel at that shape.  A separate kernel (the general one is left as it is)
-// because its code generation is sensitive: variants of these kernels with other register budgets
-// and fast-math forms have stopped with a misaligned address on some shapes; this one has passed
-// every test of its shape.
-template <typename T, int HEAD_VECS, int ROW_VECS>
-__global__ void __launch_bounds__(kBlock, 4)
-    spattn_bwd_vec_narrow(int n, int heads, float scale_inv, int blocks_a, const T *__restrict__ q,
-                   const T *__restrict__ k, const T *__restrict__ v, const T *__restrict__ dout,
-                   const float *__restrict__ z, const float *__restrict__ delta,
-                   const int *__restrict__ dst_rowptr, const int *__restrict__ dst_src,
-                   const int *__restrict__ src_rowptr, const int *__restrict__ src_dst,
-                   const int *__restrict__ src_to_dst_slot, const float *__restrict__ bias,
-                   T *__restrict__ dq, T *__restrict__ dk, T *__restrict__ dv,
-                   float *__restrict__ dbias, SegView sgd, SegView sgs) {
-    using L = VecLayout<T, HEAD_VECS, ROW_VECS>;
-    constexpr int G = L::G, VPL = L::VPL, EPW = L::EPW, VE = L::VE, UNROLL = 2;
+// ------------------------------------------------------------------------------------
+// bf16 rows of 128 elements (16 vectors of 16 B): packed-math kernels
+// ------------------------------------------------------------------------------------
+// The 65,536-token workload's row shape (H * D = 128, bf16) with its own forward and backward.
+// Lane groups of 16 lanes hold one row (one 16-byte vector of eight bf16 per lane): two edges per
+// warp instruction, UNROLL pairs in flight.  Dot products run as fma.rn.f32.bf16 straight on the
+// packed words (a bf16 x bf16 product is exact in f32, so every step equals fmaf of the widened
+// values), in an even and an odd chain added at the end; weighted sums run as packed f32x2 FMAs on
+// the widened vector; exponentials and the source role's reciprocal on the MUFU unit.  The
+// segment records are laid out as in the general kernels, so the same finish kernels serve both.
+namespace r128 {
+constexpr int G = 16;
+constexpr int RV = 16;
+
+// Read-only 16-byte load that the compiler may schedule freely (the tensors are not written by
+// the kernels that read them).
+__device__ __forceinline__ uint4 ld16(const uint4 *p) {
+    uint4 r;
+    asm("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ void fma_pair(float &d0, float &d1, uint32_t a, uint32_t b) {
+    asm("{\n\t.reg .b16 al, ah, bl, bh;\n\t"
+        "mov.b32 {al, ah}, %2;\n\t"
+        "mov.b32 {bl, bh}, %3;\n\t"
+        "fma.rn.f32.bf16 %0, al, bl, %0;\n\t"
+        "fma.rn.f32.bf16 %1, ah, bh, %1;\n\t}"
+        : "+f"(d0), "+f"(d1)
+        : "r"(a), "r"(b));
+}
+
+// sum_i a_i b_i over the eight bf16 of two vectors (even and odd elements in separate chains).
+__device__ __forceinline__ float dot8(const uint4 &a, const uint4 &b) {
+    float d0 = 0.f, d1 = 0.f;
+    fma_pair(d0, d1, a.x, b.x);
+    fma_pair(d0, d1, a.y, b.y);
+    fma_pair(d0, d1, a.z, b.z);
+    fma_pair(d0, d1, a.w, b.w);
+    return d0 + d1;
+}
+
+__device__ __forceinline__ float2 widen(uint32_t w) {
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+
+// acc[j] += s * (elements 2j, 2j + 1 of x)
+__device__ __forceinline__ void axpy8(float2 (&acc)[4], float s, const uint4 &x) {
+    const float2 ss = make_float2(s, s);
+    acc[0] = __ffma2_rn(ss, widen(x.x), acc[0]);
+    acc[1] = __ffma2_rn(ss, widen(x.y), acc[1]);
+    acc[2] = __ffma2_rn(ss, widen(x.z), acc[2]);
+    acc[3] = __ffma2_rn(ss, widen(x.w), acc[3]);
+}
+
+// Adds the two edge slots of a warp (lane groups 0 and 1).
+__device__ __forceinline__ void slot_sum(float2 (&acc)[4]) {
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        acc[j].x += __shfl_xor_sync(0xffffffffu, acc[j].x, G);
+        acc[j].y += __shfl_xor_sync(0xffffffffu, acc[j].y, G);
+    }
+}
+
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+
+__device__ __forceinline__ uint4 pack8(const float2 (&acc)[4], float s) {
+    return make_uint4(pack2(acc[0].x * s, acc[0].y * s), pack2(acc[1].x * s, acc[1].y * s),
+                      pack2(acc[2].x * s, acc[2].y * s), pack2(acc[3].x * s, acc[3].y * s));
+}
+
+__device__ __forceinline__ void store_rec(float *rec, const float2 (&acc)[4]) {
+    *reinterpret_cast<float4 *>(rec) = make_float4(acc[0].x, acc[0].y, acc[1].x, acc[1].y);
+    *reinterpret_cast<float4 *>(rec + 4) = make_float4(acc[2].x, acc[2].y, acc[3].x, acc[3].y);
+}
+}  // namespace r128
+
+template <int HEAD_VECS, int UNROLL, int MIN_BLOCKS = 4>
+__global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
+    spattn_fwd_r128(int n, int heads, float scale_inv, const __nv_bfloat16 *__restrict__ q,
+                    const __nv_bfloat16 *__restrict__ k, const __nv_bfloat16 *__restrict__ v,
+                    const int *__restrict__ rowptr, const int *__restrict__ col,
+                    const float *__restrict__ bias, __nv_bfloat16 *__restrict__ out, float *__restrict__ z,
+                    float *__restrict__ node_scores, int ns_len, int row_blocks, SegView sg) {
+    using namespace r128;
+    constexpr int EPW = 32 / G;
+    const int lane = lane_id();
+    const int sub = lane / G;
+    const int gl = lane % G;
+    const int wid = threadIdx.x >> 5;
+    int row, beg, end, seg = -1;
+    if ((int)blockIdx.x < row_blocks) {
+        row = blockIdx.x * kWarpsPerBlock + wid;
+        if (row >= n) return;
+        if (sg.first != nullptr && __ldg(sg.first + row) >= 0) return;   // done by its segments
+        beg = __ldg(rowptr + row);
+        end = __ldg(rowptr + row + 1);
+    } else {
+        seg = ((int)blockIdx.x - row_blocks) * kWarpsPerBlock + wid;
+        if (seg >= sg.nseg) return;
+        row = __ldg(sg.row + seg);
+        beg = __ldg(rowptr + row) + (seg - __ldg(sg.first + row)) * sg.edges;
+        end = min(__ldg(rowptr + row + 1), beg + sg.edges);
+    }
+    const int head = gl / HEAD_VECS;
+    const uint4 *K = reinterpret_cast<const uint4 *>(k) + gl;
+    const uint4 *V = reinterpret_cast<const uint4 *>(v) + gl;
+    const uint4 qw = ld16(reinterpret_cast<const uint4 *>(q) + (size_t)row * RV + gl);
+    float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+    float zs = 0.f;
+    for (int e0 = beg; e0 < end; e0 += EPW * UNROLL) {
+        int src[UNROLL];
+        bool ok[UNROLL];
+#pragma unroll
+        for (int u = 0; u < UNROLL; u++) {
+            const int e = e0 + sub + EPW * u;
+            ok[u] = e < end;
+            src[u] = ok[u] ? __ldg(col + e) : 0;
+        }
+        uint4 kr[UNROLL], vr[UNROLL];
+#pragma unroll
+        for (int u = 0; u < UNROLL; u++) {
+            kr[u] = ld16(K + (size_t)src[u] * RV);
+            vr[u] = ld16(V + (size_t)src[u] * RV);
+        }
+#pragma unroll
+        for (int u = 0; u < UNROLL; u++) {
+            const float d = head_reduce<HEAD_VECS>(dot8(kr[u], qw));
+            float s = fminf(fmaxf(d * scale_inv, -kClamp), kClamp);
+            if (bias != nullptr && ok[u]) s += __ldg(bias + (size_t)(e0 + sub + EPW * u) * heads + head);
+            const float p = ok[u] ? mufu_exp(s) : 0.f;
+            zs += p;
+            axpy8(acc, p, vr[u]);
+        }
+    }
+    zs += __shfl_xor_sync(0xffffffffu, zs, G);
+    slot_sum(acc);
+    if (seg >= 0) {   // partial sums of the segment: acc in row layout, then Z per head
+        if (sub == 0) {
+            float *rec = sg.part + (size_t)seg * fwd_record(heads, RV * 8);
+            store_rec(rec + gl * 8, acc);
+            if ((gl % HEAD_VECS) == 0) rec[RV * 8 + head] = zs;
+        }
+        return;
+    }
+    if (sub == 0) {
+        const float inv = 1.0f / (zs + kEps);
+        *(reinterpret_cast<uint4 *>(out) + (size_t)row * RV + gl) = pack8(acc, inv);
+        if (z != nullptr && (gl % HEAD_VECS) == 0) z[(size_t)row * heads + head] = zs;
+    }
+    // node score: head mean of Z (lane groups of one head hold equal values)
+    float hs = zs;
+#pragma unroll
+    for (int off = HEAD_VECS; off < G; off <<= 1) hs += __shfl_xor_sync(0xffffffffu, hs, off);
+    if (lane == 0 && row < ns_len) node_scores[row] = hs / (float)heads;
+}
+
+template <int HEAD_VECS, int UNROLL_A, int UNROLL_B, int MIN_BLOCKS = 4>
+__global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
+    spattn_bwd_r128(int n, int heads, float scale_inv, int blocks_a, const __nv_bfloat16 *__restrict__ q,
+                    const __nv_bfloat16 *__restrict__ k, const __nv_bfloat16 *__restrict__ v,
+                    const __nv_bfloat16 *__restrict__ dout, const float *__restrict__ z,
+                    const float *__restrict__ delta, const int *__restrict__ dst_rowptr,
+                    const int *__restrict__ dst_src, const int *__restrict__ src_rowptr,
+                    const int *__restrict__ src_dst, const int *__restrict__ src_to_dst_slot,
+                    const float *__restrict__ bias, __nv_bfloat16 *__restrict__ dq,
+                    __nv_bfloat16 *__restrict__ dk, __nv_bfloat16 *__restrict__ dv, float *__restrict__ dbias,
+                    SegView sgd, SegView sgs) {
+    using namespace r128;
+    constexpr int EPW = 32 / G;
     const int lane = lane_id();
     const int sub = lane / G;
     const int gl = lane % G;
@@ -589,200 +744,110 @@ __global__ void __launch_bounds__(kBlock, 4)
         beg = __ldg(rp + row) + (seg - __ldg((role_a ? sgd.first : sgs.first) + row)) * edges;
         end = min(__ldg(rp + row + 1), beg + edges);
     }
-    const Vec16 *Q = reinterpret_cast<const Vec16 *>(q) + gl;
-    const Vec16 *K = reinterpret_cast<const Vec16 *>(k) + gl;
-    const Vec16 *V = reinterpret_cast<const Vec16 *>(v) + gl;
-    const Vec16 *DO = reinterpret_cast<const Vec16 *>(dout) + gl;
-    const size_t rbase = (size_t)row * ROW_VECS;
-    int head[VPL];
-#pragma unroll
-    for (int t = 0; t < VPL; t++) head[t] = (gl + G * t) / HEAD_VECS;
+    const uint4 *Q = reinterpret_cast<const uint4 *>(q) + gl;
+    const uint4 *K = reinterpret_cast<const uint4 *>(k) + gl;
+    const uint4 *V = reinterpret_cast<const uint4 *>(v) + gl;
+    const uint4 *DO = reinterpret_cast<const uint4 *>(dout) + gl;
+    const size_t rbase = (size_t)row * RV;
+    const int head = gl / HEAD_VECS;
+    float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 
     if (role_a) {
         // ---- dq for destination row `row` ----
-        float qf[VPL][VE], gf[VPL][VE], inv[VPL], dl[VPL], acc[VPL][VE];
+        const uint4 qw = ld16(Q + rbase), gw = ld16(DO + rbase);
+        const float inv = 1.0f / (__ldg(z + (size_t)row * heads + head) + kEps);
+        const float dl = __ldg(delta + (size_t)row * heads + head);
+        for (int e0 = beg; e0 < end; e0 += EPW * UNROLL_A) {
+            int src[UNROLL_A];
+            bool ok[UNROLL_A];
 #pragma unroll
-        for (int t = 0; t < VPL; t++) {
-            Elem<T>::unpack(ldg16(Q + rbase + G * t), qf[t]);
-            Elem<T>::unpack(ldg16(DO + rbase + G * t), gf[t]);
-            inv[t] = 1.0f / (__ldg(z + (size_t)row * heads + head[t]) + kEps);
-            dl[t] = __ldg(delta + (size_t)row * heads + head[t]);
-#pragma unroll
-            for (int i = 0; i < VE; i++) acc[t][i] = 0.f;
-        }
-        for (int e0 = beg; e0 < end; e0 += EPW * UNROLL) {
-            int src[UNROLL];
-            bool ok[UNROLL];
-#pragma unroll
-            for (int u = 0; u < UNROLL; u++) {
+            for (int u = 0; u < UNROLL_A; u++) {
                 const int e = e0 + sub + EPW * u;
                 ok[u] = e < end;
                 src[u] = ok[u] ? __ldg(dst_src + e) : 0;
             }
-            Vec16 kr[UNROLL][VPL], vr[UNROLL][VPL];
+            uint4 kr[UNROLL_A], vr[UNROLL_A];
 #pragma unroll
-            for (int u = 0; u < UNROLL; u++)
+            for (int u = 0; u < UNROLL_A; u++) {
+                kr[u] = ld16(K + (size_t)src[u] * RV);
+                vr[u] = ld16(V + (size_t)src[u] * RV);
+            }
 #pragma unroll
-                for (int t = 0; t < VPL; t++) {
-                    kr[u][t] = ldg16(K + (size_t)src[u] * ROW_VECS + G * t);
-                    vr[u][t] = ldg16(V + (size_t)src[u] * ROW_VECS + G * t);
-                }
-#pragma unroll
-            for (int u = 0; u < UNROLL; u++) {
+            for (int u = 0; u < UNROLL_A; u++) {
                 const int e = e0 + sub + EPW * u;
-#pragma unroll
-                for (int t = 0; t < VPL; t++) {
-                    float kf[VE], vf[VE];
-                    Elem<T>::unpack(kr[u][t], kf);
-                    Elem<T>::unpack(vr[u][t], vf);
-                    float dqk = 0.f, dgv = 0.f;
-#pragma unroll
-                    for (int i = 0; i < VE; i++) {
-                        dqk = fmaf(kf[i], qf[t][i], dqk);
-                        dgv = fmaf(gf[t][i], vf[i], dgv);
-                    }
-                    dqk = head_reduce<HEAD_VECS>(dqk);
-                    dgv = head_reduce<HEAD_VECS>(dgv);
-                    const float s = dqk * scale_inv;
-                    const bool inside = s >= -kClamp && s <= kClamp;
-                    float sc = fminf(fmaxf(s, -kClamp), kClamp);
-                    if (bias != nullptr && ok[u]) sc += __ldg(bias + (size_t)e * heads + head[t]);
-                    const float p = mufu_exp(sc);
-                    const float dpre = (dgv - dl[t]) * inv[t] * p;
-                    const float ds = (ok[u] && inside) ? dpre : 0.f;
-                    if (dbias != nullptr && ok[u] && (gl % HEAD_VECS) == 0) dbias[(size_t)e * heads + head[t]] = dpre;
-#pragma unroll
-                    for (int i = 0; i < VE; i++) acc[t][i] = fmaf(ds, kf[i], acc[t][i]);
-                }
+                const float dqk = head_reduce<HEAD_VECS>(dot8(kr[u], qw));
+                const float dgv = head_reduce<HEAD_VECS>(dot8(vr[u], gw));
+                const float s = dqk * scale_inv;
+                float sc = fminf(fmaxf(s, -kClamp), kClamp);
+                const bool inside = sc == s;   // -kClamp <= s <= kClamp (false for NaN)
+                if (bias != nullptr && ok[u]) sc += __ldg(bias + (size_t)e * heads + head);
+                const float p = mufu_exp(sc);
+                const float dpre = (dgv - dl) * inv * p;
+                const float ds = (ok[u] && inside) ? dpre : 0.f;
+                if (dbias != nullptr && ok[u] && (gl % HEAD_VECS) == 0) dbias[(size_t)e * heads + head] = dpre;
+                axpy8(acc, ds, kr[u]);
             }
         }
-        if (EPW > 1) {
-#pragma unroll
-            for (int t = 0; t < VPL; t++)
-#pragma unroll
-                for (int i = 0; i < VE; i++) acc[t][i] = slot_reduce<G>(acc[t][i]);
-        }
+        slot_sum(acc);
         if (seg >= 0) {   // segment partial of dq (before the 1/sqrt(D) scale)
-            if (sub == 0) {
-                float *rec = sgd.part + (size_t)seg * ROW_VECS * VE;
-#pragma unroll
-                for (int t = 0; t < VPL; t++)
-#pragma unroll
-                    for (int i = 0; i < VE; i += 4)
-                        *reinterpret_cast<float4 *>(rec + (gl + G * t) * VE + i) =
-                            make_float4(acc[t][i], acc[t][i + 1], acc[t][i + 2], acc[t][i + 3]);
-            }
+            if (sub == 0) store_rec(sgd.part + (size_t)seg * RV * 8 + gl * 8, acc);
             return;
         }
-        if (sub == 0) {
-            Vec16 *o = reinterpret_cast<Vec16 *>(dq) + rbase + gl;
-#pragma unroll
-            for (int t = 0; t < VPL; t++) {
-                float r[VE];
-#pragma unroll
-                for (int i = 0; i < VE; i++) r[i] = acc[t][i] * scale_inv;
-                st16(o + G * t, Elem<T>::pack(r));
-            }
-        }
+        if (sub == 0) *(reinterpret_cast<uint4 *>(dq) + rbase + gl) = pack8(acc, scale_inv);
     } else {
         // ---- dk, dv for source row `row` ----
-        float kf[VPL][VE], vf[VPL][VE], ak[VPL][VE], av[VPL][VE];
+        const uint4 kw = ld16(K + rbase), vw = ld16(V + rbase);
+        float2 av[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+        for (int e0 = beg; e0 < end; e0 += EPW * UNROLL_B) {
+            int dst[UNROLL_B];
+            bool ok[UNROLL_B];
 #pragma unroll
-        for (int t = 0; t < VPL; t++) {
-            Elem<T>::unpack(ldg16(K + rbase + G * t), kf[t]);
-            Elem<T>::unpack(ldg16(V + rbase + G * t), vf[t]);
-#pragma unroll
-            for (int i = 0; i < VE; i++) ak[t][i] = av[t][i] = 0.f;
-        }
-        for (int e0 = beg; e0 < end; e0 += EPW * UNROLL) {
-            int dst[UNROLL];
-            bool ok[UNROLL];
-#pragma unroll
-            for (int u = 0; u < UNROLL; u++) {
+            for (int u = 0; u < UNROLL_B; u++) {
                 const int e = e0 + sub + EPW * u;
                 ok[u] = e < end;
                 dst[u] = ok[u] ? __ldg(src_dst + e) : 0;
             }
-            Vec16 qr[UNROLL][VPL], gr[UNROLL][VPL];
-            float zr[UNROLL][VPL], dr[UNROLL][VPL];
+            uint4 qr[UNROLL_B], gr[UNROLL_B];
+            float zr[UNROLL_B], dr[UNROLL_B];
 #pragma unroll
-            for (int u = 0; u < UNROLL; u++)
+            for (int u = 0; u < UNROLL_B; u++) {
+                qr[u] = ld16(Q + (size_t)dst[u] * RV);
+                gr[u] = ld16(DO + (size_t)dst[u] * RV);
+                zr[u] = __ldg(z + (size_t)dst[u] * heads + head);
+                dr[u] = __ldg(delta + (size_t)dst[u] * heads + head);
+            }
 #pragma unroll
-                for (int t = 0; t < VPL; t++) {
-                    qr[u][t] = ldg16(Q + (size_t)dst[u] * ROW_VECS + G * t);
-                    gr[u][t] = ldg16(DO + (size_t)dst[u] * ROW_VECS + G * t);
-                    zr[u][t] = __ldg(z + (size_t)dst[u] * heads + head[t]);
-                    dr[u][t] = __ldg(delta + (size_t)dst[u] * heads + head[t]);
-                }
-#pragma unroll
-            for (int u = 0; u < UNROLL; u++) {
+            for (int u = 0; u < UNROLL_B; u++) {
                 const int e = e0 + sub + EPW * u;
-#pragma unroll
-                for (int t = 0; t < VPL; t++) {
-                    float qf[VE], gf[VE];
-                    Elem<T>::unpack(qr[u][t], qf);
-                    Elem<T>::unpack(gr[u][t], gf);
-                    float dqk = 0.f, dgv = 0.f;
-#pragma unroll
-                    for (int i = 0; i < VE; i++) {
-                        dqk = fmaf(kf[t][i], qf[i], dqk);
-                        dgv = fmaf(gf[i], vf[t][i], dgv);
-                    }
-                    dqk = head_reduce<HEAD_VECS>(dqk);
-                    dgv = head_reduce<HEAD_VECS>(dgv);
-                    const float s = dqk * scale_inv;
-                    const bool inside = s >= -kClamp && s <= kClamp;
-                    float sc = fminf(fmaxf(s, -kClamp), kClamp);
-                    if (bias != nullptr && ok[u])
-                        sc += __ldg(bias + (size_t)__ldg(src_to_dst_slot + e) * heads + head[t]);
-                    const float p = ok[u] ? mufu_exp(sc) : 0.f;
-                    const float inv = mufu_rcp(zr[u][t] + kEps);
-                    const float a = p * inv;
-                    const float dpre = (dgv - dr[u][t]) * inv * p;
-                    const float ds = inside ? dpre : 0.f;
-#pragma unroll
-                    for (int i = 0; i < VE; i++) {
-                        av[t][i] = fmaf(a, gf[i], av[t][i]);
-                        ak[t][i] = fmaf(ds, qf[i], ak[t][i]);
-                    }
-                }
+                const float dqk = head_reduce<HEAD_VECS>(dot8(qr[u], kw));
+                const float dgv = head_reduce<HEAD_VECS>(dot8(gr[u], vw));
+                const float s = dqk * scale_inv;
+                float sc = fminf(fmaxf(s, -kClamp), kClamp);
+                const bool inside = sc == s;   // -kClamp <= s <= kClamp (false for NaN)
+                if (bias != nullptr && ok[u])
+                    sc += __ldg(bias + (size_t)__ldg(src_to_dst_slot + e) * heads + head);
+                const float p = ok[u] ? mufu_exp(sc) : 0.f;
+                const float inv = mufu_rcp(zr[u] + kEps);
+                const float a = p * inv;
+                const float dpre = (dgv - dr[u]) * inv * p;
+                const float ds = inside ? dpre : 0.f;
+                axpy8(av, a, gr[u]);
+                axpy8(acc, ds, qr[u]);
             }
         }
-        if (EPW > 1) {
-#pragma unroll
-            for (int t = 0; t < VPL; t++)
-#pragma unroll
-                for (int i = 0; i < VE; i++) {
-                    ak[t][i] = slot_reduce<G>(ak[t][i]);
-                    av[t][i] = slot_reduce<G>(av[t][i]);
-                }
-        }
+        slot_sum(acc);
+        slot_sum(av);
         if (seg >= 0) {   // segment partials of dk (unscaled) and dv
             if (sub == 0) {
-                float *rec = sgs.part + (size_t)seg * 2 * ROW_VECS * VE;
-#pragma unroll
-                for (int t = 0; t < VPL; t++)
-#pragma unroll
-                    for (int i = 0; i < VE; i += 4) {
-                        *reinterpret_cast<float4 *>(rec + (gl + G * t) * VE + i) =
-                            make_float4(ak[t][i], ak[t][i + 1], ak[t][i + 2], ak[t][i + 3]);
-                        *reinterpret_cast<float4 *>(rec + ROW_VECS * VE + (gl + G * t) * VE + i) =
-                            make_float4(av[t][i], av[t][i + 1], av[t][i + 2], av[t][i + 3]);
-                    }
+                float *rec = sgs.part + (size_t)seg * 2 * RV * 8;
+                store_rec(rec + gl * 8, acc);
+                store_rec(rec + RV * 8 + gl * 8, av);
             }
             return;
         }
         if (sub == 0) {
-            Vec16 *ok_ = reinterpret_cast<Vec16 *>(dk) + rbase + gl;
-            Vec16 *ov = reinterpret_cast<Vec16 *>(dv) + rbase + gl;
-#pragma unroll
-            for (int t = 0; t < VPL; t++) {
-                float r[VE];
-#pragma unroll
-                for (int i = 0; i < VE; i++) r[i] = ak[t][i] * scale_inv;
-                st16(ok_ + G * t, Elem<T>::pack(r));
-                st16(ov + G * t, Elem<T>::pack(av[t]));
-            }
+            *(reinterpret_cast<uint4 *>(dk) + rbase + gl) = pack8(acc, scale_inv);
+            *(reinterpret_cast<uint4 *>(dv) + rbase + gl) = pack8(av, 1.0f);
         }
     }
 }
@@ -1038,9 +1103,15 @@ int forward_t(int64_t n, int heads, int head_dim, const void *q, const void *k, 
         const int seg_blocks = ceil_div_i(sg.nseg, kWarpsPerBlock);
 #define NGT_FWD(HV, RV)                                                                          \
     if (sh.head_vecs == HV && sh.row_vecs == RV) {                                               \
-        spattn_fwd_vec<T, HV, RV><<<row_blocks + seg_blocks, kBlock, 0, st>>>(                   \
-            (int)n, heads, scale_inv, (const T *)q, (const T *)k, (const T *)v, rowptr, col,     \
-            bias, (T *)out, z, ns, (int)ns_len, row_blocks, sg);                                 \
+        if constexpr (sizeof(T) == 2 && RV == 16)                                                \
+            spattn_fwd_r128<HV, 4><<<row_blocks + seg_blocks, kBlock, 0, st>>>(                  \
+                (int)n, heads, scale_inv, (const __nv_bfloat16 *)q, (const __nv_bfloat16 *)k,    \
+                (const __nv_bfloat16 *)v, rowptr, col, bias, (__nv_bfloat16 *)out, z, ns,        \
+                (int)ns_len, row_blocks, sg);                                                    \
+        else                                                                                     \
+            spattn_fwd_vec<T, HV, RV><<<row_blocks + seg_blocks, kBlock, 0, st>>>(               \
+                (int)n, heads, scale_inv, (const T *)q, (const T *)k, (const T *)v, rowptr, col, \
+                bias, (T *)out, z, ns, (int)ns_len, row_blocks, sg);                             \
         NGT_CHECK_LAUNCH();                                                                      \
         if (sg.nseg > 0)                                                                         \
             spattn_fwd_seg_finish<T, HV, RV><<<seg_blocks, kBlock, 0, st>>>(heads, rowptr, (T *)out, z, ns, \
@@ -1088,11 +1159,12 @@ int backward_t(int64_t n, int heads, int head_dim, const void *q, const void *k,
         spattn_delta_vec<T, HV, RV><<<ceil_div_i(n, (int64_t)kWarpsPerBlock * Lay::EPW), kBlock, 0, st>>>( \
             (int)n, heads, (const T *)out, (const T *)dout, delta);                               \
         NGT_CHECK_LAUNCH();                                                                       \
-        if (sizeof(T) == 2 && HV == 2 && RV == 16)                                                \
-            spattn_bwd_vec_narrow<T, 2, 16><<<2 * blocks_a + seg_blocks, kBlock, 0, st>>>(        \
-                (int)n, heads, scale_inv, blocks_a, (const T *)q, (const T *)k, (const T *)v,     \
-                (const T *)dout, z, delta, dst_rowptr, dst_src, src_rowptr, src_dst, s2d, bias,   \
-                (T *)dq, (T *)dk, (T *)dv, dbias, sgd, sgs);                                      \
+        if constexpr (sizeof(T) == 2 && RV == 16)                                                 \
+            spattn_bwd_r128<HV, 3, 2><<<2 * blocks_a + seg_blocks, kBlock, 0, st>>>(              \
+                (int)n, heads, scale_inv, blocks_a, (const __nv_bfloat16 *)q,                     \
+                (const __nv_bfloat16 *)k, (const __nv_bfloat16 *)v, (const __nv_bfloat16 *)dout,  \
+                z, delta, dst_rowptr, dst_src, src_rowptr, src_dst, s2d, bias,                    \
+                (__nv_bfloat16 *)dq, (__nv_bfloat16 *)dk, (__nv_bfloat16 *)dv, dbias, sgd, sgs);  \
         else                                                                                      \
             spattn_bwd_vec<T, HV, RV><<<2 * blocks_a + seg_blocks, kBlock, 0, st>>>(              \
                 (int)n, heads, scale_inv, blocks_a, (const T *)q, (const T *)k, (const T *)v,     \
