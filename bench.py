@@ -284,7 +284,7 @@ def bench_attention(args, rank, world, dev):
     traffic = ncu_traffic()
     dom = "bwd" if avg_bwd >= avg_fwd else "fwd"
     achieved = (bwd_bytes / avg_bwd if dom == "bwd" else fwd_bytes / avg_fwd) / 1e9
-    roofline = {"bound": "hbm", "kernel": "spattn_delta_vec+spattn_bwd_vec" if dom == "bwd" else "spattn_fwd_vec",
+    roofline = {"bound": "hbm", "kernel": "spattn_delta_vec+spattn_bwd_r128" if dom == "bwd" else "spattn_fwd_r128",
                 "achieved": achieved, "peak": peak, "peak_kind": f"{peak_kind} hbm_gbs (burst)", "unit": "GB/s",
                 "frac": achieved / peak, "traffic": traffic.get(dom),
                 "algorithmic_bytes_per_launch": bwd_bytes if dom == "bwd" else fwd_bytes,
@@ -297,17 +297,21 @@ def bench_attention(args, rank, world, dev):
                                      "note": "Q,K,V,O once + CSR + Z + node scores; K/V (33.5 MB) can stay in L2, "
                                              "so the no-reuse algorithmic bytes and these bracket the DRAM traffic"}}
 
-    # L2-side roofline of the backward, from the committed one-kernel ncu capture of this launch
-    # (profiles/ncu_traffic.json): its L2 traffic (lts__t_sectors x 32 B) over the time measured
-    # here, and ncu's lts__throughput percentage as the fraction of the L2's sustained peak
-    lts, pct, ncu_us = traffic.get("bwd_lts"), traffic.get("bwd_lts_pct"), traffic.get("bwd_ncu_us")
-    l2_achieved = lts / avg_bwd / 1e9 if lts else None
-    l2_peak = lts / (ncu_us * 1e-6) / (pct / 100.0) / 1e9 if (lts and pct and ncu_us) else None
-    roofline["l2"] = {"traffic": lts, "achieved": l2_achieved, "unit": "GB/s", "peak": l2_peak,
-                      "frac": l2_achieved / l2_peak if l2_peak else None,
-                      "peak_kind": "L2 sustained peak implied by the committed capture (its lts__t_sectors over "
-                                   "its duration, divided by its lts__throughput percent of peak; "
-                                   "profiles/spattn_bwd_narrow_config3.md)"}
+    # L2-side rooflines, from the committed one-kernel ncu captures of these launches
+    # (profiles/ncu_traffic.json): each launch's L2 traffic (lts__t_sectors x 32 B) over the time
+    # measured here, against the L2 sustained peak the capture implies (its sectors over its
+    # duration, divided by its lts__throughput percentage)
+    def l2_roofline(key, avg):
+        lts, pct, ncu_us = traffic.get(f"{key}_lts"), traffic.get(f"{key}_lts_pct"), traffic.get(f"{key}_ncu_us")
+        achieved = lts / avg / 1e9 if lts else None
+        l2_peak = lts / (ncu_us * 1e-6) / (pct / 100.0) / 1e9 if (lts and pct and ncu_us) else None
+        return {"traffic": lts, "achieved": achieved, "unit": "GB/s", "peak": l2_peak,
+                "frac": achieved / l2_peak if l2_peak else None,
+                "peak_kind": "L2 sustained peak implied by the committed capture (profiles/spattn_r128_config3.md)"}
+
+    roofline["l2"] = l2_roofline(dom, avg_bwd if dom == "bwd" else avg_fwd)
+    roofline["fwd"]["l2"] = l2_roofline("fwd", avg_fwd)
+    roofline["bwd"]["l2"] = l2_roofline("bwd", avg_bwd)
 
     # e2e through the public API with pinned host buffers.  Every step copies its own inputs in and
     # its results out.  Pipelined: one stream per engine — host-to-device copies, the API call, and
