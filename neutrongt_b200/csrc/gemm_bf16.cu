@@ -49,6 +49,7 @@ struct GemmArgs {
     const __nv_bfloat16 *bias;   // [N] or null (forward only)
     void *out;              // bf16 [M, N] (mode 0) or fp32 partials [splits][M][N] (mode 1)
     int mode;
+    int bias_vec;           // 1: bias is 16-byte aligned, read as 16-byte vectors
 };
 
 // Shared-memory descriptor of a 128-byte-swizzled operand tile (layout type 2 in bits 61-63).
@@ -255,7 +256,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!row_ok || col0 >= p.N) continue;
                 const int ncols = min(32, p.N - col0);
                 if (p.mode == 0) {
-                    if (p.bias != nullptr) {
+                    if (p.bias != nullptr && p.bias_vec && ncols == 32) {
+                        // the chunk's 32 bias values as four 16-byte loads (one address for the warp)
+                        const uint4 *bp = reinterpret_cast<const uint4 *>(p.bias + col0);
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            const uint4 b = __ldg(bp + j);
+                            const uint32_t w[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+                            for (int i = 0; i < 4; i++) {
+                                v[8 * j + 2 * i] += __uint_as_float(w[i] << 16);
+                                v[8 * j + 2 * i + 1] += __uint_as_float(w[i] & 0xffff0000u);
+                            }
+                        }
+                    } else if (p.bias != nullptr) {
 #pragma unroll
                         for (int i = 0; i < 32; i++)
                             if (i < ncols) v[i] += __bfloat162float(p.bias[col0 + i]);
@@ -471,6 +485,7 @@ extern "C" int ngt_linear_bf16_forward(int64_t rows, int in_features, int out_fe
     p.kb_per_split = p.kb_total;
     p.splits = 1;
     p.bias = static_cast<const __nv_bfloat16 *>(bias);
+    p.bias_vec = bias != nullptr && aligned16(bias);
     p.out = y;
     p.mode = 0;
     return run(p, x, rows, in_features, weight, out_features, in_features, reinterpret_cast<cudaStream_t>(stream));
