@@ -621,7 +621,9 @@ __device__ __forceinline__ void store_rec(float *rec, const float2 (&acc)[4]) {
 }
 }  // namespace r128
 
-template <int HEAD_VECS, int UNROLL, int MIN_BLOCKS = 4>
+// PAIRS (HEAD_VECS = 2): the two lanes of a head finish different edges of an edge pair and
+// exchange the exponentials (as spattn_bwd_r128 below); the same results as without pairs.
+template <int HEAD_VECS, int UNROLL, int MIN_BLOCKS = 4, bool PAIRS = false>
 __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
     spattn_fwd_r128(int n, int heads, float scale_inv, const __nv_bfloat16 *__restrict__ q,
                     const __nv_bfloat16 *__restrict__ k, const __nv_bfloat16 *__restrict__ v,
@@ -669,14 +671,35 @@ __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
             kr[u] = ld16(K + (size_t)src[u] * RV);
             vr[u] = ld16(V + (size_t)src[u] * RV);
         }
+        if constexpr (PAIRS) {
+            static_assert(HEAD_VECS == 2 && UNROLL % 2 == 0, "pairs of edges, two lanes per head");
+            const bool odd = (gl & 1) != 0;   // this lane finishes edge u + 1 of each pair
 #pragma unroll
-        for (int u = 0; u < UNROLL; u++) {
-            const float d = head_reduce<HEAD_VECS>(dot8(kr[u], qw));
-            float s = fminf(fmaxf(d * scale_inv, -kClamp), kClamp);
-            if (bias != nullptr && ok[u]) s += __ldg(bias + (size_t)(e0 + sub + EPW * u) * heads + head);
-            const float p = ok[u] ? mufu_exp(s) : 0.f;
-            zs += p;
-            axpy8(acc, p, vr[u]);
+            for (int u = 0; u < UNROLL; u += 2) {
+                const float d0 = dot8(kr[u], qw), d1 = dot8(kr[u + 1], qw);
+                const float d = (odd ? d1 : d0) + __shfl_xor_sync(0xffffffffu, odd ? d0 : d1, 1);
+                const bool okm = odd ? ok[u + 1] : ok[u];
+                float s = fminf(fmaxf(d * scale_inv, -kClamp), kClamp);
+                if (bias != nullptr && okm)
+                    s += __ldg(bias + (size_t)(e0 + sub + EPW * u + (odd ? EPW : 0)) * heads + head);
+                const float p = okm ? mufu_exp(s) : 0.f;
+                const float pp = __shfl_xor_sync(0xffffffffu, p, 1);
+                const float p0 = odd ? pp : p, p1 = odd ? p : pp;
+                zs += p0;
+                axpy8(acc, p0, vr[u]);
+                zs += p1;
+                axpy8(acc, p1, vr[u + 1]);
+            }
+        } else {
+#pragma unroll
+            for (int u = 0; u < UNROLL; u++) {
+                const float d = head_reduce<HEAD_VECS>(dot8(kr[u], qw));
+                float s = fminf(fmaxf(d * scale_inv, -kClamp), kClamp);
+                if (bias != nullptr && ok[u]) s += __ldg(bias + (size_t)(e0 + sub + EPW * u) * heads + head);
+                const float p = ok[u] ? mufu_exp(s) : 0.f;
+                zs += p;
+                axpy8(acc, p, vr[u]);
+            }
         }
     }
     zs += __shfl_xor_sync(0xffffffffu, zs, G);
@@ -701,7 +724,12 @@ __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
     if (lane == 0 && row < ns_len) node_scores[row] = hs / (float)heads;
 }
 
-template <int HEAD_VECS, int UNROLL_A, int UNROLL_B, int MIN_BLOCKS = 4>
+// PAIRS (two lanes per head, HEAD_VECS = 2): the two lanes of a head finish different edges of an
+// edge pair.  Each sends the partner the partial dot product of the partner's edge, runs the score,
+// exponential and gradient arithmetic once for its own edge, and hands back the two scalars the
+// weighted sums need, instead of both lanes repeating that arithmetic for every edge.  The sums
+// are added in the same order as without pairs, so the results are identical.
+template <int HEAD_VECS, int UNROLL_A, int UNROLL_B, int MIN_BLOCKS = 4, bool PAIRS = false>
 __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
     spattn_bwd_r128(int n, int heads, float scale_inv, int blocks_a, const __nv_bfloat16 *__restrict__ q,
                     const __nv_bfloat16 *__restrict__ k, const __nv_bfloat16 *__restrict__ v,
@@ -772,20 +800,45 @@ __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
                 kr[u] = ld16(K + (size_t)src[u] * RV);
                 vr[u] = ld16(V + (size_t)src[u] * RV);
             }
+            if constexpr (PAIRS) {
+                static_assert(HEAD_VECS == 2 && UNROLL_A % 2 == 0, "pairs of edges, two lanes per head");
+                const bool odd = (gl & 1) != 0;   // this lane finishes edge u + 1 of each pair
 #pragma unroll
-            for (int u = 0; u < UNROLL_A; u++) {
-                const int e = e0 + sub + EPW * u;
-                const float dqk = head_reduce<HEAD_VECS>(dot8(kr[u], qw));
-                const float dgv = head_reduce<HEAD_VECS>(dot8(vr[u], gw));
-                const float s = dqk * scale_inv;
-                float sc = fminf(fmaxf(s, -kClamp), kClamp);
-                const bool inside = sc == s;   // -kClamp <= s <= kClamp (false for NaN)
-                if (bias != nullptr && ok[u]) sc += __ldg(bias + (size_t)e * heads + head);
-                const float p = mufu_exp(sc);
-                const float dpre = (dgv - dl) * inv * p;
-                const float ds = (ok[u] && inside) ? dpre : 0.f;
-                if (dbias != nullptr && ok[u] && (gl % HEAD_VECS) == 0) dbias[(size_t)e * heads + head] = dpre;
-                axpy8(acc, ds, kr[u]);
+                for (int u = 0; u < UNROLL_A; u += 2) {
+                    const float q0 = dot8(kr[u], qw), q1 = dot8(kr[u + 1], qw);
+                    const float g0 = dot8(vr[u], gw), g1 = dot8(vr[u + 1], gw);
+                    const float dqk = (odd ? q1 : q0) + __shfl_xor_sync(0xffffffffu, odd ? q0 : q1, 1);
+                    const float dgv = (odd ? g1 : g0) + __shfl_xor_sync(0xffffffffu, odd ? g0 : g1, 1);
+                    const bool okm = odd ? ok[u + 1] : ok[u];
+                    const int e = e0 + sub + EPW * u + (odd ? EPW : 0);
+                    const float s = dqk * scale_inv;
+                    float sc = fminf(fmaxf(s, -kClamp), kClamp);
+                    const bool inside = sc == s;   // -kClamp <= s <= kClamp (false for NaN)
+                    if (bias != nullptr && okm) sc += __ldg(bias + (size_t)e * heads + head);
+                    const float p = mufu_exp(sc);
+                    const float dpre = (dgv - dl) * inv * p;
+                    const float ds = (okm && inside) ? dpre : 0.f;
+                    if (dbias != nullptr && okm) dbias[(size_t)e * heads + head] = dpre;
+                    const float dsp = __shfl_xor_sync(0xffffffffu, ds, 1);
+                    axpy8(acc, odd ? dsp : ds, kr[u]);
+                    axpy8(acc, odd ? ds : dsp, kr[u + 1]);
+                }
+            } else {
+#pragma unroll
+                for (int u = 0; u < UNROLL_A; u++) {
+                    const int e = e0 + sub + EPW * u;
+                    const float dqk = head_reduce<HEAD_VECS>(dot8(kr[u], qw));
+                    const float dgv = head_reduce<HEAD_VECS>(dot8(vr[u], gw));
+                    const float s = dqk * scale_inv;
+                    float sc = fminf(fmaxf(s, -kClamp), kClamp);
+                    const bool inside = sc == s;   // -kClamp <= s <= kClamp (false for NaN)
+                    if (bias != nullptr && ok[u]) sc += __ldg(bias + (size_t)e * heads + head);
+                    const float p = mufu_exp(sc);
+                    const float dpre = (dgv - dl) * inv * p;
+                    const float ds = (ok[u] && inside) ? dpre : 0.f;
+                    if (dbias != nullptr && ok[u] && (gl % HEAD_VECS) == 0) dbias[(size_t)e * heads + head] = dpre;
+                    axpy8(acc, ds, kr[u]);
+                }
             }
         }
         slot_sum(acc);
@@ -809,30 +862,68 @@ __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
             }
             uint4 qr[UNROLL_B], gr[UNROLL_B];
             float zr[UNROLL_B], dr[UNROLL_B];
+            const bool odd = (gl & 1) != 0;
 #pragma unroll
             for (int u = 0; u < UNROLL_B; u++) {
                 qr[u] = ld16(Q + (size_t)dst[u] * RV);
                 gr[u] = ld16(DO + (size_t)dst[u] * RV);
-                zr[u] = __ldg(z + (size_t)dst[u] * heads + head);
-                dr[u] = __ldg(delta + (size_t)dst[u] * heads + head);
+                if constexpr (PAIRS) {   // Z and delta of the edge this lane finishes
+                    if (u % 2 == 0) {
+                        const int dm = odd ? dst[u + 1] : dst[u];
+                        zr[u] = __ldg(z + (size_t)dm * heads + head);
+                        dr[u] = __ldg(delta + (size_t)dm * heads + head);
+                    }
+                } else {
+                    zr[u] = __ldg(z + (size_t)dst[u] * heads + head);
+                    dr[u] = __ldg(delta + (size_t)dst[u] * heads + head);
+                }
             }
+            if constexpr (PAIRS) {
+                static_assert(HEAD_VECS == 2 && UNROLL_B % 2 == 0, "pairs of edges, two lanes per head");
 #pragma unroll
-            for (int u = 0; u < UNROLL_B; u++) {
-                const int e = e0 + sub + EPW * u;
-                const float dqk = head_reduce<HEAD_VECS>(dot8(qr[u], kw));
-                const float dgv = head_reduce<HEAD_VECS>(dot8(gr[u], vw));
-                const float s = dqk * scale_inv;
-                float sc = fminf(fmaxf(s, -kClamp), kClamp);
-                const bool inside = sc == s;   // -kClamp <= s <= kClamp (false for NaN)
-                if (bias != nullptr && ok[u])
-                    sc += __ldg(bias + (size_t)__ldg(src_to_dst_slot + e) * heads + head);
-                const float p = ok[u] ? mufu_exp(sc) : 0.f;
-                const float inv = mufu_rcp(zr[u] + kEps);
-                const float a = p * inv;
-                const float dpre = (dgv - dr[u]) * inv * p;
-                const float ds = inside ? dpre : 0.f;
-                axpy8(av, a, gr[u]);
-                axpy8(acc, ds, qr[u]);
+                for (int u = 0; u < UNROLL_B; u += 2) {
+                    const float q0 = dot8(qr[u], kw), q1 = dot8(qr[u + 1], kw);
+                    const float g0 = dot8(gr[u], vw), g1 = dot8(gr[u + 1], vw);
+                    const float dqk = (odd ? q1 : q0) + __shfl_xor_sync(0xffffffffu, odd ? q0 : q1, 1);
+                    const float dgv = (odd ? g1 : g0) + __shfl_xor_sync(0xffffffffu, odd ? g0 : g1, 1);
+                    const bool okm = odd ? ok[u + 1] : ok[u];
+                    const int e = e0 + sub + EPW * u + (odd ? EPW : 0);
+                    const float s = dqk * scale_inv;
+                    float sc = fminf(fmaxf(s, -kClamp), kClamp);
+                    const bool inside = sc == s;   // -kClamp <= s <= kClamp (false for NaN)
+                    if (bias != nullptr && okm)
+                        sc += __ldg(bias + (size_t)__ldg(src_to_dst_slot + e) * heads + head);
+                    const float p = okm ? mufu_exp(sc) : 0.f;
+                    const float inv = mufu_rcp(zr[u] + kEps);
+                    const float a = p * inv;
+                    const float dpre = (dgv - dr[u]) * inv * p;
+                    const float ds = inside ? dpre : 0.f;
+                    const float ap = __shfl_xor_sync(0xffffffffu, a, 1);
+                    const float dsp = __shfl_xor_sync(0xffffffffu, ds, 1);
+                    axpy8(av, odd ? ap : a, gr[u]);
+                    axpy8(acc, odd ? dsp : ds, qr[u]);
+                    axpy8(av, odd ? a : ap, gr[u + 1]);
+                    axpy8(acc, odd ? ds : dsp, qr[u + 1]);
+                }
+            } else {
+#pragma unroll
+                for (int u = 0; u < UNROLL_B; u++) {
+                    const int e = e0 + sub + EPW * u;
+                    const float dqk = head_reduce<HEAD_VECS>(dot8(qr[u], kw));
+                    const float dgv = head_reduce<HEAD_VECS>(dot8(gr[u], vw));
+                    const float s = dqk * scale_inv;
+                    float sc = fminf(fmaxf(s, -kClamp), kClamp);
+                    const bool inside = sc == s;   // -kClamp <= s <= kClamp (false for NaN)
+                    if (bias != nullptr && ok[u])
+                        sc += __ldg(bias + (size_t)__ldg(src_to_dst_slot + e) * heads + head);
+                    const float p = ok[u] ? mufu_exp(sc) : 0.f;
+                    const float inv = mufu_rcp(zr[u] + kEps);
+                    const float a = p * inv;
+                    const float dpre = (dgv - dr[u]) * inv * p;
+                    const float ds = inside ? dpre : 0.f;
+                    axpy8(av, a, gr[u]);
+                    axpy8(acc, ds, qr[u]);
+                }
             }
         }
         slot_sum(acc);
@@ -1104,7 +1195,7 @@ int forward_t(int64_t n, int heads, int head_dim, const void *q, const void *k, 
 #define NGT_FWD(HV, RV)                                                                          \
     if (sh.head_vecs == HV && sh.row_vecs == RV) {                                               \
         if constexpr (sizeof(T) == 2 && RV == 16)                                                \
-            spattn_fwd_r128<HV, 4><<<row_blocks + seg_blocks, kBlock, 0, st>>>(                  \
+            spattn_fwd_r128<HV, 4, 4, HV == 2><<<row_blocks + seg_blocks, kBlock, 0, st>>>(      \
                 (int)n, heads, scale_inv, (const __nv_bfloat16 *)q, (const __nv_bfloat16 *)k,    \
                 (const __nv_bfloat16 *)v, rowptr, col, bias, (__nv_bfloat16 *)out, z, ns,        \
                 (int)ns_len, row_blocks, sg);                                                    \
@@ -1160,7 +1251,7 @@ int backward_t(int64_t n, int heads, int head_dim, const void *q, const void *k,
             (int)n, heads, (const T *)out, (const T *)dout, delta);                               \
         NGT_CHECK_LAUNCH();                                                                       \
         if constexpr (sizeof(T) == 2 && RV == 16)                                                 \
-            spattn_bwd_r128<HV, 3, 2><<<2 * blocks_a + seg_blocks, kBlock, 0, st>>>(              \
+            spattn_bwd_r128<HV, HV == 2 ? 2 : 3, 2, 4, HV == 2><<<2 * blocks_a + seg_blocks, kBlock, 0, st>>>( \
                 (int)n, heads, scale_inv, blocks_a, (const __nv_bfloat16 *)q,                     \
                 (const __nv_bfloat16 *)k, (const __nv_bfloat16 *)v, (const __nv_bfloat16 *)dout,  \
                 z, delta, dst_rowptr, dst_src, src_rowptr, src_dst, s2d, bias,                    \

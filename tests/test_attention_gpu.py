@@ -83,6 +83,25 @@ def test_against_oracle(cuda, H, D, dtype):
     assert rel_err(dv, rdv) < tol
 
 
+@pytest.mark.parametrize("H,D", [(8, 16), (4, 32), (16, 8)])
+def test_bf16_with_edge_bias(cuda, H, D):
+    # the bf16 kernels for 128-element rows with an additive edge bias and its gradient, on a
+    # graph with a heavy row (segments), against the fp64 oracle
+    q, k, v, dout, ei = _random_case(300, 4000, H, D, seed=7 + H, scale=1.3, heavy=600)
+    q, k, v = (t.to(torch.bfloat16) for t in (q, k, v))
+    bias = torch.randn(1, H, 300, 300, generator=torch.Generator().manual_seed(3)) * 0.7   # [1, H, s, s]
+    x, ns, (dq, dk, dv, db) = _ours(q, k, v, ei, bias=bias, dout=dout)
+    rx, rns, _, _ = oatt.sparse_attention_forward(q.double(), k.double(), v.double(), ei, bias.double())
+    rdq, rdk, rdv, rdb = oatt.sparse_attention_backward(q.double(), k.double(), v.double(), ei,
+                                                        dout.to(torch.bfloat16).double(), bias.double())
+    assert rel_err(x, rx) < BF16_TOL
+    assert rel_err(ns, rns) < BF16_TOL
+    assert rel_err(dq, rdq) < BF16_TOL
+    assert rel_err(dk, rdk) < BF16_TOL
+    assert rel_err(dv, rdv) < BF16_TOL
+    assert rel_err(db, rdb) < BF16_TOL
+
+
 def test_rows_without_edges_and_short_node_scores(cuda):
     q, k, v, dout, _ = _random_case(40, 1, 8, 16, seed=5)
     ei = torch.tensor([[3, 4, 5, 3], [1, 1, 7, 7]])
