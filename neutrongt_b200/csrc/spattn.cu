@@ -623,7 +623,7 @@ __device__ __forceinline__ void store_rec(float *rec, const float2 (&acc)[4]) {
 
 // PAIRS (HEAD_VECS = 2): the two lanes of a head finish different edges of an edge pair and
 // exchange the exponentials (as spattn_bwd_r128 below); the same results as without pairs.
-template <int HEAD_VECS, int UNROLL, int MIN_BLOCKS = 4, bool PAIRS = false>
+template <int HEAD_VECS, int UNROLL, int MIN_BLOCKS = 4, bool PAIRS = false, bool PF = false>
 __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
     spattn_fwd_r128(int n, int heads, float scale_inv, const __nv_bfloat16 *__restrict__ q,
                     const __nv_bfloat16 *__restrict__ k, const __nv_bfloat16 *__restrict__ v,
@@ -656,6 +656,16 @@ __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
     const uint4 qw = ld16(reinterpret_cast<const uint4 *>(q) + (size_t)row * RV + gl);
     float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
     float zs = 0.f;
+    // PF: the next batch's column indices are loaded while this batch computes, so only the row
+    // gathers wait on L2 at the top of a batch
+    int nxt[UNROLL];
+    if constexpr (PF) {
+#pragma unroll
+        for (int u = 0; u < UNROLL; u++) {
+            const int e = beg + sub + EPW * u;
+            nxt[u] = e < end ? __ldg(col + e) : 0;
+        }
+    }
     for (int e0 = beg; e0 < end; e0 += EPW * UNROLL) {
         int src[UNROLL];
         bool ok[UNROLL];
@@ -663,13 +673,21 @@ __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
         for (int u = 0; u < UNROLL; u++) {
             const int e = e0 + sub + EPW * u;
             ok[u] = e < end;
-            src[u] = ok[u] ? __ldg(col + e) : 0;
+            if constexpr (PF) src[u] = nxt[u];
+            else src[u] = ok[u] ? __ldg(col + e) : 0;
         }
         uint4 kr[UNROLL], vr[UNROLL];
 #pragma unroll
         for (int u = 0; u < UNROLL; u++) {
             kr[u] = ld16(K + (size_t)src[u] * RV);
             vr[u] = ld16(V + (size_t)src[u] * RV);
+        }
+        if constexpr (PF) {
+#pragma unroll
+            for (int u = 0; u < UNROLL; u++) {
+                const int e = e0 + EPW * UNROLL + sub + EPW * u;
+                nxt[u] = e < end ? __ldg(col + e) : 0;
+            }
         }
         if constexpr (PAIRS) {
             static_assert(HEAD_VECS == 2 && UNROLL % 2 == 0, "pairs of edges, two lanes per head");
@@ -729,7 +747,7 @@ __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
 // exponential and gradient arithmetic once for its own edge, and hands back the two scalars the
 // weighted sums need, instead of both lanes repeating that arithmetic for every edge.  The sums
 // are added in the same order as without pairs, so the results are identical.
-template <int HEAD_VECS, int UNROLL_A, int UNROLL_B, int MIN_BLOCKS = 4, bool PAIRS = false>
+template <int HEAD_VECS, int UNROLL_A, int UNROLL_B, int MIN_BLOCKS = 4, bool PAIRS = false, bool PF = false>
 __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
     spattn_bwd_r128(int n, int heads, float scale_inv, int blocks_a, const __nv_bfloat16 *__restrict__ q,
                     const __nv_bfloat16 *__restrict__ k, const __nv_bfloat16 *__restrict__ v,
@@ -785,6 +803,14 @@ __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
         const uint4 qw = ld16(Q + rbase), gw = ld16(DO + rbase);
         const float inv = 1.0f / (__ldg(z + (size_t)row * heads + head) + kEps);
         const float dl = __ldg(delta + (size_t)row * heads + head);
+        int nxt[UNROLL_A];
+        if constexpr (PF) {
+#pragma unroll
+            for (int u = 0; u < UNROLL_A; u++) {
+                const int e = beg + sub + EPW * u;
+                nxt[u] = e < end ? __ldg(dst_src + e) : 0;
+            }
+        }
         for (int e0 = beg; e0 < end; e0 += EPW * UNROLL_A) {
             int src[UNROLL_A];
             bool ok[UNROLL_A];
@@ -792,13 +818,21 @@ __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
             for (int u = 0; u < UNROLL_A; u++) {
                 const int e = e0 + sub + EPW * u;
                 ok[u] = e < end;
-                src[u] = ok[u] ? __ldg(dst_src + e) : 0;
+                if constexpr (PF) src[u] = nxt[u];
+                else src[u] = ok[u] ? __ldg(dst_src + e) : 0;
             }
             uint4 kr[UNROLL_A], vr[UNROLL_A];
 #pragma unroll
             for (int u = 0; u < UNROLL_A; u++) {
                 kr[u] = ld16(K + (size_t)src[u] * RV);
                 vr[u] = ld16(V + (size_t)src[u] * RV);
+            }
+            if constexpr (PF) {
+#pragma unroll
+                for (int u = 0; u < UNROLL_A; u++) {
+                    const int e = e0 + EPW * UNROLL_A + sub + EPW * u;
+                    nxt[u] = e < end ? __ldg(dst_src + e) : 0;
+                }
             }
             if constexpr (PAIRS) {
                 static_assert(HEAD_VECS == 2 && UNROLL_A % 2 == 0, "pairs of edges, two lanes per head");
@@ -851,6 +885,14 @@ __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
         // ---- dk, dv for source row `row` ----
         const uint4 kw = ld16(K + rbase), vw = ld16(V + rbase);
         float2 av[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+        int nxt[UNROLL_B];
+        if constexpr (PF) {
+#pragma unroll
+            for (int u = 0; u < UNROLL_B; u++) {
+                const int e = beg + sub + EPW * u;
+                nxt[u] = e < end ? __ldg(src_dst + e) : 0;
+            }
+        }
         for (int e0 = beg; e0 < end; e0 += EPW * UNROLL_B) {
             int dst[UNROLL_B];
             bool ok[UNROLL_B];
@@ -858,7 +900,8 @@ __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
             for (int u = 0; u < UNROLL_B; u++) {
                 const int e = e0 + sub + EPW * u;
                 ok[u] = e < end;
-                dst[u] = ok[u] ? __ldg(src_dst + e) : 0;
+                if constexpr (PF) dst[u] = nxt[u];
+                else dst[u] = ok[u] ? __ldg(src_dst + e) : 0;
             }
             uint4 qr[UNROLL_B], gr[UNROLL_B];
             float zr[UNROLL_B], dr[UNROLL_B];
@@ -876,6 +919,13 @@ __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
                 } else {
                     zr[u] = __ldg(z + (size_t)dst[u] * heads + head);
                     dr[u] = __ldg(delta + (size_t)dst[u] * heads + head);
+                }
+            }
+            if constexpr (PF) {
+#pragma unroll
+                for (int u = 0; u < UNROLL_B; u++) {
+                    const int e = e0 + EPW * UNROLL_B + sub + EPW * u;
+                    nxt[u] = e < end ? __ldg(src_dst + e) : 0;
                 }
             }
             if constexpr (PAIRS) {
@@ -1195,7 +1245,7 @@ int forward_t(int64_t n, int heads, int head_dim, const void *q, const void *k, 
 #define NGT_FWD(HV, RV)                                                                          \
     if (sh.head_vecs == HV && sh.row_vecs == RV) {                                               \
         if constexpr (sizeof(T) == 2 && RV == 16)                                                \
-            spattn_fwd_r128<HV, 4, 4, HV == 2><<<row_blocks + seg_blocks, kBlock, 0, st>>>(      \
+            spattn_fwd_r128<HV, HV == 2 ? 2 : 4, 4, HV == 2, HV == 2><<<row_blocks + seg_blocks, kBlock, 0, st>>>( \
                 (int)n, heads, scale_inv, (const __nv_bfloat16 *)q, (const __nv_bfloat16 *)k,    \
                 (const __nv_bfloat16 *)v, rowptr, col, bias, (__nv_bfloat16 *)out, z, ns,        \
                 (int)ns_len, row_blocks, sg);                                                    \
@@ -1251,7 +1301,7 @@ int backward_t(int64_t n, int heads, int head_dim, const void *q, const void *k,
             (int)n, heads, (const T *)out, (const T *)dout, delta);                               \
         NGT_CHECK_LAUNCH();                                                                       \
         if constexpr (sizeof(T) == 2 && RV == 16)                                                 \
-            spattn_bwd_r128<HV, HV == 2 ? 2 : 3, 2, 4, HV == 2><<<2 * blocks_a + seg_blocks, kBlock, 0, st>>>( \
+            spattn_bwd_r128<HV, HV == 2 ? 2 : 3, 2, 4, HV == 2, HV == 2><<<2 * blocks_a + seg_blocks, kBlock, 0, st>>>( \
                 (int)n, heads, scale_inv, blocks_a, (const __nv_bfloat16 *)q,                     \
                 (const __nv_bfloat16 *)k, (const __nv_bfloat16 *)v, (const __nv_bfloat16 *)dout,  \
                 z, delta, dst_rowptr, dst_src, src_rowptr, src_dst, s2d, bias,                    \
