@@ -71,7 +71,7 @@ def parse_args():
     p.add_argument("--skip-layer", action="store_true")
     p.add_argument("--skip-large-ppr", action="store_true",
                    help="skip the PPR runs on the 232,965- and 2,449,029-node graphs")
-    p.add_argument("--profile-case", choices=["spattn", "gemm", "push"], default=None,
+    p.add_argument("--profile-case", choices=["spattn", "gemm", "push", "dense"], default=None,
                    help="run one small workload for an ncu capture (no JSON line): the 65,536-token window "
                         "fwd+bwd x3 with L2 flushes, the bf16 Linear 32768x768->768 fwd+bwd x3, or push PPR "
                         "(eps 1e-5) on a 40,000-node graph x2")
@@ -1004,6 +1004,16 @@ def profile_case(case):
             flush.fill_(i)
             buf.forward()
             buf.backward(dout)
+    elif case == "dense":
+        import math as _m
+        from neutrongt_b200.dense_attention import dense_attention
+        g = torch.Generator(device=dev).manual_seed(0)
+        S, H, D = 32768, 4, 24   # the GPH_Large per-rank dense window (bench_dense at N = 1)
+        q, k, v, dy = (torch.randn(S, H, D, generator=g, device=dev).to(torch.bfloat16) * 0.5 for _ in range(4))
+        qd, kd, vd = (t.requires_grad_(True) for t in (q, k, v))
+        for _ in range(3):
+            x, _ = dense_attention(qd, kd, vd, _m.sqrt(D), score_heads=32, check_status=False)
+            x.backward(dy)
     elif case == "gemm":
         from neutrongt_b200.layers import Linear
         x = torch.randn(32768, 768, device=dev).to(torch.bfloat16).requires_grad_(True)

@@ -171,8 +171,9 @@ __device__ __forceinline__ void exp2_poly(float x0, float x1, float &y0, float &
 // into the row's next four 16-byte chunks of the P and |S| tiles (chunk stride 128 bytes); one pair
 // in four takes the polynomial exp2, the rest the MUFU unit.  |s| is the packed bf16 pair with its
 // sign bits cleared (bf16 rounding is symmetric, so |bf16(s)| = bf16(|s|)).
+template <bool PT>
 __device__ __forceinline__ void chunk_fast(const float (&v)[32], f32x2 sl2x2, f32x2 nmu, f32x2 &l2, uint8_t *prow,
-                                           uint8_t *arow) {
+                                           uint8_t *arow, uint32_t (&pt)[16]) {
 #pragma unroll
     for (int c = 0; c < 4; c++) {
         uint32_t pw[4], aw[4];
@@ -191,7 +192,12 @@ __device__ __forceinline__ void chunk_fast(const float (&v)[32], f32x2 sl2x2, f3
             pw[e / 2] = tc::pack_bf16(p0, p1);
             aw[e / 2] = tc::pack_bf16(v[c * 8 + e], v[c * 8 + e + 1]) & 0x7FFF7FFFu;
         }
-        st16(prow + c * 128, pw[0], pw[1], pw[2], pw[3]);
+        if constexpr (PT) {
+#pragma unroll
+            for (int i = 0; i < 4; i++) pt[c * 4 + i] = pw[i];
+        } else {
+            st16(prow + c * 128, pw[0], pw[1], pw[2], pw[3]);
+        }
         st16(arow + c * 128, aw[0], aw[1], aw[2], aw[3]);
     }
 }
@@ -208,14 +214,15 @@ __device__ __forceinline__ void chunk_fast(const float (&v)[32], f32x2 sl2x2, f3
 // The running max is raised only when a row's max grows by more than 2^8 (P <= 256 in between,
 // exact after the final 1 / l), so O is rarely rescaled.
 // ------------------------------------------------------------------------------------
+template <bool PT>
 struct FwdL {
-    static constexpr int NKV = 2;                         // K/V stages (128-key blocks)
+    static constexpr int NKV = PT ? 3 : 2;                // K/V stages (128-key blocks)
     static constexpr int SUB = 64;                        // keys per sub-block
     static constexpr uint32_t kQ = 0;                     // 2 query tiles
     static constexpr uint32_t kKV = kQ + 2 * kTileBytes;  // NKV x {K, V}
     static constexpr uint32_t kP = kKV + NKV * 2 * kTileBytes;   // 2 tiles x P [128 q x 64 keys] bf16
     static constexpr uint32_t kPBytes = TILE * SUB * 2;
-    static constexpr uint32_t kAbs = kP + 2 * kPBytes;           // 2 tiles x 2 blocks x |S| [128 q x 128 keys]
+    static constexpr uint32_t kAbs = kP + (PT ? 0 : 2 * kPBytes);   // 2 tiles x 2 blocks x |S| [128 q x 128 keys]
     static constexpr uint32_t kAbsBytes = TILE * TILE * 2;
     static constexpr uint32_t kOnes = kAbs + 4 * kAbsBytes;      // 16 x 128 ones
     static constexpr int kOnesRows = 16;
@@ -236,20 +243,28 @@ struct FwdL {
     static constexpr uint32_t kAbort = kSlot + 4;
     static constexpr uint32_t kBytes = kAbort + 4;
 };
-static_assert(FwdL::kKV % 1024 == 0 && FwdL::kP % 1024 == 0 && FwdL::kAbs % 1024 == 0, "1 KiB alignment");
-static_assert(FwdL::kBytes <= 232448, "shared memory");
+static_assert(FwdL<false>::kKV % 1024 == 0 && FwdL<false>::kP % 1024 == 0 && FwdL<false>::kAbs % 1024 == 0,
+              "1 KiB alignment");
+static_assert(FwdL<true>::kAbs % 1024 == 0 && FwdL<true>::kOnes % 1024 == 0, "1 KiB alignment");
+static_assert(FwdL<false>::kBytes <= 232448 && FwdL<true>::kBytes <= 232448, "shared memory");
 
 // (row r, 16-byte chunk c) of a [128 x 64] bf16 tile: 8 chunks per row
 __device__ __forceinline__ uint32_t sub_off(int r, int c) {
     return (uint32_t)((r >> 3) * 1024 + c * 128 + (r & 7) * 16);
 }
 
+// PT: P_t(j) goes back into tensor memory over the 32 first columns of its S buffer (bf16 pairs)
+// and O_t += P_t V reads it from there as the A operand, so a warpgroup writes P_t(j) as soon as
+// S_t(j) is in (the MMAs of buffer j % 2 run in issue order: S(j) completing means PV(j - 2),
+// the last reader of that buffer, and the column sums of block kb - 2 have completed), and waits
+// for O_t += P_t(j - 1) V only before it may rescale O_t.  Without PT, P_t is staged in shared memory.
+template <bool PT>
 __global__ void __launch_bounds__(kThreads, 1)
     dense_fwd_tma_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v, int s, int H, int D, float scale,
                          float score_scale, float drop_p, uint32_t seed, __nv_bfloat16 *__restrict__ out,
                          float *__restrict__ lse, float *__restrict__ node_scores, int *__restrict__ status) {
-    using L = FwdL;
+    using L = FwdL<PT>;
     constexpr int SUB = L::SUB;
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::kBars);
@@ -364,9 +379,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc::fence_after_sync();
             if (leader) {   // first what the warpgroup waits for, then what is needed later
 #pragma unroll
-                for (int kk = 0; kk < SUB / 16; kk++)   // O_t += P_t V_j   (V read MN-major)
-                    tc::mma_bf16(tO, tc::smem_desc(ap + kk * 256, 128, 1024), mnmajor_tma(aV + (u * SUB + kk * 16) * 16),
-                                 idesc_pv, (j > 0 || kk > 0));
+                for (int kk = 0; kk < SUB / 16; kk++) {   // O_t += P_t V_j   (V read MN-major)
+                    if constexpr (PT)
+                        tc::mma_bf16_ts(tO, tS + u * SUB + kk * 8, mnmajor_tma(aV + (u * SUB + kk * 16) * 16), idesc_pv,
+                                        (j > 0 || kk > 0));
+                    else
+                        tc::mma_bf16(tO, tc::smem_desc(ap + kk * 256, 128, 1024),
+                                     mnmajor_tma(aV + (u * SUB + kk * 16) * 16), idesc_pv, (j > 0 || kk > 0));
+                }
                 tc::commit(&bars[L::OV + t]);
                 if (last_of_block) tc::commit(&bars[L::KVE + st]);   // every MMA reading this stage issued
             }
@@ -461,19 +481,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                 l2 = fmul2(l2, pk(alpha, alpha));
             }
             // O_t += P_t(j - 1) V done: P_t free, O_t current, and (issued before it) the column sums
-            // of block kb - 2, the last reader of this |S| buffer
-            if (j > 0 && !warp_wait(&bars[L::OV + t], (j - 1) & 1, ab)) {
-                ok = false;
-                break;
+            // of block kb - 2, the last reader of this |S| buffer (with PT, S_t(j) completing covers
+            // both buffers, and this wait moves below, before the rescale of O_t)
+            if constexpr (!PT) {
+                if (j > 0 && !warp_wait(&bars[L::OV + t], (j - 1) & 1, ab)) {
+                    ok = false;
+                    break;
+                }
+                tc::fence_after_sync();
             }
-            tc::fence_after_sync();
             const f32x2 nmu = pk(-mu, -mu);
+            uint32_t pwords[16];   // with PT: 32 P values of this row as bf16 pairs, for TMEM
             if (full && !thr) {   // every key real, no dropout: the common case
 #pragma unroll 1
                 for (int c4 = 0; c4 < SUB / 32; c4++) {
                     float v[32];
                     tc::ld32(tS + c4 * 32, v);
-                    chunk_fast(v, sl2x2, nmu, l2, pt + sub_off(r, c4 * 4), at + sq_off(r, u * (SUB / 8) + c4 * 4));
+                    chunk_fast<PT>(v, sl2x2, nmu, l2, pt + sub_off(r, c4 * 4), at + sq_off(r, u * (SUB / 8) + c4 * 4),
+                                   pwords);
+                    if constexpr (PT) tc::st16_nowait(tS + c4 * 16, pwords);   // S columns already read
                 }
             } else {
 #pragma unroll 1
@@ -499,11 +525,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                             pw[e / 2] = tc::pack_bf16(pv[0], pv[1]);
                             aw[e / 2] = tc::pack_bf16(av[0], av[1]) & 0x7FFF7FFFu;
                         }
-                        st16(pt + sub_off(r, c4 * 4 + c), pw[0], pw[1], pw[2], pw[3]);
+                        if constexpr (PT) {
+#pragma unroll
+                            for (int i = 0; i < 4; i++) pwords[c * 4 + i] = pw[i];
+                        } else {
+                            st16(pt + sub_off(r, c4 * 4 + c), pw[0], pw[1], pw[2], pw[3]);
+                        }
                         st16(at + sq_off(r, u * (SUB / 8) + c4 * 4 + c), aw[0], aw[1], aw[2], aw[3]);
                     }
+                    if constexpr (PT) tc::st16_nowait(tS + c4 * 16, pwords);
                     l2 = fadd2(l2, pk(lsum, 0.f));
                 }
+            }
+            if constexpr (PT) {
+                tc::wait_st();   // P_t(j) is in TMEM
+                if (j > 0 && !warp_wait(&bars[L::OV + t], (j - 1) & 1, ab)) {
+                    ok = false;
+                    break;
+                }
+                tc::fence_after_sync();
             }
             if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {   // O_t *= 2^(mu_old - mu_new)
                 float o[32];
@@ -1001,23 +1041,32 @@ int dq_map(CUtensorMap *m, float *base, int64_t s, int H, int D) {
 }  // namespace
 }  // namespace dtma
 
-int dense_fwd_tma(int64_t s, int heads, int head_dim, float scale, float score_scale, float drop_p, uint32_t seed,
-                  const void *q, const void *k, const void *v, void *out, float *lse, float *ns, int *status,
-                  cudaStream_t st) {
+template <bool PT>
+int dense_fwd_tma_t(int64_t s, int heads, int head_dim, float scale, float score_scale, float drop_p, uint32_t seed,
+                    const void *q, const void *k, const void *v, void *out, float *lse, float *ns, int *status,
+                    cudaStream_t st) {
     using namespace dtma;
     CUtensorMap mq, mk, mv;
     int rc;
     if ((rc = rows_map(&mq, q, s, heads, head_dim)) != NGT_OK) return rc;
     if ((rc = rows_map(&mk, k, s, heads, head_dim)) != NGT_OK) return rc;
     if ((rc = rows_map(&mv, v, s, heads, head_dim)) != NGT_OK) return rc;
-    if (cudaFuncSetAttribute(dense_fwd_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)FwdL::kBytes) !=
-        cudaSuccess)
+    if (cudaFuncSetAttribute(dense_fwd_tma_kernel<PT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)FwdL<PT>::kBytes) != cudaSuccess)
         return NGT_ERR_CUDA;
     dim3 grid((unsigned)((s + 2 * TILE - 1) / (2 * TILE)), (unsigned)heads);
-    dense_fwd_tma_kernel<<<grid, kThreads, FwdL::kBytes, st>>>(mq, mk, mv, (int)s, heads, head_dim, scale, score_scale,
-                                                               drop_p, seed, (__nv_bfloat16 *)out, lse, ns, status);
+    dense_fwd_tma_kernel<PT><<<grid, kThreads, FwdL<PT>::kBytes, st>>>(mq, mk, mv, (int)s, heads, head_dim, scale,
+                                                                   score_scale, drop_p, seed, (__nv_bfloat16 *)out,
+                                                                   lse, ns, status);
     NGT_CHECK_LAUNCH();
     return NGT_OK;
+}
+
+int dense_fwd_tma(int64_t s, int heads, int head_dim, float scale, float score_scale, float drop_p, uint32_t seed,
+                  const void *q, const void *k, const void *v, void *out, float *lse, float *ns, int *status,
+                  cudaStream_t st) {
+    return dense_fwd_tma_t<true>(s, heads, head_dim, scale, score_scale, drop_p, seed, q, k, v, out, lse, ns, status,
+                                 st);
 }
 
 int dense_bwd_tma(int64_t s, int heads, int head_dim, float scale, float drop_p, uint32_t seed, const void *q,
