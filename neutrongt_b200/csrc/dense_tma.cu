@@ -445,23 +445,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             const bool full = k0 + SUB <= s;
             float mraw = -INFINITY;
             if (full) {
-#pragma unroll 1
-                for (int c4 = 0; c4 < SUB / 32; c4++) {
-                    float v[32];
-                    tc::ld32(tS + c4 * 32, v);
-                    float a = max3(v[0], v[1], v[2]), b = max3(v[3], v[4], v[5]), c = max3(v[6], v[7], v[8]),
-                          d = max3(v[9], v[10], v[11]);
+                static_assert(SUB == 64, "one paired load covers the sub-block");
+                float v[32], w[32];
+                tc::ld32_pair(tS, v, tS + 32, w);
+                float a = max3(v[0], v[1], v[2]), b = max3(v[3], v[4], v[5]), c = max3(w[0], w[1], w[2]),
+                      d = max3(w[3], w[4], w[5]);
 #pragma unroll
-                    for (int i = 12; i < 28; i += 8) {
-                        a = max3(a, v[i], v[i + 1]);
-                        b = max3(b, v[i + 2], v[i + 3]);
-                        c = max3(c, v[i + 4], v[i + 5]);
-                        d = max3(d, v[i + 6], v[i + 7]);
-                    }
-                    a = max3(a, v[28], v[29]);
-                    b = max3(b, v[30], v[31]);
-                    mraw = max3(mraw, max3(a, b, c), d);
+                for (int i = 6; i < 30; i += 4) {
+                    a = max3(a, v[i], v[i + 1]);
+                    b = max3(b, v[i + 2], v[i + 3]);
+                    c = max3(c, w[i], w[i + 1]);
+                    d = max3(d, w[i + 2], w[i + 3]);
                 }
+                a = max3(a, v[30], v[31]);
+                c = max3(c, w[30], w[31]);
+                mraw = max3(max3(a, b, c), d, mraw);
             } else {
 #pragma unroll 1
                 for (int c4 = 0; c4 < SUB / 32; c4++) {
@@ -871,8 +869,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
                 for (int c4 = 0; c4 < KH / 32; c4++) {
                     float sv[32], dp[32];
-                    tc::ld32(tS + c4 * 32, sv);
-                    tc::ld32(tDP + c4 * 32, dp);
+                    tc::ld32_pair(tS + c4 * 32, sv, tDP + c4 * 32, dp);
                     if (c4 == KH / 32 - 1) release_s(b);   // the next S_b, dP_b may overwrite the buffer
                     const int chunk = b * (KH / 8) + c4 * 4;
                     bwd_chunk_fast(sv, dp, sl2x2, nl2, nd2, pt + sq_off(r, chunk), dst + sq_off(r, chunk));
@@ -881,8 +878,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
                 for (int c4 = 0; c4 < KH / 32; c4++) {
                     float sv[32], dp[32];
-                    tc::ld32(tS + c4 * 32, sv);
-                    tc::ld32(tDP + c4 * 32, dp);
+                    tc::ld32_pair(tS + c4 * 32, sv, tDP + c4 * 32, dp);
                     if (c4 == KH / 32 - 1) release_s(b);
 #pragma unroll
                     for (int c = 0; c < 4; c++) {

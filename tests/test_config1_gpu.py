@@ -1,4 +1,4 @@
-"""BASELINE config 1 end to end: the reference's CPU-runnable case.
+"""The reference's CPU-runnable case, end to end (the smallest benchmark configuration).
 
 Synthetic power-law graph (10,000 nodes, mean degree 8), APPNP PPR (alpha 0.15, 20 iterations,
 top-8) over every seed, 16 contiguous random windows, and one training epoch of GPH_Slim
