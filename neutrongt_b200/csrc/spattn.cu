@@ -19,8 +19,9 @@
 // Lane layout of the vector path: a row of H*D elements is ROW_VECS 16-byte vectors.  A
 // group of G = min(ROW_VECS, 32) lanes cooperates on one edge (lane gl owns vectors
 // gl + G*t), so a warp keeps 32/G edges of the same row in flight, times UNROLL.  A head
-// spans HEAD_VECS consecutive lanes; its dot product is reduced with xor shuffles.  bf16 rows of
-// 128 elements (the 65,536-token workload) run separate packed-math kernels (spattn_*_r128).
+// spans HEAD_VECS consecutive lanes; its dot product is reduced with xor shuffles.  Rows of 128
+// elements run separate packed-math kernels: spattn_*_r128 (bf16, the 65,536-token workload) and
+// spattn_*_f128 (fp32, the GT model).
 #include <mutex>
 
 #include "common.cuh"
@@ -993,6 +994,269 @@ __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
     }
 }
 
+// ------------------------------------------------------------------------------------
+// fp32 rows of 128 elements (32 vectors of 16 B): packed-math kernels
+// ------------------------------------------------------------------------------------
+// The GT model's row shape (fp32, H * D = 128; D = 4, 8, 16 or 32).  A warp holds one row, one
+// 16-byte vector of four floats per lane, one edge per warp instruction, UNROLL edges in flight,
+// and the next batch's column indices loaded ahead.  Dot products and weighted sums run as packed
+// f32x2 FMAs, exponentials and the source role's reciprocal on the MUFU unit (`ex2.approx`, relative
+// error ~2^-22, inside the fp32 parity tolerance).  Segment records are laid out as in the general
+// kernels, so the same finish kernels serve both.
+namespace f128 {
+constexpr int RV = 32;
+
+__device__ __forceinline__ float2 lo(const uint4 &x) { return make_float2(__uint_as_float(x.x), __uint_as_float(x.y)); }
+__device__ __forceinline__ float2 hi(const uint4 &x) { return make_float2(__uint_as_float(x.z), __uint_as_float(x.w)); }
+
+// sum of the four products of a gathered vector and a row-constant one (pairs, then the halves)
+__device__ __forceinline__ float dot4(const uint4 &a, float2 b0, float2 b1) {
+    const float2 d = __ffma2_rn(hi(a), b1, __fmul2_rn(lo(a), b0));
+    return d.x + d.y;
+}
+
+__device__ __forceinline__ void axpy4(float2 &a0, float2 &a1, float s, const uint4 &x) {
+    const float2 ss = make_float2(s, s);
+    a0 = __ffma2_rn(ss, lo(x), a0);
+    a1 = __ffma2_rn(ss, hi(x), a1);
+}
+}  // namespace f128
+
+template <int HEAD_VECS, int UNROLL, int MIN_BLOCKS = 4>
+__global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
+    spattn_fwd_f128(int n, int heads, float scale_inv, const float *__restrict__ q, const float *__restrict__ k,
+                    const float *__restrict__ v, const int *__restrict__ rowptr, const int *__restrict__ col,
+                    const float *__restrict__ bias, float *__restrict__ out, float *__restrict__ z,
+                    float *__restrict__ node_scores, int ns_len, int row_blocks, SegView sg) {
+    using namespace f128;
+    const int lane = lane_id();
+    const int wid = threadIdx.x >> 5;
+    int row, beg, end, seg = -1;
+    if ((int)blockIdx.x < row_blocks) {
+        row = blockIdx.x * kWarpsPerBlock + wid;
+        if (row >= n) return;
+        if (sg.first != nullptr && __ldg(sg.first + row) >= 0) return;   // done by its segments
+        beg = __ldg(rowptr + row);
+        end = __ldg(rowptr + row + 1);
+    } else {
+        seg = ((int)blockIdx.x - row_blocks) * kWarpsPerBlock + wid;
+        if (seg >= sg.nseg) return;
+        row = __ldg(sg.row + seg);
+        beg = __ldg(rowptr + row) + (seg - __ldg(sg.first + row)) * sg.edges;
+        end = min(__ldg(rowptr + row + 1), beg + sg.edges);
+    }
+    const int head = lane / HEAD_VECS;
+    const uint4 *K = reinterpret_cast<const uint4 *>(k) + lane;
+    const uint4 *V = reinterpret_cast<const uint4 *>(v) + lane;
+    const uint4 qv = r128::ld16(reinterpret_cast<const uint4 *>(q) + (size_t)row * RV + lane);
+    const float2 q0 = lo(qv), q1 = hi(qv);
+    float2 a0 = make_float2(0.f, 0.f), a1 = make_float2(0.f, 0.f);
+    float zs = 0.f;
+    int nxt[UNROLL];
+#pragma unroll
+    for (int u = 0; u < UNROLL; u++) nxt[u] = beg + u < end ? __ldg(col + beg + u) : 0;
+    for (int e0 = beg; e0 < end; e0 += UNROLL) {
+        int src[UNROLL];
+        bool ok[UNROLL];
+#pragma unroll
+        for (int u = 0; u < UNROLL; u++) {
+            ok[u] = e0 + u < end;
+            src[u] = nxt[u];
+        }
+        uint4 kr[UNROLL], vr[UNROLL];
+#pragma unroll
+        for (int u = 0; u < UNROLL; u++) {
+            kr[u] = r128::ld16(K + (size_t)src[u] * RV);
+            vr[u] = r128::ld16(V + (size_t)src[u] * RV);
+        }
+#pragma unroll
+        for (int u = 0; u < UNROLL; u++) {
+            const int e = e0 + UNROLL + u;
+            nxt[u] = e < end ? __ldg(col + e) : 0;
+        }
+#pragma unroll
+        for (int u = 0; u < UNROLL; u++) {
+            const float d = head_reduce<HEAD_VECS>(dot4(kr[u], q0, q1));
+            float s = fminf(fmaxf(d * scale_inv, -kClamp), kClamp);
+            if (bias != nullptr && ok[u]) s += __ldg(bias + (size_t)(e0 + u) * heads + head);
+            const float p = ok[u] ? mufu_exp(s) : 0.f;
+            zs += p;
+            axpy4(a0, a1, p, vr[u]);
+        }
+    }
+    if (seg >= 0) {   // partial sums of the segment: acc in row layout, then Z per head
+        float *rec = sg.part + (size_t)seg * fwd_record(heads, RV * 4);
+        *reinterpret_cast<float4 *>(rec + lane * 4) = make_float4(a0.x, a0.y, a1.x, a1.y);
+        if ((lane % HEAD_VECS) == 0) rec[RV * 4 + head] = zs;
+        return;
+    }
+    const float inv = 1.0f / (zs + kEps);
+    *(reinterpret_cast<float4 *>(out) + (size_t)row * RV + lane) = make_float4(a0.x * inv, a0.y * inv, a1.x * inv, a1.y * inv);
+    if (z != nullptr && (lane % HEAD_VECS) == 0) z[(size_t)row * heads + head] = zs;
+    // node score: head mean of Z (lanes of one head hold equal values)
+    float hs = zs;
+#pragma unroll
+    for (int off = HEAD_VECS; off < 32; off <<= 1) hs += __shfl_xor_sync(0xffffffffu, hs, off);
+    if (lane == 0 && row < ns_len) node_scores[row] = hs / (float)heads;
+}
+
+template <int HEAD_VECS, int UNROLL_A, int UNROLL_B, int MIN_BLOCKS = 4>
+__global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
+    spattn_bwd_f128(int n, int heads, float scale_inv, int blocks_a, const float *__restrict__ q,
+                    const float *__restrict__ k, const float *__restrict__ v, const float *__restrict__ dout,
+                    const float *__restrict__ z, const float *__restrict__ delta, const int *__restrict__ dst_rowptr,
+                    const int *__restrict__ dst_src, const int *__restrict__ src_rowptr,
+                    const int *__restrict__ src_dst, const int *__restrict__ src_to_dst_slot,
+                    const float *__restrict__ bias, float *__restrict__ dq, float *__restrict__ dk,
+                    float *__restrict__ dv, float *__restrict__ dbias, SegView sgd, SegView sgs) {
+    using namespace f128;
+    const int lane = lane_id();
+    const int wid = threadIdx.x >> 5;
+    const int b = blockIdx.x;
+    // blocks: [0, blocks_a) destination rows, [blocks_a, 2 blocks_a) source rows, then the
+    // destination-view segments and the source-view segments of heavy rows
+    const int seg_blocks_d = (sgd.nseg + kWarpsPerBlock - 1) / kWarpsPerBlock;
+    bool role_a;
+    int row, beg, end, seg = -1;
+    if (b < 2 * blocks_a) {
+        role_a = b < blocks_a;
+        row = (role_a ? b : b - blocks_a) * kWarpsPerBlock + wid;
+        if (row >= n) return;
+        const int32_t *first = role_a ? sgd.first : sgs.first;
+        if (first != nullptr && __ldg(first + row) >= 0) return;   // done by its segments
+        const int *rp = role_a ? dst_rowptr : src_rowptr;
+        beg = __ldg(rp + row);
+        end = __ldg(rp + row + 1);
+    } else {
+        const int sb = b - 2 * blocks_a;
+        role_a = sb < seg_blocks_d;
+        seg = (role_a ? sb : sb - seg_blocks_d) * kWarpsPerBlock + wid;
+        if (seg >= (role_a ? sgd.nseg : sgs.nseg)) return;
+        row = __ldg((role_a ? sgd.row : sgs.row) + seg);
+        const int *rp = role_a ? dst_rowptr : src_rowptr;
+        const int edges = role_a ? sgd.edges : sgs.edges;
+        beg = __ldg(rp + row) + (seg - __ldg((role_a ? sgd.first : sgs.first) + row)) * edges;
+        end = min(__ldg(rp + row + 1), beg + edges);
+    }
+    const uint4 *Q = reinterpret_cast<const uint4 *>(q) + lane;
+    const uint4 *K = reinterpret_cast<const uint4 *>(k) + lane;
+    const uint4 *V = reinterpret_cast<const uint4 *>(v) + lane;
+    const uint4 *DO = reinterpret_cast<const uint4 *>(dout) + lane;
+    const size_t rbase = (size_t)row * RV;
+    const int head = lane / HEAD_VECS;
+    float2 a0 = make_float2(0.f, 0.f), a1 = make_float2(0.f, 0.f);
+
+    if (role_a) {
+        // ---- dq for destination row `row` ----
+        const uint4 qv = r128::ld16(Q + rbase), gv = r128::ld16(DO + rbase);
+        const float2 q0 = lo(qv), q1 = hi(qv), g0 = lo(gv), g1 = hi(gv);
+        const float inv = 1.0f / (__ldg(z + (size_t)row * heads + head) + kEps);
+        const float dl = __ldg(delta + (size_t)row * heads + head);
+        int nxt[UNROLL_A];
+#pragma unroll
+        for (int u = 0; u < UNROLL_A; u++) nxt[u] = beg + u < end ? __ldg(dst_src + beg + u) : 0;
+        for (int e0 = beg; e0 < end; e0 += UNROLL_A) {
+            int src[UNROLL_A];
+            bool ok[UNROLL_A];
+#pragma unroll
+            for (int u = 0; u < UNROLL_A; u++) {
+                ok[u] = e0 + u < end;
+                src[u] = nxt[u];
+            }
+            uint4 kr[UNROLL_A], vr[UNROLL_A];
+#pragma unroll
+            for (int u = 0; u < UNROLL_A; u++) {
+                kr[u] = r128::ld16(K + (size_t)src[u] * RV);
+                vr[u] = r128::ld16(V + (size_t)src[u] * RV);
+            }
+#pragma unroll
+            for (int u = 0; u < UNROLL_A; u++) {
+                const int e = e0 + UNROLL_A + u;
+                nxt[u] = e < end ? __ldg(dst_src + e) : 0;
+            }
+#pragma unroll
+            for (int u = 0; u < UNROLL_A; u++) {
+                const int e = e0 + u;
+                const float dqk = head_reduce<HEAD_VECS>(dot4(kr[u], q0, q1));
+                const float dgv = head_reduce<HEAD_VECS>(dot4(vr[u], g0, g1));
+                const float s = dqk * scale_inv;
+                float sc = fminf(fmaxf(s, -kClamp), kClamp);
+                const bool inside = sc == s;   // -kClamp <= s <= kClamp (false for NaN)
+                if (bias != nullptr && ok[u]) sc += __ldg(bias + (size_t)e * heads + head);
+                const float p = mufu_exp(sc);
+                const float dpre = (dgv - dl) * inv * p;
+                const float ds = (ok[u] && inside) ? dpre : 0.f;
+                if (dbias != nullptr && ok[u] && (lane % HEAD_VECS) == 0) dbias[(size_t)e * heads + head] = dpre;
+                axpy4(a0, a1, ds, kr[u]);
+            }
+        }
+        if (seg >= 0) {   // segment partial of dq (before the 1/sqrt(D) scale)
+            *reinterpret_cast<float4 *>(sgd.part + (size_t)seg * RV * 4 + lane * 4) = make_float4(a0.x, a0.y, a1.x, a1.y);
+            return;
+        }
+        *(reinterpret_cast<float4 *>(dq) + rbase + lane) =
+            make_float4(a0.x * scale_inv, a0.y * scale_inv, a1.x * scale_inv, a1.y * scale_inv);
+    } else {
+        // ---- dk, dv for source row `row` ----
+        const uint4 kv = r128::ld16(K + rbase), vv = r128::ld16(V + rbase);
+        const float2 k0 = lo(kv), k1 = hi(kv), v0 = lo(vv), v1 = hi(vv);
+        float2 b0 = make_float2(0.f, 0.f), b1 = make_float2(0.f, 0.f);
+        int nxt[UNROLL_B];
+#pragma unroll
+        for (int u = 0; u < UNROLL_B; u++) nxt[u] = beg + u < end ? __ldg(src_dst + beg + u) : 0;
+        for (int e0 = beg; e0 < end; e0 += UNROLL_B) {
+            int dst[UNROLL_B];
+            bool ok[UNROLL_B];
+#pragma unroll
+            for (int u = 0; u < UNROLL_B; u++) {
+                ok[u] = e0 + u < end;
+                dst[u] = nxt[u];
+            }
+            uint4 qr[UNROLL_B], gr[UNROLL_B];
+            float zr[UNROLL_B], dr[UNROLL_B];
+#pragma unroll
+            for (int u = 0; u < UNROLL_B; u++) {
+                qr[u] = r128::ld16(Q + (size_t)dst[u] * RV);
+                gr[u] = r128::ld16(DO + (size_t)dst[u] * RV);
+                zr[u] = __ldg(z + (size_t)dst[u] * heads + head);
+                dr[u] = __ldg(delta + (size_t)dst[u] * heads + head);
+            }
+#pragma unroll
+            for (int u = 0; u < UNROLL_B; u++) {
+                const int e = e0 + UNROLL_B + u;
+                nxt[u] = e < end ? __ldg(src_dst + e) : 0;
+            }
+#pragma unroll
+            for (int u = 0; u < UNROLL_B; u++) {
+                const int e = e0 + u;
+                const float dqk = head_reduce<HEAD_VECS>(dot4(qr[u], k0, k1));
+                const float dgv = head_reduce<HEAD_VECS>(dot4(gr[u], v0, v1));
+                const float s = dqk * scale_inv;
+                float sc = fminf(fmaxf(s, -kClamp), kClamp);
+                const bool inside = sc == s;   // -kClamp <= s <= kClamp (false for NaN)
+                if (bias != nullptr && ok[u])
+                    sc += __ldg(bias + (size_t)__ldg(src_to_dst_slot + e) * heads + head);
+                const float p = ok[u] ? mufu_exp(sc) : 0.f;
+                const float inv = mufu_rcp(zr[u] + kEps);
+                const float a = p * inv;
+                const float dpre = (dgv - dr[u]) * inv * p;
+                const float ds = inside ? dpre : 0.f;
+                axpy4(b0, b1, a, gr[u]);    // dv
+                axpy4(a0, a1, ds, qr[u]);   // dk
+            }
+        }
+        if (seg >= 0) {   // segment partials of dk (unscaled) and dv
+            float *rec = sgs.part + (size_t)seg * 2 * RV * 4;
+            *reinterpret_cast<float4 *>(rec + lane * 4) = make_float4(a0.x, a0.y, a1.x, a1.y);
+            *reinterpret_cast<float4 *>(rec + RV * 4 + lane * 4) = make_float4(b0.x, b0.y, b1.x, b1.y);
+            return;
+        }
+        *(reinterpret_cast<float4 *>(dk) + rbase + lane) =
+            make_float4(a0.x * scale_inv, a0.y * scale_inv, a1.x * scale_inv, a1.y * scale_inv);
+        *(reinterpret_cast<float4 *>(dv) + rbase + lane) = make_float4(b0.x, b0.y, b1.x, b1.y);
+    }
+}
+
 // One warp per heavy row and view (the warp of its first segment): adds the segment partials in
 // segment order and writes dq (destination view) or dk, dv (source view).
 template <typename T, int HEAD_VECS, int ROW_VECS>
@@ -1249,6 +1513,10 @@ int forward_t(int64_t n, int heads, int head_dim, const void *q, const void *k, 
                 (int)n, heads, scale_inv, (const __nv_bfloat16 *)q, (const __nv_bfloat16 *)k,    \
                 (const __nv_bfloat16 *)v, rowptr, col, bias, (__nv_bfloat16 *)out, z, ns,        \
                 (int)ns_len, row_blocks, sg);                                                    \
+        else if constexpr (sizeof(T) == 4 && RV == 32)                                           \
+            spattn_fwd_f128<HV, 4><<<row_blocks + seg_blocks, kBlock, 0, st>>>(                  \
+                (int)n, heads, scale_inv, (const float *)q, (const float *)k, (const float *)v,  \
+                rowptr, col, bias, (float *)out, z, ns, (int)ns_len, row_blocks, sg);            \
         else                                                                                     \
             spattn_fwd_vec<T, HV, RV><<<row_blocks + seg_blocks, kBlock, 0, st>>>(               \
                 (int)n, heads, scale_inv, (const T *)q, (const T *)k, (const T *)v, rowptr, col, \
@@ -1306,6 +1574,11 @@ int backward_t(int64_t n, int heads, int head_dim, const void *q, const void *k,
                 (const __nv_bfloat16 *)k, (const __nv_bfloat16 *)v, (const __nv_bfloat16 *)dout,  \
                 z, delta, dst_rowptr, dst_src, src_rowptr, src_dst, s2d, bias,                    \
                 (__nv_bfloat16 *)dq, (__nv_bfloat16 *)dk, (__nv_bfloat16 *)dv, dbias, sgd, sgs);  \
+        else if constexpr (sizeof(T) == 4 && RV == 32)                                            \
+            spattn_bwd_f128<HV, 3, 2><<<2 * blocks_a + seg_blocks, kBlock, 0, st>>>(              \
+                (int)n, heads, scale_inv, blocks_a, (const float *)q, (const float *)k,           \
+                (const float *)v, (const float *)dout, z, delta, dst_rowptr, dst_src, src_rowptr, \
+                src_dst, s2d, bias, (float *)dq, (float *)dk, (float *)dv, dbias, sgd, sgs);      \
         else                                                                                      \
             spattn_bwd_vec<T, HV, RV><<<2 * blocks_a + seg_blocks, kBlock, 0, st>>>(              \
                 (int)n, heads, scale_inv, blocks_a, (const T *)q, (const T *)k, (const T *)v,     \

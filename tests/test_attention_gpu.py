@@ -62,6 +62,7 @@ def _random_case(s, E, H, D, seed, scale=1.0, heavy=0):
 SHAPES = [  # (H, D): vector path (GT, GPH_Slim, config 3), small heads, and the scalar path
     (8, 16), (8, 8), (4, 8), (8, 4), (32, 24), (8, 24), (2, 64), (1, 32),
     (16, 8), (4, 32),   # with (8, 16) and (2, 64): every head width of the 128-element bf16 rows
+    (32, 4),            # with (16, 8), (8, 16), (4, 32): every head width of the 128-element fp32 rows
 ]
 
 
