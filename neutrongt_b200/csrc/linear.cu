@@ -461,6 +461,29 @@ WgradPlan wgrad_plan(int64_t rows, int in_features, int out_features) {
     return p;
 }
 
+// Row ranges of the tensor-core weight grad: a multiple of 16 rows each, about one CTA per SM and
+// output tile, at least 64 rows, and at most 512 rows so that no range accumulates a long chain of
+// products in one fp32 accumulator (the ranges are summed in a fixed order afterwards).
+struct TcWgradPlan {
+    int64_t splits, rows_per_split;
+};
+
+TcWgradPlan tc_wgrad_plan(int64_t rows, int out_features) {
+    const int64_t m_tiles = (out_features + 127) / 128;
+    int64_t splits = sm_count() / m_tiles;
+    if (splits > rows / 64) splits = rows / 64;
+    if (splits < (rows + 511) / 512) splits = (rows + 511) / 512;
+    if (splits < 1) splits = 1;
+    TcWgradPlan p;
+    p.rows_per_split = ((rows + splits - 1) / splits + 15) / 16 * 16;
+    p.splits = (rows + p.rows_per_split - 1) / p.rows_per_split;
+    return p;
+}
+
+bool use_tc_wgrad(int64_t rows, int in_features, int out_features) {
+    return rows >= 64 && wgrad_tc_supported(in_features, out_features);
+}
+
 bool dims_ok(int64_t rows, int in_features, int out_features) {
     return rows >= 0 && rows < ((int64_t)1 << 40) && in_features > 0 && out_features > 0 && in_features % 4 == 0 &&
            out_features % 4 == 0;
@@ -502,7 +525,12 @@ extern "C" int ngt_linear_backward_input(int64_t rows, int in_features, int out_
 extern "C" int ngt_linear_weight_workspace_size(int64_t rows, int in_features, int out_features, size_t *bytes) {
     if (!bytes || !dims_ok(rows, in_features, out_features)) return NGT_ERR_INVALID_ARGUMENT;
     const WgradPlan p = wgrad_plan(rows, in_features, out_features);
-    *bytes = sizeof(float) * (size_t)p.chunks * ((size_t)in_features * out_features + out_features);
+    int64_t parts = p.chunks;
+    if (use_tc_wgrad(rows, in_features, out_features)) {
+        const TcWgradPlan t = tc_wgrad_plan(rows, out_features);
+        if (t.splits > parts) parts = t.splits;
+    }
+    *bytes = sizeof(float) * (size_t)parts * ((size_t)in_features * out_features + out_features);
     return NGT_OK;
 }
 
@@ -527,6 +555,14 @@ extern "C" int ngt_linear_backward_weight(int64_t rows, int in_features, int out
     if (workspace_bytes < need) return NGT_ERR_WORKSPACE;
     const WgradPlan p = wgrad_plan(rows, in_features, out_features);
     float *part = static_cast<float *>(workspace);
+    if (use_tc_wgrad(rows, in_features, out_features)) {   // split-TF32 tensor-core GEMM per row range
+        const TcWgradPlan t = tc_wgrad_plan(rows, out_features);
+        const int rc = launch_wgrad_tc(rows, in_features, out_features, x, dy, part, t.splits, t.rows_per_split, st);
+        if (rc != NGT_OK) return rc;
+        launch_chunk_sum((int)t.splits, nk, nk + out_features, part, dweight, dbias, st);
+        NGT_CHECK_LAUNCH();
+        return NGT_OK;
+    }
     wgrad_partial_kernel<<<dim3((unsigned)p.chunks, (unsigned)(p.n_tiles * p.k_tiles)), kWgThreads, 0, st>>>(
         rows, in_features, out_features, x, dy, part, p.rows_per_chunk, p.k_tiles);
     launch_chunk_sum((int)p.chunks, nk, nk + out_features, part, dweight, dbias, st);

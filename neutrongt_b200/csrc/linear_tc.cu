@@ -56,6 +56,10 @@ struct TcArgs {
     int ncta, np;      // columns per CTA, padded to the MMA N
     uint32_t tmem_cols;
     int trans;         // 0: B(n, k) = W[n * K + k];  1: B(n, k) = W[k * N + n]
+    int trans_a;       // 0: A(m, k) = A[m * K + k];  1: A(m, k) = A[k * M + m] (weight grad: A = dy)
+    int db;            // 1: also store the sums of A over the CTA's k range at C + M * N + m
+    int64_t k_per_cta; // reduction elements per blockIdx.z (a multiple of kKS unless it is all of K)
+    int64_t c_stride;  // floats between the outputs of consecutive blockIdx.z
     const float *bias;
     float *C;
 };
@@ -97,7 +101,10 @@ __device__ __forceinline__ void split_store(float4 v, uint8_t *hi, uint8_t *lo) 
 // Splits a landed slice into operand buffer `op`.  Raw rows are 64 bytes (item idx = row idx / 4,
 // chunk idx % 4, at idx * 16: consecutive threads read consecutive bytes); operand chunk (r, c)
 // goes to c * LBO + r * 16.
-__device__ __forceinline__ void split_slice(const TcArgs &p, const uint8_t *raw, uint8_t *op) {
+// With trans_a the raw A slice is row-major [16 k][128 m] and is transposed the same way (thread
+// tid always takes column m = tid % 128), and its four values per item are added into `asum` in a
+// fixed order (the bias gradient of the weight-grad GEMM).
+__device__ __forceinline__ void split_slice(const TcArgs &p, const uint8_t *raw, uint8_t *op, float &asum) {
     const int tid = threadIdx.x;
     const uint8_t *rb = raw + kARaw;
     const uint32_t lba = op_lbo(kM), lbb = op_lbo(p.np);
@@ -105,8 +112,17 @@ __device__ __forceinline__ void split_slice(const TcArgs &p, const uint8_t *raw,
 #pragma unroll
     for (int i = 0; i < 2; i++) {
         const int idx = tid + i * kThreads;
-        const uint32_t o = (uint32_t)(idx & 3) * lba + (uint32_t)(idx >> 2) * 16u;
-        split_store(*reinterpret_cast<const float4 *>(raw + idx * 16), a_hi + o, a_lo + o);
+        if (!p.trans_a) {
+            const uint32_t o = (uint32_t)(idx & 3) * lba + (uint32_t)(idx >> 2) * 16u;
+            split_store(*reinterpret_cast<const float4 *>(raw + idx * 16), a_hi + o, a_lo + o);
+        } else {   // raw row-major [16 k][128 m]: column m, rows 4c .. 4c + 3
+            const int m = idx % kM, c = idx / kM;
+            const float *colp = reinterpret_cast<const float *>(raw) + (4 * c) * kM + m;
+            const float4 v = make_float4(colp[0], colp[kM], colp[2 * kM], colp[3 * kM]);
+            asum += ((v.x + v.y) + v.z) + v.w;
+            const uint32_t o = (uint32_t)c * lba + (uint32_t)m * 16u;
+            split_store(v, a_hi + o, a_lo + o);
+        }
     }
     const int items = p.np * 4;
     for (int idx = tid; idx < items; idx += kThreads) {
@@ -133,24 +149,31 @@ __global__ void __launch_bounds__(kThreadsAll, 2)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t m0 = (int64_t)blockIdx.x * kM;
     const int n0 = blockIdx.y * p.ncta;
+    const int64_t kb = (int64_t)blockIdx.z * p.k_per_cta;            // this CTA's reduction range
+    const int64_t kc = p.K - kb < p.k_per_cta ? p.K - kb : p.k_per_cta;
+    float *const C = p.C + (int64_t)blockIdx.z * p.c_stride;
     const uint32_t rawb = raw_bytes(p.np), opb = op_bytes(p.np);
     uint8_t *ops = smem + STAGES * rawb;
     uint64_t *full = reinterpret_cast<uint64_t *>(ops + 2 * opb);   // [STAGES] slice landed (TMA bytes)
     uint64_t *done = full + STAGES;                                  // [2] MMAs of an operand buffer done
     uint64_t *ready = done + 2;                                      // [2] operand buffer split (256 arrivals)
     uint32_t *slot = reinterpret_cast<uint32_t *>(ready + 2);
-    const int ns = (p.K + kKS - 1) / kKS;
+    const int ns = (int)((kc + kKS - 1) / kKS);
     const bool producer = tid == kThreads;                           // warp 8, lane 0
 
     auto load = [&](int j) {   // slice j into stage j % STAGES
         uint8_t *raw = smem + (j % STAGES) * rawb;
         uint64_t *bar = &full[j % STAGES];
+        const int k = (int)(kb + (int64_t)j * kKS);
         tc::mbar_arrive_expect_tx(bar, rawb);
-        tc::tma_load_2d(raw, &tm_a, j * kKS, (int)m0, bar);
-        if (!p.trans)
-            tc::tma_load_2d(raw + kARaw, &tm_w, j * kKS, n0, bar);
+        if (!p.trans_a)
+            tc::tma_load_2d(raw, &tm_a, k, (int)m0, bar);
         else
-            tc::tma_load_2d(raw + kARaw, &tm_w, n0, j * kKS, bar);
+            tc::tma_load_2d(raw, &tm_a, (int)m0, k, bar);
+        if (!p.trans)
+            tc::tma_load_2d(raw + kARaw, &tm_w, k, n0, bar);
+        else
+            tc::tma_load_2d(raw + kARaw, &tm_w, n0, k, bar);
     };
 
     int loaded = 0, issued = 0;   // producer's counts
@@ -170,6 +193,7 @@ __global__ void __launch_bounds__(kThreadsAll, 2)
     const uint32_t tmem = *slot;
 
     bool ok = true;
+    float asum = 0.f;   // splitter thread's sum of A over its column (db only)
     if (producer) {
         // Slice s - 1's stage is free once every splitter arrived on ready for slice s - 1 (waited
         // below in the previous iteration), so slice s + STAGES - 1 can take it.
@@ -206,7 +230,7 @@ __global__ void __launch_bounds__(kThreadsAll, 2)
                 ok = false;
                 break;
             }
-            split_slice(p, smem + (s % STAGES) * rawb, ops + b * opb);
+            split_slice(p, smem + (s % STAGES) * rawb, ops + b * opb, asum);
             tc::fence_smem_for_async();
             tc::mbar_arrive(&ready[b]);
         }
@@ -242,6 +266,8 @@ __global__ void __launch_bounds__(kThreadsAll, 2)
     const int ngrp = (nv + 31) / 32;
     const int ldt = ngrp * 32 + 4;
     float *tile = reinterpret_cast<float *>(smem);
+    float *sdb = tile + kM * ldt;   // [kThreads] splitter sums of A (db only)
+    if (p.db && tid < kThreads) sdb[tid] = asum;
     const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
     for (int g = warp >> 2; warp < kThreads / 32 && g < ngrp; g += 2) {
         float v[32];
@@ -264,8 +290,10 @@ __global__ void __launch_bounds__(kThreadsAll, 2)
             o.z += bb.z;
             o.w += bb.w;
         }
-        *reinterpret_cast<float4 *>(p.C + (m0 + rr) * p.N + n0 + c) = o;
+        *reinterpret_cast<float4 *>(C + (m0 + rr) * p.N + n0 + c) = o;
     }
+    if (p.db && tid < kM && m0 + tid < p.M)   // columns m of threads tid and tid + 128
+        C[p.M * (int64_t)p.N + m0 + tid] = sdb[tid] + sdb[tid + kM];
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
@@ -374,6 +402,22 @@ int launch_stages(const CUtensorMap &ma, const CUtensorMap &mw, const TcArgs &p,
     return NGT_OK;
 }
 
+// The epilogue's output tile (and the splitter sums) reuse the stages and operand buffers.
+int launch_plan(const CUtensorMap &ma, const CUtensorMap &mw, const TcArgs &p, dim3 grid, int stages,
+                cudaStream_t st) {
+    if ((size_t)kM * (((p.ncta + 31) / 32) * 32 + 4) * 4 + (size_t)kThreads * 4 >
+        (size_t)stages * raw_bytes(p.np) + 2 * op_bytes(p.np))
+        return NGT_ERR_UNSUPPORTED;
+    switch (stages) {
+    case 8: return launch_stages<8>(ma, mw, p, grid, st);
+    case 7: return launch_stages<7>(ma, mw, p, grid, st);
+    case 6: return launch_stages<6>(ma, mw, p, grid, st);
+    case 5: return launch_stages<5>(ma, mw, p, grid, st);
+    case 4: return launch_stages<4>(ma, mw, p, grid, st);
+    default: return launch_stages<3>(ma, mw, p, grid, st);
+    }
+}
+
 }  // namespace
 
 bool linear_tc_supported(int K, int N) { return K > 0 && N > 0 && N <= kMaxN && K % 4 == 0 && N % 4 == 0; }
@@ -391,6 +435,10 @@ int launch_linear_tc(int64_t M, int K, int N, const float *A, const float *W, bo
     p.np = (p.ncta + 15) / 16 * 16;
     p.tmem_cols = tmem_cols_for(p.np);
     p.trans = trans_w ? 1 : 0;
+    p.trans_a = 0;
+    p.db = 0;
+    p.k_per_cta = K;
+    p.c_stride = 0;
     p.bias = bias;
     p.C = C;
     CUtensorMap ma, mw;
@@ -400,17 +448,42 @@ int launch_linear_tc(int64_t M, int K, int N, const float *A, const float *W, bo
         rc = trans_w ? map2d(&mw, W, K, N, p.np, kKS) : map2d(&mw, W, N, K, kKS, p.np);
     if (rc != NGT_OK) return rc;
     const dim3 grid((unsigned)gm, (unsigned)plan.split);
-    // the epilogue's output tile reuses the stages and operand buffers
-    if ((size_t)kM * (((p.ncta + 31) / 32) * 32 + 4) * 4 > (size_t)plan.stages * raw_bytes(p.np) + 2 * op_bytes(p.np))
+    return launch_plan(ma, mw, p, grid, plan.stages, st);
+}
+
+bool wgrad_tc_supported(int in_features, int out_features) {
+    return in_features > 0 && out_features > 0 && in_features <= kMaxN && in_features % 4 == 0 &&
+           out_features % 4 == 0;
+}
+
+int launch_wgrad_tc(int64_t rows, int in_features, int out_features, const float *x, const float *dy, float *part,
+                    int64_t splits, int64_t rows_per_split, cudaStream_t st) {
+    if (rows <= 0 || rows > 0x7fffffffLL - kM || splits < 1 || rows_per_split % kKS != 0 ||
+        splits * rows_per_split < rows || (splits - 1) * rows_per_split >= rows)
         return NGT_ERR_UNSUPPORTED;
-    switch (plan.stages) {
-    case 8: return launch_stages<8>(ma, mw, p, grid, st);
-    case 7: return launch_stages<7>(ma, mw, p, grid, st);
-    case 6: return launch_stages<6>(ma, mw, p, grid, st);
-    case 5: return launch_stages<5>(ma, mw, p, grid, st);
-    case 4: return launch_stages<4>(ma, mw, p, grid, st);
-    default: return launch_stages<3>(ma, mw, p, grid, st);
-    }
+    const int64_t gm = (out_features + kM - 1) / kM;
+    const TcPlan plan = tc_plan(gm * splits, in_features, sm_count_tc());
+    TcArgs p;
+    p.M = out_features;            // rows of dW
+    p.K = rows;                    // reduced over the rows of x and dy
+    p.N = in_features;             // columns of dW
+    p.ncta = in_features;
+    p.np = (in_features + 15) / 16 * 16;
+    p.tmem_cols = tmem_cols_for(p.np);
+    p.trans = 1;                   // B(n, k) = x[k * in + n]
+    p.trans_a = 1;                 // A(m, k) = dy[k * out + m]
+    p.db = 1;
+    p.k_per_cta = rows_per_split;
+    p.c_stride = (int64_t)in_features * out_features + out_features;
+    p.bias = nullptr;
+    p.C = part;
+    CUtensorMap ma, mw;
+    bind_primary_context();
+    int rc = map2d(&ma, dy, rows, out_features, kM, kKS);        // [16 k][128 m] boxes
+    if (rc == NGT_OK) rc = map2d(&mw, x, rows, in_features, p.np, kKS);   // [16 k][np n] boxes
+    if (rc != NGT_OK) return rc;
+    const dim3 grid((unsigned)gm, 1u, (unsigned)splits);
+    return launch_plan(ma, mw, p, grid, plan.stages, st);
 }
 
 int linear_tc_timeouts(int *count) {

@@ -14,6 +14,14 @@ bool linear_tc_supported(int K, int N);
 int launch_linear_tc(int64_t M, int K, int N, const float *A, const float *W, bool trans_w, const float *bias,
                      float *C, cudaStream_t st);
 
+// Weight grad on the same kernel: part[z] = (dy^T x over rows [z * rows_per_split, ...), the sums
+// of dy over those rows) for z < splits, laid out as [out * in] then [out] per split, for a
+// fixed-order sum of the splits.  in_features <= 256; rows_per_split a multiple of 16 and
+// splits = ceil(rows / rows_per_split).
+bool wgrad_tc_supported(int in_features, int out_features);
+int launch_wgrad_tc(int64_t rows, int in_features, int out_features, const float *x, const float *dy, float *part,
+                    int64_t splits, int64_t rows_per_split, cudaStream_t st);
+
 // Number of CTAs whose bounded waits ran out since the library was loaded (synchronous copy).
 int linear_tc_timeouts(int *count);
 
