@@ -325,7 +325,9 @@ NGT_API int ngt_column_sum(int64_t rows, int cols, const float *x, float *out, v
  * in_features and out_features are multiples of 4.  fp32 precision throughout: with both
  * dimensions <= 256 the forward and input grad run on the tcgen05 tensor cores with split TF32
  * operands (three TF32 products per pair: hi*hi + hi*lo + lo*hi, fp32 accumulation), otherwise
- * on CUDA-core FFMA; the weight grad is FFMA.
+ * on CUDA-core FFMA; the weight grad runs on the same split-TF32 tensor-core kernel when
+ * in_features <= 256 and rows >= 64 (row ranges of at most 512 rows, summed in a fixed order),
+ * else on FFMA.
  *   ngt_linear_forward         y = x W^T + b          in_features  <= 256 (else NGT_ERR_UNSUPPORTED)
  *   ngt_linear_backward_input  dx = dy W              out_features <= 256 (else NGT_ERR_UNSUPPORTED)
  *   ngt_linear_backward_weight dW = dy^T x, db = column sums of dy; any size; summed in a fixed

@@ -1,7 +1,8 @@
 """fp32 Linear layers (forward, input grad, weight + bias grad) against torch.
 
 Shapes with both dimensions <= 256 run the forward and input grad on the tensor cores with split
-TF32 operands (csrc/linear_tc.cu), the others on fp32 FFMA (csrc/linear.cu); the weight grad is FFMA.
+TF32 operands (csrc/linear_tc.cu), the others on fp32 FFMA (csrc/linear.cu); the weight grad runs
+on the same tensor-core kernel when the input width is <= 256 and there are >= 64 rows, else on FFMA.
 Tolerance: relative (max|a-b| / max|b|) against an fp64 torch restatement, 1e-5 -- fp32 precision
 in a different summation order than cuBLAS; torch's own fp32 result is held to the same bound.
 """
