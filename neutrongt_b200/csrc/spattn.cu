@@ -624,7 +624,9 @@ __device__ __forceinline__ void store_rec(float *rec, const float2 (&acc)[4]) {
 
 // PAIRS (HEAD_VECS = 2): the two lanes of a head finish different edges of an edge pair and
 // exchange the exponentials (as spattn_bwd_r128 below); the same results as without pairs.
-template <int HEAD_VECS, int UNROLL, int MIN_BLOCKS = 4, bool PAIRS = false, bool PF = false>
+// NB: launched without an edge bias (and, in the backward, without its gradient), so the per-edge
+// bias tests compile away.
+template <int HEAD_VECS, int UNROLL, int MIN_BLOCKS = 4, bool PAIRS = false, bool PF = false, bool NB = false>
 __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
     spattn_fwd_r128(int n, int heads, float scale_inv, const __nv_bfloat16 *__restrict__ q,
                     const __nv_bfloat16 *__restrict__ k, const __nv_bfloat16 *__restrict__ v,
@@ -699,7 +701,7 @@ __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
                 const float d = (odd ? d1 : d0) + __shfl_xor_sync(0xffffffffu, odd ? d0 : d1, 1);
                 const bool okm = odd ? ok[u + 1] : ok[u];
                 float s = fminf(fmaxf(d * scale_inv, -kClamp), kClamp);
-                if (bias != nullptr && okm)
+                if (!NB && bias != nullptr && okm)
                     s += __ldg(bias + (size_t)(e0 + sub + EPW * u + (odd ? EPW : 0)) * heads + head);
                 const float p = okm ? mufu_exp(s) : 0.f;
                 const float pp = __shfl_xor_sync(0xffffffffu, p, 1);
@@ -714,7 +716,7 @@ __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
             for (int u = 0; u < UNROLL; u++) {
                 const float d = head_reduce<HEAD_VECS>(dot8(kr[u], qw));
                 float s = fminf(fmaxf(d * scale_inv, -kClamp), kClamp);
-                if (bias != nullptr && ok[u]) s += __ldg(bias + (size_t)(e0 + sub + EPW * u) * heads + head);
+                if (!NB && bias != nullptr && ok[u]) s += __ldg(bias + (size_t)(e0 + sub + EPW * u) * heads + head);
                 const float p = ok[u] ? mufu_exp(s) : 0.f;
                 zs += p;
                 axpy8(acc, p, vr[u]);
@@ -748,7 +750,8 @@ __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
 // exponential and gradient arithmetic once for its own edge, and hands back the two scalars the
 // weighted sums need, instead of both lanes repeating that arithmetic for every edge.  The sums
 // are added in the same order as without pairs, so the results are identical.
-template <int HEAD_VECS, int UNROLL_A, int UNROLL_B, int MIN_BLOCKS = 4, bool PAIRS = false, bool PF = false>
+template <int HEAD_VECS, int UNROLL_A, int UNROLL_B, int MIN_BLOCKS = 4, bool PAIRS = false, bool PF = false,
+          bool NB = false>
 __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
     spattn_bwd_r128(int n, int heads, float scale_inv, int blocks_a, const __nv_bfloat16 *__restrict__ q,
                     const __nv_bfloat16 *__restrict__ k, const __nv_bfloat16 *__restrict__ v,
@@ -849,11 +852,11 @@ __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
                     const float s = dqk * scale_inv;
                     float sc = fminf(fmaxf(s, -kClamp), kClamp);
                     const bool inside = sc == s;   // -kClamp <= s <= kClamp (false for NaN)
-                    if (bias != nullptr && okm) sc += __ldg(bias + (size_t)e * heads + head);
+                    if (!NB && bias != nullptr && okm) sc += __ldg(bias + (size_t)e * heads + head);
                     const float p = mufu_exp(sc);
                     const float dpre = (dgv - dl) * inv * p;
                     const float ds = (okm && inside) ? dpre : 0.f;
-                    if (dbias != nullptr && okm) dbias[(size_t)e * heads + head] = dpre;
+                    if (!NB && dbias != nullptr && okm) dbias[(size_t)e * heads + head] = dpre;
                     const float dsp = __shfl_xor_sync(0xffffffffu, ds, 1);
                     axpy8(acc, odd ? dsp : ds, kr[u]);
                     axpy8(acc, odd ? ds : dsp, kr[u + 1]);
@@ -867,11 +870,11 @@ __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
                     const float s = dqk * scale_inv;
                     float sc = fminf(fmaxf(s, -kClamp), kClamp);
                     const bool inside = sc == s;   // -kClamp <= s <= kClamp (false for NaN)
-                    if (bias != nullptr && ok[u]) sc += __ldg(bias + (size_t)e * heads + head);
+                    if (!NB && bias != nullptr && ok[u]) sc += __ldg(bias + (size_t)e * heads + head);
                     const float p = mufu_exp(sc);
                     const float dpre = (dgv - dl) * inv * p;
                     const float ds = (ok[u] && inside) ? dpre : 0.f;
-                    if (dbias != nullptr && ok[u] && (gl % HEAD_VECS) == 0) dbias[(size_t)e * heads + head] = dpre;
+                    if (!NB && dbias != nullptr && ok[u] && (gl % HEAD_VECS) == 0) dbias[(size_t)e * heads + head] = dpre;
                     axpy8(acc, ds, kr[u]);
                 }
             }
@@ -942,7 +945,7 @@ __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
                     const float s = dqk * scale_inv;
                     float sc = fminf(fmaxf(s, -kClamp), kClamp);
                     const bool inside = sc == s;   // -kClamp <= s <= kClamp (false for NaN)
-                    if (bias != nullptr && okm)
+                    if (!NB && bias != nullptr && okm)
                         sc += __ldg(bias + (size_t)__ldg(src_to_dst_slot + e) * heads + head);
                     const float p = okm ? mufu_exp(sc) : 0.f;
                     const float inv = mufu_rcp(zr[u] + kEps);
@@ -965,7 +968,7 @@ __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
                     const float s = dqk * scale_inv;
                     float sc = fminf(fmaxf(s, -kClamp), kClamp);
                     const bool inside = sc == s;   // -kClamp <= s <= kClamp (false for NaN)
-                    if (bias != nullptr && ok[u])
+                    if (!NB && bias != nullptr && ok[u])
                         sc += __ldg(bias + (size_t)__ldg(src_to_dst_slot + e) * heads + head);
                     const float p = ok[u] ? mufu_exp(sc) : 0.f;
                     const float inv = mufu_rcp(zr[u] + kEps);
@@ -1495,6 +1498,44 @@ Shape vec_shape(int heads, int head_dim) {
 
 #define NGT_SCALAR_DIMS(MACRO) MACRO(4) MACRO(8) MACRO(12) MACRO(16) MACRO(24) MACRO(32) MACRO(48) MACRO(64)
 
+// bf16 128-element rows: edge pairs and index prefetch where a head spans two lanes (D = 16); the
+// per-edge bias tests compiled away when the call has no edge bias (nor its gradient).
+template <int HV>
+void launch_fwd_r128(unsigned grid, cudaStream_t st, int n, int heads, float scale_inv, const void *q, const void *k,
+                     const void *v, const int32_t *rowptr, const int32_t *col, const float *bias, void *out, float *z,
+                     float *ns, int ns_len, int row_blocks, SegView sg) {
+    constexpr int U = HV == 2 ? 2 : 4;
+    constexpr bool P = HV == 2;
+    using B = __nv_bfloat16;
+    if (bias != nullptr)
+        spattn_fwd_r128<HV, U, 4, P, P, false><<<grid, kBlock, 0, st>>>(n, heads, scale_inv, (const B *)q, (const B *)k,
+                                                                       (const B *)v, rowptr, col, bias, (B *)out, z,
+                                                                       ns, ns_len, row_blocks, sg);
+    else
+        spattn_fwd_r128<HV, U, 4, P, P, true><<<grid, kBlock, 0, st>>>(n, heads, scale_inv, (const B *)q, (const B *)k,
+                                                                      (const B *)v, rowptr, col, nullptr, (B *)out, z,
+                                                                      ns, ns_len, row_blocks, sg);
+}
+
+template <int HV>
+void launch_bwd_r128(unsigned grid, cudaStream_t st, int n, int heads, float scale_inv, int blocks_a, const void *q,
+                     const void *k, const void *v, const void *dout, const float *z, const float *delta,
+                     const int32_t *dst_rowptr, const int32_t *dst_src, const int32_t *src_rowptr,
+                     const int32_t *src_dst, const int32_t *s2d, const float *bias, void *dq, void *dk, void *dv,
+                     float *dbias, SegView sgd, SegView sgs) {
+    constexpr int UA = HV == 2 ? 2 : 3;
+    constexpr bool P = HV == 2;
+    using B = __nv_bfloat16;
+    if (bias != nullptr || dbias != nullptr)
+        spattn_bwd_r128<HV, UA, 2, 4, P, P, false><<<grid, kBlock, 0, st>>>(
+            n, heads, scale_inv, blocks_a, (const B *)q, (const B *)k, (const B *)v, (const B *)dout, z, delta,
+            dst_rowptr, dst_src, src_rowptr, src_dst, s2d, bias, (B *)dq, (B *)dk, (B *)dv, dbias, sgd, sgs);
+    else
+        spattn_bwd_r128<HV, UA, 2, 4, P, P, true><<<grid, kBlock, 0, st>>>(
+            n, heads, scale_inv, blocks_a, (const B *)q, (const B *)k, (const B *)v, (const B *)dout, z, delta,
+            dst_rowptr, dst_src, src_rowptr, src_dst, s2d, nullptr, (B *)dq, (B *)dk, (B *)dv, nullptr, sgd, sgs);
+}
+
 template <typename T>
 int forward_t(int64_t n, int heads, int head_dim, const void *q, const void *k, const void *v,
               const int32_t *rowptr, const int32_t *col, const float *bias, void *out, float *z,
@@ -1509,10 +1550,8 @@ int forward_t(int64_t n, int heads, int head_dim, const void *q, const void *k, 
 #define NGT_FWD(HV, RV)                                                                          \
     if (sh.head_vecs == HV && sh.row_vecs == RV) {                                               \
         if constexpr (sizeof(T) == 2 && RV == 16)                                                \
-            spattn_fwd_r128<HV, HV == 2 ? 2 : 4, 4, HV == 2, HV == 2><<<row_blocks + seg_blocks, kBlock, 0, st>>>( \
-                (int)n, heads, scale_inv, (const __nv_bfloat16 *)q, (const __nv_bfloat16 *)k,    \
-                (const __nv_bfloat16 *)v, rowptr, col, bias, (__nv_bfloat16 *)out, z, ns,        \
-                (int)ns_len, row_blocks, sg);                                                    \
+            launch_fwd_r128<HV>(row_blocks + seg_blocks, st, (int)n, heads, scale_inv, q, k, v,      \
+                                rowptr, col, bias, out, z, ns, (int)ns_len, row_blocks, sg);     \
         else if constexpr (sizeof(T) == 4 && RV == 32)                                           \
             spattn_fwd_f128<HV, 4><<<row_blocks + seg_blocks, kBlock, 0, st>>>(                  \
                 (int)n, heads, scale_inv, (const float *)q, (const float *)k, (const float *)v,  \
@@ -1569,11 +1608,9 @@ int backward_t(int64_t n, int heads, int head_dim, const void *q, const void *k,
             (int)n, heads, (const T *)out, (const T *)dout, delta);                               \
         NGT_CHECK_LAUNCH();                                                                       \
         if constexpr (sizeof(T) == 2 && RV == 16)                                                 \
-            spattn_bwd_r128<HV, HV == 2 ? 2 : 3, 2, 4, HV == 2, HV == 2><<<2 * blocks_a + seg_blocks, kBlock, 0, st>>>( \
-                (int)n, heads, scale_inv, blocks_a, (const __nv_bfloat16 *)q,                     \
-                (const __nv_bfloat16 *)k, (const __nv_bfloat16 *)v, (const __nv_bfloat16 *)dout,  \
-                z, delta, dst_rowptr, dst_src, src_rowptr, src_dst, s2d, bias,                    \
-                (__nv_bfloat16 *)dq, (__nv_bfloat16 *)dk, (__nv_bfloat16 *)dv, dbias, sgd, sgs);  \
+            launch_bwd_r128<HV>(2 * blocks_a + seg_blocks, st, (int)n, heads, scale_inv, blocks_a, q, k, v, \
+                                dout, z, delta, dst_rowptr, dst_src, src_rowptr, src_dst, s2d, bias, dq,  \
+                                dk, dv, dbias, sgd, sgs);                                          \
         else if constexpr (sizeof(T) == 4 && RV == 32)                                            \
             spattn_bwd_f128<HV, 3, 2><<<2 * blocks_a + seg_blocks, kBlock, 0, st>>>(              \
                 (int)n, heads, scale_inv, blocks_a, (const float *)q, (const float *)k,           \
