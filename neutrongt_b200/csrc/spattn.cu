@@ -1004,7 +1004,8 @@ __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
 // 16-byte vector of four floats per lane, one edge per warp instruction, UNROLL edges in flight,
 // and the next batch's column indices loaded ahead.  Dot products and weighted sums run as packed
 // f32x2 FMAs, exponentials and the source role's reciprocal on the MUFU unit (`ex2.approx`, relative
-// error ~2^-22, inside the fp32 parity tolerance).  Segment records are laid out as in the general
+// error ~2^-22, inside the fp32 parity tolerance).  NB: launched without an edge bias (nor its
+// gradient), the per-edge bias tests compiled out.  Segment records are laid out as in the general
 // kernels, so the same finish kernels serve both.
 namespace f128 {
 constexpr int RV = 32;
@@ -1025,7 +1026,7 @@ __device__ __forceinline__ void axpy4(float2 &a0, float2 &a1, float s, const uin
 }
 }  // namespace f128
 
-template <int HEAD_VECS, int UNROLL, int MIN_BLOCKS = 4>
+template <int HEAD_VECS, int UNROLL, int MIN_BLOCKS = 4, bool NB = false>
 __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
     spattn_fwd_f128(int n, int heads, float scale_inv, const float *__restrict__ q, const float *__restrict__ k,
                     const float *__restrict__ v, const int *__restrict__ rowptr, const int *__restrict__ col,
@@ -1081,7 +1082,7 @@ __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
         for (int u = 0; u < UNROLL; u++) {
             const float d = head_reduce<HEAD_VECS>(dot4(kr[u], q0, q1));
             float s = fminf(fmaxf(d * scale_inv, -kClamp), kClamp);
-            if (bias != nullptr && ok[u]) s += __ldg(bias + (size_t)(e0 + u) * heads + head);
+            if (!NB && bias != nullptr && ok[u]) s += __ldg(bias + (size_t)(e0 + u) * heads + head);
             const float p = ok[u] ? mufu_exp(s) : 0.f;
             zs += p;
             axpy4(a0, a1, p, vr[u]);
@@ -1103,7 +1104,7 @@ __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
     if (lane == 0 && row < ns_len) node_scores[row] = hs / (float)heads;
 }
 
-template <int HEAD_VECS, int UNROLL_A, int UNROLL_B, int MIN_BLOCKS = 4>
+template <int HEAD_VECS, int UNROLL_A, int UNROLL_B, int MIN_BLOCKS = 4, bool NB = false>
 __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
     spattn_bwd_f128(int n, int heads, float scale_inv, int blocks_a, const float *__restrict__ q,
                     const float *__restrict__ k, const float *__restrict__ v, const float *__restrict__ dout,
@@ -1185,11 +1186,11 @@ __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
                 const float s = dqk * scale_inv;
                 float sc = fminf(fmaxf(s, -kClamp), kClamp);
                 const bool inside = sc == s;   // -kClamp <= s <= kClamp (false for NaN)
-                if (bias != nullptr && ok[u]) sc += __ldg(bias + (size_t)e * heads + head);
+                if (!NB && bias != nullptr && ok[u]) sc += __ldg(bias + (size_t)e * heads + head);
                 const float p = mufu_exp(sc);
                 const float dpre = (dgv - dl) * inv * p;
                 const float ds = (ok[u] && inside) ? dpre : 0.f;
-                if (dbias != nullptr && ok[u] && (lane % HEAD_VECS) == 0) dbias[(size_t)e * heads + head] = dpre;
+                if (!NB && dbias != nullptr && ok[u] && (lane % HEAD_VECS) == 0) dbias[(size_t)e * heads + head] = dpre;
                 axpy4(a0, a1, ds, kr[u]);
             }
         }
@@ -1237,7 +1238,7 @@ __global__ void __launch_bounds__(kBlock, MIN_BLOCKS)
                 const float s = dqk * scale_inv;
                 float sc = fminf(fmaxf(s, -kClamp), kClamp);
                 const bool inside = sc == s;   // -kClamp <= s <= kClamp (false for NaN)
-                if (bias != nullptr && ok[u])
+                if (!NB && bias != nullptr && ok[u])
                     sc += __ldg(bias + (size_t)__ldg(src_to_dst_slot + e) * heads + head);
                 const float p = ok[u] ? mufu_exp(sc) : 0.f;
                 const float inv = mufu_rcp(zr[u] + kEps);
@@ -1536,6 +1537,37 @@ void launch_bwd_r128(unsigned grid, cudaStream_t st, int n, int heads, float sca
             dst_rowptr, dst_src, src_rowptr, src_dst, s2d, nullptr, (B *)dq, (B *)dk, (B *)dv, nullptr, sgd, sgs);
 }
 
+// fp32 128-element rows, with the bias tests compiled out when the call has no edge bias.
+template <int HV>
+void launch_fwd_f128(unsigned grid, cudaStream_t st, int n, int heads, float scale_inv, const void *q, const void *k,
+                     const void *v, const int32_t *rowptr, const int32_t *col, const float *bias, void *out, float *z,
+                     float *ns, int ns_len, int row_blocks, SegView sg) {
+    const float *Q = (const float *)q, *K = (const float *)k, *V = (const float *)v;
+    if (bias != nullptr)
+        spattn_fwd_f128<HV, 4, 4, false><<<grid, kBlock, 0, st>>>(n, heads, scale_inv, Q, K, V, rowptr, col, bias,
+                                                                   (float *)out, z, ns, ns_len, row_blocks, sg);
+    else
+        spattn_fwd_f128<HV, 4, 4, true><<<grid, kBlock, 0, st>>>(n, heads, scale_inv, Q, K, V, rowptr, col, nullptr,
+                                                                  (float *)out, z, ns, ns_len, row_blocks, sg);
+}
+
+template <int HV>
+void launch_bwd_f128(unsigned grid, cudaStream_t st, int n, int heads, float scale_inv, int blocks_a, const void *q,
+                     const void *k, const void *v, const void *dout, const float *z, const float *delta,
+                     const int32_t *dst_rowptr, const int32_t *dst_src, const int32_t *src_rowptr,
+                     const int32_t *src_dst, const int32_t *s2d, const float *bias, void *dq, void *dk, void *dv,
+                     float *dbias, SegView sgd, SegView sgs) {
+    const float *Q = (const float *)q, *K = (const float *)k, *V = (const float *)v, *G = (const float *)dout;
+    if (bias != nullptr || dbias != nullptr)
+        spattn_bwd_f128<HV, 3, 2, 4, false><<<grid, kBlock, 0, st>>>(
+            n, heads, scale_inv, blocks_a, Q, K, V, G, z, delta, dst_rowptr, dst_src, src_rowptr, src_dst, s2d, bias,
+            (float *)dq, (float *)dk, (float *)dv, dbias, sgd, sgs);
+    else
+        spattn_bwd_f128<HV, 3, 2, 4, true><<<grid, kBlock, 0, st>>>(
+            n, heads, scale_inv, blocks_a, Q, K, V, G, z, delta, dst_rowptr, dst_src, src_rowptr, src_dst, s2d, nullptr,
+            (float *)dq, (float *)dk, (float *)dv, nullptr, sgd, sgs);
+}
+
 template <typename T>
 int forward_t(int64_t n, int heads, int head_dim, const void *q, const void *k, const void *v,
               const int32_t *rowptr, const int32_t *col, const float *bias, void *out, float *z,
@@ -1553,9 +1585,8 @@ int forward_t(int64_t n, int heads, int head_dim, const void *q, const void *k, 
             launch_fwd_r128<HV>(row_blocks + seg_blocks, st, (int)n, heads, scale_inv, q, k, v,      \
                                 rowptr, col, bias, out, z, ns, (int)ns_len, row_blocks, sg);     \
         else if constexpr (sizeof(T) == 4 && RV == 32)                                           \
-            spattn_fwd_f128<HV, 4><<<row_blocks + seg_blocks, kBlock, 0, st>>>(                  \
-                (int)n, heads, scale_inv, (const float *)q, (const float *)k, (const float *)v,  \
-                rowptr, col, bias, (float *)out, z, ns, (int)ns_len, row_blocks, sg);            \
+            launch_fwd_f128<HV>(row_blocks + seg_blocks, st, (int)n, heads, scale_inv, q, k, v,      \
+                                rowptr, col, bias, out, z, ns, (int)ns_len, row_blocks, sg);     \
         else                                                                                     \
             spattn_fwd_vec<T, HV, RV><<<row_blocks + seg_blocks, kBlock, 0, st>>>(               \
                 (int)n, heads, scale_inv, (const T *)q, (const T *)k, (const T *)v, rowptr, col, \
@@ -1612,10 +1643,9 @@ int backward_t(int64_t n, int heads, int head_dim, const void *q, const void *k,
                                 dout, z, delta, dst_rowptr, dst_src, src_rowptr, src_dst, s2d, bias, dq,  \
                                 dk, dv, dbias, sgd, sgs);                                          \
         else if constexpr (sizeof(T) == 4 && RV == 32)                                            \
-            spattn_bwd_f128<HV, 3, 2><<<2 * blocks_a + seg_blocks, kBlock, 0, st>>>(              \
-                (int)n, heads, scale_inv, blocks_a, (const float *)q, (const float *)k,           \
-                (const float *)v, (const float *)dout, z, delta, dst_rowptr, dst_src, src_rowptr, \
-                src_dst, s2d, bias, (float *)dq, (float *)dk, (float *)dv, dbias, sgd, sgs);      \
+            launch_bwd_f128<HV>(2 * blocks_a + seg_blocks, st, (int)n, heads, scale_inv, blocks_a, q, k, v, \
+                                dout, z, delta, dst_rowptr, dst_src, src_rowptr, src_dst, s2d, bias, dq,  \
+                                dk, dv, dbias, sgd, sgs);                                          \
         else                                                                                      \
             spattn_bwd_vec<T, HV, RV><<<2 * blocks_a + seg_blocks, kBlock, 0, st>>>(              \
                 (int)n, heads, scale_inv, blocks_a, (const T *)q, (const T *)k, (const T *)v,     \
