@@ -526,10 +526,14 @@ def bench_gt_epoch(args, rank, world, dev, windows, label, warm=2, epochs=5, wit
            "attention_edges_per_epoch": edges_epoch,
            "attention_kernels_s_per_epoch": t_attn,
            "attention_share": t_attn / t_graph if t_graph > 0 else None,
+           # graph-sparse attention throughput on the 170K-node graph's windows: every layer's
+           # forward + backward over the window edges, fp32, on the ranks' own windows
+           "attention_edges_per_s": 4 * edges_epoch / t_attn if t_attn > 0 else None,
            "note": "epoch_time_s: one captured CUDA graph per window (gather, forward, loss, backward, gradient "
                    "all-reduce, AdamW) replayed per epoch; epoch_time_eager_s: the same loop eagerly; "
                    "attention_kernels_s_per_epoch: the epoch's sparse-attention launches (4 layers x windows, "
-                   "fwd+bwd) timed alone"}
+                   "fwd+bwd) timed alone; attention_edges_per_s: 4 layers x attention_edges_per_epoch over that "
+                   "time (fp32 fwd+bwd)"}
     if with_cpu:
         run(feature, 1)
         timed_h = run(feature, epochs)
