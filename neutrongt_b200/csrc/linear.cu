@@ -461,16 +461,19 @@ WgradPlan wgrad_plan(int64_t rows, int in_features, int out_features) {
     return p;
 }
 
-// Row ranges of the tensor-core weight grad: a multiple of 16 rows each, about one CTA per SM and
-// output tile, at least 64 rows, and at most 512 rows so that no range accumulates a long chain of
-// products in one fp32 accumulator (the ranges are summed in a fixed order afterwards).
+// Row ranges of the tensor-core weight grad: a multiple of 16 rows each, about one CTA per four SMs
+// and output tile (the weight grads run on a side stream beside the input-grad chain, where fewer,
+// longer CTAs overlap it best: GT epoch 28.0 ms with one CTA per SM, 27.0-27.1 with one per four,
+// 27.5 with one per two, 30.0 with one per eight), at least 64 rows, and at most 512 rows so that no
+// range accumulates a long chain of products in one fp32 accumulator (the ranges are summed in a
+// fixed order afterwards).
 struct TcWgradPlan {
     int64_t splits, rows_per_split;
 };
 
 TcWgradPlan tc_wgrad_plan(int64_t rows, int out_features) {
     const int64_t m_tiles = (out_features + 127) / 128;
-    int64_t splits = sm_count() / m_tiles;
+    int64_t splits = sm_count() / (4 * m_tiles);
     if (splits > rows / 64) splits = rows / 64;
     if (splits < (rows + 511) / 512) splits = (rows + 511) / 512;
     if (splits < 1) splits = 1;
