@@ -85,26 +85,30 @@ def test_against_oracle(cuda, H, D, dtype):
 
 
 @pytest.mark.parametrize("H,D", [(8, 16), (4, 32), (16, 8)])
-def test_bf16_with_edge_bias(cuda, H, D):
-    # the bf16 kernels for 128-element rows with an additive edge bias and its gradient, on a
-    # graph with a heavy row (segments), against the fp64 oracle
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_rows_of_128_with_edge_bias(cuda, H, D, dtype):
+    # the kernels for 128-element rows (bf16 and fp32) with an additive edge bias and its gradient,
+    # on a graph with a heavy row (segments), against the fp64 oracle
     q, k, v, dout, ei = _random_case(300, 4000, H, D, seed=7 + H, scale=1.3, heavy=600)
-    q, k, v = (t.to(torch.bfloat16) for t in (q, k, v))
+    q, k, v = (t.to(dtype) for t in (q, k, v))
     bias = torch.randn(1, H, 300, 300, generator=torch.Generator().manual_seed(3)) * 0.7   # [1, H, s, s]
     x, ns, (dq, dk, dv, db) = _ours(q, k, v, ei, bias=bias, dout=dout)
     rx, rns, _, _ = oatt.sparse_attention_forward(q.double(), k.double(), v.double(), ei, bias.double())
     rdq, rdk, rdv, rdb = oatt.sparse_attention_backward(q.double(), k.double(), v.double(), ei,
-                                                        dout.to(torch.bfloat16).double(), bias.double())
-    assert rel_err(x, rx) < BF16_TOL
-    assert rel_err(ns, rns) < BF16_TOL
-    assert rel_err(dq, rdq) < BF16_TOL
-    assert rel_err(dk, rdk) < BF16_TOL
-    assert rel_err(dv, rdv) < BF16_TOL
-    assert rel_err(db, rdb) < BF16_TOL
+                                                        dout.to(dtype).double(), bias.double())
+    tol = F32_TOL if dtype == torch.float32 else BF16_TOL
+    assert rel_err(x, rx) < tol
+    assert rel_err(ns, rns) < tol
+    assert rel_err(dq, rdq) < tol
+    assert rel_err(dk, rdk) < tol
+    assert rel_err(dv, rdv) < tol
+    assert rel_err(db, rdb) < tol
 
 
-def test_rows_without_edges_and_short_node_scores(cuda):
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_rows_without_edges_and_short_node_scores(cuda, dtype):
     q, k, v, dout, _ = _random_case(40, 1, 8, 16, seed=5)
+    q, k, v = (t.to(dtype) for t in (q, k, v))
     ei = torch.tensor([[3, 4, 5, 3], [1, 1, 7, 7]])
     x, ns, (dq, dk, dv, _) = _ours(q, k, v, ei, dout=dout)
     assert ns.shape == (8,)                       # max(dst) + 1, as torch_scatter gives
@@ -112,7 +116,8 @@ def test_rows_without_edges_and_short_node_scores(cuda):
     assert torch.count_nonzero(dq[8:]) == 0
     assert torch.count_nonzero(dk[[0, 1, 2] + list(range(6, 40))]) == 0
     rx, rns, _, _ = oatt.sparse_attention_forward(q.double(), k.double(), v.double(), ei)
-    assert rel_err(x, rx) < F32_TOL and rel_err(ns, rns) < F32_TOL
+    tol = F32_TOL if dtype == torch.float32 else BF16_TOL
+    assert rel_err(x, rx) < tol and rel_err(ns, rns) < tol
 
 
 def test_empty_edge_list(cuda):
