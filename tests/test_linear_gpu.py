@@ -23,7 +23,8 @@ TOL = 1e-5
 # tensor-core Linear picks a 7- and a 6-slice TMA ring (149-296 row tiles, two CTAs per SM).
 SHAPES = [(10583, 128, 128), (10583, 128, 256), (10583, 256, 128), (10583, 128, 64), (10583, 64, 32),
           (10583, 32, 40), (1, 4, 4), (5, 8, 12), (100, 64, 64), (1001, 256, 512), (200000, 128, 128),
-          (3, 300, 8), (30000, 128, 32), (30000, 64, 40)]
+          (3, 300, 8), (30000, 128, 32), (30000, 64, 40),
+          (3000, 40, 24), (1000, 200, 136)]   # padded input widths and a ragged second output tile
 
 
 def _ref(x, w, b, dy):
