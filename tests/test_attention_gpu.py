@@ -217,3 +217,27 @@ def test_config3_full_window_elementwise(cuda):
     errs.update(dq=rel_err(got["dq"], rdq), dk=rel_err(got["dk"], rdk), dv=rel_err(got["dv"], rdv))
     bad = {name: e for name, e in errs.items() if not e < BF16_TOL}
     assert not bad, bad
+
+
+def test_fp32_rows_of_128_large_power_law_window(cuda):
+    """The fp32 128-element-row kernels (the GT model's shape: H = 8, D = 16) on a 20,000-node window
+    with 400,000 edges and power-law in-degrees (many heavy rows split into segments), every output
+    element by element against the fp64 restatement on the GPU, fp32 tolerance 1e-5."""
+    from neutrongt_b200 import sparse_attention_bias
+    g = torch.Generator(device="cuda").manual_seed(11)
+    s, E, H, D = 20000, 400000, 8, 16
+    w = torch.rand(s, generator=g, device="cuda") ** 4 + 1e-3      # skewed destination weights
+    dst = torch.multinomial(w, E, replacement=True, generator=g)
+    src = torch.randint(0, s, (E,), generator=g, device="cuda")
+    ei = torch.stack([src, dst])
+    q, k, v, dout = (torch.randn(s, H, D, generator=g, device="cuda") * 1.2 for _ in range(4))
+    qd, kd, vd = (t.clone().requires_grad_(True) for t in (q, k, v))
+    x, ns = sparse_attention_bias(qd, kd, vd, ei, None)
+    x.backward(dout)
+    q64, k64, v64, g64 = (t.double() for t in (q, k, v, dout))
+    rx, rns, _, _ = oatt.sparse_attention_forward(q64, k64, v64, ei)
+    rdq, rdk, rdv, _ = oatt.sparse_attention_backward(q64, k64, v64, ei, g64)
+    errs = {"x": rel_err(x.detach(), rx), "node_scores": rel_err(ns, rns), "dq": rel_err(qd.grad, rdq),
+            "dk": rel_err(kd.grad, rdk), "dv": rel_err(vd.grad, rdv)}
+    bad = {name: e for name, e in errs.items() if not e < F32_TOL}
+    assert not bad, bad
