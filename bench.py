@@ -75,6 +75,10 @@ def parse_args():
                    help="run one small workload for an ncu capture (no JSON line): the 65,536-token window "
                         "fwd+bwd x3 with L2 flushes, the bf16 Linear 32768x768->768 fwd+bwd x3, or push PPR "
                         "(eps 1e-5) on a 40,000-node graph x2")
+    p.add_argument("--linear-calls", action="store_true",
+                   help="print the per-call device time of the fp32 Linear entry points at the config-2 "
+                        "window shape (14,252 rows; CUDA-graph replay of 20 back-to-back calls) instead "
+                        "of the JSON line")
     p.add_argument("--epoch-kernels", action="store_true",
                    help="print the per-kernel device time of one graph-replayed config-2 GT epoch "
                         "(torch.profiler over CUPTI) instead of the JSON line")
@@ -994,6 +998,65 @@ def epoch_kernel_table(args):
     trainer.dummy = None
 
 
+def linear_calls(rows=14252, n=20, reps=5):
+    """Per-call device time of ngt_linear_forward / _backward_input / _backward_weight on the GT
+    window's shapes, each call repeated `n` times inside one CUDA graph (no host launch cost)."""
+    from neutrongt_b200 import _lib
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    lib, ptr = _lib.lib(), _lib.ptr
+    g = torch.Generator(device=dev).manual_seed(0)
+    t = {(r, c): torch.randn(r, c, generator=g, device=dev) for r, c in
+         [(rows, 128), (rows, 256), (256, 128), (128, 256)]}
+    b = torch.randn(256, generator=g, device=dev)
+    out = {c: torch.empty(rows, c, device=dev) for c in (128, 256)}
+    dw, db = torch.empty(256, 256, device=dev), torch.empty(256, device=dev)
+    ws = {io: _lib.workspace(_lib.size_query(lib.ngt_linear_weight_workspace_size, rows, *io), dev)
+          for io in [(128, 128), (128, 256), (256, 128)]}
+    st = lambda: _lib.stream_of(b)
+    x1, x2 = t[(rows, 128)], t[(rows, 256)]
+    calls = {
+        "forward 128 -> 128": lambda: lib.ngt_linear_forward(rows, 128, 128, ptr(x1), ptr(t[(128, 256)]), ptr(b),
+                                                             ptr(out[128]), st()),
+        "forward 128 -> 256": lambda: lib.ngt_linear_forward(rows, 128, 256, ptr(x1), ptr(t[(256, 128)]), ptr(b),
+                                                             ptr(out[256]), st()),
+        "forward 256 -> 128": lambda: lib.ngt_linear_forward(rows, 256, 128, ptr(x2), ptr(t[(128, 256)]), ptr(b),
+                                                             ptr(out[128]), st()),
+        "input grad 128 <- 128": lambda: lib.ngt_linear_backward_input(rows, 128, 128, ptr(x1), ptr(t[(256, 128)]),
+                                                                       ptr(out[128]), st()),
+        "input grad 128 <- 256": lambda: lib.ngt_linear_backward_input(rows, 128, 256, ptr(x2), ptr(t[(256, 128)]),
+                                                                       ptr(out[128]), st()),
+        "input grad 256 <- 128": lambda: lib.ngt_linear_backward_input(rows, 256, 128, ptr(x1), ptr(t[(128, 256)]),
+                                                                       ptr(out[256]), st()),
+    }
+    for i, o in ws:
+        xin, gout = (x1 if i == 128 else x2), (x1 if o == 128 else x2)
+        calls[f"weight grad {o} x {i}"] = (lambda i=i, o=o, xin=xin, gout=gout: lib.ngt_linear_backward_weight(
+            rows, i, o, ptr(xin), ptr(gout), ptr(dw), ptr(db), ptr(ws[(i, o)]), ws[(i, o)].numel(), st()))
+    side = torch.cuda.Stream(device=dev)
+    for name, f in calls.items():
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                _lib.check(f(), name)
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(n):
+                f()
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        print(f"{name:24s} {e0.elapsed_time(e1) * 1000 / (reps * n):8.2f} us")
+        del graph
+
+
 def profile_case(case):
     """Small, fixed workloads for one-kernel ncu captures (profiles/*.md give the commands)."""
     dev = torch.device("cuda:0")
@@ -1041,6 +1104,9 @@ def main():
     args = parse_args()
     if args.profile_case:
         profile_case(args.profile_case)
+        return
+    if args.linear_calls:
+        linear_calls()
         return
     if args.epoch_kernels:
         epoch_kernel_table(args)

@@ -9,16 +9,18 @@
 //
 // Tiling: one CTA = 128 rows (the 128 TMEM lanes, MMA M = 128) x `ncta` output columns (MMA N,
 // padded to a multiple of 16, <= 256), the reduction dimension streamed in slices of 16 elements.
-// Thread 0 keeps STAGES - 1 slices in flight with 2-D TMA boxes of 64-byte rows: A as [128 rows]
+// One producer thread keeps STAGES - 1 slices in flight with 2-D TMA boxes of 64-byte rows: A as [128 rows]
 // [16], the forward's weight as [np rows][16], the input grad's weight (W [out, in], reduced over
-// `out`) as [16 k][np n], transposed by the threads.  All 256 threads split a landed slice into
+// `out`) as [16 k][np n], transposed by the threads.  The 512 splitter threads (16 warps: 256 measured up to 18 %
+// slower on the weight grad, as latency-bound as the split is) split a landed slice into
 // hi / lo operand buffers (two, alternating) in the no-swizzle K-major core-matrix layout: row r,
 // 16-byte chunk c at c * LBO + r * 16 with LBO = rows * 16 + 32, so the eight 16-byte stores of a
-// quarter-warp (two rows x four chunks) hit distinct banks.  Thread 0 issues the slice's 6 MMAs
+// quarter-warp (two rows x four chunks) hit distinct banks.  The producer issues the slice's 6 MMAs
 // and commits them to the buffer's mbarrier.  TMA writes through the async proxy, so the threads' proxy fence before the
 // MMAs waits only for their own split stores, never for loads in flight.  The epilogue reads the
-// accumulator with tcgen05.ld (warp w: lanes 32 (w % 4).., column groups alternating between
-// w < 4 and w >= 4) into a shared-memory tile, then stores whole rows (coalesced) with the bias.
+// accumulator with tcgen05.ld (warp w: lanes 32 (w % 4).., column groups dealt round-robin over the
+// warps of a lane quarter) into a shared-memory tile; one warp per row then stores it (coalesced)
+// with the bias.
 //
 // Every wait is bounded; a timeout is counted in a device word (ngt_linear_status), the CTA waits
 // (bounded) for its MMAs in flight, frees its TMEM and returns without storing.
@@ -41,11 +43,17 @@ namespace {
 
 constexpr int kM = 128;                        // rows per CTA = TMEM lanes = MMA M
 constexpr int kKS = 16;                        // reduction elements per slice (4 chunks of 16 B)
-constexpr int kThreads = 256;                  // splitter / epilogue threads (warps 0-7)
-constexpr int kThreadsAll = kThreads + 32;     // + warp 8: lane 0 issues the TMA loads and MMAs
+#ifndef NGT_LINEAR_TC_THREADS
+#define NGT_LINEAR_TC_THREADS 512
+#endif
+constexpr int kThreads = NGT_LINEAR_TC_THREADS;   // splitter / epilogue threads (warps 0 .. kThreads / 32 - 1)
+constexpr int kThreadsAll = kThreads + 32;       // + one warp: its lane 0 issues the TMA loads and MMAs
+static_assert(kThreads == 256 || kThreads == 512, "splitter threads");
+constexpr int kAItems = kM * 4 / kThreads;       // 16-byte A items per splitter thread and slice
+constexpr int kColParts = kThreads / kM;         // splitter threads per A column (weight grad)
 constexpr uint32_t kARaw = kM * kKS * 4;       // bytes of one A slice (raw, hi or lo): 8 KiB
 constexpr uint32_t kPolls = 1u << 26;
-constexpr int kMaxN = 256;
+constexpr int kMaxN = 256;                     // widest CTA output tile (the row stores take <= 64 vectors)
 constexpr uint32_t kSmemPerSm = 233472;        // 228 KiB per SM, 1 KiB of it reserved per CTA
 constexpr uint32_t kSmemPerCta = 232448;       // 227 KiB: the most one CTA may request
 constexpr int kMaxStages = 8;
@@ -110,7 +118,7 @@ __device__ __forceinline__ void split_slice(const TcArgs &p, const uint8_t *raw,
     const uint32_t lba = op_lbo(kM), lbb = op_lbo(p.np);
     uint8_t *a_hi = op, *a_lo = op + op_tile(kM), *b_hi = op + 2 * op_tile(kM), *b_lo = b_hi + op_tile(p.np);
 #pragma unroll
-    for (int i = 0; i < 2; i++) {
+    for (int i = 0; i < kAItems; i++) {
         const int idx = tid + i * kThreads;
         if (!p.trans_a) {
             const uint32_t o = (uint32_t)(idx & 3) * lba + (uint32_t)(idx >> 2) * 16u;
@@ -156,10 +164,10 @@ __global__ void __launch_bounds__(kThreadsAll, 2)
     uint8_t *ops = smem + STAGES * rawb;
     uint64_t *full = reinterpret_cast<uint64_t *>(ops + 2 * opb);   // [STAGES] slice landed (TMA bytes)
     uint64_t *done = full + STAGES;                                  // [2] MMAs of an operand buffer done
-    uint64_t *ready = done + 2;                                      // [2] operand buffer split (256 arrivals)
+    uint64_t *ready = done + 2;                                      // [2] operand buffer split (kThreads arrivals)
     uint32_t *slot = reinterpret_cast<uint32_t *>(ready + 2);
     const int ns = (int)((kc + kKS - 1) / kKS);
-    const bool producer = tid == kThreads;                           // warp 8, lane 0
+    const bool producer = tid == kThreads;                           // last warp, lane 0
 
     auto load = [&](int j) {   // slice j into stage j % STAGES
         uint8_t *raw = smem + (j % STAGES) * rawb;
@@ -269,7 +277,7 @@ __global__ void __launch_bounds__(kThreadsAll, 2)
     float *sdb = tile + kM * ldt;   // [kThreads] splitter sums of A (db only)
     if (p.db && tid < kThreads) sdb[tid] = asum;
     const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
-    for (int g = warp >> 2; warp < kThreads / 32 && g < ngrp; g += 2) {
+    for (int g = warp >> 2; warp < kThreads / 32 && g < ngrp; g += kThreads / 128) {
         float v[32];
         tc::ld32(taddr + (uint32_t)(g * 32), v);
         float4 *dst = reinterpret_cast<float4 *>(tile + (q * 32 + lane) * ldt + g * 32);
@@ -278,22 +286,41 @@ __global__ void __launch_bounds__(kThreadsAll, 2)
     }
     tc::fence_before_sync();
     __syncthreads();
+    // Row stores: warp w takes rows w, w + 9, ...; lane l the row's 16-byte vectors l and l + 32
+    // (nv <= 256), with the bias for those columns held in registers.
     const int vpr = nv / 4;   // 16-byte vectors per output row (N % 4 == 0)
     const int rows_here = (int)(p.M - m0 < kM ? p.M - m0 : kM);
-    for (int i = tid; i < rows_here * vpr; i += kThreadsAll) {
-        const int rr = i / vpr, c = (i - rr * vpr) * 4;
-        float4 o = *reinterpret_cast<const float4 *>(tile + rr * ldt + c);
-        if (p.bias) {
-            const float4 bb = __ldg(reinterpret_cast<const float4 *>(p.bias + n0 + c));
-            o.x += bb.x;
-            o.y += bb.y;
-            o.z += bb.z;
-            o.w += bb.w;
-        }
-        *reinterpret_cast<float4 *>(C + (m0 + rr) * p.N + n0 + c) = o;
+    float4 bias0 = make_float4(0.f, 0.f, 0.f, 0.f), bias1 = bias0;
+    if (p.bias) {
+        if (lane < vpr) bias0 = __ldg(reinterpret_cast<const float4 *>(p.bias + n0) + lane);
+        if (lane + 32 < vpr) bias1 = __ldg(reinterpret_cast<const float4 *>(p.bias + n0) + lane + 32);
     }
-    if (p.db && tid < kM && m0 + tid < p.M)   // columns m of threads tid and tid + 128
-        C[p.M * (int64_t)p.N + m0 + tid] = sdb[tid] + sdb[tid + kM];
+    for (int rr = warp; rr < rows_here; rr += kThreadsAll / 32) {
+        const float4 *trow = reinterpret_cast<const float4 *>(tile + rr * ldt);
+        float4 *crow = reinterpret_cast<float4 *>(C + (m0 + rr) * p.N + n0);
+        if (lane < vpr) {
+            float4 o = trow[lane];
+            o.x += bias0.x;
+            o.y += bias0.y;
+            o.z += bias0.z;
+            o.w += bias0.w;
+            crow[lane] = o;
+        }
+        if (lane + 32 < vpr) {
+            float4 o = trow[lane + 32];
+            o.x += bias1.x;
+            o.y += bias1.y;
+            o.z += bias1.z;
+            o.w += bias1.w;
+            crow[lane + 32] = o;
+        }
+    }
+    if (p.db && tid < kM && m0 + tid < p.M) {   // column m's partial sums: threads tid + j * 128
+        float t = sdb[tid];
+#pragma unroll
+        for (int j = 1; j < kColParts; j++) t += sdb[tid + j * kM];
+        C[p.M * (int64_t)p.N + m0 + tid] = t;
+    }
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
