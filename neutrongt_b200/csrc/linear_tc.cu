@@ -9,18 +9,24 @@
 //
 // Tiling: one CTA = 128 rows (the 128 TMEM lanes, MMA M = 128) x `ncta` output columns (MMA N,
 // padded to a multiple of 16, <= 256), the reduction dimension streamed in slices of 16 elements.
-// One producer thread keeps STAGES - 1 slices in flight with 2-D TMA boxes of 64-byte rows: A as [128 rows]
-// [16], the forward's weight as [np rows][16], the input grad's weight (W [out, in], reduced over
-// `out`) as [16 k][np n], transposed by the threads.  The 512 splitter threads (16 warps: 256 measured up to 18 %
-// slower on the weight grad, as latency-bound as the split is) split a landed slice into
-// hi / lo operand buffers (two, alternating) in the no-swizzle K-major core-matrix layout: row r,
-// 16-byte chunk c at c * LBO + r * 16 with LBO = rows * 16 + 32, so the eight 16-byte stores of a
-// quarter-warp (two rows x four chunks) hit distinct banks.  The producer issues the slice's 6 MMAs
-// and commits them to the buffer's mbarrier.  TMA writes through the async proxy, so the threads' proxy fence before the
-// MMAs waits only for their own split stores, never for loads in flight.  The epilogue reads the
-// accumulator with tcgen05.ld (warp w: lanes 32 (w % 4).., column groups dealt round-robin over the
-// warps of a lane quarter) into a shared-memory tile; one warp per row then stores it (coalesced)
-// with the bias.
+// One producer thread keeps STAGES - 1 slices in flight with 2-D TMA boxes of 64-byte rows: A as
+// [128 rows][16] (64-byte swizzle), the forward's weight as [np rows][16], the input grad's weight
+// (W [out, in], reduced over `out`) as [16 k][np n], transposed by the threads.  512 splitter
+// threads (16 warps) split a landed slice: A's hi / lo go to TMEM with tcgen05.st (A is the MMA's
+// TMEM operand: 32 columns per slice after the accumulator, four buffers), B's to one of four
+// shared-memory operand buffers in the no-swizzle K-major core-matrix layout (row r, 16-byte chunk
+// c at c * LBO + r * 16, LBO = rows * 16 + 32, so the eight 16-byte stores of a quarter-warp hit
+// distinct banks).  The producer issues the slice's 6 MMAs (A from TMEM, B from shared memory) and
+// commits them to the buffer's mbarrier.  TMA writes through the async proxy, so the splitters'
+// proxy fence before the MMAs waits only for their own stores, never for loads in flight.  The
+// epilogue reads the accumulator with tcgen05.ld (warp w: lanes 32 (w % 4).., column groups dealt
+// round-robin over the warps of a lane quarter) into a shared-memory tile; one warp per row then
+// stores it (coalesced) with the bias.
+//
+// Per-CTA clock traces of the 14,252 x 128 -> 128 forward: a slice costs ~1,100-1,600 cycles, set by
+// the splitters on the SM sub-partition that also runs the producer (its four splitter warps
+// finish last); hence the cheap split (cvt.rna, split4) and the producer's precomputed
+// descriptors.  A in TMEM halves the MMAs' shared-memory reads but measured no faster by itself.
 //
 // Every wait is bounded; a timeout is counted in a device word (ngt_linear_status), the CTA waits
 // (bounded) for its MMAs in flight, frees its TMEM and returns without storing.
@@ -43,14 +49,10 @@ namespace {
 
 constexpr int kM = 128;                        // rows per CTA = TMEM lanes = MMA M
 constexpr int kKS = 16;                        // reduction elements per slice (4 chunks of 16 B)
-#ifndef NGT_LINEAR_TC_THREADS
-#define NGT_LINEAR_TC_THREADS 512
-#endif
-constexpr int kThreads = NGT_LINEAR_TC_THREADS;   // splitter / epilogue threads (warps 0 .. kThreads / 32 - 1)
-constexpr int kThreadsAll = kThreads + 32;       // + one warp: its lane 0 issues the TMA loads and MMAs
-static_assert(kThreads == 256 || kThreads == 512, "splitter threads");
-constexpr int kAItems = kM * 4 / kThreads;       // 16-byte A items per splitter thread and slice
-constexpr int kColParts = kThreads / kM;         // splitter threads per A column (weight grad)
+constexpr int kThreads = 4 * kM;               // splitter / epilogue threads: one per A row and 4-wide k chunk
+constexpr int kThreadsAll = kThreads + 32;     // + one warp: its lane 0 issues the TMA loads and MMAs
+constexpr int kBufs = 4;                       // operand buffers (A in TMEM, B in shared memory)
+constexpr int kColParts = kThreads / kM;       // splitter threads per A row (the weight grad's column sums)
 constexpr uint32_t kARaw = kM * kKS * 4;       // bytes of one A slice (raw, hi or lo): 8 KiB
 constexpr uint32_t kPolls = 1u << 26;
 constexpr int kMaxN = 256;                     // widest CTA output tile (the row stores take <= 64 vectors)
@@ -72,15 +74,17 @@ struct TcArgs {
     float *C;
 };
 
-// Shared memory: STAGES raw slices (A, then B), two operand buffers (A hi, A lo, B hi, B lo),
-// then the mbarriers (STAGES "slice landed", 2 "MMAs done", 2 "operands split") and the TMEM address.
+// Shared memory: STAGES raw slices (A, then B), two B operand buffers (B hi, B lo), then the mbarriers
+// (STAGES "slice landed", 2 "MMAs done", 2 "operands split") and the TMEM address.  A's hi / lo
+// operands live in TMEM: two buffers of 32 columns (hi k 0..15, lo k 0..15) after the accumulator.
 __host__ __device__ constexpr uint32_t raw_bytes(int np) { return kARaw + (uint32_t)np * 64u; }
 // Operand tiles: K-chunk stride (LBO) rows * 16 + 32 bytes; a tile spans 3 LBO + rows * 16 bytes.
 __host__ __device__ constexpr uint32_t op_lbo(int rows) { return (uint32_t)rows * 16u + 32u; }
 __host__ __device__ constexpr uint32_t op_tile(int rows) { return 3 * op_lbo(rows) + (uint32_t)rows * 16u; }
-__host__ __device__ constexpr uint32_t op_bytes(int np) { return 2 * op_tile(kM) + 2 * op_tile(np); }
+__host__ __device__ constexpr uint32_t op_bytes(int np) { return 2 * op_tile(np); }
+__host__ __device__ constexpr uint32_t a_col(int np) { return (uint32_t)(np + 31) / 32u * 32u; }
 __host__ __device__ constexpr uint32_t smem_bytes(int np, int stages) {
-    return (uint32_t)stages * raw_bytes(np) + 2 * op_bytes(np) + 8 * (uint32_t)stages + 48;
+    return (uint32_t)stages * raw_bytes(np) + kBufs * op_bytes(np) + 8 * (uint32_t)(stages + 2 * kBufs) + 16;
 }
 
 // hi = x rounded to the nearest tf32 (ties away from zero; 10 mantissa bits), lo = x - hi (exact);
@@ -95,42 +99,68 @@ __device__ __forceinline__ void split1(float x, uint32_t &hi, float &lo) {
     hi = fin ? r : b;
     lo = fin ? x - __uint_as_float(hi) : 0.f;
 }
+__device__ __forceinline__ uint32_t tf32_rna(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return r;
+}
+// split1 of four values.  While all four are below 0x7F7FF000 in magnitude (so none is within
+// 2^-11 of FLT_MAX or infinite), hi is cvt.rna.tf32 — the same round-to-nearest, ties away, as
+// split1's bit arithmetic — and lo = x - hi: two instructions per value instead of split1's ten.
+// (A NaN among finite values takes the short path too; its hi and lo are NaN, as is its product.)
+__device__ __forceinline__ void split4(const float4 v, uint4 &h, float4 &l) {
+    const float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    if (__float_as_uint(m) < 0x7F7FF000u) {
+        h = make_uint4(tf32_rna(v.x), tf32_rna(v.y), tf32_rna(v.z), tf32_rna(v.w));
+        l = make_float4(v.x - __uint_as_float(h.x), v.y - __uint_as_float(h.y), v.z - __uint_as_float(h.z),
+                        v.w - __uint_as_float(h.w));
+    } else {
+        split1(v.x, h.x, l.x);
+        split1(v.y, h.y, l.y);
+        split1(v.z, h.z, l.z);
+        split1(v.w, h.w, l.w);
+    }
+}
 __device__ __forceinline__ void split_store(float4 v, uint8_t *hi, uint8_t *lo) {
     uint4 h;
     float4 l;
-    split1(v.x, h.x, l.x);
-    split1(v.y, h.y, l.y);
-    split1(v.z, h.z, l.z);
-    split1(v.w, h.w, l.w);
+    split4(v, h, l);
     *reinterpret_cast<uint4 *>(hi) = h;
     *reinterpret_cast<float4 *>(lo) = l;
 }
 
-// Splits a landed slice into operand buffer `op`.  Raw rows are 64 bytes (item idx = row idx / 4,
-// chunk idx % 4, at idx * 16: consecutive threads read consecutive bytes); operand chunk (r, c)
-// goes to c * LBO + r * 16.
-// With trans_a the raw A slice is row-major [16 k][128 m] and is transposed the same way (thread
-// tid always takes column m = tid % 128), and its four values per item are added into `asum` in a
-// fixed order (the bias gradient of the weight-grad GEMM).
-__device__ __forceinline__ void split_slice(const TcArgs &p, const uint8_t *raw, uint8_t *op, float &asum) {
+// Splits a landed slice: A into the TMEM buffer at column `ta` of this thread's lane quarter, B
+// into shared operand buffer `op`.  A: thread (m = tid % 128, c = tid / 128) takes row m's four
+// reduction elements 4c .. 4c + 3 (warp tid / 32 sits on lane quarter m / 32 as tcgen05.st needs):
+// hi to columns 4c.., lo to 16 + 4c..  The forward / input-grad raw A slice is [128 rows][16] with
+// the TMA's 64-byte swizzle (chunk c of row m at chunk c ^ ((m >> 1) & 3), so the eight rows of a
+// quarter-warp's 16-byte loads hit distinct banks); the weight grad's is row-major [16 k][128 m]
+// (thread tid always takes column m = tid % 128) and its four values are also added into `asum` in
+// a fixed order (the bias gradient of the weight-grad GEMM).  B: raw rows are 64 bytes (item idx =
+// row idx / 4, chunk idx % 4, at idx * 16: consecutive threads read consecutive bytes); operand
+// chunk (r, c) goes to c * LBO + r * 16.
+__device__ __forceinline__ void split_slice(const TcArgs &p, const uint8_t *raw, uint8_t *op, uint32_t ta,
+                                            float &asum) {
     const int tid = threadIdx.x;
     const uint8_t *rb = raw + kARaw;
-    const uint32_t lba = op_lbo(kM), lbb = op_lbo(p.np);
-    uint8_t *a_hi = op, *a_lo = op + op_tile(kM), *b_hi = op + 2 * op_tile(kM), *b_lo = b_hi + op_tile(p.np);
-#pragma unroll
-    for (int i = 0; i < kAItems; i++) {
-        const int idx = tid + i * kThreads;
+    const uint32_t lbb = op_lbo(p.np);
+    uint8_t *b_hi = op, *b_lo = op + op_tile(p.np);
+    {
+        const int m = tid % kM, c = tid / kM;
+        float4 v;
         if (!p.trans_a) {
-            const uint32_t o = (uint32_t)(idx & 3) * lba + (uint32_t)(idx >> 2) * 16u;
-            split_store(*reinterpret_cast<const float4 *>(raw + idx * 16), a_hi + o, a_lo + o);
-        } else {   // raw row-major [16 k][128 m]: column m, rows 4c .. 4c + 3
-            const int m = idx % kM, c = idx / kM;
+            v = *reinterpret_cast<const float4 *>(raw + m * 64 + ((c ^ ((m >> 1) & 3)) << 4));
+        } else {
             const float *colp = reinterpret_cast<const float *>(raw) + (4 * c) * kM + m;
-            const float4 v = make_float4(colp[0], colp[kM], colp[2 * kM], colp[3 * kM]);
+            v = make_float4(colp[0], colp[kM], colp[2 * kM], colp[3 * kM]);
             asum += ((v.x + v.y) + v.z) + v.w;
-            const uint32_t o = (uint32_t)c * lba + (uint32_t)m * 16u;
-            split_store(v, a_hi + o, a_lo + o);
         }
+        uint4 h;
+        float4 l;
+        split4(v, h, l);
+        tc::st4_nowait(ta + 4 * c, h.x, h.y, h.z, h.w);
+        tc::st4_nowait(ta + 16 + 4 * c, __float_as_uint(l.x), __float_as_uint(l.y), __float_as_uint(l.z),
+                       __float_as_uint(l.w));
     }
     const int items = p.np * 4;
     for (int idx = tid; idx < items; idx += kThreads) {
@@ -162,10 +192,10 @@ __global__ void __launch_bounds__(kThreadsAll, 2)
     float *const C = p.C + (int64_t)blockIdx.z * p.c_stride;
     const uint32_t rawb = raw_bytes(p.np), opb = op_bytes(p.np);
     uint8_t *ops = smem + STAGES * rawb;
-    uint64_t *full = reinterpret_cast<uint64_t *>(ops + 2 * opb);   // [STAGES] slice landed (TMA bytes)
+    uint64_t *full = reinterpret_cast<uint64_t *>(ops + kBufs * opb);   // [STAGES] slice landed (TMA bytes)
     uint64_t *done = full + STAGES;                                  // [2] MMAs of an operand buffer done
-    uint64_t *ready = done + 2;                                      // [2] operand buffer split (kThreads arrivals)
-    uint32_t *slot = reinterpret_cast<uint32_t *>(ready + 2);
+    uint64_t *ready = done + kBufs;                                  // [kBufs] operand buffer split (kThreads arrivals)
+    uint32_t *slot = reinterpret_cast<uint32_t *>(ready + kBufs);
     const int ns = (int)((kc + kKS - 1) / kKS);
     const bool producer = tid == kThreads;                           // last warp, lane 0
 
@@ -187,7 +217,7 @@ __global__ void __launch_bounds__(kThreadsAll, 2)
     int loaded = 0, issued = 0;   // producer's counts
     if (producer) {
         for (int st = 0; st < STAGES; st++) tc::mbar_init(&full[st], 1);
-        for (int b = 0; b < 2; b++) {
+        for (int b = 0; b < kBufs; b++) {
             tc::mbar_init(&done[b], 1);
             tc::mbar_init(&ready[b], kThreads);
         }
@@ -206,46 +236,51 @@ __global__ void __launch_bounds__(kThreadsAll, 2)
         // Slice s - 1's stage is free once every splitter arrived on ready for slice s - 1 (waited
         // below in the previous iteration), so slice s + STAGES - 1 can take it.
         const uint32_t idesc = tc::idesc_tf32(kM, p.np);
-        const uint32_t a_lbo = op_lbo(kM), b_lbo = op_lbo(p.np);
+        const uint32_t b_lbo = op_lbo(p.np);
+        // B descriptors: buffer 0's hi tile once; the others differ only in the start-address field
+        // (address >> 4, far below its 14-bit limit), so one 64-bit add selects buffer, lo / hi and k step.
+        const uint64_t desc0 = tc::smem_desc(tc::smem_addr(ops), b_lbo, 128);
+        const uint64_t step_buf = opb >> 4, step_lo = op_tile(p.np) >> 4, step_k = (2u * b_lbo) >> 4;
         for (int s = 0; s < ns; s++) {
             if (loaded < ns) load(loaded++);
-            if (!tc::mbar_wait_bounded(&ready[s & 1], (uint32_t)(s >> 1) & 1u, kPolls)) {
+            if (!tc::mbar_wait_bounded(&ready[s % kBufs], (uint32_t)(s / kBufs) & 1u, kPolls)) {
                 ok = false;
                 break;
             }
             tc::fence_after_sync();
-            const uint32_t a_hi = tc::smem_addr(ops + (s & 1) * opb), a_lo = a_hi + op_tile(kM),
-                           b_hi = a_hi + 2 * op_tile(kM), b_lo = b_hi + op_tile(p.np);
+            const uint32_t a_hi = tmem + a_col(p.np) + 32u * (uint32_t)(s % kBufs), a_lo = a_hi + 16u;
+            const uint64_t dbuf = desc0 + (uint64_t)(s % kBufs) * step_buf;
 #pragma unroll
-            for (int kk = 0; kk < kKS / 8; kk++) {   // K = 8 tf32 = two 16-byte chunks per MMA
-                const uint32_t oa = (uint32_t)kk * 2u * a_lbo, ob = (uint32_t)kk * 2u * b_lbo;
-                const uint64_t dah = tc::smem_desc(a_hi + oa, a_lbo, 128), dal = tc::smem_desc(a_lo + oa, a_lbo, 128);
-                const uint64_t dbh = tc::smem_desc(b_hi + ob, b_lbo, 128), dbl = tc::smem_desc(b_lo + ob, b_lbo, 128);
-                tc::mma_tf32(tmem, dal, dbh, idesc, (s > 0 || kk > 0) ? 1u : 0u);
-                tc::mma_tf32(tmem, dah, dbl, idesc, 1u);
-                tc::mma_tf32(tmem, dah, dbh, idesc, 1u);
+            for (int kk = 0; kk < kKS / 8; kk++) {   // K = 8 tf32 = 8 TMEM columns of A, two 16-byte chunks of B
+                const uint64_t dbh = dbuf + (uint64_t)kk * step_k, dbl = dbh + step_lo;
+                tc::mma_tf32_ts(tmem, a_lo + 8u * kk, dbh, idesc, (s > 0 || kk > 0) ? 1u : 0u);
+                tc::mma_tf32_ts(tmem, a_hi + 8u * kk, dbl, idesc, 1u);
+                tc::mma_tf32_ts(tmem, a_hi + 8u * kk, dbh, idesc, 1u);
             }
-            tc::commit(&done[s & 1]);
+            tc::commit(&done[s % kBufs]);
             issued = s + 1;
         }
     } else if (tid < kThreads) {   // splitters: no CTA-wide barrier per slice
+        const uint32_t ta = tmem + ((uint32_t)((warp & 3) * 32) << 16) + a_col(p.np);   // A buffer 0, my lanes
         for (int s = 0; s < ns; s++) {
-            const int b = s & 1;
+            const int b = s % kBufs;
             bool w = tc::mbar_wait_bounded(&full[s % STAGES], (uint32_t)(s / STAGES) & 1u, kPolls);
-            if (w && s >= 2)   // operand buffer b was last read by the MMAs of slice s - 2
-                w = tc::mbar_wait_bounded(&done[b], (uint32_t)((s - 2) >> 1) & 1u, kPolls);
-            if (!w) {
+            if (w && s >= kBufs)   // operand buffer b was last read by the MMAs of slice s - kBufs
+                w = tc::mbar_wait_bounded(&done[b], (uint32_t)((s - kBufs) / kBufs) & 1u, kPolls);
+            if (!__all_sync(0xffffffffu, w)) {   // warp-uniform: tcgen05.st below is .sync.aligned
                 ok = false;
                 break;
             }
-            split_slice(p, smem + (s % STAGES) * rawb, ops + b * opb, asum);
-            tc::fence_smem_for_async();
+            split_slice(p, smem + (s % STAGES) * rawb, ops + b * opb, ta + 32u * (uint32_t)b, asum);
+            tc::wait_st();                 // A's TMEM stores done,
+            tc::fence_smem_for_async();    // B's shared stores visible to the MMAs,
+            tc::fence_before_sync();       // ordered before the arrival
             tc::mbar_arrive(&ready[b]);
         }
     }
     {
         const int last = ns - 1;
-        const bool w = ok && tc::mbar_wait_bounded(&done[last & 1], (uint32_t)(last >> 1) & 1u, kPolls);
+        const bool w = ok && tc::mbar_wait_bounded(&done[last % kBufs], (uint32_t)(last / kBufs) & 1u, kPolls);
         ok = !__syncthreads_or(!w);
     }
     if (!ok) {
@@ -256,7 +291,7 @@ __global__ void __launch_bounds__(kThreadsAll, 2)
             for (int j = loaded - STAGES < 0 ? 0 : loaded - STAGES; j < loaded; j++)
                 tc::mbar_wait_bounded(&full[j % STAGES], (uint32_t)(j / STAGES) & 1u, kPolls);   // TMA in flight
             if (issued > 0)   // and the MMAs in flight end before the TMEM is freed (bounded)
-                tc::mbar_wait_bounded(&done[(issued - 1) & 1], (uint32_t)((issued - 1) >> 1) & 1u, kPolls);
+                tc::mbar_wait_bounded(&done[(issued - 1) % kBufs], (uint32_t)((issued - 1) / kBufs) & 1u, kPolls);
         }
         tc::fence_before_sync();
         __syncthreads();
@@ -355,7 +390,8 @@ void bind_primary_context() {
 }
 
 // Row-major fp32 [rows, cols] (cols % 4 == 0) as a 2-D map with box (box_cols, box_rows).
-int map2d(CUtensorMap *m, const float *base, int64_t rows, int cols, int box_cols, int box_rows) {
+int map2d(CUtensorMap *m, const float *base, int64_t rows, int cols, int box_cols, int box_rows,
+          CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE) {
     EncodeTiled enc = encoder();
     if (!enc) return NGT_ERR_CUDA;
     const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
@@ -363,7 +399,7 @@ int map2d(CUtensorMap *m, const float *base, int64_t rows, int cols, int box_col
     const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box, estr,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? NGT_OK : NGT_ERR_CUDA;
 }
@@ -380,9 +416,10 @@ int sm_count_tc() {
     return n;
 }
 
+// TMEM: the accumulator (np columns) and A's two 32-column operand buffers, as a power of two.
 uint32_t tmem_cols_for(int np) {
     uint32_t c = 32;
-    while (c < (uint32_t)np) c <<= 1;
+    while (c < a_col(np) + 32u * kBufs) c <<= 1;
     return c;
 }
 
@@ -397,8 +434,10 @@ struct TcPlan {
 // per SM, and each half loads and splits the whole A tile again.
 TcPlan tc_plan(int64_t gm, int N, int sms) {
     const int np = (N + 15) / 16 * 16;
+    const uint32_t tmem_per_sm = 512u / tmem_cols_for(np);
     for (int stages = kMaxStages; stages >= 3; stages--) {
-        const uint32_t per_sm = kSmemPerSm / (smem_bytes(np, stages) + 1024);
+        uint32_t per_sm = kSmemPerSm / (smem_bytes(np, stages) + 1024);
+        if (per_sm > tmem_per_sm) per_sm = tmem_per_sm;
         if (per_sm >= 1 && gm <= (int64_t)sms * (per_sm > 2 ? 2 : per_sm)) return {1, stages};
     }
     return {1, 3};
@@ -433,7 +472,7 @@ int launch_stages(const CUtensorMap &ma, const CUtensorMap &mw, const TcArgs &p,
 int launch_plan(const CUtensorMap &ma, const CUtensorMap &mw, const TcArgs &p, dim3 grid, int stages,
                 cudaStream_t st) {
     if ((size_t)kM * (((p.ncta + 31) / 32) * 32 + 4) * 4 + (size_t)kThreads * 4 >
-        (size_t)stages * raw_bytes(p.np) + 2 * op_bytes(p.np))
+        (size_t)stages * raw_bytes(p.np) + kBufs * op_bytes(p.np))
         return NGT_ERR_UNSUPPORTED;
     switch (stages) {
     case 8: return launch_stages<8>(ma, mw, p, grid, st);
@@ -470,7 +509,7 @@ int launch_linear_tc(int64_t M, int K, int N, const float *A, const float *W, bo
     p.C = C;
     CUtensorMap ma, mw;
     bind_primary_context();
-    int rc = map2d(&ma, A, M, K, kKS, kM);                     // [128 rows][16] boxes
+    int rc = map2d(&ma, A, M, K, kKS, kM, CU_TENSOR_MAP_SWIZZLE_64B);   // [128 rows][16] boxes, 64-byte swizzle
     if (rc == NGT_OK)                                            // [16 k][np n] or [np rows][16]
         rc = trans_w ? map2d(&mw, W, K, N, p.np, kKS) : map2d(&mw, W, N, K, kKS, p.np);
     if (rc != NGT_OK) return rc;

@@ -74,6 +74,17 @@ __device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
         ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]^T for tf32 operands (K = 8 per instruction: A is 8 columns of the
+// 128 lanes, one tf32 per column), one thread.
+__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}\n"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
 // Arrive on an mbarrier when all previously issued tcgen05.mma of this thread complete.
 __device__ __forceinline__ void commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
@@ -146,6 +157,41 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, int c0,
 }
 
 // Bounded wait: returns false if the phase did not complete within `limit` polls.
+// Non-blocking probe of an mbarrier phase (never suspends the thread).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// try_wait with an explicit suspend-time hint in nanoseconds.
+__device__ __forceinline__ bool mbar_try_wait_ns(uint64_t *bar, uint32_t parity, uint32_t ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool mbar_spin_bounded(uint64_t *bar, uint32_t parity, uint32_t limit) {
+    for (uint32_t i = 0; i < limit; i++)
+        if (mbar_test_wait(bar, parity)) return true;
+    return false;
+}
+__device__ __forceinline__ bool mbar_wait_ns_bounded(uint64_t *bar, uint32_t parity, uint32_t ns, uint32_t limit) {
+    for (uint32_t i = 0; i < limit; i++)
+        if (mbar_try_wait_ns(bar, parity, ns)) return true;
+    return false;
+}
+
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint32_t limit) {
     for (uint32_t i = 0; i < limit; i++)
         if (mbar_try_wait(bar, parity)) return true;
@@ -237,6 +283,12 @@ __device__ __forceinline__ void st16_nowait(uint32_t taddr, const uint32_t (&w)[
         ::"r"(taddr), "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7]),
           "r"(w[8]), "r"(w[9]), "r"(w[10]), "r"(w[11]), "r"(w[12]), "r"(w[13]), "r"(w[14]), "r"(w[15])
         : "memory");
+}
+
+// Four consecutive 32-bit columns of this thread's TMEM lane (no wait: tcgen05.wait::st follows).
+__device__ __forceinline__ void st4_nowait(uint32_t taddr, uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};"
+                 ::"r"(taddr), "r"(w0), "r"(w1), "r"(w2), "r"(w3) : "memory");
 }
 
 // One fp32 column of this thread's TMEM lane.
