@@ -731,9 +731,9 @@ def bench_ppr_large(args, rank, world, dev):
     deg = (rp[1:] - rp[:-1]).double()
     s0, s1 = balanced_ranges(deg.cpu() + 64.0, world)[rank]
     csr = {"rowptr": rp, "col": col}
-    # warm-up on the timed range itself: its per-slot workspace is then a cached block, not a fresh
-    # multi-GB allocation inside the timed call (after the earlier sections' frees, that allocation
-    # measured up to 0.07 s on a 2-GPU run)
+    # warm-up on the timed range itself, so the per-slot workspace (GBs) is already a cached block
+    # when the timed call runs (after a 500-seed warm-up a 2-GPU run timed this call at 0.087 s;
+    # repeated full-range calls take 0.011 s on the slower rank)
     personal_pagerank_torch_geometric(None, 0.15, topk=10, eps=1e-4, device=dev, csr_data=csr, source_start=s0,
                                       source_end=s1)
     st = {}
