@@ -34,6 +34,10 @@ namespace {
 
 constexpr int kPushThreads = 256;
 constexpr int kPushWarps = kPushThreads / 32;
+#ifndef NGT_PUSH_U
+#define NGT_PUSH_U 4
+#endif
+constexpr int kPushU = NGT_PUSH_U;   // 32-neighbour chunks per step of a push (loads in flight together)
 
 struct PushWs {
     double *r, *pv;
@@ -149,33 +153,62 @@ __global__ void __launch_bounds__(kPushThreads)
             if (e == b) continue;
             read += (unsigned long long)(e - b);
             const double val = __ddiv_rn(__dmul_rn(keep, res), (double)(e - b));
-            for (int64_t q0 = b; q0 < e; q0 += 32) {
-                const int64_t q = q0 + lane;
-                const bool act = q < e;
-                const int32_t v = act ? col[q] : -1;
-                const int32_t prev = __shfl_up_sync(full, v, 1);
-                const bool dup = __any_sync(full, act && lane > 0 && v == prev);
-                if (!dup) {
-                    bool fresh = false, push = false;
-                    if (act) {
-                        const uint8_t f = fl[v];
-                        const double rv = (f & kTouched) ? __dadd_rn(r[v], val) : val;
-                        r[v] = rv;
-                        fresh = !(f & kTouched);
-                        const double thr = __dmul_rn(alpha_eps, (double)(rowptr[v + 1] - rowptr[v]));
-                        push = rv >= thr && !(f & kOnStack);
-                        fl[v] = (uint8_t)(f | kTouched | (push ? kOnStack : 0));
+            for (int64_t q0 = b; q0 < e; q0 += 32 * kPushU) {
+                // kPushU chunks of 32 neighbours per step: lane l takes q0 + 32 j + l.  The loads of
+                // all chunks are issued before any update (the neighbours are distinct, so no chunk
+                // reads what another writes), then the appends run chunk by chunk in CSR order.
+                int32_t v[kPushU];
+                bool act[kPushU];
+                bool d = false;
+#pragma unroll
+                for (int j = 0; j < kPushU; j++) {
+                    const int64_t q = q0 + 32 * j + lane;
+                    act[j] = q < e;
+                    v[j] = act[j] ? col[q] : -1;
+                }
+#pragma unroll
+                for (int j = 0; j < kPushU; j++) {   // repeated neighbours: equal CSR neighbours
+                    const int32_t prev = __shfl_up_sync(full, v[j], 1);
+                    if (act[j] && lane > 0 && v[j] == prev) d = true;
+                    if (j > 0) {
+                        const int32_t last = __shfl_sync(full, v[j - 1], 31);
+                        if (act[j] && lane == 0 && v[j] == last) d = true;
                     }
-                    const unsigned bf = __ballot_sync(full, fresh), bp = __ballot_sync(full, push);
-                    if (fresh) touched[nt + __popc(bf & lt)] = v;
-                    if (push) stack[sp + __popc(bp & lt)] = v;
-                    nt += __popc(bf);
-                    sp += __popc(bp);
+                }
+                if (!__any_sync(full, d)) {
+                    uint8_t f[kPushU];
+                    double thr[kPushU];
+#pragma unroll
+                    for (int j = 0; j < kPushU; j++) {
+                        f[j] = act[j] ? fl[v[j]] : (uint8_t)0;
+                        thr[j] = act[j] ? __dmul_rn(alpha_eps, (double)(rowptr[v[j] + 1] - rowptr[v[j]])) : 0.0;
+                    }
+                    bool fresh[kPushU], push[kPushU];
+#pragma unroll
+                    for (int j = 0; j < kPushU; j++) {
+                        fresh[j] = false;
+                        push[j] = false;
+                        if (act[j]) {
+                            const double rv = (f[j] & kTouched) ? __dadd_rn(r[v[j]], val) : val;
+                            r[v[j]] = rv;
+                            fresh[j] = !(f[j] & kTouched);
+                            push[j] = rv >= thr[j] && !(f[j] & kOnStack);
+                            fl[v[j]] = (uint8_t)(f[j] | kTouched | (push[j] ? kOnStack : 0));
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < kPushU; j++) {
+                        const unsigned bf = __ballot_sync(full, fresh[j]), bp = __ballot_sync(full, push[j]);
+                        if (fresh[j]) touched[nt + __popc(bf & lt)] = v[j];
+                        if (push[j]) stack[sp + __popc(bp & lt)] = v[j];
+                        nt += __popc(bf);
+                        sp += __popc(bp);
+                    }
                 } else {
                     __syncwarp();
                     int sp2 = sp, nt2 = nt;
                     if (lane == 0)
-                        for (int64_t qq = q0; qq < e && qq < q0 + 32; qq++)
+                        for (int64_t qq = q0; qq < e && qq < q0 + 32 * kPushU; qq++)
                             relax_one(col[qq], val, alpha_eps, rowptr, r, fl, stack, touched, sp2, nt2);
                     sp = __shfl_sync(full, sp2, 0);
                     nt = __shfl_sync(full, nt2, 0);
