@@ -35,7 +35,7 @@ namespace {
 constexpr int kPushThreads = 256;
 constexpr int kPushWarps = kPushThreads / 32;
 #ifndef NGT_PUSH_U
-#define NGT_PUSH_U 4
+#define NGT_PUSH_U 8
 #endif
 constexpr int kPushU = NGT_PUSH_U;   // 32-neighbour chunks per step of a push (loads in flight together)
 
