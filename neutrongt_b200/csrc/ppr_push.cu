@@ -21,9 +21,11 @@
 // dense per-node arrays in the workspace (r, p values, flags) plus its stack, p list and the list
 // of touched nodes, through which the seed clears the flags it set (a value is only read when its
 // flag says it was written, so only the flags need clearing).  A push spreads one adjacency row
-// over the lanes, 32 neighbours per step: the neighbours of a row are distinct (columns ascend,
-// so a repeated edge shows as equal neighbouring lanes; such a step runs on lane 0 alone), so
-// their updates commute, and the stack appends are placed with a ballot in lane (= CSR) order.
+// over the lanes, kPushU chunks of 32 neighbours per step with all their loads issued before any
+// update: the neighbours of a row are distinct (columns ascend, so a repeated edge shows as equal
+// neighbouring entries; a step holding one runs on lane 0 alone), so their updates commute, and
+// the stack appends are placed with a ballot per chunk in lane (= CSR) order.  A hub seed's push
+// is one warp's walk over its row, so several chunks per step cut the tail its load latency sets.
 // Every operation is a separate IEEE fp64 rounding (__dmul_rn / __ddiv_rn / __dadd_rn) in the
 // method's own order, so the result is bit-identical to the sequential method (the CPU
 // restatement in oracle/push_oracle.c).
