@@ -25,7 +25,7 @@ The same JSON line carries:
   ppr          APPNP PPR + top-k over every seed of the 169,343-node graph (seed ranges balanced
                by degree across ranks), push PPR (eps 1e-4, top-10) on the 232,965-node graph with
                114.6 M directed edges, APPNP top-4 on the 2,449,029-node graph with 123.7 M
-               directed edges;
+               directed edges, and `csr_spgemm` on the APPNP product (PPR state x D^-1 A);
   clocks       nvidia-smi samples taken during the timed region.
 
 `--impl reference` times the reference's CPU algorithm for the same metric instead
@@ -714,6 +714,55 @@ def bench_ppr(args, rank, world, dev):
         touched = st["edges_touched"] / sample
         out["adjacency_entries_per_seed"] = touched
         out["achieved_gbs_adjacency_model"] = touched * n * 4 / t / 1e9
+    out["spgemm"] = bench_spgemm(args, rank, world, dev, rowptr, col, ei, val, s0, s1)
+    return out
+
+
+def bench_spgemm(args, rank, world, dev, rowptr, col, ei, val, s0, s1):
+    """`csr_spgemm` (the cuSPARSE extension's drop-in) on the product the APPNP step forms: C = S P,
+    S = this rank's PPR state (the rows of seeds s0..s1 with their top-8 entries, from the APPNP run
+    above), P = D^-1 A of the 169,343-node graph (fp32 values 1 / deg(row))."""
+    from neutrongt_b200.spgemm import csr_spgemm
+    peak, peak_kind = measured_hbm_peak()
+    rp_b, col_b = rowptr.to(dev), col.to(dev)
+    deg = rp_b[1:] - rp_b[:-1]
+    val_b = (1.0 / deg.clamp_min(1).to(torch.float32)).repeat_interleave(deg)
+    m = s1 - s0
+    rows = ei[0] - s0
+    order = torch.argsort(rows, stable=True)
+    rows, col_a, val_a = rows[order], ei[1][order].contiguous(), val[order].to(torch.float32).contiguous()
+    rp_a = torch.zeros(m + 1, dtype=torch.long, device=dev)
+    rp_a[1:] = torch.cumsum(torch.bincount(rows, minlength=m), 0)
+    call = lambda: csr_spgemm(rp_a, col_a, val_a, rp_b, col_b, val_b)
+    call()
+    (c_rp, c_col, c_val), t = _timed_call(call, world)
+    nnz_a, nnz_c = col_a.numel(), c_col.numel()
+    gathered = int(deg[col_a].sum())   # B entries read: the rows of B that A's entries select
+    # algorithmic bytes: A (rowptr 8, col 8 + val 4 per entry, int64 inputs), B's two row pointers per
+    # A entry (16) and its selected entries (col 8 + val 4), C written (rowptr 8, col 8 + val 4)
+    nbytes = 8 * (m + 1) + 12 * nnz_a + 16 * nnz_a + 12 * gathered + 8 * (m + 1) + 12 * nnz_c
+    achieved = allreduce_sum(float(nbytes), world) / t / 1e9
+    out = {"workload": "C = S P: S = the APPNP PPR state of every seed of the 169,343-node graph (top-8 "
+                       "entries per row), P = D^-1 A (2,332,486 entries); fp32 values, int64 CSR in and out",
+           "seconds": t, "rows_per_s": allreduce_sum(float(m), world) / t,
+           "a_entries": int(allreduce_sum(float(nnz_a), world)), "b_entries_gathered":
+               int(allreduce_sum(float(gathered), world)), "c_entries": int(allreduce_sum(float(nnz_c), world)),
+           "scaling": "strong (rows of S split with the PPR seed ranges)",
+           "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                        "frac": achieved / peak if peak else None, "peak_kind": peak_kind,
+                        "note": "no-reuse algorithmic bytes (A, B's selected rows, C); B (28 MB) is L2-resident"}}
+    if rank == 0 and not args.skip_cpu:
+        from oracle import spgemm as ospgemm
+        sample = 2000
+        ra = rp_a[:sample + 1].cpu()
+        ca, va = col_a[:int(ra[-1])].cpu(), val_a[:int(ra[-1])].cpu()
+        rb, cb, vb = rp_b.cpu(), col_b.cpu(), val_b.cpu()
+        t0 = time.perf_counter()
+        ospgemm.csr_spgemm(ra, ca, va, rb, cb, vb)
+        tc = time.perf_counter() - t0
+        out["cpu_baseline"] = {"value": sample / tc, "unit": "rows/s", "cores": 1, "kind": "port",
+                               "sample": f"rows 0..{sample - 1} of S (the hub seeds), the row-wise product "
+                                         "restated in Python (oracle/spgemm.py)"}
     return out
 
 

@@ -13,9 +13,13 @@
 // the order of the row-wise product SciPy's csr_matmat uses, bit for bit.  A step whose 32 columns
 // hold a repeated column runs on lane 0 alone, in order.
 // Two launches: a symbolic pass counts each row's columns (scanned into C's row pointer), then a
-// numeric pass accumulates, sorts the row's touched columns (warp bitonic sort, in shared memory
-// up to 1024 columns, else in the slot's global scratch) and writes them with their values.  The
+// numeric pass accumulates, orders the row's touched columns and writes them with their values.
+// Ordering: a warp bitonic sort in shared memory up to 4,096 columns; a longer row is, when B's
+// rows ascend and A's row has <= 32 entries, one ascending run per A entry, merged in pairwise
+// merge-path rounds (O(nt log runs)); otherwise a bitonic sort in the slot's global scratch.  The
 // slot arrays are reset through the touched list, so a call costs O(products), not O(rows x n).
+#include <mutex>
+
 #include "scan_sort.cuh"
 
 namespace ngt {
@@ -23,12 +27,15 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kSmemCols = 1024;   // per warp, for rows sorted in shared memory
+constexpr int kSmemCols = 4096;   // per warp, for rows sorted in shared memory (dynamic: 128 KiB per CTA)
+constexpr int kMaxRuns = 32;      // A entries per row whose ascending runs the merge path takes (one lane each)
+constexpr size_t kNumericSmem = sizeof(int32_t) * (size_t)kWarps * (kSmemCols + kMaxRuns + 1);
 
 struct SpgemmWs {
     float *acc;
     uint8_t *flag;
     int32_t *touched;          // [slots][tcap]
+    int32_t *merged;           // [slots][tcap]: the other buffer of the run merges
     int64_t tcap;              // power of two >= n
     int64_t *counts;           // [m + 1]
     int64_t *partials;
@@ -59,6 +66,7 @@ SpgemmWs carve_spgemm(void *base, int64_t m, int64_t n, int64_t slots) {
     w.acc = reinterpret_cast<float *>(take(sizeof(float) * (size_t)n * (size_t)slots));
     w.flag = reinterpret_cast<uint8_t *>(take((size_t)n * (size_t)slots));
     w.touched = reinterpret_cast<int32_t *>(take(sizeof(int32_t) * (size_t)w.tcap * (size_t)slots));
+    w.merged = reinterpret_cast<int32_t *>(take(sizeof(int32_t) * (size_t)w.tcap * (size_t)slots));
     w.used = off;
     return w;
 }
@@ -83,13 +91,60 @@ __device__ __forceinline__ void warp_bitonic(int32_t *arr, int P, int lane) {
     }
 }
 
+// out[0, la + lb) = merge of the ascending, mutually distinct a[0, la) and b[0, lb) by one warp:
+// lane l writes outputs [l L / 32, (l + 1) L / 32), its start found by a merge-path binary search.
+__device__ __forceinline__ void warp_merge(const int32_t *a, int la, const int32_t *b, int lb, int32_t *out, int lane) {
+    const int L = la + lb;
+    const int d0 = (int)((int64_t)L * lane / 32), d1 = (int)((int64_t)L * (lane + 1) / 32);
+    int lo = d0 - lb > 0 ? d0 - lb : 0, hi = d0 < la ? d0 : la;
+    while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (a[mid] < b[d0 - 1 - mid]) lo = mid + 1;
+        else hi = mid;
+    }
+    int i = lo, j = d0 - lo;
+    for (int d = d0; d < d1; d++) {
+        const bool ta = j >= lb || (i < la && a[i] < b[j]);
+        out[d] = ta ? a[i++] : b[j++];
+    }
+}
+
+// The touched list of a row is the concatenation of one ascending run per A entry (the fresh
+// columns of B's row j, in B's order) when B's rows ascend: pairwise merge rounds over the runs
+// (starts in rs[0, k), rs[k] = nt) between `src` and `dst`; returns the buffer holding the result.
+__device__ int32_t *merge_runs(int32_t *src, int32_t *dst, int32_t *rs, int k, int lane) {
+    while (k > 1) {
+        for (int r = 0; r < k; r += 2) {
+            const int a0 = rs[r], a1 = rs[r + 1];
+            if (r + 1 == k) {
+                for (int t = a0 + lane; t < a1; t += 32) dst[t] = src[t];
+            } else {
+                const int a2 = rs[r + 2];
+                warp_merge(src + a0, a1 - a0, src + a1, a2 - a1, dst + a0, lane);
+            }
+        }
+        __syncwarp();
+        const int nk = (k + 1) >> 1;
+        int v = 0;
+        if (lane <= nk) v = rs[lane < nk ? 2 * lane : k];   // new starts: every other run, then the end
+        __syncwarp();
+        if (lane <= nk) rs[lane] = v;
+        __syncwarp();
+        k = nk;
+        int32_t *t = src;
+        src = dst;
+        dst = t;
+    }
+    return src;
+}
+
 template <bool NUMERIC>
 __global__ void __launch_bounds__(kThreads)
     spgemm_rows(int m, int n, const int64_t *__restrict__ rowptr_a, const int32_t *__restrict__ col_a,
                 const float *__restrict__ val_a, const int64_t *__restrict__ rowptr_b, const int32_t *__restrict__ col_b,
                 const float *__restrict__ val_b, int slots, const int64_t *__restrict__ rowptr_c,
                 int64_t *__restrict__ col_c, float *__restrict__ val_c, SpgemmWs w) {
-    __shared__ int32_t sort_buf[kWarps][kSmemCols];
+    extern __shared__ int32_t spgemm_smem[];   // numeric pass: [kWarps][kSmemCols] sort buffers, [kWarps][kMaxRuns + 1] run starts
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     const int slot = blockIdx.x * kWarps + wib;
     if (slot >= slots) return;
@@ -103,14 +158,27 @@ __global__ void __launch_bounds__(kThreads)
         i = __shfl_sync(full, i, 0);
         if (i >= m) break;
         int nt = 0;
-        for (int64_t jj = rowptr_a[i]; jj < rowptr_a[i + 1]; jj++) {
+        const int64_t arow0 = rowptr_a[i], arow1 = rowptr_a[i + 1];
+        int32_t *rs = NUMERIC ? spgemm_smem + kWarps * kSmemCols + wib * (kMaxRuns + 1) : nullptr;
+        const bool track = NUMERIC && arow1 - arow0 <= kMaxRuns;   // record the runs of this row
+        bool ascending = true;                                      // every B row read so far ascends
+        for (int64_t jj = arow0; jj < arow1; jj++) {
             const int j = col_a[jj];
             const float a = NUMERIC ? val_a[jj] : 0.f;
             const int64_t b0 = rowptr_b[j], b1 = rowptr_b[j + 1];
+            if (track && lane == 0) rs[jj - arow0] = nt;
+            int lastc = -1;
             for (int64_t q0 = b0; q0 < b1; q0 += 32) {
                 const int64_t q = q0 + lane;
                 const bool act = q < b1;
                 const int c = act ? col_b[q] : -1 - lane;
+                if (track) {   // B's row ascending (equal neighbours allowed)?
+                    const int prev = __shfl_up_sync(full, c, 1);
+                    const bool bad = act && (lane > 0 ? c < prev : c < lastc);
+                    if (__any_sync(full, bad)) ascending = false;
+                    const int nact = (int)(b1 - q0 < 32 ? b1 - q0 : 32);
+                    lastc = __shfl_sync(full, c, nact - 1);
+                }
                 const bool dup = __any_sync(full, __popc(__match_any_sync(full, c)) > 1);
                 if (!dup) {
                     bool fresh = false;
@@ -152,13 +220,20 @@ __global__ void __launch_bounds__(kThreads)
             int P = 1;
             while (P < nt) P <<= 1;
             if (P <= kSmemCols) {
-                arr = sort_buf[wib];
+                arr = spgemm_smem + wib * kSmemCols;
                 for (int t = lane; t < P; t += 32) arr[t] = t < nt ? touched[t] : INT32_MAX;
+                __syncwarp();
+                if (nt > 1) warp_bitonic(arr, P, lane);
+            } else if (track && ascending) {   // long row: merge its ascending runs (O(nt log runs))
+                if (lane == 0) rs[arow1 - arow0] = nt;
+                __syncwarp();
+                arr = merge_runs(touched, w.merged + (size_t)slot * w.tcap, rs, (int)(arow1 - arow0), lane);
             } else {
                 for (int t = nt + lane; t < P; t += 32) arr[t] = INT32_MAX;
+                __syncwarp();
+                warp_bitonic(arr, P, lane);
             }
             __syncwarp();
-            if (nt > 1) warp_bitonic(arr, P, lane);
             const int64_t o = rowptr_c[i];
             for (int t = lane; t < nt; t += 32) {
                 const int c = arr[t];
@@ -212,7 +287,20 @@ extern "C" int ngt_csr_spgemm_numeric(int64_t m, int64_t n, const int64_t *rowpt
     if (!workspace || workspace_bytes < w.used) return NGT_ERR_WORKSPACE;
     if (m == 0) return NGT_OK;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    spgemm_rows<true><<<(unsigned)((slots + kWarps - 1) / kWarps), kThreads, 0, st>>>(
+    {   // the numeric pass's sort buffers exceed the 48 KiB default: raise the limit once per device
+        static std::mutex mu;
+        static bool set[64] = {};
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess) return NGT_ERR_CUDA;
+        std::lock_guard<std::mutex> lock(mu);
+        if (dev < 0 || dev >= 64 || !set[dev]) {
+            if (cudaFuncSetAttribute(spgemm_rows<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)kNumericSmem) != cudaSuccess)
+                return NGT_ERR_CUDA;
+            if (dev >= 0 && dev < 64) set[dev] = true;
+        }
+    }
+    spgemm_rows<true><<<(unsigned)((slots + kWarps - 1) / kWarps), kThreads, kNumericSmem, st>>>(
         (int)m, (int)n, rowptr_a, col_a, val_a, rowptr_b, col_b, val_b, (int)slots, rowptr_c, col_c, val_c, w);
     NGT_CHECK_LAUNCH();
     return NGT_OK;

@@ -64,6 +64,32 @@ def test_repeated_entries_signed_values_and_long_rows(cuda):
     assert int(np.diff(rp).max()) > 1024
 
 
+@pytest.mark.parametrize("case", ["merged runs", "many A entries", "unsorted B rows"])
+def test_rows_longer_than_the_shared_sort_buffer(cuda, case):
+    """Output rows of ~7,000 columns, beyond the 4,096-column shared-memory sort: merged from their
+    ascending per-A-entry runs (B's rows ascending, <= 32 A entries per row), or sorted in global
+    memory (an A row with more entries, or B rows out of order)."""
+    n = 20000
+    b = _rand_csr(n, n, n * 300, 11)
+    if case == "unsorted B rows":   # the same entries, each row's order shuffled
+        g = np.random.default_rng(12)
+        rows = np.repeat(np.arange(n), np.diff(b.indptr))
+        order = np.lexsort((g.random(b.nnz), rows))
+        b = sp.csr_matrix((b.data[order], b.indices[order], b.indptr.copy()), shape=(n, n))
+        assert not b.has_sorted_indices
+    per_row = 40 if case == "many A entries" else 30
+    g = np.random.default_rng(13)
+    m = 12
+    a_cols = np.stack([g.choice(n, per_row, replace=False) for _ in range(m)]).ravel()
+    a = sp.csr_matrix(((g.random(m * per_row) + 0.1).astype(np.float32), a_cols,
+                       np.arange(0, m * per_row + 1, per_row)), shape=(m, n))
+    rp, cl, vl = _ours(a, b)
+    assert int(np.diff(rp).min()) > 4096
+    orp, ocl, ovl = osg.csr_spgemm(a.indptr, a.indices, a.data, b.indptr, b.indices, b.data)
+    assert np.array_equal(rp, orp) and np.array_equal(cl, ocl)
+    assert np.array_equal(vl.view(np.uint32), ovl.view(np.uint32))
+
+
 def test_contract_checks(cuda):
     from neutrongt_b200.spgemm import csr_spgemm
     z = torch.zeros(1, dtype=torch.long, device="cuda")
