@@ -412,7 +412,8 @@ NGT_API int ngt_ppr_push_stats(const void *workspace, int64_t n, int64_t slots, 
  *   ngt_csr_spgemm_numeric   fills col_c int64 [nnz], val_c float [nnz] (after the symbolic call)
  *   rowptr_a / rowptr_b int64, col_a / col_b int32 (in [0, n)), val_a / val_b float
  *   slots    concurrent rows (one warp each); workspace from ngt_csr_spgemm_workspace_size
- *            (about 9 bytes x n per slot plus a power-of-two sort buffer)
+ *            (per slot: 5 bytes x n of accumulator and flags, plus two column buffers of
+ *            4 bytes x the power of two >= n, the touched list and its merge partner)
  * ---------------------------------------------------------------------------------- */
 NGT_API int ngt_csr_spgemm_workspace_size(int64_t m, int64_t n, int64_t slots, size_t *bytes /* host */);
 NGT_API int ngt_csr_spgemm_symbolic(int64_t m, int64_t n, const int64_t *rowptr_a, const int32_t *col_a,
