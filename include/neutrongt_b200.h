@@ -402,6 +402,19 @@ NGT_API int ngt_ppr_push_stats(const void *workspace, int64_t n, int64_t slots, 
                                ngt_stream_t stream);
 
 /* ------------------------------------------------------------------------------------
+ * CSR column check and narrowing for the PPR entry points (the reference's wrappers check the
+ * graph with torch reductions and convert it to int32 for cuSPARSE, appnp_backend.py:36-58,
+ * cusparse_ops.py:76-94; here one pass over the columns does both).
+ *   rowptr int64 [n+1], a valid row pointer (starts at 0, non-decreasing, rowptr[n] = nnz)
+ *   col    int64 [nnz] in, col32 int32 [nnz] out (the same values, narrowed)
+ *   flags  int32 [1] device: set by the call, bit 0 = a column outside [0, n), bit 1 = a column
+ *          below its predecessor within a row (rows not ascending)
+ * nnz > 0 needs n > 0.  Asynchronous on `stream`.
+ * ---------------------------------------------------------------------------------- */
+NGT_API int ngt_csr_col32_checked(int64_t n, int64_t nnz, const int64_t *rowptr, const int64_t *col, int32_t *col32,
+                                  int32_t *flags, ngt_stream_t stream);
+
+/* ------------------------------------------------------------------------------------
  * Sparse x sparse product C = A B of fp32 CSR matrices.
  *
  * Replaces csr_spgemm (NeutronGT/core/ppr_backends/cusparse_ops.py:97-114; cuSPARSE SpGEMM in

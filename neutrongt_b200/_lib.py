@@ -81,6 +81,7 @@ SIGNATURES = {
     "ngt_ppr_push_topk": [_i64, _p, _p, _dbl, _dbl, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, ctypes.c_size_t,
                           _p],
     "ngt_ppr_push_stats": [_p, _i64, _i64, _p, _p],
+    "ngt_csr_col32_checked": [_i64, _i64, _p, _p, _p, _p, _p],
     "ngt_csr_spgemm_workspace_size": [_i64, _i64, _i64, _sz_p],
     "ngt_csr_spgemm_symbolic": [_i64, _i64, _p, _p, _p, _p, _i64, _p, _p, ctypes.c_size_t, _p],
     "ngt_csr_spgemm_numeric": [_i64, _i64, _p, _p, _p, _p, _p, _p, _i64, _p, _p, _p, _p, ctypes.c_size_t, _p],

@@ -275,6 +275,55 @@ __global__ void __launch_bounds__(kPushThreads)
     }
 }
 
+// CSR column check and narrowing for the PPR kernels, one pass: each warp takes chunks of
+// kCheckChunk entries, lane l entries c0 + 32 i + l (coalesced).  Lane 0 finds the chunk's first row
+// by binary search over rowptr; each lane then advances its row while rowptr[row + 1] <= q.  Sets
+// bit 0 of *flags for a column outside [0, n), bit 1 for a column below its predecessor in the same row.
+constexpr int kCheckChunk = 1024;
+
+__global__ void __launch_bounds__(256)
+    csr_col32_kernel(int64_t n, int64_t nnz, const int64_t *__restrict__ rowptr, const int64_t *__restrict__ col,
+                     int32_t *__restrict__ col32, int32_t *__restrict__ flags) {
+    const unsigned full = 0xffffffffu;
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    int bad = 0;
+    for (int64_t c0 = warp * kCheckChunk; c0 < nnz; c0 += nwarps * kCheckChunk) {
+        int64_t row = 0;
+        if (lane == 0) {   // last row r with rowptr[r] <= c0 (rowptr[n] = nnz > c0, so r < n)
+            int64_t lo = 0, hi = n - 1;
+            while (lo < hi) {
+                const int64_t mid = (lo + hi + 1) >> 1;
+                if (rowptr[mid] <= c0) lo = mid;
+                else hi = mid - 1;
+            }
+            row = lo;
+        }
+        row = __shfl_sync(full, row, 0);
+        int64_t last = c0 > 0 ? col[c0 - 1] : 0;
+        for (int i = 0; i < kCheckChunk / 32; i++) {
+            const int64_t q = c0 + 32 * i + lane;
+            const bool act = q < nnz;
+            const int64_t c = act ? col[q] : 0;
+            int64_t r = row;
+            if (act)
+                while (rowptr[r + 1] <= q) r++;
+            const int64_t up = __shfl_up_sync(full, c, 1);
+            const int64_t prev = lane == 0 ? last : up;
+            if (act) {
+                if (c < 0 || c >= n) bad |= 1;
+                if (q != rowptr[r] && c < prev) bad |= 2;
+                col32[q] = (int32_t)c;
+            }
+            last = __shfl_sync(full, c, 31);
+            row = __shfl_sync(full, r, 31);
+            if (!__any_sync(full, q + 32 < nnz)) break;
+        }
+    }
+    if (bad) atomicOr(flags, bad);
+}
+
 }  // namespace
 }  // namespace ngt
 
@@ -331,5 +380,20 @@ extern "C" int ngt_ppr_push_stats(const void *workspace, int64_t n, int64_t slot
         return NGT_ERR_CUDA;
     pushes_and_reads[0] = (int64_t)c[1];
     pushes_and_reads[1] = (int64_t)c[2];
+    return NGT_OK;
+}
+
+extern "C" int ngt_csr_col32_checked(int64_t n, int64_t nnz, const int64_t *rowptr, const int64_t *col, int32_t *col32,
+                                     int32_t *flags, ngt_stream_t stream) {
+    if (n < 0 || nnz < 0 || !flags || !rowptr || (nnz > 0 && (n == 0 || !col || !col32)))
+        return NGT_ERR_INVALID_ARGUMENT;
+    if (n >= (int64_t)INT32_MAX || nnz >= (int64_t)INT32_MAX) return NGT_ERR_TOO_LARGE;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (cudaMemsetAsync(flags, 0, sizeof(int32_t), st) != cudaSuccess) return NGT_ERR_CUDA;
+    if (nnz == 0) return NGT_OK;
+    const int64_t chunks = (nnz + kCheckChunk - 1) / kCheckChunk;
+    const int64_t blocks = (chunks + 7) / 8 < 148 * 16 ? (chunks + 7) / 8 : 148 * 16;
+    csr_col32_kernel<<<(unsigned)blocks, 256, 0, st>>>(n, nnz, rowptr, col, col32, flags);
+    NGT_CHECK_LAUNCH();
     return NGT_OK;
 }

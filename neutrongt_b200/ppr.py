@@ -146,6 +146,22 @@ def personal_pagerank_appnp(edge_index, alpha, topk=100, num_iterations: int = 1
     return torch.stack([seeds, cols], dim=0), vals
 
 
+def _col32_checked(rowptr, col, n):
+    """col as int32 with its rows ascending, checked in one device pass (`ngt_csr_col32_checked`);
+    rows out of order are sorted first (the order PyG's get_ppr sorts the edge list into).  Needs a
+    validated rowptr."""
+    col32 = torch.empty(col.numel(), dtype=torch.int32, device=col.device)
+    flags = torch.empty(1, dtype=torch.int32, device=col.device)
+    _lib.check(_lib.lib().ngt_csr_col32_checked(n, col.numel(), _lib.ptr(rowptr), _lib.ptr(col), _lib.ptr(col32),
+                                                _lib.ptr(flags), _lib.stream_of(col)), "ngt_csr_col32_checked")
+    f = int(flags.item())
+    if f & 1:
+        raise ValueError(f"CSR col holds indices outside [0, {n})")
+    if f & 2:
+        col32 = _sorted_rows(rowptr, col, n).to(torch.int32).contiguous()
+    return col32
+
+
 def _sorted_rows(rowptr, col, n):
     """Columns ascending within each row (the order PyG's get_ppr sorts the edge list into)."""
     if col.numel() <= 1:
@@ -198,13 +214,11 @@ def personal_pagerank_torch_geometric(edge_index, alpha, topk=100, eps: float = 
         raise RuntimeError("graph exceeds the int32 index range of the PPR kernel")
     if int(rowptr[0].item()) != 0 or int(rowptr[-1].item()) != col.numel() or bool((rowptr[1:] < rowptr[:-1]).any()):
         raise ValueError("CSR rowptr must start at 0, be non-decreasing and end at col.numel()")
-    if col.numel() and (int(col.min().item()) < 0 or int(col.max().item()) >= n):
-        raise ValueError(f"CSR col holds indices outside [0, {n})")
+    col32 = _col32_checked(rowptr, col.contiguous(), n)
     s0 = 0 if source_start is None else max(0, min(int(source_start), n))
     s1 = n if source_end is None else max(s0, min(int(source_end), n))
     if s0 >= s1:
         return empty
-    col32 = _sorted_rows(rowptr, col, n).to(torch.int32).contiguous()
     nseeds = s1 - s0
     slots = _push_slots(n, nseeds, device, slots)
     L = _lib.lib()

@@ -69,6 +69,10 @@ def test_invalid_arguments_are_rejected_without_a_gpu():
     assert _lib.size_query(lib.ngt_duplicate_rerange_workspace_size, 1000, 50) >= 1000 * 4
     assert lib.ngt_halo_merge(10, None, None, None, 1, None, 0, 5, None, None, None, 0, None) == 1
     assert lib.ngt_duplicate_rerange(10, 1, None, None, 0, None, None, None, None, 0, None) == 1
+    # CSR column check: negative sizes, entries without rows and null pointers are refused
+    assert lib.ngt_csr_col32_checked(-1, 0, None, None, None, None, None) == 1
+    assert lib.ngt_csr_col32_checked(0, 5, None, None, None, None, None) == 1
+    assert lib.ngt_csr_col32_checked(4, 5, None, None, None, None, None) == 1
 
 
 def test_bf16_linear_shape_checks_without_a_gpu():

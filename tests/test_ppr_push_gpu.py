@@ -68,3 +68,42 @@ def test_dispatcher_contract(cuda):
     assert torch.equal(ei.cpu(), rei) and torch.equal(v.cpu(), rv) and v.dtype == torch.float32
     with pytest.raises(NotImplementedError):
         personal_pagerank(ei_in.cuda(), 0.15, topk=8, backend="torch_geometric", source_start=0, source_end=10)
+
+
+def test_csr_check_flags_and_unsorted_rows(cuda):
+    """`ngt_csr_col32_checked` (one pass: range check, row order, int32 narrowing) directly, and
+    through the wrapper: rows out of order give the sorted graph's result, a column outside [0, n)
+    is refused."""
+    from neutrongt_b200 import _lib, synthetic
+    from neutrongt_b200.ppr import personal_pagerank_torch_geometric
+    dev = torch.device("cuda")
+    rowptr, col = synthetic.chung_lu_graph(3000, 60000, seed=9)
+    rp, cl = rowptr.to(dev), col.to(dev)
+    n, nnz = rp.numel() - 1, cl.numel()
+
+    def flags_of(c):
+        out = torch.empty(nnz, dtype=torch.int32, device=dev)
+        f = torch.empty(1, dtype=torch.int32, device=dev)
+        _lib.check(_lib.lib().ngt_csr_col32_checked(n, nnz, _lib.ptr(rp), _lib.ptr(c), _lib.ptr(out), _lib.ptr(f),
+                                                    _lib.stream_of(c)), "ngt_csr_col32_checked")
+        return int(f.item()), out
+
+    f, out = flags_of(cl)
+    assert f == 0 and torch.equal(out.long(), cl)
+    # reverse every row: out of order wherever a row holds two or more distinct columns
+    deg = rp[1:] - rp[:-1]
+    row_of = torch.repeat_interleave(torch.arange(n, device=dev), deg)
+    rev = cl[torch.argsort(row_of * n + (n - 1 - cl), stable=True)].contiguous()
+    assert flags_of(rev)[0] == 2
+    bad = cl.clone()
+    bad[nnz // 2] = n
+    assert flags_of(bad)[0] & 1
+    bad[nnz // 2] = -1
+    assert flags_of(bad)[0] & 1
+    # through the wrapper
+    args = dict(topk=10, eps=1e-4, device=dev, return_fp64=True)
+    ei, v = personal_pagerank_torch_geometric(None, 0.15, csr_data={"rowptr": rp, "col": cl}, **args)
+    ei2, v2 = personal_pagerank_torch_geometric(None, 0.15, csr_data={"rowptr": rp, "col": rev}, **args)
+    assert torch.equal(ei, ei2) and torch.equal(v, v2)
+    with pytest.raises(ValueError):
+        personal_pagerank_torch_geometric(None, 0.15, csr_data={"rowptr": rp, "col": bad}, **args)
