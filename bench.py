@@ -753,7 +753,7 @@ def bench_spgemm(args, rank, world, dev, rowptr, col, ei, val, s0, s1):
                         "note": "no-reuse algorithmic bytes (A, B's selected rows, C); B (28 MB) is L2-resident"}}
     if rank == 0 and not args.skip_cpu:
         from oracle import spgemm as ospgemm
-        sample = 2000
+        sample = 300   # ~6 s of pure-Python row products
         ra = rp_a[:sample + 1].cpu()
         ca, va = col_a[:int(ra[-1])].cpu(), val_a[:int(ra[-1])].cpu()
         rb, cb, vb = rp_b.cpu(), col_b.cpu(), val_b.cpu()
