@@ -307,8 +307,8 @@ __global__ void __launch_bounds__(256)
             const bool act = q < nnz;
             const int64_t c = act ? col[q] : 0;
             int64_t r = row;
-            if (act)
-                while (rowptr[r + 1] <= q) r++;
+            if (act)   // bounded by the last row, so a malformed rowptr cannot walk past its end
+                while (r < n - 1 && rowptr[r + 1] <= q) r++;
             const int64_t up = __shfl_up_sync(full, c, 1);
             const int64_t prev = lane == 0 ? last : up;
             if (act) {
